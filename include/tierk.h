@@ -1,0 +1,186 @@
+/*
+ * tierk.h -- C ABI of libtierk.so, the B200 (sm_100a) frozen-weight linear
+ * path of tierlm: block-quantized weights dequantized for GEMV/GEMM, the fp16
+ * "x3" split GEMM, and the chunked-vocabulary LM head with running
+ * cross-entropy and its input gradient.
+ *
+ * The reference engine has no C ABI; its hot path is a set of internal C++
+ * statics called with raw device pointers.  Each entry point below names the
+ * reference function (file:line in the Eberhard-AIDEV/Tier tree) it replaces
+ * and keeps that function's units: row-major W[N,K] (out x in), X[M,K],
+ * Y[M,N] = X.W^T, dX[M,K] = dY.W, fp32 outputs, the reference's block
+ * layouts (tier/quant.h:25-29) and type codes (tier/quant.h:20-23).
+ *
+ * Conventions
+ *  - All data pointers are DEVICE pointers owned by the caller, except where
+ *    noted.  The library owns only its context workspace.
+ *  - Every call is asynchronous on `stream` (a cudaStream_t; NULL = legacy
+ *    default stream) and returns a status; no call aborts the process.
+ *    tk_last_error_string() describes the last failure on the calling thread.
+ *  - A context is bound to one device; use it from one host thread at a time.
+ *  - Shapes are validated on the host (block multiples, alignment); device
+ *    kernels never trap: bounded waits write a code into the context status
+ *    word, read by tk_sync_status().
+ */
+#ifndef TIERK_H
+#define TIERK_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum tk_status {
+    TK_OK = 0,
+    TK_ERR_INVALID = 1,     /* bad shape, alignment, pointer or type code        */
+    TK_ERR_UNSUPPORTED = 2, /* valid request this build does not implement       */
+    TK_ERR_CUDA = 3,        /* CUDA runtime/driver error                         */
+    TK_ERR_NOMEM = 4,       /* workspace growth failed                           */
+    TK_ERR_TIMEOUT = 5,     /* a device-side bounded wait expired                */
+    TK_ERR_DEVICE = 6       /* device kernel reported invalid input              */
+} tk_status;
+
+/* Weight block types: the reference's QT_* codes (tier/quant.h:20-23). */
+enum {
+    TK_F32 = 0, TK_F16 = 1, TK_Q4_0 = 2, TK_Q4_1 = 3, TK_Q5_0 = 6, TK_Q5_1 = 7,
+    TK_Q8_0 = 8, TK_Q2_K = 10, TK_Q3_K = 11, TK_Q4_K = 12, TK_Q5_K = 13,
+    TK_Q6_K = 14, TK_BF16 = 30,
+    /* fp32 weight stored as two fp16 planes hi = f16(W*2^s), lo = f16(W*2^s - hi);
+       plane lo starts rows*row_bytes bytes after plane hi (see tk_weight_split_f32) */
+    TK_F16X2 = 100
+};
+
+/* Element types of activations / gradients / dequant output. */
+enum { TK_DT_F32 = 0, TK_DT_F16 = 1, TK_DT_BF16 = 2 };
+
+/* Tensor-core product sets for the split GEMM.
+ *  TK_X3_REF : X (fp32) split into three fp16 parts h,m,l; W single fp16;
+ *              products W.xl + W.xm + W.xh -- the reference's fp3gemm
+ *              (tier/tier.cpp:922-943).
+ *  TK_X3_HHL : X split into h,l and W into h,l (TK_F16X2);
+ *              products Xh.Wh + Xh.Wl + Xl.Wh (near-fp32 for fp32 W).
+ *  TK_X2     : X split into h,l; W single fp16; products W.xl + W.xh.
+ *  TK_X1     : one product of fp16 X (or bf16 X converted exactly) and fp16 W.
+ *  TK_X3_AUTO: TK_X3_REF for fp32 X with fp16/quant W, TK_X3_HHL for
+ *              TK_F16X2 W, TK_X1 for fp16/bf16 X. */
+enum { TK_X3_AUTO = 0, TK_X3_REF = 1, TK_X3_HHL = 2, TK_X2 = 3, TK_X1 = 4 };
+
+typedef struct tk_ctx tk_ctx;
+
+/* A frozen weight W[rows=N, cols=K] resident in device memory. */
+typedef struct tk_weight {
+    int qtype;          /* TK_* block type                                           */
+    int rows;           /* N, output features                                        */
+    int cols;           /* K, input features (multiple of the block size)            */
+    int scale_log2;     /* TK_F16X2: planes hold W * 2^scale_log2; else 0            */
+    size_t row_bytes;   /* bytes per row (q_row_bytes(qtype, cols); fp16 plane row)  */
+    const void *data;   /* device pointer to row 0                                   */
+} tk_weight;
+
+/* ---- context ------------------------------------------------------------ */
+tk_status tk_init(int device, tk_ctx **out);
+void tk_destroy(tk_ctx *ctx);
+const char *tk_last_error_string(void);
+/* Grow the context workspace to at least `bytes` now (entry points grow it on
+ * demand otherwise, which synchronizes the device). */
+tk_status tk_reserve(tk_ctx *ctx, size_t bytes);
+size_t tk_workspace_bytes(const tk_ctx *ctx);
+/* Synchronize `stream` and report any device-side status (timeouts, invalid
+ * input detected by a kernel) raised since the last call; clears it. */
+tk_status tk_sync_status(tk_ctx *ctx, void *stream);
+/* Number of kernels this context has launched (diagnostics / bench). */
+uint64_t tk_launch_count(const tk_ctx *ctx);
+
+/* ---- block formats ------------------------------------------------------ */
+/* Bytes of one row of `cols` elements of `qtype`; 0 if unsupported or cols is
+ * not a block multiple.  Replaces q_row_bytes (tier/quant.h:33). */
+size_t tk_row_bytes(int qtype, int cols);
+
+/* ---- dequant ------------------------------------------------------------ */
+/* out[r, c] = value of element c of row r0+r, for r < nrows, as fp32, fp16
+ * (round-to-nearest-even of the fp32 value) or bf16.  Bit-exact with
+ * q_val / tier_fp16(q_val).  Replaces dq_launch / dq_k (tier/tier.cpp:294-298).
+ * Supported qtype: all TK_* block types except TK_F16X2. */
+tk_status tk_dequant(tk_ctx *ctx, int qtype, const void *blocks, size_t row_bytes,
+                     int r0, int nrows, int cols, int out_dtype, void *out, void *stream);
+
+/* ---- decode GEMV (M = 1..16) -------------------------------------------- */
+/* y[m, n] = sum_k W(n, k) * x[m, k] for m < M, n < N, fp32 x and y.
+ * qtype: TK_Q8_0, TK_Q4_K, TK_Q5_K, TK_Q6_K, TK_Q4_0, TK_F16, TK_BF16, TK_F32.
+ * Replaces gemv_q (tier/tier.cpp:300-306) and gemv<T> (tier/tier.cpp:2261-2268)
+ * as dispatched by chat_lin (tier/tier.cpp:2351-2378). */
+tk_status tk_gemv(tk_ctx *ctx, int qtype, const void *W, size_t row_bytes, int N, int K,
+                  const float *x, int ldx, int M, float *y, int ldy, void *stream);
+
+/* ---- linear layers (tensor cores) --------------------------------------- */
+/* Y[M, N] = X[M, K] . W^T (+ Y if beta == 1).  X dtype per x_dtype with row
+ * stride ldx (elements); Y fp32 with row stride ldy.  Block-quantized W is
+ * dequantized bit-exactly to fp16 first (as the reference's training path,
+ * tier/tier.cpp:513-518), then multiplied on tcgen05 tensor cores with fp32
+ * accumulation.  Replaces linear / low3_linear (tier/tier.cpp:1186-1216). */
+tk_status tk_linear_fwd(tk_ctx *ctx, const tk_weight *W, const void *X, int x_dtype, int M,
+                        int ldx, float *Y, int ldy, float beta, int products, void *stream);
+
+/* dX[M, K] = dY[M, N] . W (+ dX if beta == 1).  Replaces linear_dx and
+ * linear_dx_acc (tier/tier.cpp:1217-1238). */
+tk_status tk_linear_dx(tk_ctx *ctx, const tk_weight *W, const void *dY, int dy_dtype, int M,
+                       int lddy, float *dX, int lddx, float beta, int products, void *stream);
+
+/* Split an fp32 weight into the TK_F16X2 planes: planes[0 .. rows*cols) = hi,
+ * planes[rows*cols .. 2*rows*cols) = lo, both W * 2^s with s chosen so that
+ * max|W| * 2^s lies in [2^14, 2^15).  *scale_log2 receives s (written after the
+ * stream work completes; the call synchronizes `stream`).  New in this
+ * library: the reference keeps one fp16 copy of W (tier/tier.cpp:2507-2512). */
+tk_status tk_weight_split_f32(tk_ctx *ctx, const float *W32, int rows, int cols, uint16_t *planes,
+                              int *scale_log2, void *stream);
+
+/* h = f16(x), m = f16(x - h), l = f16((x - h) - m) elementwise, unscaled --
+ * exactly split3_fp_k (tier/tier.cpp:869-870). */
+tk_status tk_split3(tk_ctx *ctx, const float *x, size_t n, uint16_t *h, uint16_t *m, uint16_t *l,
+                    void *stream);
+
+/* ---- LM head + cross-entropy over a vocabulary shard --------------------- */
+/* The reference runs two passes over vocab chunks (tier/tier.cpp:3184-3266).
+ * W: fp16 [V_shard, H] rows v0 .. v0+V_shard of the full head; X: fp32 [T, H]
+ * (final normed hidden); labels: int32 [T] (row t predicts labels[t+1]);
+ * mask: uint8 [T] (loss mask, row T-1 never predicts).  softcap > 0 applies
+ * cap*tanh(l/cap).  `chunk` = vocab rows per chunk (multiple of 256).
+ * `products`: TK_X3_REF (3 parts of X and of dlogit) or TK_X2 (2 parts).
+ *
+ * Pass 1 merges this shard's logits into the running state, in vocabulary
+ * order: rmax/rsum (fp64, init -1e30 / 0), amax (init -1) and tgt (init 0),
+ * each [T-1].  Replaces the lse_chunk_kernel loop (tier/tier.cpp:3209-3222,
+ * 750-759). */
+tk_status tk_lmhead_stats(tk_ctx *ctx, const uint16_t *W, int v0, int V_shard, int H,
+                          const float *X, int T, const int32_t *labels, const uint8_t *mask,
+                          float softcap, int chunk, int products, double *rmax, double *rsum,
+                          int32_t *amax, float *tgt, void *stream);
+
+/* Pass 2: dX[T, H] += sum_v dlogit[t, v] * W[v, :] with dlogit as
+ * dlogit_kernel (tier/tier.cpp:736-748) from the FINAL (all-shard) rmax/rsum.
+ * n_loss = number of rows with mask != 0 among rows 0..T-2.
+ * Replaces the pass-2 loop (tier/tier.cpp:3247-3266). */
+tk_status tk_lmhead_grad(tk_ctx *ctx, const uint16_t *W, int v0, int V_shard, int H,
+                         const float *X, int T, const int32_t *labels, const uint8_t *mask,
+                         int n_loss, float softcap, int chunk, int products, const double *rmax,
+                         const double *rsum, float *dX, void *stream);
+
+/* loss_sum = sum over masked rows t < T-1 of (rmax + log(rsum) - tgt);
+ * hits = count of amax[t] == labels[t+1] (tier/tier.cpp:3227-3228).
+ * Writes one double and one int to device memory. */
+tk_status tk_lmhead_loss(tk_ctx *ctx, int T, const int32_t *labels, const uint8_t *mask,
+                         const double *rmax, const double *rsum, const int32_t *amax,
+                         const float *tgt, double *loss_sum, int32_t *hits, void *stream);
+
+/* Vocab-sharded merge helper: rsum *= exp(rmax_local - rmax_global) and
+ * rmax_local = rmax_global, for rows t < n (run between an all-reduce MAX of
+ * rmax and an all-reduce SUM of rsum). */
+tk_status tk_lmhead_rescale(tk_ctx *ctx, int n, double *rmax_local, double *rsum_local,
+                            const double *rmax_global, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* TIERK_H */

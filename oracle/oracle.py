@@ -1,0 +1,177 @@
+"""ctypes wrapper of the CPU checkers.  TEST INFRASTRUCTURE ONLY: imported by
+tests/, __graft_entry__.smoke() and bench.py's CPU-baseline legs, never by the
+product (tier_b200/).
+
+  Oracle      -- oracle/libtkoracle.so, this repository's C restatement of the
+                 reference arithmetic (tk_oracle.c, citations there).
+  RefOracle   -- oracle/_ref/libtkref.so, the reference's own quant.h and
+                 kernel bodies compiled from its sources (ref_harness.cpp);
+                 absent when the reference tree was not available at build time.
+"""
+from __future__ import annotations
+
+import ctypes
+import subprocess
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+P = ctypes.c_void_p
+
+
+def _p(a: np.ndarray):
+    return a.ctypes.data_as(P)
+
+
+def build(quiet: bool = True) -> None:
+    """Run oracle/Makefile (compiles _ref too when the reference tree exists)."""
+    r = subprocess.run(["make", "-C", str(HERE)], capture_output=True, text=True)
+    if r.returncode:
+        raise RuntimeError("oracle build failed:\n" + r.stdout + r.stderr)
+    if not quiet:
+        print(r.stdout)
+
+
+class Oracle:
+    def __init__(self):
+        so = HERE / "libtkoracle.so"
+        if not so.exists():
+            build()
+        L = ctypes.CDLL(str(so))
+        L.tko_q_val.restype = ctypes.c_float
+        L.tko_row_bytes.restype = ctypes.c_size_t
+        L.tko_h2f.restype = ctypes.c_float
+        L.tko_h2f.argtypes = [ctypes.c_uint16]
+        L.tko_f2h.restype = ctypes.c_uint16
+        L.tko_f2h.argtypes = [ctypes.c_float]
+        L.tko_f2bf.restype = ctypes.c_uint16
+        L.tko_f2bf.argtypes = [ctypes.c_float]
+        self.L = L
+
+    def row_bytes(self, qtype: int, cols: int) -> int:
+        return int(self.L.tko_row_bytes(qtype, cols))
+
+    def dequant(self, blocks: np.ndarray, qtype: int, rows: int, cols: int, out_dtype: int = 0,
+                row_bytes: int | None = None) -> np.ndarray:
+        rb = row_bytes or self.row_bytes(qtype, cols)
+        b = np.ascontiguousarray(blocks, dtype=np.uint8)
+        out = np.zeros((rows, cols), np.float32 if out_dtype == 0 else np.uint16)
+        self.L.tko_dequant(_p(b), ctypes.c_size_t(rb), qtype, 0, rows, cols, out_dtype, _p(out))
+        return out
+
+    def gemv_warp_order(self, blocks, qtype, N, K, x):
+        b = np.ascontiguousarray(blocks, dtype=np.uint8)
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        y = np.zeros(N, np.float32)
+        self.L.tko_gemv_q_warp_order(_p(b), ctypes.c_size_t(self.row_bytes(qtype, K)), qtype, _p(x), _p(y), N, K)
+        return y
+
+    def qgemm_f64(self, blocks, qtype, N, K, X):
+        b = np.ascontiguousarray(blocks, dtype=np.uint8)
+        X = np.ascontiguousarray(X, dtype=np.float32)
+        M = X.shape[0]
+        Y = np.zeros((M, N), np.float64)
+        self.L.tko_qgemm_f64(_p(b), ctypes.c_size_t(self.row_bytes(qtype, K)), qtype, _p(X), _p(Y), M, N, K)
+        return Y
+
+    def split3(self, x):
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        n = x.size
+        h, m, l = (np.zeros(n, np.uint16) for _ in range(3))
+        self.L.tko_split3_f16(_p(x), _p(h), _p(m), _p(l), ctypes.c_size_t(n))
+        return h, m, l
+
+    def dlogit(self, lg, rmax, rsum, labels, mask, v0, n_loss, cap):
+        T, vc = lg.shape
+        dl = np.zeros((T, vc), np.float32)
+        self.L.tko_dlogit(_p(np.ascontiguousarray(lg, np.float32)), _p(np.ascontiguousarray(rmax, np.float64)),
+                          _p(np.ascontiguousarray(rsum, np.float64)), _p(np.ascontiguousarray(labels, np.int32)),
+                          _p(dl), T, vc, v0, n_loss, _p(np.ascontiguousarray(mask, np.uint8)), ctypes.c_float(cap))
+        return dl
+
+    def lse_chunk(self, lg, rmax, rsum, amax, tgt, labels, mask, v0):
+        n_pred = rmax.size
+        T, vc = lg.shape
+        self.L.tko_lse_chunk(_p(np.ascontiguousarray(lg, np.float32)), _p(rmax), _p(rsum), _p(amax), _p(tgt),
+                             _p(np.ascontiguousarray(labels, np.int32)), _p(np.ascontiguousarray(mask, np.uint8)),
+                             n_pred, vc, v0)
+
+    def lmhead_f64(self, W16: np.ndarray, X: np.ndarray, labels, mask, cap: float, chunk: int):
+        """Whole two-pass LM head in fp64 (tier/tier.cpp:3184-3266).
+        Returns (loss_sum, n_loss, amax[T-1], dX[T,H] float64)."""
+        V, H = W16.shape
+        T = X.shape[0]
+        W16 = np.ascontiguousarray(W16, np.uint16)
+        X = np.ascontiguousarray(X, np.float32)
+        labels = np.ascontiguousarray(labels, np.int32)
+        mask = np.ascontiguousarray(mask, np.uint8)
+        loss = ctypes.c_double(0)
+        n_loss = ctypes.c_int(0)
+        amax = np.zeros(T - 1, np.int32)
+        dX = np.zeros((T, H), np.float64)
+        lg = np.zeros(T * min(chunk, V), np.float32)
+        rmax = np.zeros(T - 1, np.float64)
+        rsum = np.zeros(T - 1, np.float64)
+        tgt = np.zeros(T - 1, np.float32)
+        self.L.tko_lmhead_f64(_p(W16), V, H, _p(X), T, _p(labels), _p(mask), ctypes.c_float(cap), chunk,
+                              ctypes.byref(loss), ctypes.byref(n_loss), _p(amax), _p(dX), _p(lg), _p(rmax),
+                              _p(rsum), _p(tgt))
+        return loss.value, n_loss.value, amax, dX, rmax, rsum, tgt
+
+
+class RefOracle:
+    """The reference's own code (quant.h, extracted kernel bodies) built in place."""
+
+    SO = HERE / "_ref" / "libtkref.so"
+
+    @classmethod
+    def available(cls) -> bool:
+        return cls.SO.exists()
+
+    def __init__(self):
+        L = ctypes.CDLL(str(self.SO))
+        L.ref_q_val.restype = ctypes.c_float
+        L.ref_row_bytes.restype = ctypes.c_size_t
+        self.L = L
+
+    def dequant(self, blocks, qtype, rows, cols, out_dtype=0):
+        rb = int(self.L.ref_row_bytes(qtype, cols))
+        b = np.ascontiguousarray(blocks, dtype=np.uint8)
+        out = np.zeros((rows, cols), np.float32 if out_dtype == 0 else np.uint16)
+        self.L.ref_dequant(_p(b), ctypes.c_size_t(rb), qtype, 0, rows, cols, out_dtype, _p(out))
+        return out
+
+    def quantize_row(self, qtype, x):
+        x = np.ascontiguousarray(x, np.float32)
+        rb = int(self.L.ref_row_bytes(qtype, x.size))
+        o = np.zeros(rb, np.uint8)
+        assert self.L.ref_q_row(qtype, _p(x), _p(o), x.size) == 1
+        return o
+
+    def split3(self, x):
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        n = x.size
+        h, m, l = (np.zeros(n, np.uint16) for _ in range(3))
+        self.L.ref_split3_fp16(_p(x), _p(h), _p(m), _p(l), ctypes.c_size_t(n))
+        return h, m, l
+
+    def qgemm_fwd(self, blocks, qtype, n0, nrows, K, X, threads):
+        """CPU baseline: Y[M, nrows] via q_val row expansion + fp32 dots."""
+        b = np.ascontiguousarray(blocks, dtype=np.uint8)
+        X = np.ascontiguousarray(X, np.float32)
+        M = X.shape[0]
+        Y = np.zeros((M, nrows), np.float32)
+        rb = int(self.L.ref_row_bytes(qtype, K))
+        self.L.ref_cpu_qgemm_fwd(_p(b), ctypes.c_size_t(rb), qtype, n0, nrows, K, _p(X), M, _p(Y), nrows, threads)
+        return Y
+
+    def qgemm_dx(self, blocks, qtype, n0, nrows, K, dY, threads):
+        b = np.ascontiguousarray(blocks, dtype=np.uint8)
+        dY = np.ascontiguousarray(dY, np.float32)
+        M = dY.shape[0]
+        dX = np.zeros((M, K), np.float32)
+        rb = int(self.L.ref_row_bytes(qtype, K))
+        self.L.ref_cpu_qgemm_dx(_p(b), ctypes.c_size_t(rb), qtype, n0, nrows, K, _p(dY), dY.shape[1], M, _p(dX),
+                                threads)
+        return dX

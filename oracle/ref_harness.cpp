@@ -1,0 +1,172 @@
+// ref_harness.cpp -- thin C-ABI shim over the REFERENCE's own code, for tests
+// and the timed CPU baseline only (never linked into the product).
+//
+// It is compiled (oracle/Makefile) against the reference's quant.h where it
+// lies (tier/quant.h, tier/quant_tables.h) and against kernel bodies that
+// oracle/extract_ref.py copies out of tier/tier.cpp into oracle/_ref/ at build
+// time -- the same extraction the reference's own test tier/cpu_gpu_sim.py:13-27
+// performs.  Nothing from the reference is stored in this repository; the
+// built .so lives in oracle/_ref/ (git-ignored).
+//
+// Exports:
+//   ref_q_val / ref_dequant      tier/quant.h:59-121 (q_val), tier/tier.cpp:294-296 (dq_k)
+//   ref_q_row                    tier/quant.h:201-204 (CPU quantizers)
+//   ref_split3_fp16              tier/tier.cpp:869-870 (split3_fp_k, extracted)
+//   ref_dlogit                   tier/tier.cpp:736-748 (dlogit_kernel, extracted)
+//   ref_softcap                  tier/tier.cpp:728 (softcap_kernel, extracted)
+//   ref_cpu_qgemm_fwd / _dx      CPU baseline: q_val row expansion + the
+//                                cpu_gemm_fwd / cpu_gemm_dx loop structure
+//                                (tier/tier.cpp:1049-1099) over fp32 rows,
+//                                rows split across threads like pool_run
+//                                (tier/tier.cpp:1041-1046).
+#include "quant.h"
+#include <cstdint>
+#include <cstring>
+#include <cmath>
+#include <thread>
+#include <vector>
+#include <algorithm>
+#include <functional>
+
+// ---- emulated CUDA launch environment for the extracted kernel bodies ----
+namespace refsim {
+struct dim { unsigned x = 0, y = 0, z = 0; };
+static thread_local dim threadIdx, blockIdx, blockDim;
+}
+using refsim::threadIdx;
+using refsim::blockIdx;
+using refsim::blockDim;
+#define __host__
+#define __device__
+#define __global__
+typedef unsigned short ref_u16;
+#include "ref_kernels.inc"   // generated: tier_fp16 + split3_fp_k + dlogit_kernel + softcap_kernel
+
+extern "C" {
+
+float ref_q_val(const uint8_t* row, int type, int col) { return q_val(row, type, col); }
+
+size_t ref_row_bytes(int type, int cols) { return q_row_bytes(type, cols); }
+
+// out_dtype: 0 fp32, 1 fp16 (tier_fp16 RNE, the training storage path)
+void ref_dequant(const uint8_t* W, size_t rb, int type, int r0, int nrows, int cols, int out_dtype, void* out)
+{
+    for (int r = 0; r < nrows; ++r) {
+        const uint8_t* row = W + (size_t)(r0 + r) * rb;
+        for (int c = 0; c < cols; ++c) {
+            float v = q_val(row, type, c);
+            size_t o = (size_t)r * cols + c;
+            if (out_dtype == 0) ((float*)out)[o] = v;
+            else ((uint16_t*)out)[o] = tier_fp16(v).bits;
+        }
+    }
+}
+
+int ref_q_row(int type, const float* x, uint8_t* o, int k) { return q_row(type, x, o, k) ? 1 : 0; }
+
+void ref_split3_fp16(const float* x, uint16_t* h, uint16_t* m, uint16_t* l, size_t n)
+{
+    blockDim.x = 256;
+    for (size_t i = 0; i < n; ++i) {
+        blockIdx.x = (unsigned)(i / 256); threadIdx.x = (unsigned)(i % 256);
+        split3_fp_k(x, (tier_fp16*)h, (tier_fp16*)m, (tier_fp16*)l, n);
+    }
+}
+
+void ref_dlogit(const float* lg, const double* rmax, const double* rsum, const int32_t* tokens, float* dl,
+                int seq_len, int vc, int v0, int n_loss, const unsigned char* mask, float cap)
+{
+    blockDim.x = 256;
+    size_t n = (size_t)seq_len * vc;
+    for (size_t i = 0; i < n; ++i) {
+        blockIdx.x = (unsigned)(i / 256); threadIdx.x = (unsigned)(i % 256);
+        dlogit_kernel(lg, rmax, rsum, tokens, dl, seq_len, vc, v0, n_loss, mask, cap);
+    }
+}
+
+void ref_softcap(float* lg, float cap, size_t n)
+{
+    blockDim.x = 256;
+    for (size_t i = 0; i < n; ++i) {
+        blockIdx.x = (unsigned)(i / 256); threadIdx.x = (unsigned)(i % 256);
+        softcap_kernel(lg, cap, n);
+    }
+}
+
+// ---- CPU baseline ----------------------------------------------------------
+static void run_rows(int n_items, int threads, const std::function<void(int, int)>& f)
+{
+    if (threads < 2) { f(0, n_items); return; }
+    std::vector<std::thread> th;
+    for (int t = 0; t < threads; ++t) {
+        int a = (int)((long long)n_items * t / threads), b = (int)((long long)n_items * (t + 1) / threads);
+        if (b > a) th.emplace_back(f, a, b);
+    }
+    for (auto& x : th) x.join();
+}
+
+// Y[m, n0+i] = sum_k X[m,k] * q_val(W[n0+i], k) for i < nrows.  ldy = row
+// stride of Y.  Each worker expands one weight row to fp32 with q_val and
+// dots it against 4 token rows at a time (cpu_gemm_fwd's blocking).
+void ref_cpu_qgemm_fwd(const uint8_t* W, size_t rb, int type, int n0, int nrows, int K,
+                       const float* X, int M, float* Y, int ldy, int threads)
+{
+    run_rows(nrows, threads, [&](int a, int b) {
+        std::vector<float> w(K);
+        for (int i = a; i < b; ++i) {
+            const uint8_t* row = W + (size_t)(n0 + i) * rb;
+            for (int k = 0; k < K; ++k) w[k] = q_val(row, type, k);
+            for (int m = 0; m < M; m += 4) {
+                int mm = std::min(4, M - m);
+                float r[4] = {0, 0, 0, 0};
+                for (int j = 0; j < mm; ++j) {
+                    const float* x = X + (size_t)(m + j) * K;
+                    float acc = 0;
+#pragma omp simd reduction(+ : acc)
+                    for (int k = 0; k < K; ++k) acc += w[k] * x[k];
+                    r[j] = acc;
+                }
+                for (int j = 0; j < mm; ++j) Y[(size_t)(m + j) * ldy + i] = r[j];
+            }
+        }
+    });
+}
+
+// dX[m,k] = sum_{i<nrows} dY[m, i] * q_val(W[n0+i], k); per-thread partial
+// [M,K] accumulators summed at the end (cpu_gemm_dx's structure).
+void ref_cpu_qgemm_dx(const uint8_t* W, size_t rb, int type, int n0, int nrows, int K,
+                      const float* dY, int lddy, int M, float* dX, int threads)
+{
+    int T = threads < 1 ? 1 : threads;
+    std::vector<std::vector<float>> part(T);
+    std::vector<std::thread> th;
+    auto job = [&](int id, int a, int b) {
+        auto& acc = part[id];
+        acc.assign((size_t)M * K, 0.0f);
+        std::vector<float> w(K);
+        for (int i = a; i < b; ++i) {
+            const uint8_t* row = W + (size_t)(n0 + i) * rb;
+            for (int k = 0; k < K; ++k) w[k] = q_val(row, type, k);
+            for (int m = 0; m < M; ++m) {
+                float c = dY[(size_t)m * lddy + i];
+                if (c == 0.0f) continue;
+                float* o = acc.data() + (size_t)m * K;
+#pragma omp simd
+                for (int k = 0; k < K; ++k) o[k] += c * w[k];
+            }
+        }
+    };
+    for (int t = 0; t < T; ++t) {
+        int a = (int)((long long)nrows * t / T), b = (int)((long long)nrows * (t + 1) / T);
+        th.emplace_back(job, t, a, b);
+    }
+    for (auto& x : th) x.join();
+    std::memset(dX, 0, (size_t)M * K * sizeof(float));
+    for (int t = 0; t < T; ++t) {
+        if (part[t].size() != (size_t)M * K) continue;
+        const float* a = part[t].data();
+        for (size_t i = 0, n = (size_t)M * K; i < n; ++i) dX[i] += a[i];
+    }
+}
+
+}  // extern "C"

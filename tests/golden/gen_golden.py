@@ -1,0 +1,184 @@
+#!/usr/bin/env python3
+"""Generate the committed golden fixtures under tests/golden/.
+
+Run in a container that has the reference tree and gguf-py 0.19.0 (the
+reference's own dequant oracle, tier/check_quant.py:5,71); the outputs are small
+.npz files that travel with the repository, so the tests never need either.
+
+Sources of truth recorded per fixture:
+  dequant_golden.npz   random blocks generated like tier/check_quant.py:27-48
+                       (random bytes, valid fp16 scale fields); expected fp32
+                       values from gguf-py `quants.dequantize`, cross-checked
+                       bit-for-bit against the reference's quant.h q_val built
+                       in place (oracle/_ref/libtkref.so), plus the fp16-storage
+                       values tier_fp16(q_val) the training path stores
+                       (tier/tier.cpp:294-296).
+  quantize_golden.npz  reference q_row bytes (tier/quant.h:201-204) for
+                       Q8_0/Q4_K/Q5_K/Q6_K on seeded rows; Q8_0 also equals
+                       gguf-py's quantizer (tier/check_quant.py:114).
+  split3_golden.npz    reference split3_fp_k (tier/tier.cpp:869-870), run
+                       from the extracted kernel body, on seeded and edge values.
+  dlogit_golden.npz    reference dlogit_kernel (tier/tier.cpp:736-748) on a
+                       small seeded chunk, with and without softcap.
+
+usage: python tests/golden/gen_golden.py   (from the repository root)
+"""
+import ctypes
+import os
+import sys
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parents[2]
+HERE = Path(__file__).resolve().parent
+
+
+def load_ref():
+    so = ROOT / "oracle" / "_ref" / "libtkref.so"
+    if not so.exists():
+        sys.exit("build oracle/_ref first: make -C oracle")
+    lib = ctypes.CDLL(str(so))
+    lib.ref_q_val.restype = ctypes.c_float
+    lib.ref_row_bytes.restype = ctypes.c_size_t
+    return lib
+
+
+P = ctypes.c_void_p
+
+
+def ptr(a):
+    return a.ctypes.data_as(P)
+
+
+# (type code, gguf name, elems/block, bytes/block, fp16 scale byte offsets)
+TYPES = [
+    (0, "F32", 1, 4, []),
+    (1, "F16", 1, 2, []),
+    (30, "BF16", 1, 2, []),
+    (2, "Q4_0", 32, 18, [0]),
+    (3, "Q4_1", 32, 20, [0, 2]),
+    (6, "Q5_0", 32, 22, [0]),
+    (7, "Q5_1", 32, 24, [0, 2]),
+    (8, "Q8_0", 32, 34, [0]),
+    (10, "Q2_K", 256, 84, [80, 82]),
+    (11, "Q3_K", 256, 110, [108]),
+    (12, "Q4_K", 256, 144, [0, 2]),
+    (13, "Q5_K", 256, 176, [0, 2]),
+    (14, "Q6_K", 256, 210, [208]),
+]
+ROWS, COLS = 4, 512
+
+
+def gen_dequant(ref):
+    from gguf import quants, constants
+    rng = np.random.default_rng(7)
+    out = {}
+    for code, name, be, bb, halfs in TYPES:
+        gt = getattr(constants.GGMLQuantizationType, name)
+        if be == 1:
+            if name == "F32":
+                x = rng.standard_normal(ROWS * COLS).astype(np.float32)
+                b = x.view(np.uint8)
+            elif name == "F16":
+                x = rng.standard_normal(ROWS * COLS).astype(np.float16)
+                b = x.view(np.uint8)
+            else:
+                x = rng.standard_normal(ROWS * COLS).astype(np.float32)
+                b = (x.view(np.uint32) >> 16).astype(np.uint16).view(np.uint8)
+            b = b.reshape(ROWS, -1).copy()
+        else:
+            nb = ROWS * COLS // be
+            b = rng.integers(0, 256, size=(nb, bb), dtype=np.uint8)
+            for o in halfs:
+                h = (rng.standard_normal(nb) * 0.02).astype(np.float16).view(np.uint8).reshape(nb, 2)
+                b[:, o:o + 2] = h
+            b = b.reshape(ROWS, -1).copy()
+        want = quants.dequantize(b.reshape(-1), gt).reshape(ROWS, COLS).astype(np.float32)
+        rb = ref.ref_row_bytes(code, COLS)
+        assert rb == b.shape[1], (name, rb, b.shape)
+        got = np.zeros((ROWS, COLS), np.float32)
+        ref.ref_dequant(ptr(b), ctypes.c_size_t(rb), code, 0, ROWS, COLS, 0, ptr(got))
+        if not np.array_equal(got.view(np.uint32), want.view(np.uint32)):
+            sys.exit(f"{name}: reference quant.h disagrees with gguf-py -- not writing fixtures")
+        f16 = np.zeros((ROWS, COLS), np.uint16)
+        ref.ref_dequant(ptr(b), ctypes.c_size_t(rb), code, 0, ROWS, COLS, 1, ptr(f16))
+        out[f"{name}_blocks"] = b
+        out[f"{name}_f32"] = want
+        out[f"{name}_f16"] = f16
+        out[f"{name}_type"] = np.int32(code)
+        print(f"{name:6s} dequant: gguf-py == reference quant.h (bit-exact), {ROWS}x{COLS}")
+    np.savez_compressed(HERE / "dequant_golden.npz", **out)
+
+
+def gen_quantize(ref):
+    from gguf import quants, constants
+    rng = np.random.default_rng(11)
+    x = (rng.standard_normal((4, 1024)) * 0.02).astype(np.float32)
+    out = {"x": x}
+    for code, name, bb in [(8, "Q8_0", 34), (12, "Q4_K", 144), (13, "Q5_K", 176), (14, "Q6_K", 210)]:
+        rb = ref.ref_row_bytes(code, 1024)
+        q = np.zeros((4, rb), np.uint8)
+        for r in range(4):
+            row = np.ascontiguousarray(x[r])
+            assert ref.ref_q_row(code, ptr(row), ptr(q[r]), 1024) == 1
+        out[f"{name}_bytes"] = q
+        if name == "Q8_0":
+            g = quants.quantize(x, constants.GGMLQuantizationType.Q8_0).reshape(4, -1)
+            assert np.array_equal(g, q), "Q8_0 quantizer bytes differ from gguf-py"
+        print(f"{name:6s} quantize: {q.shape[1]} bytes/row")
+    np.savez_compressed(HERE / "quantize_golden.npz", **out)
+
+
+def gen_split3(ref):
+    rng = np.random.default_rng(5)
+    edge = np.array([0.0, -0.0, 1.0, -1.0, 65504.0, 65520.0, 7e4, -7e4, 6.1e-5, 5.96e-8, 2.98e-8, 1e-10,
+                     3.14159265, -2.718281828, 1e-4 + 1e-9, 0.02, 1.0009765625, 2049.0], np.float32)
+    x = np.concatenate([edge, rng.standard_normal(4000).astype(np.float32),
+                        (rng.standard_normal(2000) * 0.02).astype(np.float32),
+                        (rng.standard_normal(1000) * 1e3).astype(np.float32)])
+    n = x.size
+    h = np.zeros(n, np.uint16)
+    m = np.zeros(n, np.uint16)
+    lo = np.zeros(n, np.uint16)
+    ref.ref_split3_fp16(ptr(x), ptr(h), ptr(m), ptr(lo), ctypes.c_size_t(n))
+    np.savez_compressed(HERE / "split3_golden.npz", x=x, h=h, m=m, l=lo)
+    print(f"split3: {n} values")
+
+
+def gen_dlogit(ref):
+    rng = np.random.default_rng(9)
+    T, vc, v0, V = 6, 64, 128, 512
+    out = {}
+    for cap in (0.0, 30.0):
+        lg = (rng.standard_normal((T, vc)) * 3).astype(np.float32)
+        if cap > 0:
+            lg = (cap * np.tanh(lg / cap)).astype(np.float32)
+        rmax = (lg.max(axis=1).astype(np.float64) + rng.uniform(0, 1, T)).astype(np.float64)
+        rsum = rng.uniform(50, 200, T).astype(np.float64)
+        labels = rng.integers(v0 - 8, v0 + vc + 8, size=T).astype(np.int32)
+        labels[2] = v0 + 5
+        mask = np.array([1, 1, 0, 1, 1, 1], np.uint8)
+        n_loss = int(mask[:T - 1].sum())
+        dl = np.zeros((T, vc), np.float32)
+        ref.ref_dlogit(ptr(lg), ptr(rmax), ptr(rsum), ptr(labels), ptr(dl), T, vc, v0, n_loss, ptr(mask),
+                       ctypes.c_float(cap))
+        k = f"cap{int(cap)}"
+        out.update({f"{k}_lg": lg, f"{k}_rmax": rmax, f"{k}_rsum": rsum, f"{k}_labels": labels,
+                    f"{k}_mask": mask, f"{k}_dl": dl, f"{k}_meta": np.array([T, vc, v0, n_loss], np.int32)})
+    _ = V
+    np.savez_compressed(HERE / "dlogit_golden.npz", **out)
+    print("dlogit: 2 cases")
+
+
+def main():
+    ref = load_ref()
+    gen_dequant(ref)
+    gen_quantize(ref)
+    gen_split3(ref)
+    gen_dlogit(ref)
+
+
+if __name__ == "__main__":
+    os.chdir(ROOT)
+    main()

@@ -1,0 +1,69 @@
+"""The C ABI library builds, loads, and exports exactly what include/tierk.h
+declares; host-side validation works without a GPU."""
+import ctypes
+import re
+import subprocess
+
+import pytest
+
+from conftest import ROOT
+
+
+def declared_symbols():
+    text = (ROOT / "include" / "tierk.h").read_text()
+    return sorted(set(re.findall(r"\b(tk_[a-z0-9_]+)\s*\(", text)))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    from tier_b200 import build
+    build.build()
+    import tier_b200
+    return tier_b200.load()
+
+
+def test_every_declared_symbol_is_exported(lib):
+    so = ROOT / "tier_b200" / "libtierk.so"
+    out = subprocess.run(["nm", "-D", "--defined-only", str(so)], capture_output=True, text=True).stdout
+    exported = {l.split()[-1] for l in out.splitlines() if " T " in l}
+    missing = [s for s in declared_symbols() if s not in exported]
+    assert not missing, missing
+    assert all(s.startswith("tk_") for s in exported), "only the tk_* C ABI may be exported"
+
+
+def test_binding_covers_header():
+    import tier_b200
+    bound = {name for name, _, _ in tier_b200.SIGNATURES}
+    assert bound == set(declared_symbols())
+
+
+def test_row_bytes_matches_oracle(lib, oracle):
+    for t in (0, 1, 2, 3, 6, 7, 8, 10, 11, 12, 13, 14, 30):
+        for cols in (256, 4096, 5120, 14336):
+            assert lib.tk_row_bytes(t, cols) == oracle.row_bytes(t, cols), (t, cols)
+    assert lib.tk_row_bytes(12, 100) == 0          # not a block multiple
+    assert lib.tk_row_bytes(99, 256) == 0          # unknown type
+
+
+def test_null_context_is_rejected_not_crashed(lib):
+    st = lib.tk_dequant(None, 8, None, 0, 0, 1, 32, 0, None, None)
+    assert st == 1  # TK_ERR_INVALID
+    assert b"null context" in lib.tk_last_error_string()
+    st = lib.tk_gemv(None, 8, None, 34, 1, 32, None, 32, 1, None, 1, None)
+    assert st == 1
+
+
+def test_init_without_gpu_reports_error(lib):
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is present")
+    h = ctypes.c_void_p()
+    st = lib.tk_init(0, ctypes.byref(h))
+    assert st != 0 and not h.value
+    assert lib.tk_last_error_string()
+
+
+def test_product_sets_and_types_exposed():
+    import tier_b200 as tk
+    assert (tk.X3_AUTO, tk.X3_REF, tk.X3_HHL, tk.X2, tk.X1) == (0, 1, 2, 3, 4)
+    assert tk.Q8_0 == 8 and tk.Q4_K == 12 and tk.Q5_K == 13   # tier/quant.h:20-23

@@ -1,0 +1,93 @@
+"""GPU parity: dequant (bit-exact) and decode GEMV (tolerance vs fp64) through
+the C ABI against the golden vectors and the CPU oracle."""
+import numpy as np
+import pytest
+
+from conftest import GOLDEN
+from gen import blocks_for, rel_fro
+
+pytestmark = pytest.mark.gpu
+
+DQ = np.load(GOLDEN / "dequant_golden.npz")
+NAMES = sorted({k.rsplit("_", 1)[0] for k in DQ.files if k.endswith("_type")})
+
+
+def dev(a):
+    import torch
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def host(t):
+    import torch
+    torch.cuda.synchronize()
+    return t.cpu().numpy()
+
+
+@pytest.mark.parametrize("name", NAMES)
+def test_dequant_golden_bit_exact(ctx, name):
+    import torch
+    import tier_b200 as tk
+    b = DQ[f"{name}_blocks"]
+    t = int(DQ[f"{name}_type"])
+    R, C = DQ[f"{name}_f32"].shape
+    bd = dev(b)
+    o32 = torch.empty(R, C, dtype=torch.float32, device="cuda")
+    ctx.dequant(t, bd, R, C, o32, out_dtype=tk.DT_F32)
+    assert np.array_equal(host(o32).view(np.uint32), DQ[f"{name}_f32"].view(np.uint32)), name
+    o16 = torch.empty(R, C, dtype=torch.float16, device="cuda")
+    ctx.dequant(t, bd, R, C, o16, out_dtype=tk.DT_F16)
+    assert np.array_equal(host(o16).view(np.uint16), DQ[f"{name}_f16"]), name
+    ob = torch.empty(R, C, dtype=torch.bfloat16, device="cuda")
+    ctx.dequant(t, bd, R, C, ob, out_dtype=tk.DT_BF16)
+    want_bf = torch.from_numpy(DQ[f"{name}_f32"]).to(torch.bfloat16).view(torch.int16).numpy()
+    assert np.array_equal(host(ob.view(torch.int16)), want_bf), name
+    ctx.sync_status()
+
+
+@pytest.mark.parametrize("qtype", [8, 12, 13, 14, 2, 10, 11])
+def test_dequant_large_rows_and_offset(ctx, oracle, qtype):
+    import torch
+    import tier_b200 as tk
+    rng = np.random.default_rng(100 + qtype)
+    R, C = 96, 4096
+    b = blocks_for(rng, qtype, R, C)
+    want = oracle.dequant(b, qtype, R, C, 0)
+    bd = dev(b)
+    out = torch.empty(R - 5, C, dtype=torch.float32, device="cuda")
+    ctx.dequant(qtype, bd, R - 5, C, out, r0=5)
+    assert np.array_equal(host(out).view(np.uint32), want[5:].view(np.uint32))
+    o16 = torch.empty(R, C, dtype=torch.float16, device="cuda")
+    ctx.dequant(qtype, bd, R, C, o16, out_dtype=tk.DT_F16)
+    assert np.array_equal(host(o16).view(np.uint16), oracle.dequant(b, qtype, R, C, 1))
+
+
+@pytest.mark.parametrize("qtype,N,K", [(8, 4096, 4096), (12, 1024, 4096), (13, 512, 5120), (1, 768, 3840),
+                                        (30, 256, 2048), (0, 256, 1024), (14, 256, 2048), (2, 256, 2048)])
+@pytest.mark.parametrize("M", [1, 3, 16])
+def test_gemv_vs_f64(ctx, oracle, qtype, N, K, M):
+    import torch
+    rng = np.random.default_rng(qtype * 31 + M)
+    b = blocks_for(rng, qtype, N, K)
+    x = rng.standard_normal((M, K)).astype(np.float32)
+    y = torch.full((M, N), float("nan"), dtype=torch.float32, device="cuda")
+    ctx.gemv(qtype, dev(b), N, K, dev(x), y, M=M)
+    got = host(y)
+    ref = oracle.qgemm_f64(b, qtype, N, K, x)
+    assert rel_fro(got, ref) < 2e-3             # BASELINE tolerance; fp32 accumulation gives ~1e-7
+    assert rel_fro(got, ref) < 1e-5
+    ctx.sync_status()
+
+
+def test_gemv_c1_matches_reference_order_closely(ctx, oracle):
+    """C1: q8_0 4096x4096, M=1 -- also compare with the reference's own
+    lane-stride / shuffle-tree summation order."""
+    import torch
+    rng = np.random.default_rng(0)
+    N = K = 4096
+    b = blocks_for(rng, 8, N, K)
+    x = rng.standard_normal(K).astype(np.float32)
+    y = torch.empty(1, N, dtype=torch.float32, device="cuda")
+    ctx.gemv(8, dev(b), N, K, dev(x[None]), y)
+    got = host(y)[0]
+    ref_order = oracle.gemv_warp_order(b[:256], 8, 256, K, x)
+    assert np.abs(got[:256] - ref_order).max() / np.abs(ref_order).max() < 1e-5

@@ -1,0 +1,217 @@
+"""tier_b200 -- B200-native (sm_100a) frozen-weight linear path of tierlm.
+
+The product is the C ABI in include/tierk.h, implemented by libtierk.so (built
+in-tree by ``python -m tier_b200.build``).  This module is its host-side mirror:
+a ctypes binding of every entry point plus thin helpers that take torch
+tensors for device memory and streams.  The operation names follow the
+reference's C++ hot path (tier/tier.cpp): ``dequant`` = dq_launch (294-298),
+``gemv`` = gemv_q / gemv<T> (300-306, 2261-2268), ``linear`` / ``linear_dx`` /
+``linear_dx_acc`` = the linear operators (1202-1238), ``lmhead_*`` = the
+chunked LM-head loops (3184-3266).
+
+There is no CPU fallback: if libtierk.so is missing or fails to load, importing
+the binding raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from pathlib import Path
+
+_PKG = Path(__file__).resolve().parent
+LIB_PATH = _PKG / "libtierk.so"
+
+# status codes (tk_status)
+TK_OK, TK_ERR_INVALID, TK_ERR_UNSUPPORTED, TK_ERR_CUDA, TK_ERR_NOMEM, TK_ERR_TIMEOUT, TK_ERR_DEVICE = range(7)
+# block types = the reference's QT_* codes (tier/quant.h:20-23)
+F32, F16, Q4_0, Q4_1, Q5_0, Q5_1, Q8_0 = 0, 1, 2, 3, 6, 7, 8
+Q2_K, Q3_K, Q4_K, Q5_K, Q6_K, BF16, F16X2 = 10, 11, 12, 13, 14, 30, 100
+QTYPES = {"F32": F32, "F16": F16, "BF16": BF16, "Q4_0": Q4_0, "Q4_1": Q4_1, "Q5_0": Q5_0, "Q5_1": Q5_1,
+          "Q8_0": Q8_0, "Q2_K": Q2_K, "Q3_K": Q3_K, "Q4_K": Q4_K, "Q5_K": Q5_K, "Q6_K": Q6_K}
+BLOCK = {F32: (1, 4), F16: (1, 2), BF16: (1, 2), Q4_0: (32, 18), Q4_1: (32, 20), Q5_0: (32, 22), Q5_1: (32, 24),
+         Q8_0: (32, 34), Q2_K: (256, 84), Q3_K: (256, 110), Q4_K: (256, 144), Q5_K: (256, 176), Q6_K: (256, 210)}
+# activation dtypes
+DT_F32, DT_F16, DT_BF16 = 0, 1, 2
+# product sets
+X3_AUTO, X3_REF, X3_HHL, X2, X1 = 0, 1, 2, 3, 4
+
+
+class TierkError(RuntimeError):
+    def __init__(self, status: int, msg: str):
+        super().__init__(f"tierk status {status}: {msg}")
+        self.status = status
+
+
+class Weight(ctypes.Structure):
+    """tk_weight: a frozen W[rows, cols] resident on the device."""
+    _fields_ = [("qtype", ctypes.c_int), ("rows", ctypes.c_int), ("cols", ctypes.c_int),
+                ("scale_log2", ctypes.c_int), ("row_bytes", ctypes.c_size_t), ("data", ctypes.c_void_p)]
+
+
+_P = ctypes.c_void_p
+_I = ctypes.c_int
+_SZ = ctypes.c_size_t
+_F = ctypes.c_float
+
+# (name, restype, argtypes) -- mirrors include/tierk.h
+SIGNATURES = [
+    ("tk_init", _I, [_I, ctypes.POINTER(_P)]),
+    ("tk_destroy", None, [_P]),
+    ("tk_last_error_string", ctypes.c_char_p, []),
+    ("tk_reserve", _I, [_P, _SZ]),
+    ("tk_workspace_bytes", _SZ, [_P]),
+    ("tk_sync_status", _I, [_P, _P]),
+    ("tk_launch_count", ctypes.c_uint64, [_P]),
+    ("tk_row_bytes", _SZ, [_I, _I]),
+    ("tk_dequant", _I, [_P, _I, _P, _SZ, _I, _I, _I, _I, _P, _P]),
+    ("tk_gemv", _I, [_P, _I, _P, _SZ, _I, _I, _P, _I, _I, _P, _I, _P]),
+    ("tk_linear_fwd", _I, [_P, ctypes.POINTER(Weight), _P, _I, _I, _I, _P, _I, _F, _I, _P]),
+    ("tk_linear_dx", _I, [_P, ctypes.POINTER(Weight), _P, _I, _I, _I, _P, _I, _F, _I, _P]),
+    ("tk_weight_split_f32", _I, [_P, _P, _I, _I, _P, ctypes.POINTER(_I), _P]),
+    ("tk_split3", _I, [_P, _P, _SZ, _P, _P, _P, _P]),
+    ("tk_lmhead_stats", _I, [_P, _P, _I, _I, _I, _P, _I, _P, _P, _F, _I, _I, _P, _P, _P, _P, _P]),
+    ("tk_lmhead_grad", _I, [_P, _P, _I, _I, _I, _P, _I, _P, _P, _I, _F, _I, _I, _P, _P, _P, _P]),
+    ("tk_lmhead_loss", _I, [_P, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P]),
+    ("tk_lmhead_rescale", _I, [_P, _I, _P, _P, _P, _P]),
+]
+
+_lib = None
+
+
+def load(path: str | os.PathLike | None = None) -> ctypes.CDLL:
+    """Load libtierk.so (raises if absent -- there is no fallback)."""
+    global _lib
+    if _lib is not None and path is None:
+        return _lib
+    p = Path(path) if path else LIB_PATH
+    if not p.exists():
+        raise RuntimeError(f"libtierk.so not built ({p}); run `python -m tier_b200.build`")
+    lib = ctypes.CDLL(str(p))
+    for name, res, args in SIGNATURES:
+        f = getattr(lib, name)
+        f.restype = res
+        f.argtypes = args
+    if path is None:
+        _lib = lib
+    return lib
+
+
+def row_bytes(qtype: int, cols: int) -> int:
+    be, bb = BLOCK[qtype]
+    return cols // be * bb
+
+
+def _check(st: int):
+    if st != TK_OK:
+        raise TierkError(st, load().tk_last_error_string().decode())
+
+
+def _ptr(t) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _stream(stream) -> int | None:
+    if stream is None:
+        import torch
+        return torch.cuda.current_stream().cuda_stream
+    return getattr(stream, "cuda_stream", stream)
+
+
+class Context:
+    """A tk_ctx bound to one CUDA device."""
+
+    def __init__(self, device: int = 0):
+        self.lib = load()
+        h = _P()
+        _check(self.lib.tk_init(device, ctypes.byref(h)))
+        self.h = h
+        self.device = device
+
+    def close(self):
+        if self.h:
+            self.lib.tk_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    # ---- diagnostics ----
+    def launches(self) -> int:
+        return int(self.lib.tk_launch_count(self.h))
+
+    def sync_status(self, stream=None):
+        _check(self.lib.tk_sync_status(self.h, _stream(stream)))
+
+    def reserve(self, nbytes: int):
+        _check(self.lib.tk_reserve(self.h, nbytes))
+
+    # ---- operations (torch tensors in, device pointers to the C ABI) ----
+    def dequant(self, qtype, blocks, rows, cols, out, r0=0, out_dtype=DT_F32, row_bytes_=None, stream=None):
+        rb = row_bytes_ if row_bytes_ is not None else row_bytes(qtype, cols)
+        _check(self.lib.tk_dequant(self.h, qtype, _ptr(blocks), rb, r0, rows, cols, out_dtype, _ptr(out),
+                                   _stream(stream)))
+        return out
+
+    def gemv(self, qtype, W, N, K, x, y, M=1, ldx=None, ldy=None, row_bytes_=None, stream=None):
+        rb = row_bytes_ if row_bytes_ is not None else row_bytes(qtype, K)
+        _check(self.lib.tk_gemv(self.h, qtype, _ptr(W), rb, N, K, _ptr(x), ldx or K, M, _ptr(y), ldy or N,
+                                _stream(stream)))
+        return y
+
+    def linear(self, W: Weight, X, M, Y, x_dtype=DT_F32, ldx=None, ldy=None, beta=0.0, products=X3_AUTO,
+               stream=None):
+        _check(self.lib.tk_linear_fwd(self.h, ctypes.byref(W), _ptr(X), x_dtype, M, ldx or W.cols, _ptr(Y),
+                                      ldy or W.rows, beta, products, _stream(stream)))
+        return Y
+
+    def linear_dx(self, W: Weight, dY, M, dX, dy_dtype=DT_F32, lddy=None, lddx=None, beta=0.0, products=X3_AUTO,
+                  stream=None):
+        _check(self.lib.tk_linear_dx(self.h, ctypes.byref(W), _ptr(dY), dy_dtype, M, lddy or W.rows, _ptr(dX),
+                                     lddx or W.cols, beta, products, _stream(stream)))
+        return dX
+
+    def linear_dx_acc(self, W: Weight, dY, M, dX, **kw):
+        return self.linear_dx(W, dY, M, dX, beta=1.0, **kw)
+
+    def weight_split_f32(self, W32, rows, cols, planes, stream=None) -> int:
+        sc = _I(0)
+        _check(self.lib.tk_weight_split_f32(self.h, _ptr(W32), rows, cols, _ptr(planes), ctypes.byref(sc),
+                                            _stream(stream)))
+        return sc.value
+
+    def split3(self, x, h, m, l, stream=None):
+        _check(self.lib.tk_split3(self.h, _ptr(x), x.numel(), _ptr(h), _ptr(m), _ptr(l), _stream(stream)))
+
+    def lmhead_stats(self, W, v0, V_shard, H, X, T, labels, mask, softcap, chunk, rmax, rsum, amax, tgt,
+                     products=X3_REF, stream=None):
+        _check(self.lib.tk_lmhead_stats(self.h, _ptr(W), v0, V_shard, H, _ptr(X), T, _ptr(labels), _ptr(mask),
+                                        softcap, chunk, products, _ptr(rmax), _ptr(rsum), _ptr(amax), _ptr(tgt),
+                                        _stream(stream)))
+
+    def lmhead_grad(self, W, v0, V_shard, H, X, T, labels, mask, n_loss, softcap, chunk, rmax, rsum, dX,
+                    products=X3_REF, stream=None):
+        _check(self.lib.tk_lmhead_grad(self.h, _ptr(W), v0, V_shard, H, _ptr(X), T, _ptr(labels), _ptr(mask),
+                                       n_loss, softcap, chunk, products, _ptr(rmax), _ptr(rsum), _ptr(dX),
+                                       _stream(stream)))
+
+    def lmhead_loss(self, T, labels, mask, rmax, rsum, amax, tgt, loss, hits, stream=None):
+        _check(self.lib.tk_lmhead_loss(self.h, T, _ptr(labels), _ptr(mask), _ptr(rmax), _ptr(rsum), _ptr(amax),
+                                       _ptr(tgt), _ptr(loss), _ptr(hits), _stream(stream)))
+
+    def lmhead_rescale(self, n, rmax_local, rsum_local, rmax_global, stream=None):
+        _check(self.lib.tk_lmhead_rescale(self.h, n, _ptr(rmax_local), _ptr(rsum_local), _ptr(rmax_global),
+                                          _stream(stream)))
+
+
+def make_weight(qtype: int, rows: int, cols: int, data, scale_log2: int = 0) -> Weight:
+    """Describe a device weight tensor (uint8 blocks or fp16 planes) for the C ABI."""
+    rb = cols * 2 if qtype in (F16, F16X2) else row_bytes(qtype, cols)
+    return Weight(qtype, rows, cols, scale_log2, rb, data.data_ptr())
+
+
+from .host import LinearPath, LMHead  # noqa: E402  (host-side mirror of the reference's operators)
+
+__all__ = ["Context", "Weight", "make_weight", "load", "row_bytes", "LinearPath", "LMHead", "TierkError"]

@@ -1,0 +1,458 @@
+// tk_api.cu -- the extern "C" entry points of libtierk.so (include/tierk.h):
+// argument validation, workspace management, and the composition of the
+// kernels into the reference's operations.
+#include <cmath>
+#include <cstring>
+#include <string>
+#include "tk_device.cuh"
+#include "tk_internal.h"
+
+namespace tk {
+
+static thread_local std::string g_last_error;
+
+tk_status fail(tk_status st, const std::string& msg) {
+    g_last_error = msg;
+    return st;
+}
+tk_status cuda_fail(cudaError_t e, const char* what) {
+    if (e == cudaSuccess) return TK_OK;
+    g_last_error = std::string(what) + ": " + cudaGetErrorString(e);
+    return e == cudaErrorMemoryAllocation ? TK_ERR_NOMEM : TK_ERR_CUDA;
+}
+
+tk_status ws_ensure(tk_ctx* ctx, size_t bytes, cudaStream_t stream) {
+    if (bytes <= ctx->ws_bytes) return TK_OK;
+    // Work queued on any stream may still use the old buffer.
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) return cuda_fail(e, "workspace growth sync");
+    (void)stream;
+    if (ctx->ws) cudaFree(ctx->ws);
+    ctx->ws = nullptr;
+    ctx->ws_bytes = 0;
+    size_t want = align256(bytes + (bytes >> 3));
+    e = cudaMalloc(&ctx->ws, want);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        e = cudaMalloc(&ctx->ws, align256(bytes));
+        if (e != cudaSuccess) return cuda_fail(e, "workspace allocation");
+        want = align256(bytes);
+    }
+    ctx->ws_bytes = want;
+    return TK_OK;
+}
+
+struct Carve {
+    char* p;
+    size_t used = 0;
+    explicit Carve(void* base) : p(static_cast<char*>(base)) {}
+    template <class T>
+    T* take(size_t n) {
+        T* r = reinterpret_cast<T*>(p + used);
+        used += align256(n * sizeof(T));
+        return r;
+    }
+};
+
+static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+// Planes / products for one linear call.
+struct Plan {
+    int x_planes = 1;
+    int nprod = 1;
+    int pa[3] = {0, 0, 0}, pb[3] = {0, 0, 0};
+    bool w_two = false;
+};
+
+static tk_status plan_products(const tk_weight* W, int x_dtype, int products, Plan& pl) {
+    const bool wx2 = W->qtype == TK_F16X2;
+    int mode = products;
+    if (mode == TK_X3_AUTO) mode = wx2 ? TK_X3_HHL : (x_dtype == TK_DT_F32 ? TK_X3_REF : TK_X1);
+    switch (mode) {
+        case TK_X3_REF:   // W.xl + W.xm + W.xh (low parts first)
+            pl.x_planes = 3; pl.nprod = 3;
+            pl.pa[0] = 2; pl.pa[1] = 1; pl.pa[2] = 0;
+            break;
+        case TK_X3_HHL:   // Xl.Wh + Xh.Wl + Xh.Wh
+            if (!wx2) return fail(TK_ERR_INVALID, "TK_X3_HHL needs a TK_F16X2 weight");
+            pl.x_planes = 2; pl.nprod = 3; pl.w_two = true;
+            pl.pa[0] = 1; pl.pb[0] = 0;
+            pl.pa[1] = 0; pl.pb[1] = 1;
+            pl.pa[2] = 0; pl.pb[2] = 0;
+            break;
+        case TK_X2:
+            pl.x_planes = 2; pl.nprod = 2;
+            pl.pa[0] = 1; pl.pa[1] = 0;
+            break;
+        case TK_X1:
+            pl.x_planes = 1; pl.nprod = 1;
+            break;
+        default: return fail(TK_ERR_INVALID, "unknown product set " + std::to_string(products));
+    }
+    return TK_OK;
+}
+
+static tk_status check_weight(const tk_weight* W, const char* fn) {
+    if (!W || !W->data) return fail(TK_ERR_INVALID, std::string(fn) + ": null weight");
+    if (W->rows <= 0 || W->cols <= 0) return fail(TK_ERR_INVALID, std::string(fn) + ": empty weight");
+    if (!aligned16(W->data)) return fail(TK_ERR_INVALID, std::string(fn) + ": weight must be 16-byte aligned");
+    if (W->qtype == TK_F16X2 || W->qtype == TK_F16) {
+        if (W->row_bytes != (size_t)W->cols * 2 || W->cols % 8)
+            return fail(TK_ERR_INVALID, std::string(fn) + ": fp16 weight rows must be dense with cols % 8 == 0");
+        return TK_OK;
+    }
+    if (!dequant_supported(W->qtype) || W->qtype == TK_F32 || W->qtype == TK_BF16)
+        return fail(TK_ERR_UNSUPPORTED, std::string(fn) + ": weight type " + std::to_string(W->qtype) +
+                                            " not supported on the tensor-core path");
+    if (W->cols % block_elems(W->qtype) || W->row_bytes != (size_t)(W->cols / block_elems(W->qtype)) * block_bytes(W->qtype))
+        return fail(TK_ERR_INVALID, std::string(fn) + ": row_bytes does not match the block layout");
+    if (W->cols % 8) return fail(TK_ERR_INVALID, std::string(fn) + ": cols must be a multiple of 8");
+    return TK_OK;
+}
+
+// Shared body of fwd (dx == false) and dX (dx == true).
+static tk_status linear(tk_ctx* ctx, const tk_weight* W, const void* A, int a_dtype, int M, int lda, float* D,
+                        int ldd, float beta, int products, cudaStream_t s, bool dx) {
+    const char* fn = dx ? "tk_linear_dx" : "tk_linear_fwd";
+    if (!ctx) return fail(TK_ERR_INVALID, std::string(fn) + ": null context");
+    tk_status st = check_weight(W, fn);
+    if (st != TK_OK) return st;
+    if (M < 0) return fail(TK_ERR_INVALID, std::string(fn) + ": negative M");
+    if (M == 0) return TK_OK;
+    if (!A || !D) return fail(TK_ERR_INVALID, std::string(fn) + ": null activation or output");
+    if (beta != 0.0f && beta != 1.0f) return fail(TK_ERR_INVALID, std::string(fn) + ": beta must be 0 or 1");
+    const int N = W->rows, K = W->cols;
+    const int a_cols = dx ? N : K, d_cols = dx ? K : N;
+    if (lda < a_cols || ldd < d_cols) return fail(TK_ERR_INVALID, std::string(fn) + ": leading dimension too small");
+    if (a_dtype != TK_DT_F32 && a_dtype != TK_DT_F16 && a_dtype != TK_DT_BF16)
+        return fail(TK_ERR_INVALID, std::string(fn) + ": activation dtype");
+    if (a_cols % 8) return fail(TK_ERR_INVALID, std::string(fn) + ": activation width must be a multiple of 8");
+    if (!aligned16(D) || ldd % 4) return fail(TK_ERR_INVALID, std::string(fn) + ": output must be 16-byte aligned, ld % 4 == 0");
+    Plan pl;
+    st = plan_products(W, a_dtype, products, pl);
+    if (st != TK_OK) return st;
+
+    const bool quant = W->qtype != TK_F16 && W->qtype != TK_F16X2;
+    const size_t plane_elems = (size_t)M * a_cols;
+    const size_t need = align256(plane_elems * 2 * pl.x_planes) + align256((size_t)M * 4) +
+                        (quant ? align256((size_t)N * K * 2) : 0);
+    st = ws_ensure(ctx, need, s);
+    if (st != TK_OK) return st;
+    Carve cv(ctx->ws);
+    // plane p of the split activation at pbase + p * M * a_cols (16-byte aligned: a_cols % 8 == 0)
+    uint16_t* pbase = cv.take<uint16_t>(plane_elems * pl.x_planes);
+    int* row_exp = cv.take<int>(M);
+    const uint16_t* wplanes[2] = {nullptr, nullptr};
+    if (quant) {
+        uint16_t* wf = cv.take<uint16_t>((size_t)N * K);
+        st = launch_dequant(ctx, W->qtype, W->data, W->row_bytes, 0, N, K, TK_DT_F16, wf, s);
+        if (st != TK_OK) return st;
+        wplanes[0] = wf;
+    } else {
+        wplanes[0] = static_cast<const uint16_t*>(W->data);
+        if (W->qtype == TK_F16X2) wplanes[1] = wplanes[0] + (size_t)N * K;
+    }
+    if (pl.w_two && !wplanes[1]) return fail(TK_ERR_INVALID, std::string(fn) + ": product set needs two weight planes");
+    st = launch_act_split(ctx, A, a_dtype, M, a_cols, lda, pl.x_planes, true, pbase, row_exp, s);
+    if (st != TK_OK) return st;
+
+    GemmDesc g;
+    for (int i = 0; i < pl.x_planes; ++i) g.A[i] = pbase + (size_t)i * plane_elems;
+    g.B[0] = wplanes[0];
+    g.B[1] = wplanes[1];
+    g.lda = a_cols;
+    g.ldb = K;
+    g.b_mn = dx;
+    g.M = M;
+    g.N = d_cols;
+    g.K = a_cols;
+    g.nprod = pl.nprod;
+    for (int i = 0; i < 3; ++i) { g.pa[i] = pl.pa[i]; g.pb[i] = pl.pb[i]; }
+    g.D = D;
+    g.ldd = ldd;
+    g.beta = beta != 0.0f;
+    g.row_exp = row_exp;
+    g.col_exp = W->qtype == TK_F16X2 ? W->scale_log2 : 0;
+    return launch_gemm(ctx, g, s);
+}
+
+}  // namespace tk
+
+using namespace tk;
+
+extern "C" {
+
+const char* tk_last_error_string(void) { return g_last_error.c_str(); }
+
+tk_status tk_init(int device, tk_ctx** out) {
+    if (!out) return fail(TK_ERR_INVALID, "tk_init: null out");
+    *out = nullptr;
+    int n = 0;
+    cudaError_t e = cudaGetDeviceCount(&n);
+    if (e != cudaSuccess) return cuda_fail(e, "tk_init: cudaGetDeviceCount");
+    if (device < 0 || device >= n) return fail(TK_ERR_INVALID, "tk_init: no such device");
+    e = cudaSetDevice(device);
+    if (e != cudaSuccess) return cuda_fail(e, "tk_init: cudaSetDevice");
+    cudaDeviceProp prop;
+    e = cudaGetDeviceProperties(&prop, device);
+    if (e != cudaSuccess) return cuda_fail(e, "tk_init: properties");
+    if (prop.major != 10) return fail(TK_ERR_UNSUPPORTED, "tk_init: libtierk is built for sm_100a (B200)");
+    tk_ctx* c = new tk_ctx();
+    c->device = device;
+    c->num_sms = prop.multiProcessorCount;
+    e = cudaMalloc(&c->status, sizeof(int));
+    if (e == cudaSuccess) e = cudaMemset(c->status, 0, sizeof(int));
+    if (e != cudaSuccess) {
+        delete c;
+        return cuda_fail(e, "tk_init: status word");
+    }
+    *out = c;
+    return TK_OK;
+}
+
+void tk_destroy(tk_ctx* ctx) {
+    if (!ctx) return;
+    cudaSetDevice(ctx->device);
+    cudaDeviceSynchronize();
+    if (ctx->ws) cudaFree(ctx->ws);
+    if (ctx->status) cudaFree(ctx->status);
+    delete ctx;
+}
+
+tk_status tk_reserve(tk_ctx* ctx, size_t bytes) {
+    if (!ctx) return fail(TK_ERR_INVALID, "tk_reserve: null context");
+    return ws_ensure(ctx, bytes, nullptr);
+}
+
+size_t tk_workspace_bytes(const tk_ctx* ctx) { return ctx ? ctx->ws_bytes : 0; }
+
+uint64_t tk_launch_count(const tk_ctx* ctx) { return ctx ? ctx->launches : 0; }
+
+tk_status tk_sync_status(tk_ctx* ctx, void* stream) {
+    if (!ctx) return fail(TK_ERR_INVALID, "tk_sync_status: null context");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    cudaError_t e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) return cuda_fail(e, "tk_sync_status: stream");
+    int code = 0;
+    e = cudaMemcpy(&code, ctx->status, sizeof(int), cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) return cuda_fail(e, "tk_sync_status: read");
+    if (code) {
+        cudaMemset(ctx->status, 0, sizeof(int));
+        if (code == DEV_TIMEOUT) return fail(TK_ERR_TIMEOUT, "a device-side bounded wait expired");
+        return fail(TK_ERR_DEVICE, "a kernel reported invalid input (code " + std::to_string(code) + ")");
+    }
+    return TK_OK;
+}
+
+size_t tk_row_bytes(int qtype, int cols) {
+    const int be = block_elems(qtype), bb = block_bytes(qtype);
+    if (be <= 0 || cols < 0 || cols % be) return 0;
+    return (size_t)(cols / be) * bb;
+}
+
+tk_status tk_dequant(tk_ctx* ctx, int qtype, const void* blocks, size_t row_bytes, int r0, int nrows, int cols,
+                     int out_dtype, void* out, void* stream) {
+    if (!ctx) return fail(TK_ERR_INVALID, "tk_dequant: null context");
+    if (!dequant_supported(qtype)) return fail(TK_ERR_UNSUPPORTED, "tk_dequant: block type " + std::to_string(qtype));
+    if (nrows < 0 || r0 < 0 || cols <= 0) return fail(TK_ERR_INVALID, "tk_dequant: bad row range / cols");
+    if (nrows == 0) return TK_OK;
+    if (!blocks || !out) return fail(TK_ERR_INVALID, "tk_dequant: null pointer");
+    if (tk_row_bytes(qtype, cols) == 0 || row_bytes < tk_row_bytes(qtype, cols))
+        return fail(TK_ERR_INVALID, "tk_dequant: cols not a block multiple or row_bytes too small");
+    if (cols % 8) return fail(TK_ERR_INVALID, "tk_dequant: cols must be a multiple of 8");
+    if (out_dtype != TK_DT_F32 && out_dtype != TK_DT_F16 && out_dtype != TK_DT_BF16)
+        return fail(TK_ERR_INVALID, "tk_dequant: out dtype");
+    if (!aligned16(out)) return fail(TK_ERR_INVALID, "tk_dequant: output must be 16-byte aligned");
+    if ((qtype == TK_Q4_K || qtype == TK_Q5_K || qtype == TK_F16) && (!aligned16(blocks) || row_bytes % 16))
+        return fail(TK_ERR_INVALID, "tk_dequant: Q4_K/Q5_K/F16 rows must be 16-byte aligned");
+    return launch_dequant(ctx, qtype, blocks, row_bytes, r0, nrows, cols, out_dtype, out,
+                          static_cast<cudaStream_t>(stream));
+}
+
+tk_status tk_gemv(tk_ctx* ctx, int qtype, const void* W, size_t row_bytes, int N, int K, const float* x, int ldx,
+                  int M, float* y, int ldy, void* stream) {
+    if (!ctx) return fail(TK_ERR_INVALID, "tk_gemv: null context");
+    if (!gemv_supported(qtype)) return fail(TK_ERR_UNSUPPORTED, "tk_gemv: weight type " + std::to_string(qtype));
+    if (M < 1 || M > 16) return fail(TK_ERR_INVALID, "tk_gemv: M must be 1..16 (use tk_linear_fwd beyond)");
+    if (N < 0 || K <= 0) return fail(TK_ERR_INVALID, "tk_gemv: bad shape");
+    if (N == 0) return TK_OK;
+    if (!W || !x || !y) return fail(TK_ERR_INVALID, "tk_gemv: null pointer");
+    if (tk_row_bytes(qtype, K) == 0 || row_bytes < tk_row_bytes(qtype, K))
+        return fail(TK_ERR_INVALID, "tk_gemv: K not a block multiple or row_bytes too small");
+    if (K % 8 || ldx < K || ldx % 4 || !aligned16(x) || ldy < N)
+        return fail(TK_ERR_INVALID, "tk_gemv: x must be 16-byte aligned, K % 8 == 0, ldx % 4 == 0");
+    const bool staged = qtype == TK_Q8_0 || qtype == TK_Q4_0 || qtype == TK_Q4_K || qtype == TK_Q5_K;
+    const bool dense = qtype == TK_F16 || qtype == TK_BF16 || qtype == TK_F32;
+    if ((staged || dense) && (!aligned16(W) || row_bytes % 16))
+        return fail(TK_ERR_INVALID, "tk_gemv: weight rows must be 16-byte aligned");
+    if ((qtype == TK_Q8_0 || qtype == TK_Q4_0) && K % 256)
+        return fail(TK_ERR_INVALID, "tk_gemv: Q8_0/Q4_0 rows need K % 256 == 0");
+    return launch_gemv(ctx, qtype, W, row_bytes, N, K, x, ldx, M, y, ldy, static_cast<cudaStream_t>(stream));
+}
+
+tk_status tk_linear_fwd(tk_ctx* ctx, const tk_weight* W, const void* X, int x_dtype, int M, int ldx, float* Y, int ldy,
+                        float beta, int products, void* stream) {
+    return linear(ctx, W, X, x_dtype, M, ldx, Y, ldy, beta, products, static_cast<cudaStream_t>(stream), false);
+}
+
+tk_status tk_linear_dx(tk_ctx* ctx, const tk_weight* W, const void* dY, int dy_dtype, int M, int lddy, float* dX,
+                       int lddx, float beta, int products, void* stream) {
+    return linear(ctx, W, dY, dy_dtype, M, lddy, dX, lddx, beta, products, static_cast<cudaStream_t>(stream), true);
+}
+
+tk_status tk_weight_split_f32(tk_ctx* ctx, const float* W32, int rows, int cols, uint16_t* planes, int* scale_log2,
+                              void* stream) {
+    if (!ctx || !W32 || !planes || !scale_log2) return fail(TK_ERR_INVALID, "tk_weight_split_f32: null argument");
+    if (rows <= 0 || cols <= 0) return fail(TK_ERR_INVALID, "tk_weight_split_f32: empty weight");
+    return weight_split_f32(ctx, W32, rows, cols, planes, scale_log2, static_cast<cudaStream_t>(stream));
+}
+
+tk_status tk_split3(tk_ctx* ctx, const float* x, size_t n, uint16_t* h, uint16_t* m, uint16_t* l, void* stream) {
+    if (!ctx || (n && (!x || !h || !m || !l))) return fail(TK_ERR_INVALID, "tk_split3: null argument");
+    return launch_split3_raw(ctx, x, n, h, m, l, static_cast<cudaStream_t>(stream));
+}
+
+// ---- LM head -------------------------------------------------------------
+static tk_status lm_check(tk_ctx* ctx, const uint16_t* W, int V_shard, int H, const float* X, int T,
+                          const int32_t* labels, const uint8_t* mask, int chunk, int products, const char* fn) {
+    if (!ctx || !W || !X || !labels || !mask) return fail(TK_ERR_INVALID, std::string(fn) + ": null argument");
+    if (V_shard <= 0 || H <= 0 || T < 2) return fail(TK_ERR_INVALID, std::string(fn) + ": bad shape");
+    if (H % 8 || !aligned16(W) || !aligned16(X))
+        return fail(TK_ERR_INVALID, std::string(fn) + ": H % 8 == 0 and 16-byte aligned W, X required");
+    if (chunk <= 0 || chunk % 256 || V_shard % 256)
+        return fail(TK_ERR_INVALID, std::string(fn) + ": chunk and V_shard must be multiples of 256");
+    if (products != TK_X3_REF && products != TK_X2 && products != TK_X3_AUTO)
+        return fail(TK_ERR_INVALID, std::string(fn) + ": products must be TK_X3_REF or TK_X2");
+    return TK_OK;
+}
+
+// X planes for the head: nplanes x [T-1, H] with per-row exponents.
+static tk_status lm_split_x(tk_ctx* ctx, Carve& cv, const float* X, int T, int H, int np, uint16_t** planes,
+                            int** row_exp, cudaStream_t s) {
+    const size_t pe = (size_t)(T - 1) * H;
+    uint16_t* base = cv.take<uint16_t>(pe * np);
+    *row_exp = cv.take<int>(T);
+    *planes = base;
+    return launch_act_split(ctx, X, TK_DT_F32, T - 1, H, H, np, true, base, *row_exp, s);
+}
+
+tk_status tk_lmhead_stats(tk_ctx* ctx, const uint16_t* W, int v0, int V_shard, int H, const float* X, int T,
+                          const int32_t* labels, const uint8_t* mask, float softcap, int chunk, int products,
+                          double* rmax, double* rsum, int32_t* amax, float* tgt, void* stream) {
+    tk_status st = lm_check(ctx, W, V_shard, H, X, T, labels, mask, chunk, products, "tk_lmhead_stats");
+    if (st != TK_OK) return st;
+    if (!rmax || !rsum || !amax || !tgt) return fail(TK_ERR_INVALID, "tk_lmhead_stats: null state");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const int np = products == TK_X2 ? 2 : 3;
+    const int rows = T - 1;
+    const int ntiles = chunk / 256;
+    const size_t need = align256((size_t)rows * H * 2 * np) + align256((size_t)T * 4) +
+                        align256((size_t)rows * ntiles * 4) * 3 + align256((size_t)rows * ntiles * 8);
+    st = ws_ensure(ctx, need, s);
+    if (st != TK_OK) return st;
+    Carve cv(ctx->ws);
+    uint16_t* xp;
+    int* rexp;
+    st = lm_split_x(ctx, cv, X, T, H, np, &xp, &rexp, s);
+    if (st != TK_OK) return st;
+    float* pmax = cv.take<float>((size_t)rows * ntiles);
+    int32_t* parg = cv.take<int32_t>((size_t)rows * ntiles);
+    float* ptgt = cv.take<float>((size_t)rows * ntiles);
+    double* psum = cv.take<double>((size_t)rows * ntiles);
+    for (int c0 = 0; c0 < V_shard; c0 += chunk) {
+        const int vc = V_shard - c0 < chunk ? V_shard - c0 : chunk;
+        GemmDesc g;
+        for (int p = 0; p < np; ++p) g.A[p] = xp + (size_t)p * rows * H;
+        g.B[0] = W + (size_t)c0 * H;
+        g.lda = H; g.ldb = H; g.b_mn = false;
+        g.M = rows; g.N = vc; g.K = H;
+        g.nprod = np;
+        for (int p = 0; p < np; ++p) { g.pa[p] = np - 1 - p; g.pb[p] = 0; }
+        g.D = reinterpret_cast<float*>(pmax);   // unused by this epilogue; must be valid & aligned
+        g.ldd = 4;
+        g.row_exp = rexp;
+        LseDesc e;
+        e.pmax = pmax; e.parg = parg; e.psum = psum; e.ptgt = ptgt;
+        e.labels = labels; e.v0 = v0 + c0; e.cap = softcap; e.ld_part = ntiles;
+        st = launch_gemm_lse(ctx, g, e, s);
+        if (st != TK_OK) return st;
+        st = launch_lse_merge(ctx, pmax, parg, psum, ptgt, ntiles, (vc + 255) / 256, rows, vc, v0 + c0, labels, mask,
+                              rmax, rsum, amax, tgt, s);
+        if (st != TK_OK) return st;
+    }
+    return TK_OK;
+}
+
+tk_status tk_lmhead_grad(tk_ctx* ctx, const uint16_t* W, int v0, int V_shard, int H, const float* X, int T,
+                         const int32_t* labels, const uint8_t* mask, int n_loss, float softcap, int chunk, int products,
+                         const double* rmax, const double* rsum, float* dX, void* stream) {
+    tk_status st = lm_check(ctx, W, V_shard, H, X, T, labels, mask, chunk, products, "tk_lmhead_grad");
+    if (st != TK_OK) return st;
+    if (!rmax || !rsum || !dX) return fail(TK_ERR_INVALID, "tk_lmhead_grad: null state");
+    if (n_loss <= 0) return TK_OK;   // every row masked: dlogit is zero
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const int np = products == TK_X2 ? 2 : 3;
+    const int rows = T - 1;
+    const size_t need = align256((size_t)rows * H * 2 * np) + align256((size_t)T * 4) +
+                        align256((size_t)rows * chunk * 2) * np;
+    st = ws_ensure(ctx, need, s);
+    if (st != TK_OK) return st;
+    Carve cv(ctx->ws);
+    uint16_t* xp;
+    int* rexp;
+    st = lm_split_x(ctx, cv, X, T, H, np, &xp, &rexp, s);
+    if (st != TK_OK) return st;
+    const size_t pstride = (size_t)rows * chunk;
+    uint16_t* dl = cv.take<uint16_t>(pstride * np);
+    // |dlogit| <= mask/n_loss <= 255/n_loss; 2^dl_exp * 255/n_loss < 2^15.
+    const int dl_exp = 7 + (int)std::floor(std::log2((double)n_loss));
+    for (int c0 = 0; c0 < V_shard; c0 += chunk) {
+        const int vc = V_shard - c0 < chunk ? V_shard - c0 : chunk;
+        GemmDesc g;
+        for (int p = 0; p < np; ++p) g.A[p] = xp + (size_t)p * rows * H;
+        g.B[0] = W + (size_t)c0 * H;
+        g.lda = H; g.ldb = H; g.b_mn = false;
+        g.M = rows; g.N = vc; g.K = H;
+        g.nprod = np;
+        for (int p = 0; p < np; ++p) { g.pa[p] = np - 1 - p; g.pb[p] = 0; }
+        g.D = dX; g.ldd = H;           // unused by this epilogue
+        g.row_exp = rexp;
+        DlogitDesc e;
+        e.rmax = rmax; e.rsum = rsum; e.labels = labels; e.mask = mask;
+        e.T = T; e.v0 = v0 + c0; e.n_loss = n_loss; e.cap = softcap; e.dl_exp = dl_exp; e.nplanes = np;
+        e.planes = dl; e.plane_stride = (long)pstride; e.ld = vc;
+        st = launch_gemm_dlogit(ctx, g, e, s);
+        if (st != TK_OK) return st;
+        GemmDesc d;
+        for (int p = 0; p < np; ++p) d.A[p] = dl + (size_t)p * pstride;
+        d.B[0] = W + (size_t)c0 * H;
+        d.lda = vc; d.ldb = H; d.b_mn = true;
+        d.M = rows; d.N = H; d.K = vc;
+        d.nprod = np;
+        for (int p = 0; p < np; ++p) { d.pa[p] = np - 1 - p; d.pb[p] = 0; }
+        d.D = dX; d.ldd = H; d.beta = 1;
+        d.col_exp = dl_exp;
+        st = launch_gemm(ctx, d, s);
+        if (st != TK_OK) return st;
+    }
+    return TK_OK;
+}
+
+tk_status tk_lmhead_loss(tk_ctx* ctx, int T, const int32_t* labels, const uint8_t* mask, const double* rmax,
+                         const double* rsum, const int32_t* amax, const float* tgt, double* loss_sum, int32_t* hits,
+                         void* stream) {
+    if (!ctx || !labels || !mask || !rmax || !rsum || !amax || !tgt || !loss_sum || !hits)
+        return fail(TK_ERR_INVALID, "tk_lmhead_loss: null argument");
+    if (T < 2) return fail(TK_ERR_INVALID, "tk_lmhead_loss: T < 2");
+    return launch_lm_loss(ctx, T, labels, mask, rmax, rsum, amax, tgt, loss_sum, hits,
+                          static_cast<cudaStream_t>(stream));
+}
+
+tk_status tk_lmhead_rescale(tk_ctx* ctx, int n, double* rmax_local, double* rsum_local, const double* rmax_global,
+                            void* stream) {
+    if (!ctx || (n > 0 && (!rmax_local || !rsum_local || !rmax_global)))
+        return fail(TK_ERR_INVALID, "tk_lmhead_rescale: null argument");
+    return launch_lm_rescale(ctx, n, rmax_local, rsum_local, rmax_global, static_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

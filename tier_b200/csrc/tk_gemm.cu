@@ -1,0 +1,447 @@
+// tk_gemm.cu -- the tensor-core GEMM of the path (tcgen05 + TMEM + TMA).
+//
+//   D[M, N] = sum_p A_{pa[p]}[M, K] . B_{pb[p]}^T     (fp16 x fp16 -> fp32)
+//
+// One kernel serves every product set of the split GEMM: the reference's
+// fp3gemm (tier/tier.cpp:922-943) issues three cuBLASLt GEMMs over the
+// planes {xl, xm, xh} and re-reads W three times; here all products of one
+// output tile accumulate into the same TMEM accumulator inside one launch,
+// each k-block stage pairing one A plane with one B plane.
+//
+// Layout: persistent CTAs (one per SM), 128 x 256 output tiles, BK = 64.
+//   warp 0      TMA producer: A tile [128 x 64] and B tile [256 x 64]
+//               (K-major, one box) or [64 x 256] (N-major, four 64-wide boxes)
+//               per stage, 128-byte swizzle, 4-stage mbarrier ring.
+//   warp 1      allocates 512 TMEM columns (two 256-column fp32
+//               accumulators), one lane issues tcgen05.mma (M=128, N=256,
+//               K=16) and tcgen05.commit to release stages / publish tiles.
+//   warps 2-5   epilogue: tcgen05.ld rows of the finished accumulator while
+//               the MMA warp fills the other one; scale, optional beta,
+//               store (or the LM-head statistics / dlogit epilogues).
+// All waits are bounded (tk_device.cuh); a timeout records a status code and
+// the roles drain out instead of hanging.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <mutex>
+#include "tk_device.cuh"
+#include "tk_internal.h"
+
+namespace tk {
+
+constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4;
+constexpr int A_BYTES = BM * BK * 2;                 // 16 KB
+constexpr int B_BYTES = BN * BK * 2;                 // 32 KB
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr int TMEM_COLS = 512;
+constexpr int GEMM_THREADS = 192;
+constexpr size_t GEMM_SMEM = (size_t)STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+
+enum { EPI_STORE = 0, EPI_LSE = 1, EPI_DLOGIT = 2 };
+
+struct __align__(64) GemmParams {
+    CUtensorMap tmA[3];
+    CUtensorMap tmB[2];
+    int M, N, K;
+    int nprod;
+    int pa[3], pb[3];
+    int tiles_m, tiles_n;
+    float* D;
+    long ldd;
+    int beta;
+    const int* row_exp;
+    int col_exp;
+    int* status;
+};
+
+struct EpiParams {
+    LseDesc lse;
+    DlogitDesc dl;
+};
+
+__device__ __forceinline__ float exp2i(int e) {   // exact 2^e for e in [-126, 127]
+    return __uint_as_float((uint32_t)(e + 127) << 23);
+}
+
+template <bool B_MN, int EPI>
+__global__ void __launch_bounds__(GEMM_THREADS, 1)
+    gemm_tc_kernel(const __grid_constant__ GemmParams p, const __grid_constant__ EpiParams ep) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* sA = smem;
+    uint8_t* sB = smem + STAGES * A_BYTES;
+    uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * B_BYTES);
+    uint64_t* empty = full + STAGES;
+    uint64_t* tfull = empty + STAGES;
+    uint64_t* tempty = tfull + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(&tfull[a], 1);
+            mbar_init(&tempty[a], 128);
+        }
+        fence_mbar_init();
+        fence_async_shared();
+    }
+    if (warp == 0 && lane == 0) {
+        for (int i = 0; i < p.nprod; ++i) tma_prefetch_desc(&p.tmA[p.pa[i]]);
+        tma_prefetch_desc(&p.tmB[0]);
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, TMEM_COLS);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    const int num_tiles = p.tiles_m * p.tiles_n;
+    const int kblocks = (p.K + BK - 1) / BK;
+    const int stages_per_tile = kblocks * p.nprod;
+
+    if (warp == 0) {
+        // ---------------- TMA producer ----------------
+        if (lane == 0) {
+            int s = 0;
+            uint32_t ph = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+                const int mb = tile % p.tiles_m, nb = tile / p.tiles_m;
+                for (int kb = 0; kb < kblocks && ok; ++kb) {
+                    for (int q = 0; q < p.nprod; ++q) {
+                        if (!mbar_wait(&empty[s], ph ^ 1, p.status)) { ok = false; break; }
+                        mbar_arrive_expect_tx(&full[s], STAGE_BYTES);
+                        tma_load_2d(sA + s * A_BYTES, &p.tmA[p.pa[q]], &full[s], kb * BK, mb * BM);
+                        if constexpr (!B_MN) {
+                            tma_load_2d(sB + s * B_BYTES, &p.tmB[p.pb[q]], &full[s], kb * BK, nb * BN);
+                        } else {
+#pragma unroll
+                            for (int j = 0; j < BN / 64; ++j)
+                                tma_load_2d(sB + s * B_BYTES + j * (64 * BK * 2), &p.tmB[p.pb[q]], &full[s],
+                                            nb * BN + 64 * j, kb * BK);
+                        }
+                        if (++s == STAGES) { s = 0; ph ^= 1; }
+                    }
+                }
+            }
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        // ---------------- MMA issuer ----------------
+        if (lane == 0) {
+            constexpr uint32_t idesc = idesc_f16(BM, BN, 0, 0, B_MN ? 1 : 0);
+            int s = 0;
+            uint32_t ph = 0;
+            bool ok = true;
+            int it = 0;
+            for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++it) {
+                const int acc = it & 1;
+                if (!mbar_wait(&tempty[acc], ((it >> 1) & 1) ^ 1, p.status)) break;
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + acc * BN;
+                for (int st = 0; st < stages_per_tile; ++st) {
+                    if (!mbar_wait(&full[s], ph, p.status)) { ok = false; break; }
+                    tc_fence_after();
+                    const uint32_t a0 = smem_u32(sA + s * A_BYTES), b0 = smem_u32(sB + s * B_BYTES);
+#pragma unroll
+                    for (int kk = 0; kk < BK / 16; ++kk) {
+                        const uint64_t ad = sdesc_sw128(a0 + kk * 32, 16, 1024);
+                        const uint64_t bd = B_MN ? sdesc_sw128(b0 + kk * 2048, 64 * BK * 2, 1024)
+                                                 : sdesc_sw128(b0 + kk * 32, 16, 1024);
+                        tc_mma_f16(d_tmem, ad, bd, idesc, (st | kk) ? 1u : 0u);
+                    }
+                    tc_commit(&empty[s]);
+                    if (++s == STAGES) { s = 0; ph ^= 1; }
+                }
+                if (ok) tc_commit(&tfull[acc]);
+            }
+        }
+        __syncwarp();
+    } else {
+        // ---------------- epilogue (warps 2..5) ----------------
+        const int quarter = warp & 3;                 // TMEM lanes this warp may access
+        int it = 0;
+        for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++it) {
+            const int acc = it & 1;
+            const int mb = tile % p.tiles_m, nb = tile / p.tiles_m;
+            if (!mbar_wait(&tfull[acc], (it >> 1) & 1, p.status)) break;
+            tc_fence_after();
+            const int row = mb * BM + quarter * 32 + lane;
+            const bool row_ok = row < p.M;
+            const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN;
+            const int e = (p.row_exp && row_ok ? p.row_exp[row] : 0) + p.col_exp;
+            const float f = ldexpf(1.0f, -e);
+            const int col_base = nb * BN;
+
+            if constexpr (EPI == EPI_STORE) {
+                float* drow = p.D + (size_t)(row_ok ? row : 0) * p.ldd;
+#pragma unroll 1
+                for (int c = 0; c < BN; c += 32) {
+                    uint32_t r[32];
+                    tc_ld_32x32b_x32(taddr + c, r);
+                    tc_wait_ld();
+                    if (row_ok) {
+                        const int col0 = col_base + c;
+                        if (col0 + 32 <= p.N) {
+#pragma unroll
+                            for (int j = 0; j < 32; j += 4) {
+                                float4 v = make_float4(__uint_as_float(r[j]) * f, __uint_as_float(r[j + 1]) * f,
+                                                       __uint_as_float(r[j + 2]) * f, __uint_as_float(r[j + 3]) * f);
+                                float4* dp = reinterpret_cast<float4*>(drow + col0 + j);
+                                if (p.beta) {
+                                    const float4 o = *dp;
+                                    v.x += o.x; v.y += o.y; v.z += o.z; v.w += o.w;
+                                }
+                                *dp = v;
+                            }
+                        } else {
+#pragma unroll
+                            for (int j = 0; j < 32; ++j) {
+                                if (col0 + j < p.N) {
+                                    float v = __uint_as_float(r[j]) * f;
+                                    if (p.beta) v += drow[col0 + j];
+                                    drow[col0 + j] = v;
+                                }
+                            }
+                        }
+                    }
+                }
+            } else if constexpr (EPI == EPI_LSE) {
+                // Per (row, tile) partial statistics of the softcapped logits:
+                // max, lowest index of the max, sum exp(l - max) in fp64, and
+                // the label's logit when the label falls in this tile.
+                const LseDesc& L = ep.lse;
+                const int label = row_ok ? L.labels[row + 1] - L.v0 : -1;
+                float mx = -1e30f;
+                int arg = 0x7fffffff;
+                double sum = 0.0;
+                float tgt = 0.0f;
+#pragma unroll 1
+                for (int c = 0; c < BN; c += 32) {
+                    uint32_t r[32];
+                    tc_ld_32x32b_x32(taddr + c, r);
+                    tc_wait_ld();
+                    const int col0 = col_base + c;
+                    float v[32];
+                    float cm = -1e30f;
+                    int ci = 0x7fffffff;
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        float l = __uint_as_float(r[j]) * f;
+                        if (L.cap > 0.0f) l = L.cap * tanhf(l / L.cap);
+                        const bool valid = col0 + j < p.N;
+                        v[j] = valid ? l : -INFINITY;
+                        if (valid && l > cm) { cm = l; ci = col0 + j; }
+                        if (col0 + j == label) tgt = l;
+                    }
+                    if (cm > mx) {
+                        sum *= exp((double)mx - (double)cm);
+                        mx = cm;
+                        arg = ci;
+                    }
+#pragma unroll
+                    for (int j = 0; j < 32; ++j)
+                        if (col0 + j < p.N) sum += exp((double)v[j] - (double)mx);
+                }
+                if (row_ok) {
+                    const size_t o = (size_t)row * L.ld_part + nb;
+                    L.pmax[o] = mx;
+                    L.parg[o] = arg;
+                    L.psum[o] = sum;
+                    L.ptgt[o] = tgt;
+                }
+            } else {
+                // dlogit = ((softmax - onehot) / n_loss) * (1 - y^2) * mask,
+                // scaled by 2^dl_exp and split into fp16 planes.
+                const DlogitDesc& G = ep.dl;
+                const bool live = row_ok && row < G.T - 1 && G.mask[row] != 0;
+                const double lse = live ? G.rmax[row] + log(G.rsum[row]) : 0.0;
+                const int label = live ? G.labels[row + 1] - G.v0 : -1;
+                const float mval = live ? (float)G.mask[row] : 0.0f;
+                const float sc = exp2i(G.dl_exp);
+#pragma unroll 1
+                for (int c = 0; c < BN; c += 32) {
+                    uint32_t r[32];
+                    tc_ld_32x32b_x32(taddr + c, r);
+                    tc_wait_ld();
+                    if (!row_ok) continue;
+                    const int col0 = col_base + c;
+                    if (col0 >= p.N) continue;
+                    uint32_t hp[16], mp[16], lp[16];
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        float d = 0.0f;
+                        if (live) {
+                            float l = __uint_as_float(r[j]) * f;
+                            if (G.cap > 0.0f) l = G.cap * tanhf(l / G.cap);
+                            const double sm = exp((double)l - lse);
+                            const double oh = (col0 + j == label) ? 1.0 : 0.0;
+                            const float y = G.cap > 0.0f ? l / G.cap : 0.0f;
+                            d = (float)((sm - oh) / G.n_loss) * (1.0f - y * y) * mval;
+                        }
+                        const float v = d * sc;
+                        const uint16_t h = f2h_bits(v);
+                        const float rr = v - h2f_bits(h);
+                        const uint16_t m = f2h_bits(rr);
+                        const uint16_t lo = f2h_bits(rr - h2f_bits(m));
+                        const int w = j >> 1, sh = 16 * (j & 1);
+                        if (sh == 0) { hp[w] = h; mp[w] = m; lp[w] = lo; }
+                        else { hp[w] |= (uint32_t)h << 16; mp[w] |= (uint32_t)m << 16; lp[w] |= (uint32_t)lo << 16; }
+                    }
+                    // N (the chunk width) is a multiple of 256 on this path.
+                    uint16_t* base = G.planes + (size_t)row * G.ld + col0;
+                    uint4* d0 = reinterpret_cast<uint4*>(base);
+#pragma unroll
+                    for (int q = 0; q < 4; ++q)
+                        d0[q] = make_uint4(hp[4 * q], hp[4 * q + 1], hp[4 * q + 2], hp[4 * q + 3]);
+                    uint4* d1 = reinterpret_cast<uint4*>(base + G.plane_stride);
+#pragma unroll
+                    for (int q = 0; q < 4; ++q)
+                        d1[q] = make_uint4(mp[4 * q], mp[4 * q + 1], mp[4 * q + 2], mp[4 * q + 3]);
+                    if (G.nplanes > 2) {
+                        uint4* d2 = reinterpret_cast<uint4*>(base + 2 * G.plane_stride);
+#pragma unroll
+                        for (int q = 0; q < 4; ++q)
+                            d2[q] = make_uint4(lp[4 * q], lp[4 * q + 1], lp[4 * q + 2], lp[4 * q + 3]);
+                    }
+                }
+            }
+            tc_fence_before();
+            mbar_arrive(&tempty[acc]);
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, TMEM_COLS);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Host side: tensor maps (driver entry point fetched at run time) + launch.
+// ---------------------------------------------------------------------------
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    });
+    return fn;
+}
+
+// 2-D fp16 tensor [rows, cols] (cols contiguous, row stride ld elements),
+// box [box_rows, 64 cols], 128-byte swizzle, zero fill out of bounds.
+static tk_status make_map(CUtensorMap* m, const void* base, long cols, long rows, long ld, int box_rows) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return fail(TK_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+    if ((reinterpret_cast<uintptr_t>(base) & 15) || (ld * 2) % 16)
+        return fail(TK_ERR_INVALID, "GEMM operand must be 16-byte aligned with a row stride multiple of 8 elements");
+    cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
+    cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(TK_ERR_CUDA, "cuTensorMapEncodeTiled failed: " + std::to_string((int)r));
+    return TK_OK;
+}
+
+template <bool B_MN, int EPI>
+static tk_status go(tk_ctx* ctx, const GemmParams& gp, const EpiParams& ep, cudaStream_t s) {
+    static bool attr_set = false;   // per instantiation
+    if (!attr_set) {
+        cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<B_MN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)GEMM_SMEM);
+        if (e != cudaSuccess) return cuda_fail(e, "gemm smem attribute");
+        attr_set = true;
+    }
+    const int tiles = gp.tiles_m * gp.tiles_n;
+    const int grid = tiles < ctx->num_sms ? tiles : ctx->num_sms;
+    gemm_tc_kernel<B_MN, EPI><<<grid, GEMM_THREADS, GEMM_SMEM, s>>>(gp, ep);
+    ctx->launches++;
+    return cuda_fail(cudaGetLastError(), "gemm launch");
+}
+
+static tk_status build(const GemmDesc& g, tk_ctx* ctx, GemmParams& gp) {
+    if (g.M <= 0 || g.N <= 0 || g.K <= 0) return fail(TK_ERR_INVALID, "GEMM with empty shape");
+    if (g.nprod < 1 || g.nprod > 3) return fail(TK_ERR_INVALID, "GEMM product count must be 1..3");
+    if ((reinterpret_cast<uintptr_t>(g.D) & 15) || g.ldd % 4)
+        return fail(TK_ERR_INVALID, "output must be 16-byte aligned with a row stride multiple of 4");
+    memset(&gp, 0, sizeof(gp));
+    for (int i = 0; i < g.nprod; ++i) {
+        if (g.pa[i] < 0 || g.pa[i] > 2 || !g.A[g.pa[i]] || g.pb[i] < 0 || g.pb[i] > 1 || !g.B[g.pb[i]])
+            return fail(TK_ERR_INVALID, "GEMM product references a missing plane");
+    }
+    for (int i = 0; i < 3; ++i)
+        if (g.A[i]) {
+            tk_status st = make_map(&gp.tmA[i], g.A[i], g.K, g.M, g.lda, BM);
+            if (st != TK_OK) return st;
+        }
+    for (int i = 0; i < 2; ++i)
+        if (g.B[i]) {
+            tk_status st = g.b_mn ? make_map(&gp.tmB[i], g.B[i], g.N, g.K, g.ldb, BK)
+                                  : make_map(&gp.tmB[i], g.B[i], g.K, g.N, g.ldb, BN);
+            if (st != TK_OK) return st;
+        }
+    gp.M = g.M; gp.N = g.N; gp.K = g.K;
+    gp.nprod = g.nprod;
+    for (int i = 0; i < 3; ++i) { gp.pa[i] = g.pa[i]; gp.pb[i] = g.pb[i]; }
+    gp.tiles_m = (g.M + BM - 1) / BM;
+    gp.tiles_n = (g.N + BN - 1) / BN;
+    gp.D = g.D; gp.ldd = g.ldd; gp.beta = g.beta;
+    gp.row_exp = g.row_exp; gp.col_exp = g.col_exp;
+    gp.status = ctx->status;
+    (void)ctx;
+    return TK_OK;
+}
+
+tk_status launch_gemm(tk_ctx* ctx, const GemmDesc& g, cudaStream_t s) {
+    GemmParams gp;
+    tk_status st = build(g, ctx, gp);
+    if (st != TK_OK) return st;
+    EpiParams ep;
+    memset(&ep, 0, sizeof(ep));
+    return g.b_mn ? go<true, EPI_STORE>(ctx, gp, ep, s) : go<false, EPI_STORE>(ctx, gp, ep, s);
+}
+
+tk_status launch_gemm_lse(tk_ctx* ctx, const GemmDesc& g, const LseDesc& e, cudaStream_t s) {
+    GemmParams gp;
+    tk_status st = build(g, ctx, gp);
+    if (st != TK_OK) return st;
+    EpiParams ep;
+    memset(&ep, 0, sizeof(ep));
+    ep.lse = e;
+    if (g.b_mn) return fail(TK_ERR_INVALID, "LM-head logits GEMM takes a K-major head");
+    return go<false, EPI_LSE>(ctx, gp, ep, s);
+}
+
+tk_status launch_gemm_dlogit(tk_ctx* ctx, const GemmDesc& g, const DlogitDesc& e, cudaStream_t s) {
+    GemmParams gp;
+    tk_status st = build(g, ctx, gp);
+    if (st != TK_OK) return st;
+    if (g.N % BN) return fail(TK_ERR_INVALID, "dlogit epilogue needs a chunk width multiple of 256");
+    EpiParams ep;
+    memset(&ep, 0, sizeof(ep));
+    ep.dl = e;
+    if (g.b_mn) return fail(TK_ERR_INVALID, "LM-head logits GEMM takes a K-major head");
+    return go<false, EPI_DLOGIT>(ctx, gp, ep, s);
+}
+
+}  // namespace tk

@@ -1,0 +1,95 @@
+// tk_internal.h -- host-side declarations shared by the tierk .cu files.
+#pragma once
+#include <cstddef>
+#include <cstdint>
+#include <string>
+#include <cuda_runtime.h>
+#include "../../include/tierk.h"
+
+struct tk_ctx {
+    int device = 0;
+    int num_sms = 0;
+    void* ws = nullptr;          // workspace (device)
+    size_t ws_bytes = 0;
+    int* status = nullptr;       // device status word (tk::DEV_*)
+    uint64_t launches = 0;       // kernels launched through this context
+};
+
+namespace tk {
+
+// Thread-local last-error text; returns `st` for chaining.
+tk_status fail(tk_status st, const std::string& msg);
+tk_status cuda_fail(cudaError_t e, const char* what);
+
+// Workspace carving helper: 256-byte aligned sub-buffers of ctx->ws.
+tk_status ws_ensure(tk_ctx* ctx, size_t bytes, cudaStream_t stream);
+inline size_t align256(size_t b) { return (b + 255) & ~size_t(255); }
+
+// ---- tk_dequant.cu ----
+bool dequant_supported(int qtype);
+int block_elems(int qtype);
+int block_bytes(int qtype);
+tk_status launch_dequant(tk_ctx* ctx, int qtype, const void* W, size_t rb, int r0, int nrows, int cols,
+                         int out_dtype, void* out, cudaStream_t s);
+// X[M, K] (x_dtype, row stride ldx) -> nplanes fp16 planes [M, K] (plane p at
+// planes + p*M*K) of X * 2^e_m, e_m per row so that max|row|*2^e_m is in
+// [2^14, 2^15); row_exp[m] = e_m.  scaled == false uses e_m = 0.
+tk_status launch_act_split(tk_ctx* ctx, const void* X, int x_dtype, int M, int K, long ldx, int nplanes,
+                           bool scaled, uint16_t* planes, int* row_exp, cudaStream_t s);
+tk_status launch_split3_raw(tk_ctx* ctx, const float* x, size_t n, uint16_t* h, uint16_t* m, uint16_t* l,
+                            cudaStream_t s);
+tk_status weight_split_f32(tk_ctx* ctx, const float* W, int rows, int cols, uint16_t* planes, int* scale_log2,
+                           cudaStream_t s);
+
+// ---- tk_gemv.cu ----
+bool gemv_supported(int qtype);
+tk_status launch_gemv(tk_ctx* ctx, int qtype, const void* W, size_t rb, int N, int K, const float* x, int ldx,
+                      int M, float* y, int ldy, cudaStream_t s);
+
+// ---- tk_gemm.cu ----
+// D[M, N] (fp32, row stride ldd) = sum_p A_{pa[p]}[M, K] . B_{pb[p]}^T, scaled
+// per row by 2^-(row_exp[m] + col_exp) and added to D when beta != 0.
+//   A planes: fp16 [M, K] K-major, row stride lda elements.
+//   B planes: b_mn == false -> fp16 [N, K] K-major (row stride ldb);
+//             b_mn == true  -> fp16 [K, N] N-major (row stride ldb).
+struct GemmDesc {
+    const uint16_t* A[3] = {nullptr, nullptr, nullptr};
+    const uint16_t* B[2] = {nullptr, nullptr};
+    long lda = 0, ldb = 0;
+    bool b_mn = false;
+    int M = 0, N = 0, K = 0;
+    int nprod = 1;
+    int pa[3] = {0, 0, 0}, pb[3] = {0, 0, 0};
+    float* D = nullptr;
+    long ldd = 0;
+    int beta = 0;
+    const int* row_exp = nullptr;
+    int col_exp = 0;
+};
+tk_status launch_gemm(tk_ctx* ctx, const GemmDesc& g, cudaStream_t s);
+
+// LM-head epilogue variants (tk_gemm.cu)
+struct LseDesc {               // pass 1: per (row, 256-column tile) partial stats
+    float* pmax; int32_t* parg; double* psum; float* ptgt;   // [T_rows, ntiles]
+    const int32_t* labels; int v0; float cap; int ld_part;
+};
+struct DlogitDesc {            // pass 2: dlogit planes
+    const double* rmax; const double* rsum; const int32_t* labels; const uint8_t* mask;
+    int T; int v0; int n_loss; float cap; int dl_exp; int nplanes;
+    uint16_t* planes; long plane_stride; int ld;            // planes [nplanes][T, ld]
+};
+tk_status launch_gemm_lse(tk_ctx* ctx, const GemmDesc& g, const LseDesc& e, cudaStream_t s);
+tk_status launch_gemm_dlogit(tk_ctx* ctx, const GemmDesc& g, const DlogitDesc& e, cudaStream_t s);
+
+// ---- tk_lmhead.cu ----
+tk_status launch_lse_merge(tk_ctx* ctx, const float* pmax, const int32_t* parg, const double* psum,
+                           const float* ptgt, int ld_part, int ntiles, int n_pred, int vc, int v0,
+                           const int32_t* labels, const uint8_t* mask, double* rmax, double* rsum,
+                           int32_t* amax, float* tgt, cudaStream_t s);
+tk_status launch_lm_loss(tk_ctx* ctx, int T, const int32_t* labels, const uint8_t* mask, const double* rmax,
+                         const double* rsum, const int32_t* amax, const float* tgt, double* loss, int32_t* hits,
+                         cudaStream_t s);
+tk_status launch_lm_rescale(tk_ctx* ctx, int n, double* rmax_l, double* rsum_l, const double* rmax_g,
+                            cudaStream_t s);
+
+}  // namespace tk

@@ -1,0 +1,178 @@
+"""Host-side mirror of the reference's linear operators and LM-head loop.
+
+The reference (tier/tier.cpp) drives its hot path from C++ statics:
+``linear`` / ``linear_dx`` / ``linear_dx_acc`` (1202-1238), ``chat_lin``
+(2351-2378) and the two LM-head passes inside main (3184-3266).  These classes
+keep those operations' meaning on top of the libtierk C ABI, and add the
+row / vocab sharding across GPUs (one process per GPU, NCCL through
+torch.distributed) that the reference does not have.
+
+Sharding (weights split by output rows, vocab split by rows of the head):
+  * linear fwd: rank g owns W[N_g, K]; Y[:, N_g] is computed locally and, if
+    the caller wants the full Y, all-gathered.
+  * linear dX: rank g computes dY[:, N_g] . W[N_g, :] and the partial dX are
+    all-reduced (SUM).
+  * LM head: rank g owns head rows [v0_g, v0_g + V_g).  After the local pass
+    1 the running states are merged with all-reduce MAX of rmax, a local
+    rescale, all-reduce SUM of rsum and of the target logit (only the owning
+    shard has a non-zero target), and an argmax exchange; pass 2 then uses
+    the global lse and dX is all-reduced (SUM).
+"""
+from __future__ import annotations
+
+import torch
+
+from . import (BF16, DT_BF16, DT_F16, DT_F32, F16, F16X2, X2, X3_AUTO, X3_REF, Context, Weight, make_weight,
+               row_bytes)
+
+_DT = {torch.float32: DT_F32, torch.float16: DT_F16, torch.bfloat16: DT_BF16}
+
+
+def shard_rows(n: int, world: int, rank: int, align: int = 1) -> tuple[int, int]:
+    """Contiguous row range of `rank` when n rows are split over `world` ranks,
+    every boundary a multiple of `align`."""
+    units = n // align
+    a = units * rank // world * align
+    b = units * (rank + 1) // world * align if rank + 1 < world else n
+    return a, b
+
+
+class LinearPath:
+    """One frozen projection W[N, K] (block-quantized, fp16, or fp32 split into
+    fp16 hi/lo) on this rank's device, optionally row-sharded across `group`."""
+
+    def __init__(self, ctx: Context, qtype: int, rows: int, cols: int, data: torch.Tensor, scale_log2: int = 0,
+                 group=None, n_total: int | None = None, row0: int = 0):
+        self.ctx = ctx
+        self.data = data
+        self.W: Weight = make_weight(qtype, rows, cols, data, scale_log2)
+        self.N, self.K = rows, cols
+        self.group = group
+        self.n_total = n_total if n_total is not None else rows
+        self.row0 = row0
+
+    @staticmethod
+    def from_f32_split(ctx: Context, W32: torch.Tensor, **kw) -> "LinearPath":
+        rows, cols = W32.shape
+        planes = torch.empty(2 * rows * cols, dtype=torch.float16, device=W32.device)
+        s = ctx.weight_split_f32(W32, rows, cols, planes)
+        return LinearPath(ctx, F16X2, rows, cols, planes, scale_log2=s, **kw)
+
+    def forward(self, X: torch.Tensor, Y: torch.Tensor | None = None, beta: float = 0.0, products: int = X3_AUTO,
+                gather: bool = True) -> torch.Tensor:
+        """Y = X . W^T (the reference's `linear`).  With a group and gather=True
+        the output shards are all-gathered into the full [M, N_total]."""
+        M = X.shape[0]
+        local = Y if (Y is not None and self.group is None) else torch.empty(M, self.N, device=X.device,
+                                                                               dtype=torch.float32)
+        if beta and Y is not None and self.group is None:
+            local = Y
+        self.ctx.linear(self.W, X, M, local, x_dtype=_DT[X.dtype], ldx=X.stride(0), ldy=local.stride(0), beta=beta,
+                        products=products)
+        if self.group is None or not gather:
+            return local
+        import torch.distributed as dist
+        world = dist.get_world_size(self.group)
+        parts = [torch.empty(M, self.N, device=X.device, dtype=torch.float32) for _ in range(world)]
+        dist.all_gather(parts, local, group=self.group)
+        full = torch.cat(parts, dim=1)
+        if Y is not None:
+            if beta:
+                Y += full
+            else:
+                Y.copy_(full)
+            return Y
+        return full
+
+    def dx(self, dY: torch.Tensor, dX: torch.Tensor | None = None, beta: float = 0.0,
+           products: int = X3_AUTO) -> torch.Tensor:
+        """dX = dY . W (`linear_dx`; beta=1 is `linear_dx_acc`).  dY holds this
+        rank's N columns; partial results are all-reduced across the group."""
+        M = dY.shape[0]
+        if self.group is None:
+            out = dX if dX is not None else torch.empty(M, self.K, device=dY.device, dtype=torch.float32)
+            self.ctx.linear_dx(self.W, dY, M, out, dy_dtype=_DT[dY.dtype], lddy=dY.stride(0), lddx=out.stride(0),
+                               beta=beta if dX is not None else 0.0, products=products)
+            return out
+        import torch.distributed as dist
+        part = torch.empty(M, self.K, device=dY.device, dtype=torch.float32)
+        self.ctx.linear_dx(self.W, dY, M, part, dy_dtype=_DT[dY.dtype], lddy=dY.stride(0), lddx=part.stride(0),
+                           products=products)
+        dist.all_reduce(part, group=self.group)
+        if dX is None:
+            return part
+        if beta:
+            dX += part
+        else:
+            dX.copy_(part)
+        return dX
+
+
+class LMHead:
+    """Chunked-vocabulary LM head + cross-entropy over this rank's vocab shard
+    (W fp16 [V_shard, H], global rows v0 .. v0+V_shard)."""
+
+    def __init__(self, ctx: Context, W: torch.Tensor, v0: int, chunk: int = 16384, products: int = X3_REF,
+                 group=None):
+        assert W.dtype == torch.float16 and W.is_contiguous()
+        self.ctx, self.W, self.v0 = ctx, W, v0
+        self.V_shard, self.H = W.shape
+        self.chunk, self.products, self.group = chunk, products, group
+
+    def stats(self, X, labels, mask, softcap=0.0):
+        T = X.shape[0]
+        dev = X.device
+        rmax = torch.full((T - 1,), -1e30, dtype=torch.float64, device=dev)
+        rsum = torch.zeros(T - 1, dtype=torch.float64, device=dev)
+        amax = torch.full((T - 1,), -1, dtype=torch.int32, device=dev)
+        tgt = torch.zeros(T - 1, dtype=torch.float32, device=dev)
+        self.ctx.lmhead_stats(self.W, self.v0, self.V_shard, self.H, X, T, labels, mask, softcap, self.chunk, rmax,
+                              rsum, amax, tgt, products=self.products)
+        if self.group is not None:
+            import torch.distributed as dist
+            g = self.group
+            world = dist.get_world_size(g)
+            # argmax across shards: highest max, ties to the lower vocab index
+            # (shards are in vocab order, so the lower rank wins a tie).
+            allm = [torch.empty_like(rmax) for _ in range(world)]
+            alla = [torch.empty_like(amax) for _ in range(world)]
+            dist.all_gather(allm, rmax.clone(), group=g)
+            dist.all_gather(alla, amax, group=g)
+            m = torch.stack(allm)              # [world, T-1]
+            best = torch.argmax(m, dim=0)      # first maximal rank = lower vocab index
+            amax = torch.stack(alla).gather(0, best[None]).squeeze(0).contiguous()
+            gmax = rmax.clone()
+            dist.all_reduce(gmax, op=dist.ReduceOp.MAX, group=g)
+            self.ctx.lmhead_rescale(T - 1, rmax, rsum, gmax)
+            dist.all_reduce(rsum, group=g)
+            dist.all_reduce(tgt, group=g)
+        return rmax, rsum, amax, tgt
+
+    def loss(self, T, labels, mask, rmax, rsum, amax, tgt):
+        loss = torch.zeros(1, dtype=torch.float64, device=rmax.device)
+        hits = torch.zeros(1, dtype=torch.int32, device=rmax.device)
+        self.ctx.lmhead_loss(T, labels, mask, rmax, rsum, amax, tgt, loss, hits)
+        return loss, hits
+
+    def grad(self, X, labels, mask, n_loss, rmax, rsum, dX=None, softcap=0.0):
+        T, H = X.shape
+        if dX is None:
+            dX = torch.zeros(T, H, dtype=torch.float32, device=X.device)
+        self.ctx.lmhead_grad(self.W, self.v0, self.V_shard, self.H, X, T, labels, mask, n_loss, softcap, self.chunk,
+                             rmax, rsum, dX, products=self.products)
+        if self.group is not None:
+            import torch.distributed as dist
+            dist.all_reduce(dX, group=self.group)
+        return dX
+
+    def step(self, X, labels, mask, softcap=0.0, dX=None):
+        """Both passes: returns (loss_sum, n_loss, hits, amax, dX)."""
+        T = X.shape[0]
+        n_loss = int(mask[: T - 1].count_nonzero().item())
+        rmax, rsum, amax, tgt = self.stats(X, labels, mask, softcap)
+        loss, hits = self.loss(T, labels, mask, rmax, rsum, amax, tgt)
+        dX = self.grad(X, labels, mask, n_loss, rmax, rsum, dX=dX, softcap=softcap)
+        return loss, n_loss, hits, amax, dX
+
+
+__all__ = ["LinearPath", "LMHead", "shard_rows", "row_bytes", "BF16", "F16", "X2", "X3_REF"]
