@@ -93,6 +93,15 @@ tk_status tk_sync_status(tk_ctx *ctx, void *stream);
 /* Number of kernels this context has launched (diagnostics / bench). */
 uint64_t tk_launch_count(const tk_ctx *ctx);
 
+/* Per-kernel timing (diagnostics; no reference counterpart).  While enabled,
+ * every launch is bracketed by CUDA events on its own stream (up to 8192
+ * launches; later launches are not recorded).  tk_profile resets the record.
+ * tk_profile_read synchronizes the device and returns the summed event time
+ * (ms) and number of recorded launches of one kernel family. */
+enum { TK_PROF_GEMM = 0, TK_PROF_DEQUANT = 1, TK_PROF_SPLIT = 2, TK_PROF_GEMV = 3, TK_PROF_LMHEAD = 4 };
+tk_status tk_profile(tk_ctx *ctx, int enable);
+tk_status tk_profile_read(tk_ctx *ctx, int kind, double *total_ms, uint64_t *launches);
+
 /* ---- block formats ------------------------------------------------------ */
 /* Bytes of one row of `cols` elements of `qtype`; 0 if unsupported or cols is
  * not a block multiple.  Replaces q_row_bytes (tier/quant.h:33). */

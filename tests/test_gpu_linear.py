@@ -52,7 +52,7 @@ def test_fp16_single_product_fwd_dx(ctx, M, N, K):
     ctx.sync_status()
 
 
-@pytest.mark.parametrize("M,N,K", SHAPES[:4])
+@pytest.mark.parametrize("M,N,K", SHAPES[:4] + [(256, 512, 5120), (128, 256, 14336)])
 def test_x3_ref_products_fp32_activations(ctx, M, N, K):
     """The reference's fp3gemm: fp32 X split into h, m, l; single fp16 W."""
     import torch
@@ -74,7 +74,7 @@ def test_x3_ref_products_fp32_activations(ctx, M, N, K):
     assert rel_fro(host(Y1), f64(X) @ f64(W).T) > 10 * rel_fro(host(Y), f64(X) @ f64(W).T)
 
 
-@pytest.mark.parametrize("M,N,K", [(256, 512, 512), (200, 300, 192), (512, 1024, 5120)])
+@pytest.mark.parametrize("M,N,K", [(256, 512, 512), (200, 300, 192), (512, 1024, 5120), (256, 512, 14336)])
 def test_x3_hhl_fp32_weight(ctx, M, N, K):
     """fp32 W split into fp16 hi/lo: Xh.Wh + Xh.Wl + Xl.Wh vs fp64 of fp32 W (<= 1e-5)."""
     import torch

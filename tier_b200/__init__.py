@@ -34,6 +34,8 @@ BLOCK = {F32: (1, 4), F16: (1, 2), BF16: (1, 2), Q4_0: (32, 18), Q4_1: (32, 20),
 DT_F32, DT_F16, DT_BF16 = 0, 1, 2
 # product sets
 X3_AUTO, X3_REF, X3_HHL, X2, X1 = 0, 1, 2, 3, 4
+# kernel families for profiling
+PROF_GEMM, PROF_DEQUANT, PROF_SPLIT, PROF_GEMV, PROF_LMHEAD = range(5)
 
 
 class TierkError(RuntimeError):
@@ -62,6 +64,8 @@ SIGNATURES = [
     ("tk_workspace_bytes", _SZ, [_P]),
     ("tk_sync_status", _I, [_P, _P]),
     ("tk_launch_count", ctypes.c_uint64, [_P]),
+    ("tk_profile", _I, [_P, _I]),
+    ("tk_profile_read", _I, [_P, _I, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_uint64)]),
     ("tk_row_bytes", _SZ, [_I, _I]),
     ("tk_dequant", _I, [_P, _I, _P, _SZ, _I, _I, _I, _I, _P, _P]),
     ("tk_gemv", _I, [_P, _I, _P, _SZ, _I, _I, _P, _I, _I, _P, _I, _P]),
@@ -145,6 +149,15 @@ class Context:
     def sync_status(self, stream=None):
         _check(self.lib.tk_sync_status(self.h, _stream(stream)))
 
+    def profile(self, enable: bool):
+        _check(self.lib.tk_profile(self.h, 1 if enable else 0))
+
+    def profile_read(self, kind: int) -> tuple[float, int]:
+        t = ctypes.c_double(0)
+        n = ctypes.c_uint64(0)
+        _check(self.lib.tk_profile_read(self.h, kind, ctypes.byref(t), ctypes.byref(n)))
+        return t.value, int(n.value)
+
     def reserve(self, nbytes: int):
         _check(self.lib.tk_reserve(self.h, nbytes))
 
@@ -209,7 +222,9 @@ class Context:
 def make_weight(qtype: int, rows: int, cols: int, data, scale_log2: int = 0) -> Weight:
     """Describe a device weight tensor (uint8 blocks or fp16 planes) for the C ABI."""
     rb = cols * 2 if qtype in (F16, F16X2) else row_bytes(qtype, cols)
-    return Weight(qtype, rows, cols, scale_log2, rb, data.data_ptr())
+    w = Weight(qtype, rows, cols, scale_log2, rb, data.data_ptr())
+    w._owner = data   # the descriptor keeps its device memory alive
+    return w
 
 
 from .host import LinearPath, LMHead  # noqa: E402  (host-side mirror of the reference's operators)

@@ -42,6 +42,31 @@ tk_status ws_ensure(tk_ctx* ctx, size_t bytes, cudaStream_t stream) {
     return TK_OK;
 }
 
+constexpr size_t kProfPairs = 8192;
+
+int prof_begin(tk_ctx* ctx, cudaStream_t s) {
+    tk_prof& p = ctx->prof;
+    if (!p.on || p.used >= kProfPairs) return -1;
+    if (p.ev.size() < 2 * (p.used + 1)) {
+        cudaEvent_t a, b;
+        if (cudaEventCreate(&a) != cudaSuccess) return -1;
+        if (cudaEventCreate(&b) != cudaSuccess) { cudaEventDestroy(a); return -1; }
+        p.ev.push_back(a);
+        p.ev.push_back(b);
+    }
+    const int slot = (int)p.used++;
+    cudaEventRecord(p.ev[2 * slot], s);
+    return slot;
+}
+
+void prof_end(tk_ctx* ctx, cudaStream_t s, int slot, int kind) {
+    if (slot < 0) return;
+    tk_prof& p = ctx->prof;
+    cudaEventRecord(p.ev[2 * slot + 1], s);
+    if (p.kind.size() <= (size_t)slot) p.kind.resize(slot + 1);
+    p.kind[slot] = kind;
+}
+
 struct Carve {
     char* p;
     size_t used = 0;
@@ -53,6 +78,9 @@ struct Carve {
         return r;
     }
 };
+
+// k-blocks (64 each) per fp32 accumulation segment for the split product sets.
+constexpr int kSegKb = 8;
 
 static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
@@ -126,14 +154,16 @@ static tk_status linear(tk_ctx* ctx, const tk_weight* W, const void* A, int a_dt
     if (lda < a_cols || ldd < d_cols) return fail(TK_ERR_INVALID, std::string(fn) + ": leading dimension too small");
     if (a_dtype != TK_DT_F32 && a_dtype != TK_DT_F16 && a_dtype != TK_DT_BF16)
         return fail(TK_ERR_INVALID, std::string(fn) + ": activation dtype");
-    if (a_cols % 8) return fail(TK_ERR_INVALID, std::string(fn) + ": activation width must be a multiple of 8");
     if (!aligned16(D) || ldd % 4) return fail(TK_ERR_INVALID, std::string(fn) + ": output must be 16-byte aligned, ld % 4 == 0");
     Plan pl;
     st = plan_products(W, a_dtype, products, pl);
     if (st != TK_OK) return st;
 
     const bool quant = W->qtype != TK_F16 && W->qtype != TK_F16X2;
-    const size_t plane_elems = (size_t)M * a_cols;
+    // split planes use a row stride rounded up to 8 elements (16 bytes, the TMA
+    // stride rule); the GEMM's K extent stays a_cols, so the pad is never read.
+    const long a_ld = (a_cols + 7) / 8 * 8;
+    const size_t plane_elems = (size_t)M * a_ld;
     const size_t need = align256(plane_elems * 2 * pl.x_planes) + align256((size_t)M * 4) +
                         (quant ? align256((size_t)N * K * 2) : 0);
     st = ws_ensure(ctx, need, s);
@@ -153,14 +183,14 @@ static tk_status linear(tk_ctx* ctx, const tk_weight* W, const void* A, int a_dt
         if (W->qtype == TK_F16X2) wplanes[1] = wplanes[0] + (size_t)N * K;
     }
     if (pl.w_two && !wplanes[1]) return fail(TK_ERR_INVALID, std::string(fn) + ": product set needs two weight planes");
-    st = launch_act_split(ctx, A, a_dtype, M, a_cols, lda, pl.x_planes, true, pbase, row_exp, s);
+    st = launch_act_split(ctx, A, a_dtype, M, a_cols, lda, pl.x_planes, true, pbase, row_exp, s, a_ld);
     if (st != TK_OK) return st;
 
     GemmDesc g;
     for (int i = 0; i < pl.x_planes; ++i) g.A[i] = pbase + (size_t)i * plane_elems;
     g.B[0] = wplanes[0];
     g.B[1] = wplanes[1];
-    g.lda = a_cols;
+    g.lda = a_ld;
     g.ldb = K;
     g.b_mn = dx;
     g.M = M;
@@ -173,6 +203,8 @@ static tk_status linear(tk_ctx* ctx, const tk_weight* W, const void* A, int a_dt
     g.beta = beta != 0.0f;
     g.row_exp = row_exp;
     g.col_exp = W->qtype == TK_F16X2 ? W->scale_log2 : 0;
+    // fp32-accurate product sets: sum in fp32 every kSegKb k-blocks (see tk_gemm.cu)
+    g.seg_kb = pl.nprod > 1 ? kSegKb : 0;
     return launch_gemm(ctx, g, s);
 }
 
@@ -216,6 +248,7 @@ void tk_destroy(tk_ctx* ctx) {
     cudaDeviceSynchronize();
     if (ctx->ws) cudaFree(ctx->ws);
     if (ctx->status) cudaFree(ctx->status);
+    for (cudaEvent_t e : ctx->prof.ev) cudaEventDestroy(e);
     delete ctx;
 }
 
@@ -225,6 +258,34 @@ tk_status tk_reserve(tk_ctx* ctx, size_t bytes) {
 }
 
 size_t tk_workspace_bytes(const tk_ctx* ctx) { return ctx ? ctx->ws_bytes : 0; }
+
+tk_status tk_profile(tk_ctx* ctx, int enable) {
+    if (!ctx) return fail(TK_ERR_INVALID, "tk_profile: null context");
+    ctx->prof.on = enable != 0;
+    ctx->prof.used = 0;
+    return TK_OK;
+}
+
+tk_status tk_profile_read(tk_ctx* ctx, int kind, double* total_ms, uint64_t* launches) {
+    if (!ctx || !total_ms || !launches) return fail(TK_ERR_INVALID, "tk_profile_read: null argument");
+    if (kind < 0 || kind >= PK_COUNT) return fail(TK_ERR_INVALID, "tk_profile_read: kernel kind");
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) return cuda_fail(e, "tk_profile_read: sync");
+    double t = 0.0;
+    uint64_t n = 0;
+    const tk_prof& p = ctx->prof;
+    for (size_t i = 0; i < p.used; ++i) {
+        if (p.kind[i] != kind) continue;
+        float ms = 0.0f;
+        e = cudaEventElapsedTime(&ms, p.ev[2 * i], p.ev[2 * i + 1]);
+        if (e != cudaSuccess) return cuda_fail(e, "tk_profile_read: elapsed");
+        t += ms;
+        ++n;
+    }
+    *total_ms = t;
+    *launches = n;
+    return TK_OK;
+}
 
 uint64_t tk_launch_count(const tk_ctx* ctx) { return ctx ? ctx->launches : 0; }
 
@@ -432,6 +493,7 @@ tk_status tk_lmhead_grad(tk_ctx* ctx, const uint16_t* W, int v0, int V_shard, in
         for (int p = 0; p < np; ++p) { d.pa[p] = np - 1 - p; d.pb[p] = 0; }
         d.D = dX; d.ldd = H; d.beta = 1;
         d.col_exp = dl_exp;
+        d.seg_kb = kSegKb;
         st = launch_gemm(ctx, d, s);
         if (st != TK_OK) return st;
     }

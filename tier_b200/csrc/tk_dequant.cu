@@ -107,6 +107,7 @@ tk_status launch_dequant(tk_ctx* ctx, int t, const void* W, size_t rb, int r0, i
     size_t cap = (size_t)ctx->num_sms * 16;
     dim3 grid((unsigned)(want < cap ? want : cap)), block(threads);
     const uint8_t* w = static_cast<const uint8_t*>(W);
+    ProfScope ps(ctx, s, PK_DEQUANT);
     switch (t) {
         case QT_F32: dq_dispatch_out<QT_F32>(out_dtype, grid, block, s, w, rb, r0, nrows, cols, out); break;
         case QT_F16: dq_dispatch_out<QT_F16>(out_dtype, grid, block, s, w, rb, r0, nrows, cols, out); break;
@@ -149,7 +150,7 @@ __device__ __forceinline__ int row_exponent(float amax) {
 
 template <int XT, int NP>
 __global__ void __launch_bounds__(256) act_split_kernel(const void* __restrict__ X, int M, int K, long ldx,
-                                                        bool scaled, uint16_t* __restrict__ planes,
+                                                        long ldp, bool scaled, uint16_t* __restrict__ planes,
                                                         int* __restrict__ row_exp) {
     __shared__ float red[8];
     const int m = blockIdx.x;
@@ -173,7 +174,7 @@ __global__ void __launch_bounds__(256) act_split_kernel(const void* __restrict__
     }
     if (threadIdx.x == 0 && row_exp) row_exp[m] = e;
     const float f = pow2f(e);
-    const size_t pstride = (size_t)M * K, orow = (size_t)m * K;
+    const size_t pstride = (size_t)M * ldp, orow = (size_t)m * ldp;
     for (int k = threadIdx.x; k < K; k += blockDim.x) {
         const float v = ld_act<XT>(X, xrow + k) * f;
         const uint16_t h = f2h_bits(v);
@@ -192,19 +193,21 @@ __global__ void __launch_bounds__(256) act_split_kernel(const void* __restrict__
 }
 
 template <int XT>
-static void act_split_np(int np, int M, int K, long ldx, bool scaled, const void* X, uint16_t* planes, int* re,
-                         cudaStream_t s) {
-    if (np == 1) act_split_kernel<XT, 1><<<M, 256, 0, s>>>(X, M, K, ldx, scaled, planes, re);
-    else if (np == 2) act_split_kernel<XT, 2><<<M, 256, 0, s>>>(X, M, K, ldx, scaled, planes, re);
-    else act_split_kernel<XT, 3><<<M, 256, 0, s>>>(X, M, K, ldx, scaled, planes, re);
+static void act_split_np(int np, int M, int K, long ldx, long ldp, bool scaled, const void* X, uint16_t* planes,
+                         int* re, cudaStream_t s) {
+    if (np == 1) act_split_kernel<XT, 1><<<M, 256, 0, s>>>(X, M, K, ldx, ldp, scaled, planes, re);
+    else if (np == 2) act_split_kernel<XT, 2><<<M, 256, 0, s>>>(X, M, K, ldx, ldp, scaled, planes, re);
+    else act_split_kernel<XT, 3><<<M, 256, 0, s>>>(X, M, K, ldx, ldp, scaled, planes, re);
 }
 
 tk_status launch_act_split(tk_ctx* ctx, const void* X, int x_dtype, int M, int K, long ldx, int nplanes, bool scaled,
-                           uint16_t* planes, int* row_exp, cudaStream_t s) {
+                           uint16_t* planes, int* row_exp, cudaStream_t s, long ldp) {
     if (M == 0) return TK_OK;
-    if (x_dtype == TK_DT_F32) act_split_np<TK_DT_F32>(nplanes, M, K, ldx, scaled, X, planes, row_exp, s);
-    else if (x_dtype == TK_DT_F16) act_split_np<TK_DT_F16>(nplanes, M, K, ldx, scaled, X, planes, row_exp, s);
-    else if (x_dtype == TK_DT_BF16) act_split_np<TK_DT_BF16>(nplanes, M, K, ldx, scaled, X, planes, row_exp, s);
+    if (ldp <= 0) ldp = K;
+    ProfScope ps(ctx, s, PK_SPLIT);
+    if (x_dtype == TK_DT_F32) act_split_np<TK_DT_F32>(nplanes, M, K, ldx, ldp, scaled, X, planes, row_exp, s);
+    else if (x_dtype == TK_DT_F16) act_split_np<TK_DT_F16>(nplanes, M, K, ldx, ldp, scaled, X, planes, row_exp, s);
+    else if (x_dtype == TK_DT_BF16) act_split_np<TK_DT_BF16>(nplanes, M, K, ldx, ldp, scaled, X, planes, row_exp, s);
     else return fail(TK_ERR_INVALID, "activation dtype " + std::to_string(x_dtype));
     ctx->launches++;
     return cuda_fail(cudaGetLastError(), "act_split launch");
@@ -228,6 +231,7 @@ tk_status launch_split3_raw(tk_ctx* ctx, const float* x, size_t n, uint16_t* h, 
                             cudaStream_t s) {
     if (n == 0) return TK_OK;
     size_t want = (n + 255) / 256, cap = (size_t)ctx->num_sms * 16;
+    ProfScope ps(ctx, s, PK_SPLIT);
     split3_raw_kernel<<<(unsigned)(want < cap ? want : cap), 256, 0, s>>>(x, n, h, m, l);
     ctx->launches++;
     return cuda_fail(cudaGetLastError(), "split3 launch");

@@ -18,6 +18,11 @@
 //   warps 2-5   epilogue: tcgen05.ld rows of the finished accumulator while
 //               the MMA warp fills the other one; scale, optional beta,
 //               store (or the LM-head statistics / dlogit epilogues).
+// Accumulation segments: the tensor core's fp32 accumulation loses about one
+// ulp per MMA step, so a long K (and the x3 product sets, which triple the
+// steps) is cut into segments of seg_kb k-blocks.  Segments alternate between
+// the two TMEM accumulators and the epilogue sums them into D in fp32 (RNE),
+// so the error grows with the segment length, not with K.
 // All waits are bounded (tk_device.cuh); a timeout records a status code and
 // the roles drain out instead of hanging.
 #include <cuda.h>
@@ -45,6 +50,7 @@ struct __align__(64) GemmParams {
     int nprod;
     int pa[3], pb[3];
     int tiles_m, tiles_n;
+    int seg_kb;            // k-blocks per accumulation segment (>= 1)
     float* D;
     long ldd;
     int beta;
@@ -103,7 +109,6 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
 
     const int num_tiles = p.tiles_m * p.tiles_n;
     const int kblocks = (p.K + BK - 1) / BK;
-    const int stages_per_tile = kblocks * p.nprod;
 
     if (warp == 0) {
         // ---------------- TMA producer ----------------
@@ -139,39 +144,46 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             int s = 0;
             uint32_t ph = 0;
             bool ok = true;
-            int it = 0;
-            for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++it) {
-                const int acc = it & 1;
-                if (!mbar_wait(&tempty[acc], ((it >> 1) & 1) ^ 1, p.status)) break;
-                tc_fence_after();
-                const uint32_t d_tmem = tmem_base + acc * BN;
-                for (int st = 0; st < stages_per_tile; ++st) {
-                    if (!mbar_wait(&full[s], ph, p.status)) { ok = false; break; }
+            int u = 0;   // accumulation units (tile, segment) processed by this CTA
+            for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+                for (int kb0 = 0; kb0 < kblocks && ok; kb0 += p.seg_kb, ++u) {
+                    const int kb1 = kb0 + p.seg_kb < kblocks ? kb0 + p.seg_kb : kblocks;
+                    const int acc = u & 1;
+                    if (!mbar_wait(&tempty[acc], ((u >> 1) & 1) ^ 1, p.status)) { ok = false; break; }
                     tc_fence_after();
-                    const uint32_t a0 = smem_u32(sA + s * A_BYTES), b0 = smem_u32(sB + s * B_BYTES);
+                    const uint32_t d_tmem = tmem_base + acc * BN;
+                    const int nst = (kb1 - kb0) * p.nprod;
+                    for (int st = 0; st < nst; ++st) {
+                        if (!mbar_wait(&full[s], ph, p.status)) { ok = false; break; }
+                        tc_fence_after();
+                        const uint32_t a0 = smem_u32(sA + s * A_BYTES), b0 = smem_u32(sB + s * B_BYTES);
 #pragma unroll
-                    for (int kk = 0; kk < BK / 16; ++kk) {
-                        const uint64_t ad = sdesc_sw128(a0 + kk * 32, 16, 1024);
-                        const uint64_t bd = B_MN ? sdesc_sw128(b0 + kk * 2048, 64 * BK * 2, 1024)
-                                                 : sdesc_sw128(b0 + kk * 32, 16, 1024);
-                        tc_mma_f16(d_tmem, ad, bd, idesc, (st | kk) ? 1u : 0u);
+                        for (int kk = 0; kk < BK / 16; ++kk) {
+                            const uint64_t ad = sdesc_sw128(a0 + kk * 32, 16, 1024);
+                            const uint64_t bd = B_MN ? sdesc_sw128(b0 + kk * 2048, 64 * BK * 2, 1024)
+                                                     : sdesc_sw128(b0 + kk * 32, 16, 1024);
+                            tc_mma_f16(d_tmem, ad, bd, idesc, (st | kk) ? 1u : 0u);
+                        }
+                        tc_commit(&empty[s]);
+                        if (++s == STAGES) { s = 0; ph ^= 1; }
                     }
-                    tc_commit(&empty[s]);
-                    if (++s == STAGES) { s = 0; ph ^= 1; }
+                    if (ok) tc_commit(&tfull[acc]);
                 }
-                if (ok) tc_commit(&tfull[acc]);
             }
         }
         __syncwarp();
     } else {
         // ---------------- epilogue (warps 2..5) ----------------
         const int quarter = warp & 3;                 // TMEM lanes this warp may access
-        int it = 0;
-        for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++it) {
-            const int acc = it & 1;
-            const int mb = tile % p.tiles_m, nb = tile / p.tiles_m;
-            if (!mbar_wait(&tfull[acc], (it >> 1) & 1, p.status)) break;
+        int u = 0;
+        bool ok = true;
+        for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+          const int mb = tile % p.tiles_m, nb = tile / p.tiles_m;
+          for (int kb0 = 0; kb0 < kblocks; kb0 += p.seg_kb, ++u) {
+            const int acc = u & 1;
+            if (!mbar_wait(&tfull[acc], (u >> 1) & 1, p.status)) { ok = false; break; }
             tc_fence_after();
+            const bool add_prev = kb0 > 0 || p.beta;   // later segments (or beta = 1) add to D
             const int row = mb * BM + quarter * 32 + lane;
             const bool row_ok = row < p.M;
             const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN;
@@ -194,7 +206,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
                                 float4 v = make_float4(__uint_as_float(r[j]) * f, __uint_as_float(r[j + 1]) * f,
                                                        __uint_as_float(r[j + 2]) * f, __uint_as_float(r[j + 3]) * f);
                                 float4* dp = reinterpret_cast<float4*>(drow + col0 + j);
-                                if (p.beta) {
+                                if (add_prev) {
                                     const float4 o = *dp;
                                     v.x += o.x; v.y += o.y; v.z += o.z; v.w += o.w;
                                 }
@@ -205,7 +217,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
                             for (int j = 0; j < 32; ++j) {
                                 if (col0 + j < p.N) {
                                     float v = __uint_as_float(r[j]) * f;
-                                    if (p.beta) v += drow[col0 + j];
+                                    if (add_prev) v += drow[col0 + j];
                                     drow[col0 + j] = v;
                                 }
                             }
@@ -314,6 +326,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             }
             tc_fence_before();
             mbar_arrive(&tempty[acc]);
+          }
         }
     }
 
@@ -374,6 +387,7 @@ static tk_status go(tk_ctx* ctx, const GemmParams& gp, const EpiParams& ep, cuda
     }
     const int tiles = gp.tiles_m * gp.tiles_n;
     const int grid = tiles < ctx->num_sms ? tiles : ctx->num_sms;
+    ProfScope ps(ctx, s, PK_GEMM);
     gemm_tc_kernel<B_MN, EPI><<<grid, GEMM_THREADS, GEMM_SMEM, s>>>(gp, ep);
     ctx->launches++;
     return cuda_fail(cudaGetLastError(), "gemm launch");
@@ -405,6 +419,11 @@ static tk_status build(const GemmDesc& g, tk_ctx* ctx, GemmParams& gp) {
     for (int i = 0; i < 3; ++i) { gp.pa[i] = g.pa[i]; gp.pb[i] = g.pb[i]; }
     gp.tiles_m = (g.M + BM - 1) / BM;
     gp.tiles_n = (g.N + BN - 1) / BN;
+    {
+        const int kblocks = (g.K + BK - 1) / BK;
+        int seg = g.seg_kb > 0 ? g.seg_kb : kblocks;
+        gp.seg_kb = seg < kblocks ? seg : kblocks;
+    }
     gp.D = g.D; gp.ldd = g.ldd; gp.beta = g.beta;
     gp.row_exp = g.row_exp; gp.col_exp = g.col_exp;
     gp.status = ctx->status;
@@ -425,6 +444,7 @@ tk_status launch_gemm_lse(tk_ctx* ctx, const GemmDesc& g, const LseDesc& e, cuda
     GemmParams gp;
     tk_status st = build(g, ctx, gp);
     if (st != TK_OK) return st;
+    gp.seg_kb = (g.K + BK - 1) / BK;   // statistics need the complete logit
     EpiParams ep;
     memset(&ep, 0, sizeof(ep));
     ep.lse = e;
@@ -437,6 +457,7 @@ tk_status launch_gemm_dlogit(tk_ctx* ctx, const GemmDesc& g, const DlogitDesc& e
     tk_status st = build(g, ctx, gp);
     if (st != TK_OK) return st;
     if (g.N % BN) return fail(TK_ERR_INVALID, "dlogit epilogue needs a chunk width multiple of 256");
+    gp.seg_kb = (g.K + BK - 1) / BK;
     EpiParams ep;
     memset(&ep, 0, sizeof(ep));
     ep.dl = e;

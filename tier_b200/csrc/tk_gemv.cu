@@ -222,6 +222,7 @@ tk_status launch_gemv(tk_ctx* ctx, int t, const void* Wv, size_t rb, int N, int 
     const uint8_t* W = static_cast<const uint8_t*>(Wv);
     const int rows_per_block = GEMV_WARPS;
     int blocks = (N + rows_per_block - 1) / rows_per_block;
+    ProfScope ps(ctx, s, PK_GEMV);
     switch (t) {
         case QT_Q8_0: gemv_m<QT_Q8_0>(M, blocks, s, W, rb, N, K, x, ldx, y, ldy); break;
         case QT_Q4_0: gemv_m<QT_Q4_0>(M, blocks, s, W, rb, N, K, x, ldx, y, ldy); break;

@@ -3,8 +3,18 @@
 #include <cstddef>
 #include <cstdint>
 #include <string>
+#include <vector>
 #include <cuda_runtime.h>
 #include "../../include/tierk.h"
+
+// Optional per-kernel timing: CUDA events recorded on the launching stream
+// around each kernel (enabled with tk_profile; read with tk_profile_read).
+struct tk_prof {
+    bool on = false;
+    std::vector<cudaEvent_t> ev;   // pairs (start, stop)
+    std::vector<int> kind;         // one per pair
+    size_t used = 0;               // pairs recorded
+};
 
 struct tk_ctx {
     int device = 0;
@@ -13,9 +23,20 @@ struct tk_ctx {
     size_t ws_bytes = 0;
     int* status = nullptr;       // device status word (tk::DEV_*)
     uint64_t launches = 0;       // kernels launched through this context
+    tk_prof prof;
 };
 
 namespace tk {
+
+// Kernel families for tk_profile_read (TK_PROF_* in tierk.h).
+enum ProfKind { PK_GEMM = 0, PK_DEQUANT = 1, PK_SPLIT = 2, PK_GEMV = 3, PK_LMHEAD = 4, PK_COUNT = 5 };
+int prof_begin(tk_ctx* ctx, cudaStream_t s);
+void prof_end(tk_ctx* ctx, cudaStream_t s, int slot, int kind);
+struct ProfScope {
+    tk_ctx* c; cudaStream_t s; int slot; int kind;
+    ProfScope(tk_ctx* c_, cudaStream_t s_, int k) : c(c_), s(s_), slot(prof_begin(c_, s_)), kind(k) {}
+    ~ProfScope() { prof_end(c, s, slot, kind); }
+};
 
 // Thread-local last-error text; returns `st` for chaining.
 tk_status fail(tk_status st, const std::string& msg);
@@ -35,7 +56,7 @@ tk_status launch_dequant(tk_ctx* ctx, int qtype, const void* W, size_t rb, int r
 // planes + p*M*K) of X * 2^e_m, e_m per row so that max|row|*2^e_m is in
 // [2^14, 2^15); row_exp[m] = e_m.  scaled == false uses e_m = 0.
 tk_status launch_act_split(tk_ctx* ctx, const void* X, int x_dtype, int M, int K, long ldx, int nplanes,
-                           bool scaled, uint16_t* planes, int* row_exp, cudaStream_t s);
+                           bool scaled, uint16_t* planes, int* row_exp, cudaStream_t s, long ldp = 0);
 tk_status launch_split3_raw(tk_ctx* ctx, const float* x, size_t n, uint16_t* h, uint16_t* m, uint16_t* l,
                             cudaStream_t s);
 tk_status weight_split_f32(tk_ctx* ctx, const float* W, int rows, int cols, uint16_t* planes, int* scale_log2,
@@ -65,6 +86,7 @@ struct GemmDesc {
     int beta = 0;
     const int* row_exp = nullptr;
     int col_exp = 0;
+    int seg_kb = 0;        // k-blocks (of 64) per fp32 accumulation segment; 0 = whole K
 };
 tk_status launch_gemm(tk_ctx* ctx, const GemmDesc& g, cudaStream_t s);
 

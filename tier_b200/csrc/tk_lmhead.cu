@@ -54,6 +54,7 @@ tk_status launch_lse_merge(tk_ctx* ctx, const float* pmax, const int32_t* parg, 
                            cudaStream_t s) {
     if (n_pred <= 0) return TK_OK;
     const int warps = 8;
+    ProfScope ps(ctx, s, PK_LMHEAD);
     lse_merge_kernel<<<(n_pred + warps - 1) / warps, warps * 32, 0, s>>>(pmax, parg, psum, ptgt, ld_part, ntiles,
                                                                           n_pred, vc, v0, labels, mask, rmax, rsum,
                                                                           amax, tgt);
@@ -94,6 +95,7 @@ __global__ void lm_loss_kernel(int T, const int32_t* __restrict__ labels, const 
 tk_status launch_lm_loss(tk_ctx* ctx, int T, const int32_t* labels, const uint8_t* mask, const double* rmax,
                          const double* rsum, const int32_t* amax, const float* tgt, double* loss, int32_t* hits,
                          cudaStream_t s) {
+    ProfScope ps(ctx, s, PK_LMHEAD);
     lm_loss_kernel<<<1, 256, 0, s>>>(T, labels, mask, rmax, rsum, amax, tgt, loss, hits);
     ctx->launches++;
     return cuda_fail(cudaGetLastError(), "lm loss launch");
@@ -110,6 +112,7 @@ __global__ void lm_rescale_kernel(int n, double* rmax_l, double* rsum_l, const d
 tk_status launch_lm_rescale(tk_ctx* ctx, int n, double* rmax_l, double* rsum_l, const double* rmax_g,
                             cudaStream_t s) {
     if (n <= 0) return TK_OK;
+    ProfScope ps(ctx, s, PK_LMHEAD);
     lm_rescale_kernel<<<(n + 255) / 256, 256, 0, s>>>(n, rmax_l, rsum_l, rmax_g);
     ctx->launches++;
     return cuda_fail(cudaGetLastError(), "lm rescale launch");
