@@ -137,6 +137,20 @@ tk_status tk_linear_fwd(tk_ctx *ctx, const tk_weight *W, const void *X, int x_dt
 tk_status tk_linear_dx(tk_ctx *ctx, const tk_weight *W, const void *dY, int dy_dtype, int M,
                        int lddy, float *dX, int lddx, float beta, int products, void *stream);
 
+/* tk_linear_fwd for callers that cannot allocate device memory -- an engine
+ * that budgets all VRAM through its own arena, or code that must not call
+ * cudaMalloc once running.  No counterpart in the reference.  Same arguments
+ * and results as tk_linear_fwd, restricted to TK_F16 / TK_F16X2 weights; it
+ * calls no cudaMalloc/cudaFree and never touches the context workspace.  Its
+ * scratch is a static 24 MiB device array inside libtierk.so (held on every
+ * GPU that loads the library until exit): 2 * parts * M * round8(K) + 4 * M
+ * bytes (each term rounded up to 256) must fit, else TK_ERR_INVALID.  The
+ * first call on a device looks up the array's address; make it before any
+ * stream capture.  Calls on one device share the array, so calls whose GPU
+ * work overlaps race: order them on one stream. */
+tk_status tk_linear_fwd_noalloc(tk_ctx *ctx, const tk_weight *W, const void *X, int x_dtype, int M,
+                                int ldx, float *Y, int ldy, float beta, int products, void *stream);
+
 /* Split an fp32 weight into the TK_F16X2 planes: planes[0 .. rows*cols) = hi,
  * planes[rows*cols .. 2*rows*cols) = lo, both W * 2^s with s chosen so that
  * max|W| * 2^s lies in [2^14, 2^15).  *scale_log2 receives s (written after the

@@ -71,6 +71,7 @@ SIGNATURES = [
     ("tk_gemv", _I, [_P, _I, _P, _SZ, _I, _I, _P, _I, _I, _P, _I, _P]),
     ("tk_linear_fwd", _I, [_P, ctypes.POINTER(Weight), _P, _I, _I, _I, _P, _I, _F, _I, _P]),
     ("tk_linear_dx", _I, [_P, ctypes.POINTER(Weight), _P, _I, _I, _I, _P, _I, _F, _I, _P]),
+    ("tk_linear_fwd_noalloc", _I, [_P, ctypes.POINTER(Weight), _P, _I, _I, _I, _P, _I, _F, _I, _P]),
     ("tk_weight_split_f32", _I, [_P, _P, _I, _I, _P, ctypes.POINTER(_I), _P]),
     ("tk_split3", _I, [_P, _P, _SZ, _P, _P, _P, _P]),
     ("tk_lmhead_stats", _I, [_P, _P, _I, _I, _I, _P, _I, _P, _P, _F, _I, _I, _P, _P, _P, _P, _P]),
