@@ -1,15 +1,15 @@
 #!/usr/bin/env python3
 """Benchmark of the tierk frozen-weight linear path on B200.
 
-Default workload (the metric's single-GPU config):
+Default workload (the metric's single-GPU configuration):
   Q4_K weight W[14336, 4096] (SwiGLU up-proj), X bf16 [4096, 4096], dY bf16
   [4096, 14336]; one step = forward Y = X.W^T plus input gradient dX = dY.W,
   both through the C ABI (tk_linear_fwd / tk_linear_dx): bit-exact dequant of
   W to fp16, activation conversion, tcgen05 GEMM with fp32 accumulation.
   Useful work per step: 2 x 2*M*N*K = 962.1 GFLOP.
 
-Multi-GPU (torchrun, one process per GPU, NCCL): W is split by output rows
-(north_star's partition); each rank computes its Y columns and its partial
+Multi-GPU (torchrun, one process per GPU, NCCL): W is split by output rows;
+each rank computes its Y columns and its partial
 dX; Y shards are all-gathered and dX partials all-reduced inside the step.
 Total work is fixed (strong scaling); value = total FLOP / max-over-ranks time.
 
@@ -62,7 +62,7 @@ class Clocks:
     def start(self):
         try:
             self.p = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}",
-                                       "--format=csv,noheader,nounits", "-lms", "200"],
+                                       "--format=csv,noheader,nounits", "-lms", "100"],
                                       stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.p = None
@@ -219,11 +219,18 @@ def run_ours(args):
         torch.cuda.synchronize(dev)
 
     # ---- device-resident timing ----
+    # Clocks are sampled from before the warm-up to after the timed steps; the
+    # warm-up is extended to >= 1 s of load so the 100 ms samples see the GPU busy.
+    clocks = Clocks(local)
+    clocks.start()
+    t0 = time.perf_counter()
     for _ in range(args.warmup):
         step(Xd, dYd)
     barrier()
-    clocks = Clocks(local)
-    clocks.start()
+    while time.perf_counter() - t0 < 1.0:
+        for _ in range(10):
+            step(Xd, dYd)
+        barrier()
     n0 = ctx.launches()
     ctx.profile(True)
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -289,13 +296,12 @@ def run_ours(args):
         gemm_avg_ms = gemm_ms / max(gemm_n, 1)
         gemm_flop_launch = flop_step / 2 / world      # one direction on this rank's rows
         achieved = gemm_flop_launch / (gemm_avg_ms * 1e-3) / 1e12
-        traffic = None
-        tf = ROOT / "profiles" / "gemm_traffic.json"
+        traffic = None   # dram read+write bytes per GEMM launch from the committed ncu summary
+        tf = ROOT / "profiles" / "gemm_tc_kernel_c2_q4k_m4096.md"
         if tf.exists():
-            try:
-                traffic = json.loads(tf.read_text()).get("c2_bytes_per_launch")
-            except Exception:
-                traffic = None
+            for ln in tf.read_text().splitlines():
+                if ln.startswith("traffic_bytes_per_launch:"):
+                    traffic = float(ln.split(":")[1].split()[0])
         line = {
             "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "strong",

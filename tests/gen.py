@@ -1,4 +1,4 @@
-"""Seeded synthetic inputs for the BASELINE configurations (numpy default_rng;
+"""Seeded synthetic inputs for the benchmark configurations (numpy default_rng;
 generation order fixed here).  No dataset is involved: the reference measures
 this path on no public suite, so these stand in with the stated shapes and
 value distributions.
