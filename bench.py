@@ -329,6 +329,176 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+# ---------------------------------------------------------------------------
+# Secondary configurations (not the driver's headline line): --config c1|c3|c4
+def _timed(ctx, fn, steps, warmup, kind):
+    import torch
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    while time.perf_counter() - t0 < 0.5:
+        fn()
+        torch.cuda.synchronize()
+    clocks = Clocks(torch.cuda.current_device())
+    clocks.start()
+    time.sleep(0.25)
+    ctx.profile(True)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record()
+    for _ in range(steps):
+        fn()
+    ev1.record()
+    torch.cuda.synchronize()
+    t_ms = ev0.elapsed_time(ev1)
+    k_ms, k_n = ctx.profile_read(kind)
+    ctx.profile(False)
+    return t_ms, k_ms, k_n, clocks.stop()
+
+
+def run_c1(args):
+    """C1: q8_0 decode GEMV W[4096, 4096], M = 1, rotating over distinct
+    weight copies (>= 4x the 126 MB L2) so every launch reads HBM.  The
+    launches are captured in one CUDA graph and the graph is replayed, so the
+    timing measures back-to-back kernels, not the host's launch rate."""
+    import numpy as np
+    import torch
+    import tier_b200 as tk
+    from gen import q8_0_blocks
+    ctx = tk.Context(0)
+    N = K = 4096
+    rng = np.random.default_rng(0)
+    out = {}
+    for M in (1, 4, 16):
+        b = q8_0_blocks(rng, N, K)
+        wbytes = b.nbytes
+        copies = int(np.ceil(4 * 126e6 / wbytes))
+        W = torch.from_numpy(b).cuda()
+        pool = [W.clone() for _ in range(copies)]
+        x = torch.from_numpy(rng.standard_normal((M, K)).astype(np.float32)).cuda()
+        y = torch.empty(M, N, device="cuda")
+        ctx.gemv(tk.Q8_0, pool[0], N, K, x, y, M=M)            # module load / attributes outside capture
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            for w in pool:
+                ctx.gemv(tk.Q8_0, w, N, K, x, y, M=M)
+        for _ in range(3):
+            g.replay()
+        torch.cuda.synchronize()
+        clocks = Clocks(torch.cuda.current_device())
+        clocks.start()
+        t0 = time.perf_counter()
+        while time.perf_counter() - t0 < 0.4:
+            g.replay()
+            torch.cuda.synchronize()
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ev0.record()
+        for _ in range(args.steps):
+            g.replay()
+        ev1.record()
+        torch.cuda.synchronize()
+        clk = clocks.stop()
+        per_launch = ev0.elapsed_time(ev1) / (args.steps * copies)
+        bytes_launch = wbytes + 4 * K * M + 4 * N * M
+        gbs = bytes_launch / (per_launch * 1e-3) / 1e9
+        out[M] = (per_launch, gbs, copies, clk)
+        del pool, g
+    hbm = peaks()[0]
+    per_launch, gbs, copies, clk = out[1]
+    print(json.dumps({"metric": "decode GEMV HBM GB/s (q8_0 4096x4096, M=1)", "value": gbs, "unit": "GB/s",
+                      "n_gpus": 1, "steps": args.steps, "higher_is_better": True,
+                      "us_per_launch": per_launch * 1e3,
+                      "by_M": {m: {"us_per_launch": v[0] * 1e3, "GB_s": v[1]} for m, v in out.items()},
+                      "config": {"workload": "C1 q8_0 GEMV 4096x4096", "rotating_copies": copies,
+                                 "bytes_per_launch_M1": 17825792 + 4 * 4096 * 2, "timing": "CUDA graph replay"},
+                      "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s",
+                                   "frac": gbs / hbm}, "clocks": clk}))
+
+
+def run_c3(args):
+    """C3: the seven projections of one 12B-class layer (hidden 5120, q 4096,
+    k/v 1024, o, SwiGLU 14336), fp32 weights split into fp16 hi/lo, fp32 X
+    (M = 4096 tokens); forward + dX of every projection per step, products
+    Xh.Wh + Xh.Wl + Xl.Wh."""
+    import torch
+    import tier_b200 as tk
+    from tier_b200.host import LinearPath
+    ctx = tk.Context(0)
+    M, H, I = 4096, 5120, 14336
+    shapes = [(4096, H), (1024, H), (1024, H), (H, 4096), (I, H), (I, H), (H, I)]   # q k v o gate up down
+    g = torch.Generator(device="cuda").manual_seed(2)
+    lps, xs, dys = [], {}, []
+    for (n, k) in shapes:
+        W = torch.randn(n, k, device="cuda", generator=g) * 0.02
+        lps.append(LinearPath.from_f32_split(ctx, W))
+        del W
+        if k not in xs:
+            xs[k] = torch.randn(M, k, device="cuda", generator=g)
+        dys.append(torch.randn(M, n, device="cuda", generator=g))
+    outs = [torch.empty(M, n, device="cuda") for (n, _) in shapes]
+    dxs = [torch.empty(M, k, device="cuda") for (_, k) in shapes]
+
+    def fn():
+        for lp, (n, k), y, dy, dx in zip(lps, shapes, outs, dys, dxs):
+            ctx.linear(lp.W, xs[k], M, y, products=tk.X3_HHL)
+            ctx.linear_dx(lp.W, dy, M, dx, products=tk.X3_HHL)
+
+    t_ms, k_ms, k_n, clk = _timed(ctx, fn, args.steps, 3, tk.PROF_GEMM)
+    snk = sum(n * k for n, k in shapes)
+    useful = 2 * 2.0 * M * snk
+    ms = t_ms / args.steps
+    tf_burst = peaks()[1]
+    gemm_tf_exec = 3 * useful / (k_ms / args.steps * 1e-3) / 1e12
+    print(json.dumps({"metric": "fp16 x3 split GEMM TFLOP/s (12B layer, fwd + dX)", "value": useful / (ms * 1e-3) / 1e12,
+                      "unit": "TFLOP/s (fp32-equivalent useful)", "executed_tflops": 3 * useful / (ms * 1e-3) / 1e12,
+                      "ms_per_step": ms, "steps": args.steps, "n_gpus": 1,
+                      "config": {"workload": "C3 12B layer x3 (Xh.Wh+Xh.Wl+Xl.Wh), M=4096, fp32 X and W",
+                                 "useful_tflop_per_step": useful / 1e12},
+                      "roofline": {"bound": "tensor", "achieved": gemm_tf_exec, "peak": tf_burst, "unit": "TFLOP/s",
+                                   "frac": gemm_tf_exec / tf_burst, "kernel": "gemm_tc_kernel (executed products)"},
+                      "clocks": clk}))
+
+
+def run_c4(args):
+    """C4: chunked-vocab LM head + CE: W fp16 [262144, 3840], hidden fp32
+    [8192, 3840], labels uniform, chunk 16384; pass 1 (stats), loss, pass 2
+    (dX) per step with the three-part split of X and of dlogit."""
+    import torch
+    import tier_b200 as tk
+    from tier_b200.host import LMHead
+    ctx = tk.Context(0)
+    V, H, T, chunk = 262144, 3840, 8192, 16384
+    g = torch.Generator(device="cuda").manual_seed(3)
+    W = (torch.randn(V, H, device="cuda", generator=g) * 0.02).half()
+    X = torch.randn(T, H, device="cuda", generator=g)
+    labels = torch.randint(0, V, (T,), device="cuda", generator=g, dtype=torch.int32)
+    mask = torch.ones(T, dtype=torch.uint8, device="cuda")
+    head = LMHead(ctx, W, 0, chunk=chunk, products=tk.X3_REF)
+    dX = torch.zeros(T, H, device="cuda")
+    n_loss = T - 1
+
+    def fn():
+        rmax, rsum, amax, tgt = head.stats(X, labels, mask)
+        head.loss(T, labels, mask, rmax, rsum, amax, tgt)
+        head.grad(X, labels, mask, n_loss, rmax, rsum, dX=dX)
+
+    steps = max(1, min(args.steps, 5))
+    t_ms, k_ms, k_n, clk = _timed(ctx, fn, steps, 1, tk.PROF_GEMM)
+    ms = t_ms / steps
+    useful = 2 * 2.0 * T * V * H
+    executed = 3 * 3 * 2.0 * T * V * H
+    tf_burst = peaks()[1]
+    gemm_exec = executed / (k_ms / steps * 1e-3) / 1e12
+    print(json.dumps({"metric": "LM head + CE TFLOP/s (useful: logits + dX GEMMs)", "value": useful / (ms * 1e-3) / 1e12,
+                      "unit": "TFLOP/s", "executed_tflops": executed / (ms * 1e-3) / 1e12, "ms_per_step": ms,
+                      "steps": steps, "n_gpus": 1,
+                      "config": {"workload": "C4 V=262144 H=3840 T=8192 chunk=16384, two-pass, x3 split"},
+                      "roofline": {"bound": "tensor", "achieved": gemm_exec, "peak": tf_burst, "unit": "TFLOP/s",
+                                   "frac": gemm_exec / tf_burst, "kernel": "gemm_tc_kernel (executed products)"},
+                      "clocks": clk}))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -337,8 +507,12 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--ref-seconds", type=float, default=10.0, help="CPU baseline sample size (seconds)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--config", default="c2", choices=["c1", "c2", "c3", "c4"],
+                    help="c2 (default, the headline) or a secondary configuration on one GPU")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    if args.impl == "ours" and args.config != "c2":
+        return {"c1": run_c1, "c3": run_c3, "c4": run_c4}[args.config](args)
     if args.impl == "reference":
         run_reference(args)
     else:

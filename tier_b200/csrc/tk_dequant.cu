@@ -49,9 +49,13 @@ __device__ __forceinline__ void decode8(const uint8_t* row, int c, float (&v)[8]
     } else if constexpr (T == QT_Q8_0) {
         const uint8_t* b = row + (size_t)(c >> 5) * 34;
         const float d = blk_scale(b);
-        const uint8_t* q = b + 2 + (c & 31);
+        const uint16_t* q = reinterpret_cast<const uint16_t*>(b + 2 + (c & 31));   // 2-byte aligned
 #pragma unroll
-        for (int j = 0; j < 8; ++j) v[j] = __fmul_rn(d, (float)(int8_t)q[j]);
+        for (int j = 0; j < 4; ++j) {
+            const uint32_t w = q[j] ^ 0x8080u;                 // int8 pair -> biased uint8 pair
+            v[2 * j] = __fmul_rn(d, small_u2f(w & 0xffu) - 128.0f);
+            v[2 * j + 1] = __fmul_rn(d, small_u2f(w >> 8) - 128.0f);
+        }
     } else if constexpr (T == QT_F16) {
         const uint4 w = *reinterpret_cast<const uint4*>(row + (size_t)c * 2);
         const uint32_t u[4] = {w.x, w.y, w.z, w.w};
@@ -63,29 +67,67 @@ __device__ __forceinline__ void decode8(const uint8_t* row, int c, float (&v)[8]
     }
 }
 
-template <int T, int OUT>
-__global__ void __launch_bounds__(256) dequant_kernel(const uint8_t* __restrict__ W, size_t rb, int r0, int nrows,
-                                                      int cols, void* __restrict__ out) {
-    const int gpr = cols >> 3;                       // 8-element groups per row
-    const size_t total = (size_t)nrows * gpr;
-    for (size_t g = blockIdx.x * (size_t)blockDim.x + threadIdx.x; g < total; g += (size_t)gridDim.x * blockDim.x) {
-        const int r = (int)(g / gpr), c = (int)(g % gpr) * 8;
-        float v[8];
-        decode8<T>(W + (size_t)(r0 + r) * rb, c, v);
-        const size_t o = (size_t)r * cols + c;
-        if constexpr (OUT == TK_DT_F32) {
-            float4* p = reinterpret_cast<float4*>(static_cast<float*>(out) + o);
-            p[0] = make_float4(v[0], v[1], v[2], v[3]);
-            p[1] = make_float4(v[4], v[5], v[6], v[7]);
-        } else {
-            uint32_t u[4];
+constexpr int DQ_UNROLL = 4;   // independent 8-element groups in flight per thread
+
+template <int OUT>
+__device__ __forceinline__ void store8(void* __restrict__ out, size_t o, const float (&v)[8]) {
+    if constexpr (OUT == TK_DT_F32) {
+        float4* p = reinterpret_cast<float4*>(static_cast<float*>(out) + o);
+        p[0] = make_float4(v[0], v[1], v[2], v[3]);
+        p[1] = make_float4(v[4], v[5], v[6], v[7]);
+    } else if constexpr (OUT == TK_DT_F16) {
+        // packed round-to-nearest-even; NaN needs the reference's bit pattern
+        // (sign | 0x7e00), so fall back per element only if one is present.
+        const bool nan = (v[0] != v[0]) | (v[1] != v[1]) | (v[2] != v[2]) | (v[3] != v[3]) | (v[4] != v[4]) |
+                         (v[5] != v[5]) | (v[6] != v[6]) | (v[7] != v[7]);
+        uint32_t u[4];
+        if (!nan) {
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
-                uint16_t lo = OUT == TK_DT_F16 ? f2h_bits(v[2 * j]) : f2bf_bits(v[2 * j]);
-                uint16_t hi = OUT == TK_DT_F16 ? f2h_bits(v[2 * j + 1]) : f2bf_bits(v[2 * j + 1]);
-                u[j] = (uint32_t)lo | ((uint32_t)hi << 16);
+                const __half2 h = __floats2half2_rn(v[2 * j], v[2 * j + 1]);
+                u[j] = *reinterpret_cast<const uint32_t*>(&h);
             }
-            *reinterpret_cast<uint4*>(static_cast<uint16_t*>(out) + o) = make_uint4(u[0], u[1], u[2], u[3]);
+        } else {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) u[j] = (uint32_t)f2h_bits(v[2 * j]) | ((uint32_t)f2h_bits(v[2 * j + 1]) << 16);
+        }
+        *reinterpret_cast<uint4*>(static_cast<uint16_t*>(out) + o) = make_uint4(u[0], u[1], u[2], u[3]);
+    } else {
+        uint32_t u[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            uint16_t lo = OUT == TK_DT_F16 ? f2h_bits(v[2 * j]) : f2bf_bits(v[2 * j]);
+            uint16_t hi = OUT == TK_DT_F16 ? f2h_bits(v[2 * j + 1]) : f2bf_bits(v[2 * j + 1]);
+            u[j] = (uint32_t)lo | ((uint32_t)hi << 16);
+        }
+        *reinterpret_cast<uint4*>(static_cast<uint16_t*>(out) + o) = make_uint4(u[0], u[1], u[2], u[3]);
+    }
+}
+
+// Grid: x = chunks of DQ_THREADS*DQ_UNROLL groups within a row, y = rows
+// (strided).  No integer division on the device.
+constexpr int DQ_THREADS = 128;
+
+template <int T, int OUT>
+__global__ void __launch_bounds__(DQ_THREADS) dequant_kernel(const uint8_t* __restrict__ W, size_t rb, int r0,
+                                                             int nrows, int cols, void* __restrict__ out) {
+    const int gpr = cols >> 3;                       // 8-element groups per row
+    for (int r = blockIdx.y; r < nrows; r += gridDim.y) {
+        const uint8_t* row = W + (size_t)(r0 + r) * rb;
+        const size_t orow = (size_t)r * cols;
+        for (int base = blockIdx.x * DQ_THREADS * DQ_UNROLL + threadIdx.x; base < gpr;
+             base += gridDim.x * DQ_THREADS * DQ_UNROLL) {
+            float v[DQ_UNROLL][8];
+#pragma unroll
+            for (int u = 0; u < DQ_UNROLL; ++u) {
+                const int g = base + u * DQ_THREADS;
+                if (g < gpr) decode8<T>(row, g * 8, v[u]);
+            }
+#pragma unroll
+            for (int u = 0; u < DQ_UNROLL; ++u) {
+                const int g = base + u * DQ_THREADS;
+                if (g < gpr) store8<OUT>(out, orow + (size_t)g * 8, v[u]);
+            }
         }
     }
 }
@@ -101,11 +143,11 @@ static void dq_dispatch_out(int out_dtype, dim3 g, dim3 b, cudaStream_t s, const
 tk_status launch_dequant(tk_ctx* ctx, int t, const void* W, size_t rb, int r0, int nrows, int cols, int out_dtype,
                          void* out, cudaStream_t s) {
     if (nrows == 0) return TK_OK;
-    const size_t groups = (size_t)nrows * (cols / 8);
-    const int threads = 256;
-    size_t want = (groups + threads - 1) / threads;
-    size_t cap = (size_t)ctx->num_sms * 16;
-    dim3 grid((unsigned)(want < cap ? want : cap)), block(threads);
+    const int gpr = cols / 8;
+    const int gx = (gpr + DQ_THREADS * DQ_UNROLL - 1) / (DQ_THREADS * DQ_UNROLL);
+    const int gy_cap = (ctx->num_sms * 16 + gx - 1) / gx;      // ~16 blocks per SM in flight
+    const int gy = nrows < gy_cap ? nrows : (gy_cap < 65535 ? gy_cap : 65535);
+    dim3 grid((unsigned)gx, (unsigned)gy), block(DQ_THREADS);
     const uint8_t* w = static_cast<const uint8_t*>(W);
     ProfScope ps(ctx, s, PK_DEQUANT);
     switch (t) {
@@ -192,6 +234,87 @@ __global__ void __launch_bounds__(256) act_split_kernel(const void* __restrict__
     }
 }
 
+// Vector variant: K % 8 == 0, 16-byte aligned rows.  The row stays in
+// registers between the max pass and the split, so X is read from HBM once;
+// loads are 16 B (bf16/fp16) or 2 x 16 B (fp32), plane stores 16 B.
+constexpr int AS_THREADS = 256, AS_MAXCH = 8;    // rows up to 256*8*8 = 16384 elements
+
+template <int XT>
+__device__ __forceinline__ void ld8(const void* X, size_t i, float (&v)[8]) {
+    if constexpr (XT == TK_DT_F32) {
+        const float4 a = *reinterpret_cast<const float4*>(static_cast<const float*>(X) + i);
+        const float4 b = *reinterpret_cast<const float4*>(static_cast<const float*>(X) + i + 4);
+        v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+    } else {
+        const uint4 w = *reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(X) + i);
+        const uint32_t u[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const uint16_t h = (uint16_t)(u[j >> 1] >> (16 * (j & 1)));
+            v[j] = XT == TK_DT_F16 ? h2f_bits(h) : __uint_as_float((uint32_t)h << 16);
+        }
+    }
+}
+
+__device__ __forceinline__ void st8h(uint16_t* p, const uint16_t (&h)[8]) {
+    *reinterpret_cast<uint4*>(p) = make_uint4((uint32_t)h[0] | ((uint32_t)h[1] << 16), (uint32_t)h[2] | ((uint32_t)h[3] << 16),
+                                              (uint32_t)h[4] | ((uint32_t)h[5] << 16), (uint32_t)h[6] | ((uint32_t)h[7] << 16));
+}
+
+template <int XT, int NP>
+__global__ void __launch_bounds__(AS_THREADS) act_split_vec_kernel(const void* __restrict__ X, int M, int K, long ldx,
+                                                                   long ldp, bool scaled, uint16_t* __restrict__ planes,
+                                                                   int* __restrict__ row_exp) {
+    __shared__ float red[AS_THREADS / 32];
+    const int m = blockIdx.x;
+    const int nch = K >> 3;
+    float v[AS_MAXCH][8];
+    float a = 0.0f;
+#pragma unroll
+    for (int i = 0; i < AS_MAXCH; ++i) {
+        const int c = threadIdx.x + i * AS_THREADS;
+        if (c < nch) {
+            ld8<XT>(X, (size_t)m * ldx + (size_t)c * 8, v[i]);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) a = fmaxf(a, fabsf(v[i][j]));
+        }
+    }
+    int e = 0;
+    if (scaled) {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
+        if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = a;
+        __syncthreads();
+        a = red[0];
+#pragma unroll
+        for (int w = 1; w < AS_THREADS / 32; ++w) a = fmaxf(a, red[w]);
+        e = row_exponent(a);
+    }
+    if (threadIdx.x == 0 && row_exp) row_exp[m] = e;
+    const float f = pow2f(e);
+    const size_t pstride = (size_t)M * ldp;
+    uint16_t* orow = planes + (size_t)m * ldp;
+#pragma unroll
+    for (int i = 0; i < AS_MAXCH; ++i) {
+        const int c = threadIdx.x + i * AS_THREADS;
+        if (c >= nch) continue;
+        uint16_t h[8], mm[8], l[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const float x = v[i][j] * f;
+            h[j] = f2h_bits(x);
+            if constexpr (NP >= 2) {
+                const float r = x - h2f_bits(h[j]);
+                mm[j] = f2h_bits(r);
+                if constexpr (NP == 3) l[j] = f2h_bits(r - h2f_bits(mm[j]));
+            }
+        }
+        st8h(orow + (size_t)c * 8, h);
+        if constexpr (NP >= 2) st8h(orow + pstride + (size_t)c * 8, mm);
+        if constexpr (NP == 3) st8h(orow + 2 * pstride + (size_t)c * 8, l);
+    }
+}
+
 template <int XT>
 static void act_split_np(int np, int M, int K, long ldx, long ldp, bool scaled, const void* X, uint16_t* planes,
                          int* re, cudaStream_t s) {
@@ -205,6 +328,25 @@ tk_status launch_act_split(tk_ctx* ctx, const void* X, int x_dtype, int M, int K
     if (M == 0) return TK_OK;
     if (ldp <= 0) ldp = K;
     ProfScope ps(ctx, s, PK_SPLIT);
+    const size_t esz = x_dtype == TK_DT_F32 ? 4 : 2;
+    const bool vec = K % 8 == 0 && ldx % 8 == 0 && ldp % 8 == 0 && K <= AS_THREADS * AS_MAXCH * 8 &&
+                     (reinterpret_cast<uintptr_t>(X) % 16) == 0 && (reinterpret_cast<uintptr_t>(planes) % 16) == 0 &&
+                     (ldx * esz) % 16 == 0;
+    if (vec) {
+#define TK_SPLIT_VEC(XT)                                                                                              \
+    do {                                                                                                              \
+        if (nplanes == 1) act_split_vec_kernel<XT, 1><<<M, AS_THREADS, 0, s>>>(X, M, K, ldx, ldp, scaled, planes, row_exp); \
+        else if (nplanes == 2) act_split_vec_kernel<XT, 2><<<M, AS_THREADS, 0, s>>>(X, M, K, ldx, ldp, scaled, planes, row_exp); \
+        else act_split_vec_kernel<XT, 3><<<M, AS_THREADS, 0, s>>>(X, M, K, ldx, ldp, scaled, planes, row_exp);          \
+    } while (0)
+        if (x_dtype == TK_DT_F32) TK_SPLIT_VEC(TK_DT_F32);
+        else if (x_dtype == TK_DT_F16) TK_SPLIT_VEC(TK_DT_F16);
+        else if (x_dtype == TK_DT_BF16) TK_SPLIT_VEC(TK_DT_BF16);
+        else return fail(TK_ERR_INVALID, "activation dtype " + std::to_string(x_dtype));
+#undef TK_SPLIT_VEC
+        ctx->launches++;
+        return cuda_fail(cudaGetLastError(), "act_split launch");
+    }
     if (x_dtype == TK_DT_F32) act_split_np<TK_DT_F32>(nplanes, M, K, ldx, ldp, scaled, X, planes, row_exp, s);
     else if (x_dtype == TK_DT_F16) act_split_np<TK_DT_F16>(nplanes, M, K, ldx, ldp, scaled, X, planes, row_exp, s);
     else if (x_dtype == TK_DT_BF16) act_split_np<TK_DT_BF16>(nplanes, M, K, ldx, ldp, scaled, X, planes, row_exp, s);

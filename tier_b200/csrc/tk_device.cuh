@@ -151,6 +151,63 @@ __device__ __forceinline__ void tc_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)[3
         : "r"(taddr));
 }
 
+// ---- CTA pairs (cluster of 2, cta_group::2) ----
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+// shared::cluster address of the same shared-memory offset in CTA `rank`.
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+    return r;
+}
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// Arrive on an mbarrier given by its shared::cluster address (possibly the peer's).
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+// Tiled TMA load into this CTA's shared memory whose completion is counted on
+// an mbarrier that may live in the peer CTA of the pair (cluster address).
+// Plain load: no multicast.
+__device__ __forceinline__ void tma_load_2d_cg2(void* smem_dst, const void* tmap, uint32_t bar_cluster, int x, int y) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
+            smem_u32(smem_dst)),
+        "l"(reinterpret_cast<uint64_t>(tmap)), "r"(bar_cluster), "r"(x), "r"(y)
+        : "memory");
+}
+__device__ __forceinline__ void tmem_alloc_cg2(uint32_t* smem_result, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(smem_result)),
+                 "r"(ncols)
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish_cg2() {
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc_cg2(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+// Pair MMA: D (rows split over the two CTAs' TMEM) (+)= A (rows split over the
+// two CTAs' shared memory) * B (columns split over the two CTAs' shared memory).
+__device__ __forceinline__ void tc_mma_f16_cg2(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                               uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+// Arrive on one mbarrier (cluster address) once the pair's issued MMAs retire.
+__device__ __forceinline__ void tc_commit_cg2(uint32_t bar_cluster) {
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar_cluster)
+                 : "memory");
+}
+
 // Shared-memory matrix descriptor (tcgen05 "version 1"), 128-byte swizzle.
 //   K-major tile: rows of 64 fp16 (128 B), 8-row atoms 1024 B apart (SBO).
 //   MN-major tile: 64 MN-elements (128 B) per K-row, K-rows 128 B apart,
@@ -298,20 +355,38 @@ __device__ __forceinline__ float qval(const uint8_t* row, int type, int col) {
 // eight consecutive bytes.  (d*sc)*q is exact in fp32 (11+6+4 significant
 // bits), so a single fused multiply-subtract rounds exactly like the
 // reference's separate multiply and subtract.
+// Exact float of a small non-negative integer (< 2^23) without the
+// int-to-float conversion pipe: OR it into the mantissa of 2^23, subtract 2^23.
+__device__ __forceinline__ float small_u2f(uint32_t q) { return __uint_as_float(0x4B000000u | q) - 8388608.0f; }
+
+// Sub-block scale and min from the 12 packed bytes held in registers
+// (hdr.y, hdr.z, hdr.w of the 16-byte super-block header).
+// Bytes 0-3 of the packed area are hdr.y, 4-7 hdr.z, 8-11 hdr.w; sub-block
+// j and j-4 (or j+4) always sit at the same byte position jj = j & 3.
+__device__ __forceinline__ void kq_scale_min_reg(int j, uint4 hdr, int& sc, int& mn) {
+    const int sh = 8 * (j & 3);
+    const int b0 = (hdr.y >> sh) & 0xff, b1 = (hdr.z >> sh) & 0xff, b2 = (hdr.w >> sh) & 0xff;
+    const int sc_lo = b0 & 63, mn_lo = b1 & 63;                                   // j < 4
+    const int sc_hi = (b2 & 0x0f) | ((b0 >> 6) << 4), mn_hi = (b2 >> 4) | ((b1 >> 6) << 4);   // j >= 4
+    sc = j < 4 ? sc_lo : sc_hi;
+    mn = j < 4 ? mn_lo : mn_hi;
+}
+
 __device__ __forceinline__ void q4k_decode8(const uint8_t* row, int c, float (&v)[8]) {
     const uint8_t* b = row + (size_t)(c >> 8) * 144;
     const int i = c & 255, g = i >> 6, l = i & 63;
-    int sc, mn;
-    kq_scale_min(2 * g + (l >= 32), b + 4, sc, mn);
-    const float a = __fmul_rn(blk_scale(b), (float)sc);
-    const float m = __fmul_rn(blk_scale(b + 2), (float)mn);
+    const uint4 hdr = *reinterpret_cast<const uint4*>(b);           // d, dmin, 12 scale bytes
     const uint2 w = *reinterpret_cast<const uint2*>(b + 16 + g * 32 + (l & 31));
+    int sc, mn;
+    kq_scale_min_reg(2 * g + (l >= 32), hdr, sc, mn);
+    const float a = __fmul_rn(h2f_bits((uint16_t)(hdr.x & 0xffff)), (float)sc);
+    const float m = __fmul_rn(h2f_bits((uint16_t)(hdr.x >> 16)), (float)mn);
     const int sh = l < 32 ? 0 : 4;
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
         uint32_t word = j < 4 ? w.x : w.y;
-        int q = (word >> (8 * (j & 3) + sh)) & 15;
-        v[j] = __fmaf_rn(a, (float)q, -m);
+        const uint32_t q = (word >> (8 * (j & 3) + sh)) & 15u;
+        v[j] = __fmaf_rn(a, small_u2f(q), -m);
     }
 }
 
@@ -320,19 +395,20 @@ __device__ __forceinline__ void q4k_decode8(const uint8_t* row, int c, float (&v
 __device__ __forceinline__ void q5k_decode8(const uint8_t* row, int c, float (&v)[8]) {
     const uint8_t* b = row + (size_t)(c >> 8) * 176;
     const int i = c & 255, g = i >> 6, l = i & 63;
-    int sc, mn;
-    kq_scale_min(2 * g + (l >= 32), b + 4, sc, mn);
-    const float a = __fmul_rn(blk_scale(b), (float)sc);
-    const float m = __fmul_rn(blk_scale(b + 2), (float)mn);
+    const uint4 hdr = *reinterpret_cast<const uint4*>(b);
     const uint2 w = *reinterpret_cast<const uint2*>(b + 48 + g * 32 + (l & 31));
     const uint2 hb = *reinterpret_cast<const uint2*>(b + 16 + (i & 31));
+    int sc, mn;
+    kq_scale_min_reg(2 * g + (l >= 32), hdr, sc, mn);
+    const float a = __fmul_rn(h2f_bits((uint16_t)(hdr.x & 0xffff)), (float)sc);
+    const float m = __fmul_rn(h2f_bits((uint16_t)(hdr.x >> 16)), (float)mn);
     const int sh = l < 32 ? 0 : 4, hsh = i >> 5;
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
         uint32_t word = j < 4 ? w.x : w.y;
         uint32_t hw = j < 4 ? hb.x : hb.y;
-        int q = ((word >> (8 * (j & 3) + sh)) & 15) | (((hw >> (8 * (j & 3) + hsh)) & 1) << 4);
-        v[j] = __fmaf_rn(a, (float)q, -m);
+        const uint32_t q = ((word >> (8 * (j & 3) + sh)) & 15u) | (((hw >> (8 * (j & 3) + hsh)) & 1u) << 4);
+        v[j] = __fmaf_rn(a, small_u2f(q), -m);
     }
 }
 

@@ -33,13 +33,23 @@
 
 namespace tk {
 
-constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4;
-constexpr int A_BYTES = BM * BK * 2;                 // 16 KB
-constexpr int B_BYTES = BN * BK * 2;                 // 32 KB
-constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr int BM = 128, BN = 256, BK = 64;     // BM: accumulator rows per CTA; BN: tile columns
 constexpr int TMEM_COLS = 512;
 constexpr int GEMM_THREADS = 192;
-constexpr size_t GEMM_SMEM = (size_t)STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+
+// Per CTA-group geometry.  CG = 1: one CTA computes a 128 x 256 tile.
+// CG = 2: a CTA pair (cluster of 2) computes a 256 x 256 tile with
+// tcgen05.mma.cta_group::2; each CTA holds its 128 rows of A, its 128
+// columns of B, and its 128 accumulator rows in TMEM.
+template <int CG>
+struct Geo {
+    static constexpr int STAGES = CG == 1 ? 4 : 6;
+    static constexpr int B_ROWS = BN / CG;                 // B rows (output columns) per CTA
+    static constexpr int A_BYTES = BM * BK * 2;            // 16 KB
+    static constexpr int B_BYTES = B_ROWS * BK * 2;        // 32 KB (CG 1) or 16 KB (CG 2)
+    static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+    static constexpr size_t SMEM = (size_t)STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+};
 
 enum { EPI_STORE = 0, EPI_LSE = 1, EPI_DLOGIT = 2 };
 
@@ -49,7 +59,7 @@ struct __align__(64) GemmParams {
     int M, N, K;
     int nprod;
     int pa[3], pb[3];
-    int tiles_m, tiles_n;
+    int tiles_m, tiles_n;  // in tiles of (128 * CG) x 256
     int seg_kb;            // k-blocks per accumulation segment (>= 1)
     float* D;
     long ldd;
@@ -68,20 +78,24 @@ __device__ __forceinline__ float exp2i(int e) {   // exact 2^e for e in [-126, 1
     return __uint_as_float((uint32_t)(e + 127) << 23);
 }
 
-template <bool B_MN, int EPI>
+template <int CG, bool B_MN, int EPI>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ GemmParams p, const __grid_constant__ EpiParams ep) {
+    using G = Geo<CG>;
+    constexpr int STAGES = G::STAGES;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* sA = smem;
-    uint8_t* sB = smem + STAGES * A_BYTES;
-    uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * B_BYTES);
+    uint8_t* sB = smem + STAGES * G::A_BYTES;
+    uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * G::B_BYTES);
     uint64_t* empty = full + STAGES;
     uint64_t* tfull = empty + STAGES;
     uint64_t* tempty = tfull + 2;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = CG == 2 ? cluster_ctarank() : 0;
+    const int cid = blockIdx.x / CG, ncl = gridDim.x / CG;      // tile-group index / count
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
             mbar_init(&full[s], 1);
@@ -89,7 +103,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         }
         for (int a = 0; a < 2; ++a) {
             mbar_init(&tfull[a], 1);
-            mbar_init(&tempty[a], 128);
+            mbar_init(&tempty[a], CG == 1 ? 128 : 8);   // CG 2: one arrival per epilogue warp of both CTAs
         }
         fence_mbar_init();
         fence_async_shared();
@@ -99,11 +113,17 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         tma_prefetch_desc(&p.tmB[0]);
     }
     if (warp == 1) {
-        tmem_alloc(tmem_slot, TMEM_COLS);
-        tmem_relinquish();
+        if constexpr (CG == 2) {
+            tmem_alloc_cg2(tmem_slot, TMEM_COLS);
+            tmem_relinquish_cg2();
+        } else {
+            tmem_alloc(tmem_slot, TMEM_COLS);
+            tmem_relinquish();
+        }
     }
     tc_fence_before();
     __syncthreads();
+    if constexpr (CG == 2) cluster_sync();   // peer barriers initialised before any remote signal
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
 
@@ -111,25 +131,44 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     const int kblocks = (p.K + BK - 1) / BK;
 
     if (warp == 0) {
-        // ---------------- TMA producer ----------------
+        // ---------------- TMA producer (each CTA loads its own operands) ----------------
         if (lane == 0) {
             int s = 0;
             uint32_t ph = 0;
             bool ok = true;
-            for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+            for (int tile = cid; tile < num_tiles && ok; tile += ncl) {
                 const int mb = tile % p.tiles_m, nb = tile / p.tiles_m;
+                const int arow = (mb * CG + (int)rank) * BM;
+                const int bcol = nb * BN + (int)rank * G::B_ROWS;
                 for (int kb = 0; kb < kblocks && ok; ++kb) {
                     for (int q = 0; q < p.nprod; ++q) {
                         if (!mbar_wait(&empty[s], ph ^ 1, p.status)) { ok = false; break; }
-                        mbar_arrive_expect_tx(&full[s], STAGE_BYTES);
-                        tma_load_2d(sA + s * A_BYTES, &p.tmA[p.pa[q]], &full[s], kb * BK, mb * BM);
-                        if constexpr (!B_MN) {
-                            tma_load_2d(sB + s * B_BYTES, &p.tmB[p.pb[q]], &full[s], kb * BK, nb * BN);
-                        } else {
+                        uint8_t* a_dst = sA + s * G::A_BYTES;
+                        uint8_t* b_dst = sB + s * G::B_BYTES;
+                        const void* ma = &p.tmA[p.pa[q]];
+                        const void* mbm = &p.tmB[p.pb[q]];
+                        if constexpr (CG == 1) {
+                            mbar_arrive_expect_tx(&full[s], G::STAGE_BYTES);
+                            tma_load_2d(a_dst, ma, &full[s], kb * BK, arow);
+                            if constexpr (!B_MN) {
+                                tma_load_2d(b_dst, mbm, &full[s], kb * BK, bcol);
+                            } else {
 #pragma unroll
-                            for (int j = 0; j < BN / 64; ++j)
-                                tma_load_2d(sB + s * B_BYTES + j * (64 * BK * 2), &p.tmB[p.pb[q]], &full[s],
-                                            nb * BN + 64 * j, kb * BK);
+                                for (int j = 0; j < G::B_ROWS / 64; ++j)
+                                    tma_load_2d(b_dst + j * (64 * BK * 2), mbm, &full[s], bcol + 64 * j, kb * BK);
+                            }
+                        } else {
+                            // both CTAs' loads complete on the leader's barrier
+                            const uint32_t fb = mapa_shared(smem_u32(&full[s]), 0);
+                            if (rank == 0) mbar_arrive_expect_tx(&full[s], 2 * G::STAGE_BYTES);
+                            tma_load_2d_cg2(a_dst, ma, fb, kb * BK, arow);
+                            if constexpr (!B_MN) {
+                                tma_load_2d_cg2(b_dst, mbm, fb, kb * BK, bcol);
+                            } else {
+#pragma unroll
+                                for (int j = 0; j < G::B_ROWS / 64; ++j)
+                                    tma_load_2d_cg2(b_dst + j * (64 * BK * 2), mbm, fb, bcol + 64 * j, kb * BK);
+                            }
                         }
                         if (++s == STAGES) { s = 0; ph ^= 1; }
                     }
@@ -138,14 +177,14 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         }
         __syncwarp();
     } else if (warp == 1) {
-        // ---------------- MMA issuer ----------------
-        if (lane == 0) {
-            constexpr uint32_t idesc = idesc_f16(BM, BN, 0, 0, B_MN ? 1 : 0);
+        // ---------------- MMA issuer (the leader CTA of a pair) ----------------
+        if (lane == 0 && rank == 0) {
+            constexpr uint32_t idesc = idesc_f16(BM * CG, BN, 0, 0, B_MN ? 1 : 0);
             int s = 0;
             uint32_t ph = 0;
             bool ok = true;
-            int u = 0;   // accumulation units (tile, segment) processed by this CTA
-            for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+            int u = 0;   // accumulation units (tile, segment) processed
+            for (int tile = cid; tile < num_tiles && ok; tile += ncl) {
                 for (int kb0 = 0; kb0 < kblocks && ok; kb0 += p.seg_kb, ++u) {
                     const int kb1 = kb0 + p.seg_kb < kblocks ? kb0 + p.seg_kb : kblocks;
                     const int acc = u & 1;
@@ -156,18 +195,33 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
                     for (int st = 0; st < nst; ++st) {
                         if (!mbar_wait(&full[s], ph, p.status)) { ok = false; break; }
                         tc_fence_after();
-                        const uint32_t a0 = smem_u32(sA + s * A_BYTES), b0 = smem_u32(sB + s * B_BYTES);
+                        const uint32_t a0 = smem_u32(sA + s * G::A_BYTES), b0 = smem_u32(sB + s * G::B_BYTES);
 #pragma unroll
                         for (int kk = 0; kk < BK / 16; ++kk) {
                             const uint64_t ad = sdesc_sw128(a0 + kk * 32, 16, 1024);
                             const uint64_t bd = B_MN ? sdesc_sw128(b0 + kk * 2048, 64 * BK * 2, 1024)
                                                      : sdesc_sw128(b0 + kk * 32, 16, 1024);
-                            tc_mma_f16(d_tmem, ad, bd, idesc, (st | kk) ? 1u : 0u);
+                            if constexpr (CG == 2) tc_mma_f16_cg2(d_tmem, ad, bd, idesc, (st | kk) ? 1u : 0u);
+                            else tc_mma_f16(d_tmem, ad, bd, idesc, (st | kk) ? 1u : 0u);
                         }
-                        tc_commit(&empty[s]);
+                        if constexpr (CG == 2) {
+                            const uint32_t e = smem_u32(&empty[s]);
+                            tc_commit_cg2(mapa_shared(e, 0));
+                            tc_commit_cg2(mapa_shared(e, 1));
+                        } else {
+                            tc_commit(&empty[s]);
+                        }
                         if (++s == STAGES) { s = 0; ph ^= 1; }
                     }
-                    if (ok) tc_commit(&tfull[acc]);
+                    if (ok) {
+                        if constexpr (CG == 2) {
+                            const uint32_t f = smem_u32(&tfull[acc]);
+                            tc_commit_cg2(mapa_shared(f, 0));
+                            tc_commit_cg2(mapa_shared(f, 1));
+                        } else {
+                            tc_commit(&tfull[acc]);
+                        }
+                    }
                 }
             }
         }
@@ -177,20 +231,19 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         const int quarter = warp & 3;                 // TMEM lanes this warp may access
         int u = 0;
         bool ok = true;
-        for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        for (int tile = cid; tile < num_tiles && ok; tile += ncl) {
           const int mb = tile % p.tiles_m, nb = tile / p.tiles_m;
           for (int kb0 = 0; kb0 < kblocks; kb0 += p.seg_kb, ++u) {
             const int acc = u & 1;
             if (!mbar_wait(&tfull[acc], (u >> 1) & 1, p.status)) { ok = false; break; }
             tc_fence_after();
             const bool add_prev = kb0 > 0 || p.beta;   // later segments (or beta = 1) add to D
-            const int row = mb * BM + quarter * 32 + lane;
+            const int row = (mb * CG + (int)rank) * BM + quarter * 32 + lane;
             const bool row_ok = row < p.M;
             const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN;
             const int e = (p.row_exp && row_ok ? p.row_exp[row] : 0) + p.col_exp;
             const float f = ldexpf(1.0f, -e);
             const int col_base = nb * BN;
-
             if constexpr (EPI == EPI_STORE) {
                 float* drow = p.D + (size_t)(row_ok ? row : 0) * p.ldd;
 #pragma unroll 1
@@ -325,16 +378,23 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
                 }
             }
             tc_fence_before();
-            mbar_arrive(&tempty[acc]);
+            if constexpr (CG == 2) {
+                __syncwarp();
+                if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&tempty[acc]), 0));
+            } else {
+                mbar_arrive(&tempty[acc]);
+            }
           }
         }
     }
 
     tc_fence_before();
     __syncthreads();
+    if constexpr (CG == 2) cluster_sync();   // the pair finishes together: no remote signal after exit
     if (warp == 1) {
         tc_fence_after();
-        tmem_dealloc(tmem_base, TMEM_COLS);
+        if constexpr (CG == 2) tmem_dealloc_cg2(tmem_base, TMEM_COLS);
+        else tmem_dealloc(tmem_base, TMEM_COLS);
     }
 }
 
@@ -376,24 +436,39 @@ static tk_status make_map(CUtensorMap* m, const void* base, long cols, long rows
     return TK_OK;
 }
 
-template <bool B_MN, int EPI>
+template <int CG, bool B_MN, int EPI>
 static tk_status go(tk_ctx* ctx, const GemmParams& gp, const EpiParams& ep, cudaStream_t s) {
+    using G = Geo<CG>;
     static bool attr_set = false;   // per instantiation
+    auto kern = gemm_tc_kernel<CG, B_MN, EPI>;
     if (!attr_set) {
-        cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<B_MN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             (int)GEMM_SMEM);
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)G::SMEM);
         if (e != cudaSuccess) return cuda_fail(e, "gemm smem attribute");
         attr_set = true;
     }
     const int tiles = gp.tiles_m * gp.tiles_n;
-    const int grid = tiles < ctx->num_sms ? tiles : ctx->num_sms;
+    const int groups_max = ctx->num_sms / CG;
+    const int groups = tiles < groups_max ? tiles : groups_max;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(groups * CG, 1, 1);
+    cfg.blockDim = dim3(GEMM_THREADS, 1, 1);
+    cfg.dynamicSmemBytes = G::SMEM;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = CG;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
     ProfScope ps(ctx, s, PK_GEMM);
-    gemm_tc_kernel<B_MN, EPI><<<grid, GEMM_THREADS, GEMM_SMEM, s>>>(gp, ep);
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kern, gp, ep);
     ctx->launches++;
+    if (e != cudaSuccess) return cuda_fail(e, "gemm launch");
     return cuda_fail(cudaGetLastError(), "gemm launch");
 }
 
-static tk_status build(const GemmDesc& g, tk_ctx* ctx, GemmParams& gp) {
+static tk_status build(const GemmDesc& g, tk_ctx* ctx, GemmParams& gp, int cg) {
     if (g.M <= 0 || g.N <= 0 || g.K <= 0) return fail(TK_ERR_INVALID, "GEMM with empty shape");
     if (g.nprod < 1 || g.nprod > 3) return fail(TK_ERR_INVALID, "GEMM product count must be 1..3");
     if ((reinterpret_cast<uintptr_t>(g.D) & 15) || g.ldd % 4)
@@ -411,13 +486,13 @@ static tk_status build(const GemmDesc& g, tk_ctx* ctx, GemmParams& gp) {
     for (int i = 0; i < 2; ++i)
         if (g.B[i]) {
             tk_status st = g.b_mn ? make_map(&gp.tmB[i], g.B[i], g.N, g.K, g.ldb, BK)
-                                  : make_map(&gp.tmB[i], g.B[i], g.K, g.N, g.ldb, BN);
+                                  : make_map(&gp.tmB[i], g.B[i], g.K, g.N, g.ldb, BN / cg);
             if (st != TK_OK) return st;
         }
     gp.M = g.M; gp.N = g.N; gp.K = g.K;
     gp.nprod = g.nprod;
     for (int i = 0; i < 3; ++i) { gp.pa[i] = g.pa[i]; gp.pb[i] = g.pb[i]; }
-    gp.tiles_m = (g.M + BM - 1) / BM;
+    gp.tiles_m = (g.M + BM * cg - 1) / (BM * cg);
     gp.tiles_n = (g.N + BN - 1) / BN;
     {
         const int kblocks = (g.K + BK - 1) / BK;
@@ -431,38 +506,46 @@ static tk_status build(const GemmDesc& g, tk_ctx* ctx, GemmParams& gp) {
     return TK_OK;
 }
 
+// CTA pairs for every GEMM with more than one 128-row block of output rows;
+// a single CTA otherwise (a pair would leave half its tensor cores idle).
+static int pick_cg(const GemmDesc& g) { return g.M > BM ? 2 : 1; }
+
 tk_status launch_gemm(tk_ctx* ctx, const GemmDesc& g, cudaStream_t s) {
+    const int cg = pick_cg(g);
     GemmParams gp;
-    tk_status st = build(g, ctx, gp);
+    tk_status st = build(g, ctx, gp, cg);
     if (st != TK_OK) return st;
     EpiParams ep;
     memset(&ep, 0, sizeof(ep));
-    return g.b_mn ? go<true, EPI_STORE>(ctx, gp, ep, s) : go<false, EPI_STORE>(ctx, gp, ep, s);
+    if (cg == 2) return g.b_mn ? go<2, true, EPI_STORE>(ctx, gp, ep, s) : go<2, false, EPI_STORE>(ctx, gp, ep, s);
+    return g.b_mn ? go<1, true, EPI_STORE>(ctx, gp, ep, s) : go<1, false, EPI_STORE>(ctx, gp, ep, s);
 }
 
 tk_status launch_gemm_lse(tk_ctx* ctx, const GemmDesc& g, const LseDesc& e, cudaStream_t s) {
+    if (g.b_mn) return fail(TK_ERR_INVALID, "LM-head logits GEMM takes a K-major head");
+    const int cg = pick_cg(g);
     GemmParams gp;
-    tk_status st = build(g, ctx, gp);
+    tk_status st = build(g, ctx, gp, cg);
     if (st != TK_OK) return st;
     gp.seg_kb = (g.K + BK - 1) / BK;   // statistics need the complete logit
     EpiParams ep;
     memset(&ep, 0, sizeof(ep));
     ep.lse = e;
-    if (g.b_mn) return fail(TK_ERR_INVALID, "LM-head logits GEMM takes a K-major head");
-    return go<false, EPI_LSE>(ctx, gp, ep, s);
+    return cg == 2 ? go<2, false, EPI_LSE>(ctx, gp, ep, s) : go<1, false, EPI_LSE>(ctx, gp, ep, s);
 }
 
 tk_status launch_gemm_dlogit(tk_ctx* ctx, const GemmDesc& g, const DlogitDesc& e, cudaStream_t s) {
-    GemmParams gp;
-    tk_status st = build(g, ctx, gp);
-    if (st != TK_OK) return st;
+    if (g.b_mn) return fail(TK_ERR_INVALID, "LM-head logits GEMM takes a K-major head");
     if (g.N % BN) return fail(TK_ERR_INVALID, "dlogit epilogue needs a chunk width multiple of 256");
+    const int cg = pick_cg(g);
+    GemmParams gp;
+    tk_status st = build(g, ctx, gp, cg);
+    if (st != TK_OK) return st;
     gp.seg_kb = (g.K + BK - 1) / BK;
     EpiParams ep;
     memset(&ep, 0, sizeof(ep));
     ep.dl = e;
-    if (g.b_mn) return fail(TK_ERR_INVALID, "LM-head logits GEMM takes a K-major head");
-    return go<false, EPI_DLOGIT>(ctx, gp, ep, s);
+    return cg == 2 ? go<2, false, EPI_DLOGIT>(ctx, gp, ep, s) : go<1, false, EPI_DLOGIT>(ctx, gp, ep, s);
 }
 
 }  // namespace tk

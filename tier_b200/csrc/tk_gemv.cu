@@ -219,6 +219,20 @@ static int popcount_chunks(int M) {
 tk_status launch_gemv(tk_ctx* ctx, int t, const void* Wv, size_t rb, int N, int K, const float* x, int ldx, int M,
                       float* y, int ldy, cudaStream_t s) {
     if (N == 0 || M == 0) return TK_OK;
+    // Streaming kernel (tk_gemv2.cu) for Q8_0 / Q4_K / Q5_K when x fits in
+    // shared memory: token chunks of 4, 2 and 1.
+    if (gemv_stream_ok(t, rb, K, 1) && (reinterpret_cast<uintptr_t>(Wv) & 15) == 0) {
+        int m0 = 0;
+        while (m0 < M) {
+            const int r = M - m0;
+            const int c = (r >= 4 && gemv_stream_ok(t, rb, K, 4)) ? 4 : (r >= 2 && gemv_stream_ok(t, rb, K, 2)) ? 2 : 1;
+            tk_status st = launch_gemv_stream(ctx, t, Wv, rb, N, K, x + (size_t)m0 * ldx, ldx, c, y + (size_t)m0 * ldy,
+                                              ldy, s);
+            if (st != TK_OK) return st;
+            m0 += c;
+        }
+        return TK_OK;
+    }
     const uint8_t* W = static_cast<const uint8_t*>(Wv);
     const int rows_per_block = GEMV_WARPS;
     int blocks = (N + rows_per_block - 1) / rows_per_block;
