@@ -9,8 +9,9 @@ Default workload (the metric's single-GPU configuration):
   Useful work per step: 2 x 2*M*N*K = 962.1 GFLOP.
 
 Multi-GPU (torchrun, one process per GPU, NCCL): W is split by output rows;
-each rank computes its Y columns and its partial
-dX; Y shards are all-gathered and dX partials all-reduced inside the step.
+each rank computes its Y columns (kept sharded, as a column-parallel layer's
+consumer takes them; --gather-y all-gathers the full Y) and its partial dX,
+which is all-reduced in M-chunks overlapped with the next chunk's GEMM.
 Total work is fixed (strong scaling); value = total FLOP / max-over-ranks time.
 
 --impl reference: the reference's CPU implementation of the same operation
@@ -186,7 +187,7 @@ def run_ours(args):
     if world > 1:
         import datetime
         import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=60),
                                 device_id=torch.device("cuda", local))
         group = dist.group.WORLD
     ctx = tk.Context(local)
@@ -201,16 +202,28 @@ def run_ours(args):
     Xd, dYd = Xb.to(dev), dYb.to(dev)
     Y = torch.empty(M_TOK, n_loc, dtype=torch.float32, device=dev)
     dX = torch.empty(M_TOK, K_IN, dtype=torch.float32, device=dev)
-    Yfull = torch.empty(world, M_TOK, n_loc, dtype=torch.float32, device=dev) if world > 1 else None
+    Yfull = torch.empty(world, M_TOK, n_loc, dtype=torch.float32, device=dev) if (world > 1 and args.gather_y) else None
     stream = torch.cuda.current_stream(dev)
+
+    chunks = args.dx_chunks if world > 1 else 1
+    mc = M_TOK // chunks
 
     def step(Xin, dYin):
         ctx.linear(w, Xin, M_TOK, Y, x_dtype=tk.DT_BF16)
-        ctx.linear_dx(w, dYin, M_TOK, dX, dy_dtype=tk.DT_BF16)
-        if world > 1:
-            import torch.distributed as dist
-            dist.all_gather_into_tensor(Yfull, Y, group=group)
-            dist.all_reduce(dX, group=group)
+        if world == 1:
+            ctx.linear_dx(w, dYin, M_TOK, dX, dy_dtype=tk.DT_BF16)
+            return
+        import torch.distributed as dist
+        # NCCL runs on its own stream: the Y all-gather (if the consumer wants
+        # the full Y) and each dX chunk's all-reduce overlap the next GEMM.
+        works = []
+        if args.gather_y:
+            works.append(dist.all_gather_into_tensor(Yfull, Y, group=group, async_op=True))
+        for c in range(chunks):
+            ctx.linear_dx(w, dYin[c * mc:(c + 1) * mc], mc, dX[c * mc:(c + 1) * mc], dy_dtype=tk.DT_BF16)
+            works.append(dist.all_reduce(dX[c * mc:(c + 1) * mc], group=group, async_op=True))
+        for wk in works:
+            wk.wait()
 
     def barrier():
         if world > 1:
@@ -223,14 +236,21 @@ def run_ours(args):
     # warm-up is extended to >= 1 s of load so the 100 ms samples see the GPU busy.
     clocks = Clocks(local)
     clocks.start()
-    t0 = time.perf_counter()
     for _ in range(args.warmup):
         step(Xd, dYd)
     barrier()
-    while time.perf_counter() - t0 < 1.0:
-        for _ in range(10):
-            step(Xd, dYd)
-        barrier()
+    # extra untimed steps up to ~1 s of load; every rank runs the same count
+    # (agreed with an all-reduce) so all ranks issue the same collectives.
+    t0 = time.perf_counter()
+    step(Xd, dYd)
+    barrier()
+    n_extra = torch.tensor([int(1.0 / max(time.perf_counter() - t0, 1e-4))], device=dev)
+    if world > 1:
+        import torch.distributed as dist
+        dist.all_reduce(n_extra, op=dist.ReduceOp.MAX, group=group)
+    for _ in range(int(n_extra.item())):
+        step(Xd, dYd)
+    barrier()
     n0 = ctx.launches()
     ctx.profile(True)
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -308,7 +328,11 @@ def run_ours(args):
             "vs_baseline": None, "dtype": "fp16 tensor-core products, fp32 accumulate (Q4_K -> fp16 exact dequant)",
             "data": "synthetic (seeded, tests/gen.py)",
             "config": {"workload": "C2 Q4_K 14336x4096, M=4096 tokens, fwd + dX per step",
-                       "x_dtype": "bf16", "partition": f"W rows split over {world} GPU(s)" if world > 1 else "1 GPU",
+                       "x_dtype": "bf16",
+                       "partition": (f"W rows split over {world} GPUs; Y " + ("all-gathered" if args.gather_y else
+                                     "kept row-sharded (column-parallel: consumed where produced)") +
+                                     f"; dX all-reduced in {chunks} M-chunks overlapped with the GEMMs")
+                       if world > 1 else "1 GPU",
                        "l2": "working set per step ~0.5 GB > 126 MB L2 (no explicit flush)"},
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": tf_burst, "unit": "TFLOP/s",
                          "frac": achieved / tf_burst, "traffic": traffic,
@@ -507,6 +531,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--ref-seconds", type=float, default=10.0, help="CPU baseline sample size (seconds)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--gather-y", action="store_true", help="multi-GPU: all-gather the full Y every step")
+    ap.add_argument("--dx-chunks", type=int, default=4, help="multi-GPU: dX GEMM / all-reduce pipeline chunks")
     ap.add_argument("--config", default="c2", choices=["c1", "c2", "c3", "c4"],
                     help="c2 (default, the headline) or a secondary configuration on one GPU")
     args = ap.parse_args()

@@ -66,6 +66,13 @@ enum { TK_DT_F32 = 0, TK_DT_F16 = 1, TK_DT_BF16 = 2 };
  *  TK_X3_AUTO: TK_X3_REF for fp32 X with fp16/quant W, TK_X3_HHL for
  *              TK_F16X2 W, TK_X1 for fp16/bf16 X. */
 enum { TK_X3_AUTO = 0, TK_X3_REF = 1, TK_X3_HHL = 2, TK_X2 = 3, TK_X1 = 4 };
+/* OR-able flag for `products` of tk_linear_fwd / tk_linear_dx with a
+ * block-quantized weight: decode W inside the GEMM (converter warps write the
+ * fp16 operand tiles in shared memory) instead of expanding it to fp16 in the
+ * workspace first.  Needs M > 128 and K % 256 == 0 (otherwise ignored).  The
+ * decode is repeated for every 256-row tile of M, so it is slower than the
+ * default at every M measured on B200 so far. */
+enum { TK_QFUSED = 0x100 };
 
 typedef struct tk_ctx tk_ctx;
 

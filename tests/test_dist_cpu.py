@@ -1,0 +1,71 @@
+"""Host-side sharding logic on CPU with gloo, world size 2: the row split
+used by the linear path and the vocab-shard merge of the running
+cross-entropy state (max, rescaled sum, target, argmax with the reference's
+lowest-index tie rule)."""
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _cpu_rescale(rl, sl, rg):
+    sl.mul_(torch.exp(rl - rg))
+    rl.copy_(rg)
+
+
+def _stats(lg, v0):
+    """Running state of one shard's logits [T, V] (rows with mask 1)."""
+    m, i = lg.max(dim=1)
+    s = torch.exp(lg.double() - m.double()[:, None]).sum(1)
+    return m.double(), s, (i + v0).int()
+
+
+def _worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from tier_b200.host import merge_vocab_shards, shard_rows
+        g = torch.Generator().manual_seed(0)
+        T, V = 33, 1000
+        lg = torch.randn(T, V, generator=g, dtype=torch.float64).float()
+        lg[5, 100] = lg[5, 900] = lg[5].max() + 1.0          # exact tie across shards
+        labels = torch.randint(0, V, (T,), generator=g)
+        a, b = shard_rows(V, world, rank, align=8)
+        rmax, rsum, amax = _stats(lg[:, a:b], a)
+        tgt = torch.tensor([float(lg[t, labels[t]]) if a <= labels[t] < b else 0.0 for t in range(T)])
+        amax = merge_vocab_shards(rmax, rsum, amax, tgt, dist.group.WORLD, _cpu_rescale)
+        fm, fs, fa = _stats(lg, 0)
+        ok = (torch.allclose(rmax, fm) and torch.allclose(rsum, fs, rtol=1e-12)
+              and torch.equal(amax, fa) and int(amax[5]) == 100
+              and torch.allclose(tgt, lg[torch.arange(T), labels]))
+        # row shards tile the range, boundaries aligned
+        parts = [shard_rows(14336, 8, r, align=256) for r in range(8)]
+        ok = ok and parts[0][0] == 0 and parts[-1][1] == 14336 and all(
+            parts[i][1] == parts[i + 1][0] and parts[i][1] % 256 == 0 for i in range(7))
+        q.put((rank, bool(ok)))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_vocab_merge_and_row_split_gloo():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=120) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+    assert res == {0: True, 1: True}

@@ -94,7 +94,7 @@ def test_x3_hhl_fp32_weight(ctx, M, N, K):
 
 
 @pytest.mark.parametrize("qtype", [12, 8, 13])
-@pytest.mark.parametrize("M,N,K", [(256, 512, 1024), (300, 384, 2048)])
+@pytest.mark.parametrize("M,N,K", [(256, 512, 1024), (300, 384, 2048), (64, 256, 512), (520, 640, 1280)])
 def test_quant_weight_bf16_activations(ctx, oracle, qtype, M, N, K):
     """Quant W dequantized bit-exactly to fp16, bf16 X / dY: <= 2e-3 vs fp64."""
     import torch
@@ -146,3 +146,97 @@ def test_invalid_shapes_rejected(ctx):
     Y = torch.empty(4, 256, device="cuda")
     with pytest.raises(tk.TierkError):
         ctx.linear(w, torch.zeros(4, 100, device="cuda"), 4, Y)
+
+
+@pytest.mark.parametrize("qtype", [12, 8])
+def test_quant_weight_fp32_activations_x3(ctx, oracle, qtype):
+    """fp32 X with a quantized W: the three activation parts share one
+    dequantized W (the reference's training path: dequant to fp16, then
+    fp3gemm), compared with fp64 of the fp16-rounded weight: <= 1e-5."""
+    import torch
+    import tier_b200 as tk
+    rng = np.random.default_rng(qtype)
+    M, N, K = 384, 512, 2048
+    b = blocks_for(rng, qtype, N, K)
+    W16 = oracle.dequant(b, qtype, N, K, 1).view(np.float16)
+    X = rng.standard_normal((M, K)).astype(np.float32)
+    dY = rng.standard_normal((M, N)).astype(np.float32)
+    w = tk.make_weight(qtype, N, K, dev(b))
+    Y = torch.empty(M, N, dtype=torch.float32, device="cuda")
+    ctx.linear(w, dev(X), M, Y, products=tk.X3_REF)
+    assert rel_fro(host(Y), f64(X) @ f64(W16).T) < 1e-5
+    dX = torch.empty(M, K, dtype=torch.float32, device="cuda")
+    ctx.linear_dx(w, dev(dY), M, dX, products=tk.X3_REF)
+    assert rel_fro(host(dX), f64(dY) @ f64(W16)) < 1e-5
+
+
+@pytest.mark.parametrize("qtype", [12, 13, 8])
+@pytest.mark.parametrize("M,N,K,prods", [(256, 512, 1024, 4), (300, 384, 2048, 4), (384, 512, 2048, 1)])
+def test_quant_fused_decode_matches(ctx, oracle, qtype, M, N, K, prods):
+    """TK_QFUSED (decode inside the GEMM) agrees with fp64 of the fp16-rounded
+    weight: 2e-3 for one bf16 product, 1e-5 for the fp32 three-part split."""
+    import torch
+    import tier_b200 as tk
+    rng = np.random.default_rng(qtype * 7 + M)
+    b = blocks_for(rng, qtype, N, K)
+    W16 = oracle.dequant(b, qtype, N, K, 1).view(np.float16)
+    w = tk.make_weight(qtype, N, K, dev(b))
+    if prods == tk.X1:
+        X = torch.from_numpy(rng.standard_normal((M, K)).astype(np.float32)).to(torch.bfloat16)
+        dY = torch.from_numpy(rng.standard_normal((M, N)).astype(np.float32)).to(torch.bfloat16)
+        xdt, tol = tk.DT_BF16, 2e-3
+        Xf, dYf = X.float().numpy(), dY.float().numpy()
+        X, dY = X.cuda(), dY.cuda()
+    else:
+        Xf = rng.standard_normal((M, K)).astype(np.float32)
+        dYf = rng.standard_normal((M, N)).astype(np.float32)
+        X, dY, xdt, tol = dev(Xf), dev(dYf), tk.DT_F32, 1e-5
+    Y = torch.empty(M, N, dtype=torch.float32, device="cuda")
+    ctx.linear(w, X, M, Y, x_dtype=xdt, products=prods | tk.QFUSED)
+    assert rel_fro(host(Y), f64(Xf) @ f64(W16).T) < tol
+    dX = torch.empty(M, K, dtype=torch.float32, device="cuda")
+    ctx.linear_dx(w, dY, M, dX, dy_dtype=xdt, products=prods | tk.QFUSED)
+    assert rel_fro(host(dX), f64(dYf) @ f64(W16)) < tol
+    ctx.sync_status()
+
+
+@pytest.mark.parametrize("M,N,K,prods", [(300, 1000, 4096, "X1"), (256, 520, 8192, "X3_REF"), (2048, 2048, 14336, "X1")])
+def test_split_k_shapes(ctx, M, N, K, prods):
+    """Few output tiles and long K: the GEMM splits K in two and adds the
+    halves in fp32.  Results hold the path's tolerance, with beta = 1 and a
+    padded output stride too, and are bit-identical across runs (every
+    arrival order of the two halves computes the same fp32 sum)."""
+    import torch
+    import tier_b200 as tk
+    p = getattr(tk, prods)
+    rng = np.random.default_rng(N + K)
+    W = (rng.standard_normal((N, K)) * 0.02).astype(np.float16)
+    if p == tk.X1:
+        X = rng.standard_normal((M, K)).astype(np.float16)
+        dY = rng.standard_normal((M, N)).astype(np.float16)
+        # one fp16 product: fp32 tensor-core accumulation over K = 14336 measures ~1.6e-5
+        xdt, tol = tk.DT_F16, 5e-5
+    else:
+        X = rng.standard_normal((M, K)).astype(np.float32)
+        dY = rng.standard_normal((M, N)).astype(np.float32)
+        xdt, tol = tk.DT_F32, 1e-5
+    w = tk.make_weight(tk.F16, N, K, dev(W))
+    Xd, dYd = dev(X), dev(dY)
+    want = f64(X) @ f64(W).T
+    Y0 = rng.standard_normal((M, N + 4)).astype(np.float32)
+    outs = []
+    for _ in range(2):
+        Y = dev(Y0)
+        ctx.linear(w, Xd, M, Y, x_dtype=xdt, ldy=N + 4, beta=1.0, products=p)
+        outs.append(host(Y))
+    assert np.array_equal(outs[0], outs[1])
+    full = Y0.astype(np.float64)
+    full[:, :N] += want
+    assert rel_fro(outs[0], full) < tol
+    dX = torch.empty(M, K, dtype=torch.float32, device="cuda")
+    ctx.linear_dx(w, dYd, M, dX, dy_dtype=xdt, products=p)
+    d1 = host(dX)
+    ctx.linear_dx(w, dYd, M, dX, dy_dtype=xdt, products=p)
+    assert np.array_equal(d1, host(dX))
+    assert rel_fro(d1, f64(dY) @ f64(W)) < tol
+    ctx.sync_status()

@@ -1,0 +1,93 @@
+"""Row-sharded linear and vocab-sharded LM head across 2 GPUs (one process
+per GPU, NCCL): every rank's gathered / reduced result equals the single-GPU
+result within the path's tolerance.  Skipped with fewer than 2 GPUs."""
+import os
+import socket
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _worker(rank, world, port, q):
+    import datetime
+    import torch
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    out = {}
+    try:
+        import tier_b200 as tk
+        from tier_b200.host import LinearPath, LMHead, shard_rows
+        ctx = tk.Context(rank)
+        g = torch.Generator(device="cuda").manual_seed(0)
+        # --- linear, Q4_K rows split ---
+        import sys
+        sys.path.insert(0, os.path.join(os.path.dirname(__file__)))
+        from gen import q4_k_blocks
+        rng = np.random.default_rng(1)
+        N, K, M = 1024, 2048, 256
+        Wq = q4_k_blocks(rng, N, K)
+        X = torch.from_numpy(rng.standard_normal((M, K)).astype(np.float32)).cuda()
+        dY = torch.from_numpy(rng.standard_normal((M, N)).astype(np.float32)).cuda()
+        a, b = shard_rows(N, world, rank)
+        lp = LinearPath(ctx, tk.Q4_K, b - a, K, torch.from_numpy(Wq[a:b].copy()).cuda(), group=dist.group.WORLD)
+        Y = lp.forward(X)
+        dX = lp.dx(dY[:, a:b].contiguous())
+        full = LinearPath(ctx, tk.Q4_K, N, K, torch.from_numpy(Wq).cuda())
+        Y1, dX1 = full.forward(X), full.dx(dY)
+        torch.cuda.synchronize()
+        out["lin_fwd"] = float((Y - Y1).norm() / Y1.norm())
+        out["lin_dx"] = float((dX - dX1).norm() / dX1.norm())
+        # --- LM head, vocab split ---
+        V, H, T = 4096, 256, 64
+        W = (torch.randn(V, H, device="cuda", generator=g) * 0.02).half()
+        Xh = torch.randn(T, H, device="cuda", generator=g)
+        labels = torch.randint(0, V, (T,), device="cuda", generator=g, dtype=torch.int32)
+        mask = torch.ones(T, dtype=torch.uint8, device="cuda")
+        va, vb = shard_rows(V, world, rank, align=256)
+        hs = LMHead(ctx, W[va:vb].contiguous(), va, chunk=512, group=dist.group.WORLD)
+        loss, n, hits, amax, dXh = hs.step(Xh, labels, mask)
+        h1 = LMHead(ctx, W, 0, chunk=512)
+        loss1, _, hits1, amax1, dXh1 = h1.step(Xh, labels, mask)
+        torch.cuda.synchronize()
+        out["lm_loss"] = abs(loss.item() - loss1.item()) / abs(loss1.item())
+        out["lm_dx"] = float((dXh - dXh1).norm() / dXh1.norm())
+        out["lm_amax"] = bool(torch.equal(amax, amax1)) and hits.item() == hits1.item()
+        ctx.close()
+    except Exception as e:  # report, never hang the other rank
+        out["error"] = repr(e)
+    finally:
+        dist.destroy_process_group()
+    q.put((rank, out))
+
+
+def test_two_gpu_shards_match_single_gpu():
+    import torch
+    import torch.multiprocessing as mp
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=300) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+    for r, o in res.items():
+        assert "error" not in o, o
+        assert o["lin_fwd"] < 1e-6 and o["lin_dx"] < 1e-5, o
+        assert o["lm_loss"] < 1e-6 and o["lm_dx"] < 1e-5 and o["lm_amax"], o

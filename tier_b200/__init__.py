@@ -34,6 +34,7 @@ BLOCK = {F32: (1, 4), F16: (1, 2), BF16: (1, 2), Q4_0: (32, 18), Q4_1: (32, 20),
 DT_F32, DT_F16, DT_BF16 = 0, 1, 2
 # product sets
 X3_AUTO, X3_REF, X3_HHL, X2, X1 = 0, 1, 2, 3, 4
+QFUSED = 0x100   # OR into `products`: decode a quantized W inside the GEMM
 # kernel families for profiling
 PROF_GEMM, PROF_DEQUANT, PROF_SPLIT, PROF_GEMV, PROF_LMHEAD = range(5)
 

@@ -80,7 +80,15 @@ struct Carve {
 };
 
 // k-blocks (64 each) per fp32 accumulation segment for the split product sets.
-constexpr int kSegKb = 8;
+// The error of the tensor-core fp32 accumulation grows with the segment
+// length, not with K (measured relative error vs fp64 on B200, x3 REF / HHL:
+// 8 -> 1.2e-6 / 1.7e-6, 16 -> 2.4e-6 / 3.5e-6, 32 -> 4.5e-6 / 7.1e-6), while
+// each segment costs one fp32 read-modify-write of the tile.  16 keeps a 3x
+// margin under the 1e-5 bound.
+#ifndef TK_SEG_KB
+#define TK_SEG_KB 16
+#endif
+constexpr int kSegKb = TK_SEG_KB;
 
 static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
@@ -155,23 +163,65 @@ static tk_status linear(tk_ctx* ctx, const tk_weight* W, const void* A, int a_dt
     if (a_dtype != TK_DT_F32 && a_dtype != TK_DT_F16 && a_dtype != TK_DT_BF16)
         return fail(TK_ERR_INVALID, std::string(fn) + ": activation dtype");
     if (!aligned16(D) || ldd % 4) return fail(TK_ERR_INVALID, std::string(fn) + ": output must be 16-byte aligned, ld % 4 == 0");
+    const bool want_fused = (products & TK_QFUSED) != 0;
+    products &= ~TK_QFUSED;
     Plan pl;
     st = plan_products(W, a_dtype, products, pl);
     if (st != TK_OK) return st;
 
     const bool quant = W->qtype != TK_F16 && W->qtype != TK_F16X2;
+    // Quantized weights go through the fused-dequant GEMM (no fp16 copy of W)
+    // when the shape allows it: CTA-pair tiles (M > 128), whole 256-column
+    // slabs, 16-byte-aligned rows.
+    // On request (TK_QFUSED) the weight is decoded inside the GEMM; the
+    // default expands it to fp16 once and runs the plain GEMM (the fused decode
+    // repeats for every 256-row tile of M).
+    const bool fused = want_fused && quant && gemm_q_supported(W->qtype) && M > 128 && K % 256 == 0 &&
+                       W->row_bytes % 16 == 0 && !pl.w_two;
     // split planes use a row stride rounded up to 8 elements (16 bytes, the TMA
     // stride rule); the GEMM's K extent stays a_cols, so the pad is never read.
     const long a_ld = (a_cols + 7) / 8 * 8;
     const size_t plane_elems = (size_t)M * a_ld;
+    // split-K slab (fp32, [M, d_cols rounded to 4]) when the GEMM splits K
+    GemmDesc probe;
+    probe.M = M;
+    probe.N = d_cols;
+    probe.K = a_cols;
+    probe.b_mn = dx;
+    const long s_ld = (d_cols + 3) / 4 * 4;
+    const bool split = !fused && gemm_splits(ctx, probe) == 2;
     const size_t need = align256(plane_elems * 2 * pl.x_planes) + align256((size_t)M * 4) +
-                        (quant ? align256((size_t)N * K * 2) : 0);
+                        (quant && !fused ? align256((size_t)N * K * 2) : 0) +
+                        (split ? align256((size_t)M * s_ld * 4) : 0);
     st = ws_ensure(ctx, need, s);
     if (st != TK_OK) return st;
     Carve cv(ctx->ws);
     // plane p of the split activation at pbase + p * M * a_cols (16-byte aligned: a_cols % 8 == 0)
     uint16_t* pbase = cv.take<uint16_t>(plane_elems * pl.x_planes);
     int* row_exp = cv.take<int>(M);
+    if (fused) {
+        st = launch_act_split(ctx, A, a_dtype, M, a_cols, lda, pl.x_planes, true, pbase, row_exp, s, a_ld);
+        if (st != TK_OK) return st;
+        GemmQDesc q;
+        for (int i = 0; i < pl.x_planes; ++i) q.A[i] = pbase + (size_t)i * plane_elems;
+        q.lda = a_ld;
+        q.nprod = pl.nprod;
+        for (int i = 0; i < 3; ++i) q.pa[i] = pl.pa[i];
+        q.qtype = W->qtype;
+        q.W = W->data;
+        q.w_row_bytes = W->row_bytes;
+        q.w_rows = N;
+        q.dx = dx;
+        q.M = M;
+        q.N = d_cols;
+        q.K = a_cols;
+        q.D = D;
+        q.ldd = ldd;
+        q.beta = beta != 0.0f;
+        q.row_exp = row_exp;
+        q.seg_kb = pl.nprod > 1 ? kSegKb : 0;
+        return launch_gemm_q(ctx, q, s);
+    }
     const uint16_t* wplanes[2] = {nullptr, nullptr};
     if (quant) {
         uint16_t* wf = cv.take<uint16_t>((size_t)N * K);
@@ -205,6 +255,10 @@ static tk_status linear(tk_ctx* ctx, const tk_weight* W, const void* A, int a_dt
     g.col_exp = W->qtype == TK_F16X2 ? W->scale_log2 : 0;
     // fp32-accurate product sets: sum in fp32 every kSegKb k-blocks (see tk_gemm.cu)
     g.seg_kb = pl.nprod > 1 ? kSegKb : 0;
+    if (split) {
+        g.split_ws = cv.take<float>((size_t)M * s_ld);
+        g.split_ld = s_ld;
+    }
     return launch_gemm(ctx, g, s);
 }
 
@@ -234,6 +288,11 @@ tk_status tk_init(int device, tk_ctx** out) {
     c->num_sms = prop.multiProcessorCount;
     e = cudaMalloc(&c->status, sizeof(int));
     if (e == cudaSuccess) e = cudaMemset(c->status, 0, sizeof(int));
+    if (e == cudaSuccess) {
+        c->flags_len = 1 << 16;
+        e = cudaMalloc(&c->flags, sizeof(int) * c->flags_len);
+        if (e == cudaSuccess) e = cudaMemset(c->flags, 0, sizeof(int) * c->flags_len);
+    }
     if (e != cudaSuccess) {
         delete c;
         return cuda_fail(e, "tk_init: status word");
@@ -248,6 +307,7 @@ void tk_destroy(tk_ctx* ctx) {
     cudaDeviceSynchronize();
     if (ctx->ws) cudaFree(ctx->ws);
     if (ctx->status) cudaFree(ctx->status);
+    if (ctx->flags) cudaFree(ctx->flags);
     for (cudaEvent_t e : ctx->prof.ev) cudaEventDestroy(e);
     delete ctx;
 }

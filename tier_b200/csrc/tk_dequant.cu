@@ -132,6 +132,26 @@ __global__ void __launch_bounds__(DQ_THREADS) dequant_kernel(const uint8_t* __re
     }
 }
 
+// ---------------------------------------------------------------------------
+// Sub-block kernel for Q4_K / Q5_K / Q8_0 -> fp16 (the tensor-core path's
+// format): one thread per 32-element sub-block (decoder sub32_to_f16 in
+// tk_device.cuh), 64 B of output per thread as four 16-byte stores.
+// Threads run flat over (row, sub-block): one 32-bit division per 32 weights.
+template <int T>
+__global__ void __launch_bounds__(256) dequant_sub_f16_kernel(const uint8_t* __restrict__ W, size_t rb, int r0,
+                                                              int nrows, int cols, uint16_t* __restrict__ out) {
+    const unsigned spr = (unsigned)cols >> 5;       // sub-blocks per row
+    const unsigned total = (unsigned)nrows * spr;
+    for (unsigned g = blockIdx.x * blockDim.x + threadIdx.x; g < total; g += gridDim.x * blockDim.x) {
+        const unsigned r = g / spr, sb = g - r * spr;
+        uint32_t h[16];
+        sub32_to_f16<T>(W + (size_t)(r0 + r) * rb, (int)sb, h);
+        uint4* o = reinterpret_cast<uint4*>(out + (size_t)r * cols + (size_t)sb * 32);
+#pragma unroll
+        for (int c = 0; c < 4; ++c) o[c] = make_uint4(h[4 * c], h[4 * c + 1], h[4 * c + 2], h[4 * c + 3]);
+    }
+}
+
 template <int T>
 static void dq_dispatch_out(int out_dtype, dim3 g, dim3 b, cudaStream_t s, const uint8_t* W, size_t rb, int r0,
                             int nrows, int cols, void* out) {
@@ -143,6 +163,22 @@ static void dq_dispatch_out(int out_dtype, dim3 g, dim3 b, cudaStream_t s, const
 tk_status launch_dequant(tk_ctx* ctx, int t, const void* W, size_t rb, int r0, int nrows, int cols, int out_dtype,
                          void* out, cudaStream_t s) {
     if (nrows == 0) return TK_OK;
+    if (out_dtype == TK_DT_F16 && (t == QT_Q4_K || t == QT_Q5_K || t == QT_Q8_0) &&
+        (reinterpret_cast<uintptr_t>(W) & 15) == 0 && rb % 16 == 0) {
+        if ((size_t)nrows * (cols / 32) >= (1ull << 32))
+            return fail(TK_ERR_INVALID, "tk_dequant: more than 2^32 sub-blocks in one call");
+        const size_t total = (size_t)nrows * (cols / 32);
+        size_t want = (total + 255) / 256, cap = (size_t)ctx->num_sms * 32;
+        const dim3 grid((unsigned)(want < cap ? want : cap));
+        ProfScope ps(ctx, s, PK_DEQUANT);
+        const uint8_t* w = static_cast<const uint8_t*>(W);
+        uint16_t* o = static_cast<uint16_t*>(out);
+        if (t == QT_Q4_K) dequant_sub_f16_kernel<QT_Q4_K><<<grid, 256, 0, s>>>(w, rb, r0, nrows, cols, o);
+        else if (t == QT_Q5_K) dequant_sub_f16_kernel<QT_Q5_K><<<grid, 256, 0, s>>>(w, rb, r0, nrows, cols, o);
+        else dequant_sub_f16_kernel<QT_Q8_0><<<grid, 256, 0, s>>>(w, rb, r0, nrows, cols, o);
+        ctx->launches++;
+        return cuda_fail(cudaGetLastError(), "dequant launch");
+    }
     const int gpr = cols / 8;
     const int gx = (gpr + DQ_THREADS * DQ_UNROLL - 1) / (DQ_THREADS * DQ_UNROLL);
     const int gy_cap = (ctx->num_sms * 16 + gx - 1) / gx;      // ~16 blocks per SM in flight
@@ -261,6 +297,37 @@ __device__ __forceinline__ void st8h(uint16_t* p, const uint16_t (&h)[8]) {
                                               (uint32_t)h[4] | ((uint32_t)h[5] << 16), (uint32_t)h[6] | ((uint32_t)h[7] << 16));
 }
 
+// The raw 16-byte chunks (8 elements of a 16-bit type, or 4 of fp32 in two
+// halves) stay in registers between the max and split passes and are decoded
+// twice; keeping raw bits instead of floats halves the register footprint.
+template <int XT>
+struct RawChunk {
+    uint4 a, b;   // b unused for 16-bit types
+};
+template <int XT>
+__device__ __forceinline__ void ld_raw(const void* X, size_t i, RawChunk<XT>& r) {
+    if constexpr (XT == TK_DT_F32) {
+        r.a = *reinterpret_cast<const uint4*>(static_cast<const float*>(X) + i);
+        r.b = *reinterpret_cast<const uint4*>(static_cast<const float*>(X) + i + 4);
+    } else {
+        r.a = *reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(X) + i);
+    }
+}
+template <int XT>
+__device__ __forceinline__ void dec_raw(const RawChunk<XT>& r, float (&v)[8]) {
+    if constexpr (XT == TK_DT_F32) {
+        v[0] = __uint_as_float(r.a.x); v[1] = __uint_as_float(r.a.y); v[2] = __uint_as_float(r.a.z); v[3] = __uint_as_float(r.a.w);
+        v[4] = __uint_as_float(r.b.x); v[5] = __uint_as_float(r.b.y); v[6] = __uint_as_float(r.b.z); v[7] = __uint_as_float(r.b.w);
+    } else {
+        const uint32_t u[4] = {r.a.x, r.a.y, r.a.z, r.a.w};
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const uint16_t h = (uint16_t)(u[j >> 1] >> (16 * (j & 1)));
+            v[j] = XT == TK_DT_F16 ? h2f_bits(h) : __uint_as_float((uint32_t)h << 16);
+        }
+    }
+}
+
 template <int XT, int NP>
 __global__ void __launch_bounds__(AS_THREADS) act_split_vec_kernel(const void* __restrict__ X, int M, int K, long ldx,
                                                                    long ldp, bool scaled, uint16_t* __restrict__ planes,
@@ -268,15 +335,21 @@ __global__ void __launch_bounds__(AS_THREADS) act_split_vec_kernel(const void* _
     __shared__ float red[AS_THREADS / 32];
     const int m = blockIdx.x;
     const int nch = K >> 3;
-    float v[AS_MAXCH][8];
+    RawChunk<XT> raw[AS_MAXCH];
     float a = 0.0f;
 #pragma unroll
     for (int i = 0; i < AS_MAXCH; ++i) {
         const int c = threadIdx.x + i * AS_THREADS;
-        if (c < nch) {
-            ld8<XT>(X, (size_t)m * ldx + (size_t)c * 8, v[i]);
+        if (c < nch) ld_raw<XT>(X, (size_t)m * ldx + (size_t)c * 8, raw[i]);
+    }
 #pragma unroll
-            for (int j = 0; j < 8; ++j) a = fmaxf(a, fabsf(v[i][j]));
+    for (int i = 0; i < AS_MAXCH; ++i) {
+        const int c = threadIdx.x + i * AS_THREADS;
+        if (c < nch) {
+            float v[8];
+            dec_raw<XT>(raw[i], v);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) a = fmaxf(a, fabsf(v[j]));
         }
     }
     int e = 0;
@@ -298,10 +371,12 @@ __global__ void __launch_bounds__(AS_THREADS) act_split_vec_kernel(const void* _
     for (int i = 0; i < AS_MAXCH; ++i) {
         const int c = threadIdx.x + i * AS_THREADS;
         if (c >= nch) continue;
+        float v[8];
+        dec_raw<XT>(raw[i], v);
         uint16_t h[8], mm[8], l[8];
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-            const float x = v[i][j] * f;
+            const float x = v[j] * f;
             h[j] = f2h_bits(x);
             if constexpr (NP >= 2) {
                 const float r = x - h2f_bits(h[j]);

@@ -90,6 +90,13 @@ __device__ __forceinline__ void tma_load_2d(void* smem_dst, const void* tmap, ui
         "l"(reinterpret_cast<uint64_t>(tmap)), "r"(smem_u32(bar)), "r"(x), "r"(y)
         : "memory");
 }
+__device__ __forceinline__ void tma_load_3d(void* smem_dst, const void* tmap, uint64_t* bar, int x, int y, int z) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(
+            smem_u32(smem_dst)),
+        "l"(reinterpret_cast<uint64_t>(tmap)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z)
+        : "memory");
+}
 // Untiled bulk copy global -> shared (both 16-byte aligned, bytes % 16 == 0).
 __device__ __forceinline__ void bulk_load(void* smem_dst, const void* gsrc, uint32_t bytes, uint64_t* bar) {
     asm volatile(
@@ -411,5 +418,83 @@ __device__ __forceinline__ void q5k_decode8(const uint8_t* row, int c, float (&v
         v[j] = __fmaf_rn(a, small_u2f(q), -m);
     }
 }
+
+// One 32-element sub-block of a Q4_K / Q5_K / Q8_0 row as 16 packed fp16
+// pairs, bit-exact tier_fp16(q_val) (tier/quant.h:68, 83-87):
+//   Q8_0: d*q is exact in fp32 and in the fp16 multiply (11 + 8 bits), so one
+//         packed fp16 RNE multiply of d by the exact half q gives the value;
+//   K-quants: fp32 fused (d*sc)*q - dmin*m (the product is exact), then RNE.
+// Nibbles become floats by byte-permuting them into the mantissa of 2^23.
+// A block with a non-finite scale takes the per-element path so that NaN bit
+// patterns match the reference's conversion as well.
+template <int T>
+__device__ __forceinline__ void sub32_to_f16(const uint8_t* __restrict__ row, int sub, uint32_t (&h)[16]) {
+    if constexpr (T == QT_Q8_0) {
+        const uint8_t* blk = row + (size_t)sub * 34;
+        const uint16_t dbits = ld_u16(blk);
+        const uint16_t* q = reinterpret_cast<const uint16_t*>(blk + 2);
+        if (((dbits >> 10) & 0x1f) == 0x1f) {   // inf/NaN scale
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+                const float d = h2f_bits(dbits);
+                const uint16_t w = q[j];
+                h[j] = (uint32_t)f2h_bits(__fmul_rn(d, (float)(int8_t)(w & 0xff))) |
+                       ((uint32_t)f2h_bits(__fmul_rn(d, (float)(int8_t)(w >> 8))) << 16);
+            }
+            return;
+        }
+        const __half2 d2 = __halves2half2(__ushort_as_half(dbits), __ushort_as_half(dbits));
+        const __half2 off = __halves2half2(__ushort_as_half((uint16_t)0x6480), __ushort_as_half((uint16_t)0x6480));   // 1152
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+            const uint32_t w = (uint32_t)q[j] ^ 0x8080u;                   // int8 pair -> q + 128
+            const uint32_t mg = __byte_perm(w, 0x64006400u, 0x7170);        // half2 (1024 + b0, 1024 + b1)
+            const __half2 v = __hmul2(d2, __hsub2(*reinterpret_cast<const __half2*>(&mg), off));
+            h[j] = *reinterpret_cast<const uint32_t*>(&v);
+        }
+    } else {
+        constexpr int SBB = T == QT_Q4_K ? 144 : 176;
+        constexpr int QS = T == QT_Q4_K ? 16 : 48;
+        const uint8_t* b = row + (size_t)(sub >> 3) * SBB;
+        const int j = sub & 7;
+        const uint4 hdr = *reinterpret_cast<const uint4*>(b);
+        int sc, mn;
+        kq_scale_min_reg(j, hdr, sc, mn);
+        const float a = __fmul_rn(h2f_bits((uint16_t)(hdr.x & 0xffff)), (float)sc);
+        const float m = __fmul_rn(h2f_bits((uint16_t)(hdr.x >> 16)), (float)mn);
+        const uint4 q0 = *reinterpret_cast<const uint4*>(b + QS + 32 * (j >> 1));
+        const uint4 q1 = *reinterpret_cast<const uint4*>(b + QS + 32 * (j >> 1) + 16);
+        const uint32_t qw[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+        uint32_t hw[8];
+        if constexpr (T == QT_Q5_K) {
+            const uint4 a0 = *reinterpret_cast<const uint4*>(b + 16);
+            const uint4 a1 = *reinterpret_cast<const uint4*>(b + 32);
+            hw[0] = a0.x; hw[1] = a0.y; hw[2] = a0.z; hw[3] = a0.w; hw[4] = a1.x; hw[5] = a1.y; hw[6] = a1.z; hw[7] = a1.w;
+        }
+        const bool finite = fabsf(a) < INFINITY && fabsf(m) < INFINITY;
+        const uint32_t sh = (j & 1) * 4;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            // four nibbles of bytes 4k..4k+3, each placed into the mantissa of 2^23
+            uint32_t nib = (qw[k] >> sh) & 0x0F0F0F0Fu;
+            if constexpr (T == QT_Q5_K) nib |= ((hw[k] >> j) & 0x01010101u) << 4;
+            float v[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const float q = __uint_as_float(__byte_perm(nib, 0x4B000000u, 0x7440 + e)) - 8388608.0f;
+                v[e] = __fmaf_rn(a, q, -m);
+            }
+            if (finite) {
+                const __half2 p0 = __floats2half2_rn(v[0], v[1]), p1 = __floats2half2_rn(v[2], v[3]);
+                h[2 * k] = *reinterpret_cast<const uint32_t*>(&p0);
+                h[2 * k + 1] = *reinterpret_cast<const uint32_t*>(&p1);
+            } else {
+                h[2 * k] = (uint32_t)f2h_bits(v[0]) | ((uint32_t)f2h_bits(v[1]) << 16);
+                h[2 * k + 1] = (uint32_t)f2h_bits(v[2]) | ((uint32_t)f2h_bits(v[3]) << 16);
+            }
+        }
+    }
+}
+
 
 }  // namespace tk

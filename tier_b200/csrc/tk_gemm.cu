@@ -23,6 +23,14 @@
 // steps) is cut into segments of seg_kb k-blocks.  Segments alternate between
 // the two TMEM accumulators and the epilogue sums them into D in fp32 (RNE),
 // so the error grows with the segment length, not with K.
+// Split-K (long K, few tiles): work units are (tile, split) for 2 splits,
+// every first split ordered before every second one.  Split 0 accumulates
+// into D, split 1 into a workspace slab; whichever finishes second adds the
+// slab into D ("last arrival fixes up", one atomic per warp quarter, no
+// waiting), or split 1 adds straight into D when split 0 is already done.
+// Every path computes D = fl(P0 + P1), so the result does not depend on the
+// order.  No CTA ever waits for another, so the kernel cannot deadlock when
+// other kernels (e.g. NCCL) hold some SMs.
 // All waits are bounded (tk_device.cuh); a timeout records a status code and
 // the roles drain out instead of hanging.
 #include <cuda.h>
@@ -59,8 +67,14 @@ struct __align__(64) GemmParams {
     int M, N, K;
     int nprod;
     int pa[3], pb[3];
-    int tiles_m, tiles_n;  // in tiles of (128 * CG) x 256
+    int tiles_m, tiles_n;  // in tiles of (128 * CG) x bn
+    int bn;                // tile width (output columns): 256, 224, 192 or 128
     int seg_kb;            // k-blocks per accumulation segment (>= 1)
+    int splits;            // K splits per tile: 1 or 2 (work unit = tile x split)
+    int* flags;            // split arrivals per (tile, CTA half, warp quarter)
+    int epoch;             // this launch's flag stamp (flags of older launches are lower)
+    float* sws;            // split 1's partial sums [M, sws_ld] (fp32)
+    long sws_ld;
     float* D;
     long ldd;
     int beta;
@@ -76,6 +90,12 @@ struct EpiParams {
 
 __device__ __forceinline__ float exp2i(int e) {   // exact 2^e for e in [-126, 127]
     return __uint_as_float((uint32_t)(e + 127) << 23);
+}
+
+__device__ __forceinline__ int ld_acquire_gpu(const int* p) {
+    int v;
+    asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
 }
 
 template <int CG, bool B_MN, int EPI>
@@ -128,7 +148,9 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     const uint32_t tmem_base = *tmem_slot;
 
     const int num_tiles = p.tiles_m * p.tiles_n;
+    const int num_units = num_tiles * p.splits;
     const int kblocks = (p.K + BK - 1) / BK;
+    const int kb_per_split = (kblocks + p.splits - 1) / p.splits;
 
     if (warp == 0) {
         // ---------------- TMA producer (each CTA loads its own operands) ----------------
@@ -136,37 +158,39 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             int s = 0;
             uint32_t ph = 0;
             bool ok = true;
-            for (int tile = cid; tile < num_tiles && ok; tile += ncl) {
+            for (int u0 = cid; u0 < num_units && ok; u0 += ncl) {
+                const int tile = u0 % num_tiles, sp = u0 / num_tiles;
                 const int mb = tile % p.tiles_m, nb = tile / p.tiles_m;
                 const int arow = (mb * CG + (int)rank) * BM;
-                const int bcol = nb * BN + (int)rank * G::B_ROWS;
-                for (int kb = 0; kb < kblocks && ok; ++kb) {
+                const int brows = p.bn / CG;                          // B rows this CTA loads
+                const int bcol = nb * p.bn + (int)rank * brows;
+                const int kbs = sp * kb_per_split, kbe = kbs + kb_per_split < kblocks ? kbs + kb_per_split : kblocks;
+                for (int kb = kbs; kb < kbe && ok; ++kb) {
                     for (int q = 0; q < p.nprod; ++q) {
                         if (!mbar_wait(&empty[s], ph ^ 1, p.status)) { ok = false; break; }
                         uint8_t* a_dst = sA + s * G::A_BYTES;
                         uint8_t* b_dst = sB + s * G::B_BYTES;
                         const void* ma = &p.tmA[p.pa[q]];
                         const void* mbm = &p.tmB[p.pb[q]];
+                        const uint32_t stage_tx = (uint32_t)(G::A_BYTES + brows * BK * 2);
                         if constexpr (CG == 1) {
-                            mbar_arrive_expect_tx(&full[s], G::STAGE_BYTES);
+                            mbar_arrive_expect_tx(&full[s], stage_tx);
                             tma_load_2d(a_dst, ma, &full[s], kb * BK, arow);
                             if constexpr (!B_MN) {
                                 tma_load_2d(b_dst, mbm, &full[s], kb * BK, bcol);
                             } else {
-#pragma unroll
-                                for (int j = 0; j < G::B_ROWS / 64; ++j)
+                                for (int j = 0; j < brows / 64; ++j)
                                     tma_load_2d(b_dst + j * (64 * BK * 2), mbm, &full[s], bcol + 64 * j, kb * BK);
                             }
                         } else {
                             // both CTAs' loads complete on the leader's barrier
                             const uint32_t fb = mapa_shared(smem_u32(&full[s]), 0);
-                            if (rank == 0) mbar_arrive_expect_tx(&full[s], 2 * G::STAGE_BYTES);
+                            if (rank == 0) mbar_arrive_expect_tx(&full[s], 2 * stage_tx);
                             tma_load_2d_cg2(a_dst, ma, fb, kb * BK, arow);
                             if constexpr (!B_MN) {
                                 tma_load_2d_cg2(b_dst, mbm, fb, kb * BK, bcol);
                             } else {
-#pragma unroll
-                                for (int j = 0; j < G::B_ROWS / 64; ++j)
+                                for (int j = 0; j < brows / 64; ++j)
                                     tma_load_2d_cg2(b_dst + j * (64 * BK * 2), mbm, fb, bcol + 64 * j, kb * BK);
                             }
                         }
@@ -179,18 +203,20 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     } else if (warp == 1) {
         // ---------------- MMA issuer (the leader CTA of a pair) ----------------
         if (lane == 0 && rank == 0) {
-            constexpr uint32_t idesc = idesc_f16(BM * CG, BN, 0, 0, B_MN ? 1 : 0);
+            const uint32_t idesc = idesc_f16(BM * CG, p.bn, 0, 0, B_MN ? 1 : 0);
             int s = 0;
             uint32_t ph = 0;
             bool ok = true;
-            int u = 0;   // accumulation units (tile, segment) processed
-            for (int tile = cid; tile < num_tiles && ok; tile += ncl) {
-                for (int kb0 = 0; kb0 < kblocks && ok; kb0 += p.seg_kb, ++u) {
-                    const int kb1 = kb0 + p.seg_kb < kblocks ? kb0 + p.seg_kb : kblocks;
+            int u = 0;   // accumulation units (tile, split, segment) processed
+            for (int u0 = cid; u0 < num_units && ok; u0 += ncl) {
+                const int sp = u0 / num_tiles;
+                const int kbs = sp * kb_per_split, kbe = kbs + kb_per_split < kblocks ? kbs + kb_per_split : kblocks;
+                for (int kb0 = kbs; kb0 < kbe && ok; kb0 += p.seg_kb, ++u) {
+                    const int kb1 = kb0 + p.seg_kb < kbe ? kb0 + p.seg_kb : kbe;
                     const int acc = u & 1;
                     if (!mbar_wait(&tempty[acc], ((u >> 1) & 1) ^ 1, p.status)) { ok = false; break; }
                     tc_fence_after();
-                    const uint32_t d_tmem = tmem_base + acc * BN;
+                    const uint32_t d_tmem = tmem_base + acc * 256;
                     const int nst = (kb1 - kb0) * p.nprod;
                     for (int st = 0; st < nst; ++st) {
                         if (!mbar_wait(&full[s], ph, p.status)) { ok = false; break; }
@@ -231,49 +257,114 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         const int quarter = warp & 3;                 // TMEM lanes this warp may access
         int u = 0;
         bool ok = true;
-        for (int tile = cid; tile < num_tiles && ok; tile += ncl) {
+        for (int u0 = cid; u0 < num_units && ok; u0 += ncl) {
+          const int tile = u0 % num_tiles, sp = u0 / num_tiles;
           const int mb = tile % p.tiles_m, nb = tile / p.tiles_m;
-          for (int kb0 = 0; kb0 < kblocks; kb0 += p.seg_kb, ++u) {
+          const int kbs = sp * kb_per_split, kbe = kbs + kb_per_split < kblocks ? kbs + kb_per_split : kblocks;
+          // one flag per (tile, CTA half, warp quarter): the same warp quarter of
+          // both splits owns the same 32 rows, so warps pair up one to one
+          int* flag = p.splits > 1 ? p.flags + ((size_t)tile * CG + rank) * 4 + quarter : nullptr;
+          const int arrived = p.epoch * 16 + 1;
+          for (int kb0 = kbs; kb0 < kbe; kb0 += p.seg_kb, ++u) {
             const int acc = u & 1;
-            if (!mbar_wait(&tfull[acc], (u >> 1) & 1, p.status)) { ok = false; break; }
+            const bool w = mbar_wait(&tfull[acc], (u >> 1) & 1, p.status);
+            if (!__all_sync(0xffffffffu, w)) { ok = false; break; }   // warp-uniform exit
             tc_fence_after();
-            const bool add_prev = kb0 > 0 || p.beta;   // later segments (or beta = 1) add to D
             const int row = (mb * CG + (int)rank) * BM + quarter * 32 + lane;
             const bool row_ok = row < p.M;
-            const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN;
+            const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * 256;
             const int e = (p.row_exp && row_ok ? p.row_exp[row] : 0) + p.col_exp;
             const float f = ldexpf(1.0f, -e);
-            const int col_base = nb * BN;
+            const int col_base = nb * p.bn;
             if constexpr (EPI == EPI_STORE) {
-                float* drow = p.D + (size_t)(row_ok ? row : 0) * p.ldd;
+                const bool last_seg = kb0 + p.seg_kb >= kbe;
+                // split 1 on its last segment adds straight into D once split 0
+                // has arrived; otherwise it accumulates in the workspace slab
+                bool direct = false;
+                if (sp > 0 && last_seg) {
+                    int v = 0;
+                    if (lane == 0) v = ld_acquire_gpu(flag);
+                    direct = __shfl_sync(0xffffffffu, v, 0) == arrived;
+                }
+                float* dst = (sp == 0 || direct) ? p.D : p.sws;
+                const long ldst = (sp == 0 || direct) ? p.ldd : p.sws_ld;
+                float* drow = dst + (size_t)(row_ok ? row : 0) * ldst;
+                const float* wrow = p.sws ? p.sws + (size_t)(row_ok ? row : 0) * p.sws_ld : nullptr;
+                // partial of earlier segments of this split: in dst, except for a
+                // direct split 1, whose earlier segments sit in the slab
+                const bool add_own = kb0 > kbs || (sp == 0 && p.beta);
+                const bool own_in_ws = direct && kb0 > kbs;
+                const bool add_d = add_own || direct;   // direct: D holds split 0's sum
 #pragma unroll 1
-                for (int c = 0; c < BN; c += 32) {
+                for (int c = 0; c < p.bn; c += 32) {
+                    const int col0 = col_base + c;
+                    const bool full_chunk = row_ok && col0 + 32 <= p.N;
+                    // issue this chunk's global reads before the TMEM read and
+                    // before any store, so the 8 (or 16) loads overlap instead
+                    // of each waiting behind the previous store
+                    float4 od[8], ow[8];
+                    if (full_chunk && add_d) {
+#pragma unroll
+                        for (int q = 0; q < 8; ++q) od[q] = reinterpret_cast<const float4*>(drow + col0)[q];
+                    }
+                    if (full_chunk && own_in_ws) {
+#pragma unroll
+                        for (int q = 0; q < 8; ++q) ow[q] = reinterpret_cast<const float4*>(wrow + col0)[q];
+                    }
                     uint32_t r[32];
                     tc_ld_32x32b_x32(taddr + c, r);
                     tc_wait_ld();
-                    if (row_ok) {
-                        const int col0 = col_base + c;
-                        if (col0 + 32 <= p.N) {
+                    if (full_chunk) {
+                        float4* dp = reinterpret_cast<float4*>(drow + col0);
 #pragma unroll
-                            for (int j = 0; j < 32; j += 4) {
-                                float4 v = make_float4(__uint_as_float(r[j]) * f, __uint_as_float(r[j + 1]) * f,
-                                                       __uint_as_float(r[j + 2]) * f, __uint_as_float(r[j + 3]) * f);
-                                float4* dp = reinterpret_cast<float4*>(drow + col0 + j);
-                                if (add_prev) {
-                                    const float4 o = *dp;
-                                    v.x += o.x; v.y += o.y; v.z += o.z; v.w += o.w;
-                                }
-                                *dp = v;
+                        for (int q = 0; q < 8; ++q) {
+                            float4 v = make_float4(__uint_as_float(r[4 * q]) * f, __uint_as_float(r[4 * q + 1]) * f,
+                                                   __uint_as_float(r[4 * q + 2]) * f, __uint_as_float(r[4 * q + 3]) * f);
+                            if (own_in_ws) { v.x += ow[q].x; v.y += ow[q].y; v.z += ow[q].z; v.w += ow[q].w; }
+                            if (add_d) {
+                                v.x = od[q].x + v.x; v.y = od[q].y + v.y; v.z = od[q].z + v.z; v.w = od[q].w + v.w;
                             }
-                        } else {
+                            dp[q] = v;
+                        }
+                    } else if (row_ok) {
 #pragma unroll
-                            for (int j = 0; j < 32; ++j) {
-                                if (col0 + j < p.N) {
-                                    float v = __uint_as_float(r[j]) * f;
-                                    if (add_prev) v += drow[col0 + j];
-                                    drow[col0 + j] = v;
+                        for (int j = 0; j < 32; ++j) {
+                            if (col0 + j < p.N) {
+                                float v = __uint_as_float(r[j]) * f;
+                                if (own_in_ws) v += wrow[col0 + j];
+                                if (add_d) v = drow[col0 + j] + v;
+                                drow[col0 + j] = v;
+                            }
+                        }
+                    }
+                }
+                if (flag && last_seg && !direct) {
+                    // arrive; the second arrival adds the slab into D
+                    __threadfence();
+                    __syncwarp();
+                    int old = 0;
+                    if (lane == 0) old = atomicMax(flag, arrived);
+                    old = __shfl_sync(0xffffffffu, old, 0);
+                    if (old == arrived) {
+                        __threadfence();
+                        if (row_ok) {
+                            float* drw = p.D + (size_t)row * p.ldd;
+                            const int cend = col_base + p.bn < p.N ? col_base + p.bn : p.N;
+                            int c = col_base;
+                            for (; c + 32 <= cend; c += 32) {   // 8 + 8 loads in flight, then stores
+                                float4 o[8], w4[8];
+#pragma unroll
+                                for (int q = 0; q < 8; ++q) {
+                                    o[q] = reinterpret_cast<const float4*>(drw + c)[q];
+                                    w4[q] = reinterpret_cast<const float4*>(wrow + c)[q];
+                                }
+#pragma unroll
+                                for (int q = 0; q < 8; ++q) {
+                                    o[q].x += w4[q].x; o[q].y += w4[q].y; o[q].z += w4[q].z; o[q].w += w4[q].w;
+                                    reinterpret_cast<float4*>(drw + c)[q] = o[q];
                                 }
                             }
+                            for (; c < cend; ++c) drw[c] += wrow[c];
                         }
                     }
                 }
@@ -288,7 +379,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
                 double sum = 0.0;
                 float tgt = 0.0f;
 #pragma unroll 1
-                for (int c = 0; c < BN; c += 32) {
+                for (int c = 0; c < p.bn; c += 32) {
                     uint32_t r[32];
                     tc_ld_32x32b_x32(taddr + c, r);
                     tc_wait_ld();
@@ -331,7 +422,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
                 const float mval = live ? (float)G.mask[row] : 0.0f;
                 const float sc = exp2i(G.dl_exp);
 #pragma unroll 1
-                for (int c = 0; c < BN; c += 32) {
+                for (int c = 0; c < p.bn; c += 32) {
                     uint32_t r[32];
                     tc_ld_32x32b_x32(taddr + c, r);
                     tc_wait_ld();
@@ -446,7 +537,7 @@ static tk_status go(tk_ctx* ctx, const GemmParams& gp, const EpiParams& ep, cuda
         if (e != cudaSuccess) return cuda_fail(e, "gemm smem attribute");
         attr_set = true;
     }
-    const int tiles = gp.tiles_m * gp.tiles_n;
+    const int tiles = gp.tiles_m * gp.tiles_n * gp.splits;   // work units
     const int groups_max = ctx->num_sms / CG;
     const int groups = tiles < groups_max ? tiles : groups_max;
     cudaLaunchConfig_t cfg = {};
@@ -468,7 +559,7 @@ static tk_status go(tk_ctx* ctx, const GemmParams& gp, const EpiParams& ep, cuda
     return cuda_fail(cudaGetLastError(), "gemm launch");
 }
 
-static tk_status build(const GemmDesc& g, tk_ctx* ctx, GemmParams& gp, int cg) {
+static tk_status build(const GemmDesc& g, tk_ctx* ctx, GemmParams& gp, int cg, int bn) {
     if (g.M <= 0 || g.N <= 0 || g.K <= 0) return fail(TK_ERR_INVALID, "GEMM with empty shape");
     if (g.nprod < 1 || g.nprod > 3) return fail(TK_ERR_INVALID, "GEMM product count must be 1..3");
     if ((reinterpret_cast<uintptr_t>(g.D) & 15) || g.ldd % 4)
@@ -486,14 +577,20 @@ static tk_status build(const GemmDesc& g, tk_ctx* ctx, GemmParams& gp, int cg) {
     for (int i = 0; i < 2; ++i)
         if (g.B[i]) {
             tk_status st = g.b_mn ? make_map(&gp.tmB[i], g.B[i], g.N, g.K, g.ldb, BK)
-                                  : make_map(&gp.tmB[i], g.B[i], g.K, g.N, g.ldb, BN / cg);
+                                  : make_map(&gp.tmB[i], g.B[i], g.K, g.N, g.ldb, bn / cg);
             if (st != TK_OK) return st;
         }
     gp.M = g.M; gp.N = g.N; gp.K = g.K;
     gp.nprod = g.nprod;
     for (int i = 0; i < 3; ++i) { gp.pa[i] = g.pa[i]; gp.pb[i] = g.pb[i]; }
     gp.tiles_m = (g.M + BM * cg - 1) / (BM * cg);
-    gp.tiles_n = (g.N + BN - 1) / BN;
+    gp.tiles_n = (g.N + bn - 1) / bn;
+    gp.bn = bn;
+    gp.splits = 1;
+    gp.flags = nullptr;
+    gp.epoch = 0;
+    gp.sws = nullptr;
+    gp.sws_ld = 0;
     {
         const int kblocks = (g.K + BK - 1) / BK;
         int seg = g.seg_kb > 0 ? g.seg_kb : kblocks;
@@ -510,11 +607,68 @@ static tk_status build(const GemmDesc& g, tk_ctx* ctx, GemmParams& gp, int cg) {
 // a single CTA otherwise (a pair would leave half its tensor cores idle).
 static int pick_cg(const GemmDesc& g) { return g.M > BM ? 2 : 1; }
 
+// Tile width: the persistent grid runs ceil(tiles / groups) waves of tiles, so
+// pick the width with the least (waves x width x per-FLOP premium); narrower
+// tiles move more operand bytes per MMA and pay for it.  An N-major B is
+// loaded in 64-column boxes per CTA, which allows 256 and 128 (CTA pairs).
+static int pick_bn(const GemmDesc& g, int cg, int num_sms) {
+    const int groups = num_sms / cg;
+    const int tiles_m = (g.M + BM * cg - 1) / (BM * cg);
+    static const int cand[4] = {256, 224, 192, 128};
+    // measured on B200 (CTA pairs, K = 4096..14336): 224 ~1.12x, 128 ~1.45x
+    // the time per FLOP of 256-wide tiles
+    static const double premium[4] = {1.0, 1.12, 1.25, 1.45};
+    int best = 256;
+    double best_cost = 1e300;
+    for (int i = 0; i < 4; ++i) {
+        const int bn = cand[i];
+        if (g.b_mn && (bn / cg) % 64) continue;
+        const long tiles = (long)tiles_m * ((g.N + bn - 1) / bn);
+        const long waves = (tiles + groups - 1) / groups;
+        const double cost = (double)waves * bn * premium[i];
+        if (cost < best_cost - 1e-9) { best_cost = cost; best = bn; }
+    }
+    return best;
+}
+
+// K splits: the waves of (tile, split) units against the fp32 read-modify-
+// write a later split adds (about 5 k-blocks of MMA time per tile).
+static int pick_splits(int tiles_m, int tiles_n, int cg, int num_sms, int kblocks, int max_tiles) {
+    const long groups = num_sms / cg, tiles = (long)tiles_m * tiles_n;
+    if (tiles > max_tiles) return 1;
+    const double c1 = (double)((tiles + groups - 1) / groups) * kblocks;
+    const double c2 = (double)((2 * tiles + groups - 1) / groups) * ((kblocks + 1) / 2) + 5.0;
+    return (kblocks >= 32 && c2 < 0.95 * c1) ? 2 : 1;
+}
+
+int gemm_splits(const tk_ctx* ctx, const GemmDesc& g) {
+    if (!ctx->flags || g.M <= 0 || g.N <= 0 || g.K <= 0) return 1;
+    const int cg = pick_cg(g), bn = pick_bn(g, cg, ctx->num_sms);
+    const int tiles_m = (g.M + BM * cg - 1) / (BM * cg), tiles_n = (g.N + bn - 1) / bn;
+    return pick_splits(tiles_m, tiles_n, cg, ctx->num_sms, (g.K + BK - 1) / BK, ctx->flags_len / (4 * cg));
+}
+
 tk_status launch_gemm(tk_ctx* ctx, const GemmDesc& g, cudaStream_t s) {
     const int cg = pick_cg(g);
     GemmParams gp;
-    tk_status st = build(g, ctx, gp, cg);
+    tk_status st = build(g, ctx, gp, cg, pick_bn(g, cg, ctx->num_sms));
     if (st != TK_OK) return st;
+    if (g.split_ws && gemm_splits(ctx, g) == 2) {
+        if ((reinterpret_cast<uintptr_t>(g.split_ws) & 15) || g.split_ld < g.N || g.split_ld % 4)
+            return fail(TK_ERR_INVALID, "split-K workspace misaligned");
+        // flags hold epoch*16 + 1 once a split arrived; stamps only grow, so no
+        // reset is needed until the stamp wraps
+        if (++ctx->epoch >= (1u << 26)) {
+            cudaError_t e = cudaMemsetAsync(ctx->flags, 0, sizeof(int) * ctx->flags_len, s);
+            if (e != cudaSuccess) return fail(TK_ERR_CUDA, "split-K flag reset failed");
+            ctx->epoch = 1;
+        }
+        gp.splits = 2;
+        gp.flags = ctx->flags;
+        gp.epoch = (int)ctx->epoch;
+        gp.sws = g.split_ws;
+        gp.sws_ld = g.split_ld;
+    }
     EpiParams ep;
     memset(&ep, 0, sizeof(ep));
     if (cg == 2) return g.b_mn ? go<2, true, EPI_STORE>(ctx, gp, ep, s) : go<2, false, EPI_STORE>(ctx, gp, ep, s);
@@ -525,7 +679,7 @@ tk_status launch_gemm_lse(tk_ctx* ctx, const GemmDesc& g, const LseDesc& e, cuda
     if (g.b_mn) return fail(TK_ERR_INVALID, "LM-head logits GEMM takes a K-major head");
     const int cg = pick_cg(g);
     GemmParams gp;
-    tk_status st = build(g, ctx, gp, cg);
+    tk_status st = build(g, ctx, gp, cg, BN);
     if (st != TK_OK) return st;
     gp.seg_kb = (g.K + BK - 1) / BK;   // statistics need the complete logit
     EpiParams ep;
@@ -539,7 +693,7 @@ tk_status launch_gemm_dlogit(tk_ctx* ctx, const GemmDesc& g, const DlogitDesc& e
     if (g.N % BN) return fail(TK_ERR_INVALID, "dlogit epilogue needs a chunk width multiple of 256");
     const int cg = pick_cg(g);
     GemmParams gp;
-    tk_status st = build(g, ctx, gp, cg);
+    tk_status st = build(g, ctx, gp, cg, BN);
     if (st != TK_OK) return st;
     gp.seg_kb = (g.K + BK - 1) / BK;
     EpiParams ep;

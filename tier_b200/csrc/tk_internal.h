@@ -23,6 +23,9 @@ struct tk_ctx {
     size_t ws_bytes = 0;
     int* status = nullptr;       // device status word (tk::DEV_*)
     uint64_t launches = 0;       // kernels launched through this context
+    int* flags = nullptr;        // split-K progress flags (device), flags_len ints
+    int flags_len = 0;
+    uint32_t epoch = 0;          // stamps split-K flags per launch (no reset needed)
     tk_prof prof;
 };
 
@@ -92,8 +95,36 @@ struct GemmDesc {
     const int* row_exp = nullptr;
     int col_exp = 0;
     int seg_kb = 0;        // k-blocks (of 64) per fp32 accumulation segment; 0 = whole K
+    float* split_ws = nullptr;   // fp32 [M, split_ld] slab; enables split-K when given
+    long split_ld = 0;
 };
+// K splits launch_gemm would use for g given a split workspace (1 or 2).
+int gemm_splits(const tk_ctx* ctx, const GemmDesc& g);
 tk_status launch_gemm(tk_ctx* ctx, const GemmDesc& g, cudaStream_t s);
+
+// Fused-dequant GEMM (tk_gemm_q.cu): B is the raw quantized weight W[w_rows,
+// row_bytes]; dx == false: D[M, N] = A . W^T with N = w_rows, K = cols of W;
+// dx == true: D[M, N] = A . W with K = w_rows, N = cols of W.  CTA pairs only
+// (M > 128).  Every product multiplies an A plane by the same dequantized W.
+struct GemmQDesc {
+    const uint16_t* A[3] = {nullptr, nullptr, nullptr};
+    long lda = 0;
+    int nprod = 1;
+    int pa[3] = {0, 0, 0};
+    int qtype = 0;
+    const void* W = nullptr;
+    size_t w_row_bytes = 0;
+    int w_rows = 0;
+    bool dx = false;
+    int M = 0, N = 0, K = 0;
+    float* D = nullptr;
+    long ldd = 0;
+    int beta = 0;
+    const int* row_exp = nullptr;
+    int seg_kb = 0;
+};
+bool gemm_q_supported(int qtype);
+tk_status launch_gemm_q(tk_ctx* ctx, const GemmQDesc& g, cudaStream_t s);
 
 // LM-head epilogue variants (tk_gemm.cu)
 struct LseDesc {               // pass 1: per (row, 256-column tile) partial stats

@@ -37,6 +37,33 @@ def shard_rows(n: int, world: int, rank: int, align: int = 1) -> tuple[int, int]
     return a, b
 
 
+def merge_vocab_shards(rmax, rsum, amax, tgt, group, rescale):
+    """Merge per-shard running CE state into the global one, in place for
+    rmax / rsum / tgt; returns the merged argmax.  Shards are in vocab order
+    (rank r holds a lower vocab range than rank r+1).
+
+      argmax: all-gather (max, index); the highest max wins, a tie goes to the
+              lower rank, i.e. the lower vocab index (the reference's rule).
+      rmax:   all-reduce MAX.
+      rsum:   each shard rescales its sum to the global max
+              (rescale(rmax_local, rsum_local, rmax_global)), then all-reduce SUM.
+      tgt:    all-reduce SUM (only the shard holding the label has it non-zero)."""
+    import torch.distributed as dist
+    world = dist.get_world_size(group)
+    allm = [torch.empty_like(rmax) for _ in range(world)]
+    alla = [torch.empty_like(amax) for _ in range(world)]
+    dist.all_gather(allm, rmax.clone(), group=group)
+    dist.all_gather(alla, amax.clone(), group=group)
+    best = torch.argmax(torch.stack(allm), dim=0)          # first maximal rank
+    merged = torch.stack(alla).gather(0, best[None]).squeeze(0).contiguous()
+    gmax = rmax.clone()
+    dist.all_reduce(gmax, op=dist.ReduceOp.MAX, group=group)
+    rescale(rmax, rsum, gmax)
+    dist.all_reduce(rsum, group=group)
+    dist.all_reduce(tgt, group=group)
+    return merged
+
+
 class LinearPath:
     """One frozen projection W[N, K] (block-quantized, fp16, or fp32 split into
     fp16 hi/lo) on this rank's device, optionally row-sharded across `group`."""
@@ -65,8 +92,6 @@ class LinearPath:
         M = X.shape[0]
         local = Y if (Y is not None and self.group is None) else torch.empty(M, self.N, device=X.device,
                                                                                dtype=torch.float32)
-        if beta and Y is not None and self.group is None:
-            local = Y
         self.ctx.linear(self.W, X, M, local, x_dtype=_DT[X.dtype], ldx=X.stride(0), ldy=local.stride(0), beta=beta,
                         products=products)
         if self.group is None or not gather:
@@ -129,23 +154,8 @@ class LMHead:
         self.ctx.lmhead_stats(self.W, self.v0, self.V_shard, self.H, X, T, labels, mask, softcap, self.chunk, rmax,
                               rsum, amax, tgt, products=self.products)
         if self.group is not None:
-            import torch.distributed as dist
-            g = self.group
-            world = dist.get_world_size(g)
-            # argmax across shards: highest max, ties to the lower vocab index
-            # (shards are in vocab order, so the lower rank wins a tie).
-            allm = [torch.empty_like(rmax) for _ in range(world)]
-            alla = [torch.empty_like(amax) for _ in range(world)]
-            dist.all_gather(allm, rmax.clone(), group=g)
-            dist.all_gather(alla, amax, group=g)
-            m = torch.stack(allm)              # [world, T-1]
-            best = torch.argmax(m, dim=0)      # first maximal rank = lower vocab index
-            amax = torch.stack(alla).gather(0, best[None]).squeeze(0).contiguous()
-            gmax = rmax.clone()
-            dist.all_reduce(gmax, op=dist.ReduceOp.MAX, group=g)
-            self.ctx.lmhead_rescale(T - 1, rmax, rsum, gmax)
-            dist.all_reduce(rsum, group=g)
-            dist.all_reduce(tgt, group=g)
+            amax = merge_vocab_shards(rmax, rsum, amax, tgt, self.group,
+                                      lambda rl, sl, rg: self.ctx.lmhead_rescale(T - 1, rl, sl, rg))
         return rmax, rsum, amax, tgt
 
     def loss(self, T, labels, mask, rmax, rsum, amax, tgt):
@@ -175,4 +185,4 @@ class LMHead:
         return loss, n_loss, hits, amax, dX
 
 
-__all__ = ["LinearPath", "LMHead", "shard_rows", "row_bytes", "BF16", "F16", "X2", "X3_REF"]
+__all__ = ["LinearPath", "LMHead", "shard_rows", "merge_vocab_shards"]
