@@ -313,9 +313,10 @@ def run_ours(args):
 
     if rank == 0:
         hbm, tf_burst, tf_sus, src = peaks()
-        gemm_avg_ms = gemm_ms / max(gemm_n, 1)
-        gemm_flop_launch = flop_step / 2 / world      # one direction on this rank's rows
-        achieved = gemm_flop_launch / (gemm_avg_ms * 1e-3) / 1e12
+        # this rank's GEMM FLOPs per step (fwd + dX over its rows) over its GEMM
+        # time per step; launches per step vary (dX may run in M-chunks)
+        gemm_ms_step = gemm_ms / args.steps
+        achieved = flop_step / world / (gemm_ms_step * 1e-3) / 1e12
         traffic = None   # dram read+write bytes per GEMM launch from the committed ncu summary
         tf = ROOT / "profiles" / "gemm_tc_kernel_c2_q4k_m4096.md"
         if tf.exists():

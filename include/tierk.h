@@ -73,6 +73,8 @@ enum { TK_X3_AUTO = 0, TK_X3_REF = 1, TK_X3_HHL = 2, TK_X2 = 3, TK_X1 = 4 };
  * decode is repeated for every 256-row tile of M, so it is slower than the
  * default at every M measured on B200 so far. */
 enum { TK_QFUSED = 0x100 };
+/* OR-ed into tk_gemv's qtype: W is frozen (see tk_gemv). */
+enum { TK_WFROZEN = 0x200 };
 
 typedef struct tk_ctx tk_ctx;
 
@@ -124,7 +126,11 @@ tk_status tk_dequant(tk_ctx *ctx, int qtype, const void *blocks, size_t row_byte
 
 /* ---- decode GEMV (M = 1..16) -------------------------------------------- */
 /* y[m, n] = sum_k W(n, k) * x[m, k] for m < M, n < N, fp32 x and y.
- * qtype: TK_Q8_0, TK_Q4_K, TK_Q5_K, TK_Q6_K, TK_Q4_0, TK_F16, TK_BF16, TK_F32.
+ * qtype: TK_Q8_0, TK_Q4_K, TK_Q5_K, TK_Q6_K, TK_Q4_0, TK_F16, TK_BF16, TK_F32,
+ * optionally OR TK_WFROZEN: the caller guarantees that no kernel enqueued
+ * earlier on the stream writes W (frozen weights), so the Q8_0 / Q4_K / Q5_K
+ * kernel may start fetching W before the preceding kernel has finished
+ * (x is still read only after it); without the flag nothing is read early.
  * Replaces gemv_q (tier/tier.cpp:300-306) and gemv<T> (tier/tier.cpp:2261-2268)
  * as dispatched by chat_lin (tier/tier.cpp:2351-2378). */
 tk_status tk_gemv(tk_ctx *ctx, int qtype, const void *W, size_t row_bytes, int N, int K,

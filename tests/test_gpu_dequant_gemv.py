@@ -62,7 +62,9 @@ def test_dequant_large_rows_and_offset(ctx, oracle, qtype):
 
 
 @pytest.mark.parametrize("qtype,N,K", [(8, 4096, 4096), (12, 1024, 4096), (13, 512, 5120), (1, 768, 3840),
-                                        (30, 256, 2048), (0, 256, 1024), (14, 256, 2048), (2, 256, 2048)])
+                                        (30, 256, 2048), (0, 256, 1024), (14, 256, 2048), (2, 256, 2048),
+                                        # fewer rows than SMs, ragged slots, shared-memory ring reuse
+                                        (8, 100, 256), (8, 32768, 1024), (12, 20000, 2048), (13, 9000, 1280)])
 @pytest.mark.parametrize("M", [1, 3, 16])
 def test_gemv_vs_f64(ctx, oracle, qtype, N, K, M):
     import torch
@@ -91,3 +93,27 @@ def test_gemv_c1_matches_reference_order_closely(ctx, oracle):
     got = host(y)[0]
     ref_order = oracle.gemv_warp_order(b[:256], 8, 256, K, x)
     assert np.abs(got[:256] - ref_order).max() / np.abs(ref_order).max() < 1e-5
+
+
+@pytest.mark.parametrize("qtype", [8, 12])
+def test_gemv_frozen_chain(ctx, oracle, qtype):
+    """TK_WFROZEN lets a GEMV fetch its (never written) weight before the
+    previous kernel ends, but x is still read after it: a chain whose x is
+    the previous GEMV's y gives the same bits as the chain without the flag."""
+    import torch
+    import tier_b200 as tk
+    rng = np.random.default_rng(9 + qtype)
+    K = 4096
+    bs = [dev(blocks_for(rng, qtype, K, K)) for _ in range(3)]
+    x0 = dev(rng.standard_normal((1, K)).astype(np.float32))
+    outs = []
+    for flag in (0, tk.WFROZEN):
+        ys = [torch.empty(1, K, device="cuda") for _ in bs]
+        x = x0
+        for b, y in zip(bs, ys):
+            ctx.gemv(qtype | flag, b, K, K, x, y)
+            x = y
+        outs.append([host(y) for y in ys])
+    for a, b in zip(*outs):
+        assert np.array_equal(a, b)
+    ctx.sync_status()

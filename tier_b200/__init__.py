@@ -35,6 +35,7 @@ DT_F32, DT_F16, DT_BF16 = 0, 1, 2
 # product sets
 X3_AUTO, X3_REF, X3_HHL, X2, X1 = 0, 1, 2, 3, 4
 QFUSED = 0x100   # OR into `products`: decode a quantized W inside the GEMM
+WFROZEN = 0x200  # OR into tk_gemv's qtype: W is never written by earlier kernels (early weight fetch)
 # kernel families for profiling
 PROF_GEMM, PROF_DEQUANT, PROF_SPLIT, PROF_GEMV, PROF_LMHEAD = range(5)
 
@@ -171,7 +172,7 @@ class Context:
         return out
 
     def gemv(self, qtype, W, N, K, x, y, M=1, ldx=None, ldy=None, row_bytes_=None, stream=None):
-        rb = row_bytes_ if row_bytes_ is not None else row_bytes(qtype, K)
+        rb = row_bytes_ if row_bytes_ is not None else row_bytes(qtype & ~WFROZEN, K)
         _check(self.lib.tk_gemv(self.h, qtype, _ptr(W), rb, N, K, _ptr(x), ldx or K, M, _ptr(y), ldy or N,
                                 _stream(stream)))
         return y

@@ -393,6 +393,8 @@ tk_status tk_dequant(tk_ctx* ctx, int qtype, const void* blocks, size_t row_byte
 tk_status tk_gemv(tk_ctx* ctx, int qtype, const void* W, size_t row_bytes, int N, int K, const float* x, int ldx,
                   int M, float* y, int ldy, void* stream) {
     if (!ctx) return fail(TK_ERR_INVALID, "tk_gemv: null context");
+    const bool frozen = (qtype & TK_WFROZEN) != 0;
+    qtype &= ~TK_WFROZEN;
     if (!gemv_supported(qtype)) return fail(TK_ERR_UNSUPPORTED, "tk_gemv: weight type " + std::to_string(qtype));
     if (M < 1 || M > 16) return fail(TK_ERR_INVALID, "tk_gemv: M must be 1..16 (use tk_linear_fwd beyond)");
     if (N < 0 || K <= 0) return fail(TK_ERR_INVALID, "tk_gemv: bad shape");
@@ -408,7 +410,7 @@ tk_status tk_gemv(tk_ctx* ctx, int qtype, const void* W, size_t row_bytes, int N
         return fail(TK_ERR_INVALID, "tk_gemv: weight rows must be 16-byte aligned");
     if ((qtype == TK_Q8_0 || qtype == TK_Q4_0) && K % 256)
         return fail(TK_ERR_INVALID, "tk_gemv: Q8_0/Q4_0 rows need K % 256 == 0");
-    return launch_gemv(ctx, qtype, W, row_bytes, N, K, x, ldx, M, y, ldy, static_cast<cudaStream_t>(stream));
+    return launch_gemv(ctx, qtype, W, row_bytes, N, K, x, ldx, M, y, ldy, static_cast<cudaStream_t>(stream), frozen);
 }
 
 tk_status tk_linear_fwd(tk_ctx* ctx, const tk_weight* W, const void* X, int x_dtype, int M, int ldx, float* Y, int ldy,

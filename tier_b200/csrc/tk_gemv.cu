@@ -217,9 +217,23 @@ static int popcount_chunks(int M) {
 }
 
 tk_status launch_gemv(tk_ctx* ctx, int t, const void* Wv, size_t rb, int N, int K, const float* x, int ldx, int M,
-                      float* y, int ldy, cudaStream_t s) {
+                      float* y, int ldy, cudaStream_t s, bool frozen) {
     if (N == 0 || M == 0) return TK_OK;
-    // Streaming kernel (tk_gemv2.cu) for Q8_0 / Q4_K / Q5_K when x fits in
+    // Tensor-core kernel (tk_gemv5.cu) for Q8_0 / Q4_K / Q5_K when x fits in
+    // shared memory: token chunks of up to 8.
+    if (gemv_mma_ok(t, rb, K, 1) && (reinterpret_cast<uintptr_t>(Wv) & 15) == 0) {
+        int m0 = 0;
+        while (m0 < M) {
+            int c = M - m0 < 8 ? M - m0 : 8;
+            while (c > 1 && !gemv_mma_ok(t, rb, K, c)) --c;
+            tk_status st = launch_gemv_mma(ctx, t, Wv, rb, N, K, x + (size_t)m0 * ldx, ldx, c, y + (size_t)m0 * ldy,
+                                           ldy, frozen, s);
+            if (st != TK_OK) return st;
+            m0 += c;
+        }
+        return TK_OK;
+    }
+    // Streaming kernel (tk_gemv4.cu) for Q8_0 / Q4_K / Q5_K when x fits in
     // shared memory: token chunks of 4, 2 and 1.
     if (gemv_stream_ok(t, rb, K, 1) && (reinterpret_cast<uintptr_t>(Wv) & 15) == 0) {
         int m0 = 0;
@@ -227,7 +241,7 @@ tk_status launch_gemv(tk_ctx* ctx, int t, const void* Wv, size_t rb, int N, int 
             const int r = M - m0;
             const int c = (r >= 4 && gemv_stream_ok(t, rb, K, 4)) ? 4 : (r >= 2 && gemv_stream_ok(t, rb, K, 2)) ? 2 : 1;
             tk_status st = launch_gemv_stream(ctx, t, Wv, rb, N, K, x + (size_t)m0 * ldx, ldx, c, y + (size_t)m0 * ldy,
-                                              ldy, s);
+                                              ldy, frozen, s);
             if (st != TK_OK) return st;
             m0 += c;
         }

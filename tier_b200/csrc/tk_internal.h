@@ -65,15 +65,19 @@ tk_status launch_split3_raw(tk_ctx* ctx, const float* x, size_t n, uint16_t* h, 
 tk_status weight_split_f32(tk_ctx* ctx, const float* W, int rows, int cols, uint16_t* planes, int* scale_log2,
                            cudaStream_t s);
 
-// ---- tk_gemv2.cu (streaming decode GEMV, Q8_0 / Q4_K / Q5_K, M in {1, 2, 4}) ----
+// ---- tk_gemv4.cu (streaming decode GEMV, Q8_0 / Q4_K / Q5_K, M in {1, 2, 4}) ----
 bool gemv_stream_ok(int qtype, size_t rb, int K, int M);
 tk_status launch_gemv_stream(tk_ctx* ctx, int qtype, const void* W, size_t rb, int N, int K, const float* x, int ldx,
-                             int M, float* y, int ldy, cudaStream_t s);
+                             int M, float* y, int ldy, bool frozen, cudaStream_t s);
+// ---- tk_gemv5.cu (decode GEMV on mma.sync tensor cores, Q8_0 / Q4_K / Q5_K, M <= 8) ----
+bool gemv_mma_ok(int qtype, size_t rb, int K, int M);
+tk_status launch_gemv_mma(tk_ctx* ctx, int qtype, const void* W, size_t rb, int N, int K, const float* x, int ldx,
+                          int M, float* y, int ldy, bool frozen, cudaStream_t s);
 
 // ---- tk_gemv.cu ----
 bool gemv_supported(int qtype);
 tk_status launch_gemv(tk_ctx* ctx, int qtype, const void* W, size_t rb, int N, int K, const float* x, int ldx,
-                      int M, float* y, int ldy, cudaStream_t s);
+                      int M, float* y, int ldy, cudaStream_t s, bool frozen = false);
 
 // ---- tk_gemm.cu ----
 // D[M, N] (fp32, row stride ldd) = sum_p A_{pa[p]}[M, K] . B_{pb[p]}^T, scaled
