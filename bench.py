@@ -487,8 +487,10 @@ def run_c3(args):
 
 def run_c4(args):
     """C4: chunked-vocab LM head + CE: W fp16 [262144, 3840], hidden fp32
-    [8192, 3840], labels uniform, chunk 16384; pass 1 (stats), loss, pass 2
-    (dX) per step with the three-part split of X and of dlogit."""
+    [8192, 3840], labels uniform, chunk 16384.  Default: the single pass
+    (one logits GEMM per chunk with the x3 split of X, then the dX GEMM with
+    the hi/lo probabilities); --c4-two-pass runs the reference's two passes
+    (logits recomputed in pass 2, dlogit split in three)."""
     import torch
     import tier_b200 as tk
     from tier_b200.host import LMHead
@@ -502,25 +504,34 @@ def run_c4(args):
     head = LMHead(ctx, W, 0, chunk=chunk, products=tk.X3_REF)
     dX = torch.zeros(T, H, device="cuda")
     n_loss = T - 1
+    two_pass = args.c4_two_pass
 
     def fn():
-        rmax, rsum, amax, tgt = head.stats(X, labels, mask)
-        head.loss(T, labels, mask, rmax, rsum, amax, tgt)
-        head.grad(X, labels, mask, n_loss, rmax, rsum, dX=dX)
+        if two_pass:
+            rmax, rsum, amax, tgt = head.stats(X, labels, mask)
+            head.loss(T, labels, mask, rmax, rsum, amax, tgt)
+            head.grad(X, labels, mask, n_loss, rmax, rsum, dX=dX)
+        else:
+            head.step_fused(X, labels, mask, n_loss=n_loss)
 
     steps = max(1, min(args.steps, 5))
     t_ms, k_ms, k_n, clk = _timed(ctx, fn, steps, 1, tk.PROF_GEMM)
     ms = t_ms / steps
     useful = 2 * 2.0 * T * V * H
-    executed = 3 * 3 * 2.0 * T * V * H
+    # executed products: logits x3 (+ x3 recompute + x3 dX in two passes;
+    # + hi/lo dX in the single pass)
+    executed = (3 + 3 + 3 if two_pass else 3 + 2) * 2.0 * T * V * H
     tf_burst = peaks()[1]
     gemm_exec = executed / (k_ms / steps * 1e-3) / 1e12
     print(json.dumps({"metric": "LM head + CE TFLOP/s (useful: logits + dX GEMMs)", "value": useful / (ms * 1e-3) / 1e12,
                       "unit": "TFLOP/s", "executed_tflops": executed / (ms * 1e-3) / 1e12, "ms_per_step": ms,
                       "steps": steps, "n_gpus": 1,
-                      "config": {"workload": "C4 V=262144 H=3840 T=8192 chunk=16384, two-pass, x3 split"},
+                      "config": {"workload": "C4 V=262144 H=3840 T=8192 chunk=16384, " +
+                                 ("two-pass, x3 split of X and dlogit" if two_pass else
+                                  "single pass, x3 split of X, hi/lo probabilities")},
                       "roofline": {"bound": "tensor", "achieved": gemm_exec, "peak": tf_burst, "unit": "TFLOP/s",
                                    "frac": gemm_exec / tf_burst, "kernel": "gemm_tc_kernel (executed products)"},
+                      "gemm_ms_per_step": k_ms / steps,
                       "clocks": clk}))
 
 
@@ -534,6 +545,7 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--gather-y", action="store_true", help="multi-GPU: all-gather the full Y every step")
     ap.add_argument("--dx-chunks", type=int, default=4, help="multi-GPU: dX GEMM / all-reduce pipeline chunks")
+    ap.add_argument("--c4-two-pass", action="store_true", help="c4: the reference's two passes")
     ap.add_argument("--config", default="c2", choices=["c1", "c2", "c3", "c4"],
                     help="c2 (default, the headline) or a secondary configuration on one GPU")
     args = ap.parse_args()

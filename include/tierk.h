@@ -203,6 +203,28 @@ tk_status tk_lmhead_grad(tk_ctx *ctx, const uint16_t *W, int v0, int V_shard, in
                          int n_loss, float softcap, int chunk, int products, const double *rmax,
                          const double *rsum, float *dX, void *stream);
 
+/* Single pass (one logits GEMM per chunk, where the reference's two passes
+ * need two): runs pass 1 exactly as tk_lmhead_stats (same rmax/rsum/amax/tgt
+ * updates) and accumulates, in dX [T, H] (overwritten; rows >= T-1 or
+ * masked stay 0), the UNNORMALISED sum_v exp(l[t,v] - rmax[t]) g(l) W[v, :]
+ * with g(l) = 1 - (l/softcap)^2 (1 without softcap), rescaled chunk by chunk
+ * to the running max.  The probabilities go to the GEMM as fp16 hi + lo
+ * (about 2^-22 relative).  tk_lmhead_finish turns dX into the gradient.
+ * No counterpart in the reference (tier/tier.cpp:3184-3266 recomputes the
+ * logits in pass 2). */
+tk_status tk_lmhead_fused(tk_ctx *ctx, const uint16_t *W, int v0, int V_shard, int H,
+                          const float *X, int T, const int32_t *labels, const uint8_t *mask,
+                          float softcap, int chunk, int products, double *rmax, double *rsum,
+                          int32_t *amax, float *tgt, float *dX, void *stream);
+
+/* dX[t] = dX[t] / (n_loss * rsum[t]) - g(tgt[t]) * W[labels[t+1] - v0] / n_loss
+ * (the W term only when the label lies in this shard) for rows with loss,
+ * 0 for the rest: the dlogit of tier/tier.cpp:736-748 summed against W.
+ * rsum must be the final (all-shard) sum relative to the final max. */
+tk_status tk_lmhead_finish(tk_ctx *ctx, const uint16_t *W, int v0, int V_shard, int H, int T,
+                           const int32_t *labels, const uint8_t *mask, int n_loss, float softcap,
+                           const double *rsum, const float *tgt, float *dX, void *stream);
+
 /* loss_sum = sum over masked rows t < T-1 of (rmax + log(rsum) - tgt);
  * hits = count of amax[t] == labels[t+1] (tier/tier.cpp:3227-3228).
  * Writes one double and one int to device memory. */
@@ -212,9 +234,10 @@ tk_status tk_lmhead_loss(tk_ctx *ctx, int T, const int32_t *labels, const uint8_
 
 /* Vocab-sharded merge helper: rsum *= exp(rmax_local - rmax_global) and
  * rmax_local = rmax_global, for rows t < n (run between an all-reduce MAX of
- * rmax and an all-reduce SUM of rsum). */
+ * rmax and an all-reduce SUM of rsum); with dX (nullable, [n, H]) the
+ * single-pass accumulator rows are scaled by the same factor. */
 tk_status tk_lmhead_rescale(tk_ctx *ctx, int n, double *rmax_local, double *rsum_local,
-                            const double *rmax_global, void *stream);
+                            const double *rmax_global, float *dX, int H, void *stream);
 
 #ifdef __cplusplus
 }

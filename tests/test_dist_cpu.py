@@ -1,7 +1,8 @@
 """Host-side sharding logic on CPU with gloo, world size 2: the row split
-used by the linear path and the vocab-shard merge of the running
+used by the linear path, the vocab-shard merge of the running
 cross-entropy state (max, rescaled sum, target, argmax with the reference's
-lowest-index tie rule)."""
+lowest-index tie rule), and the single-pass head's dX accumulator merge
+(rescale to the global max, finish against the global sum, all-reduce)."""
 import os
 import socket
 
@@ -19,8 +20,11 @@ def _free_port():
     return p
 
 
-def _cpu_rescale(rl, sl, rg):
-    sl.mul_(torch.exp(rl - rg))
+def _cpu_rescale(rl, sl, rg, dX=None):
+    f = torch.exp(rl - rg)
+    sl.mul_(f)
+    if dX is not None:
+        dX[: f.shape[0]].mul_(f.float()[:, None])
     rl.copy_(rg)
 
 
@@ -53,7 +57,27 @@ def _worker(rank, world, port, q):
         parts = [shard_rows(14336, 8, r, align=256) for r in range(8)]
         ok = ok and parts[0][0] == 0 and parts[-1][1] == 14336 and all(
             parts[i][1] == parts[i + 1][0] and parts[i][1] % 256 == 0 for i in range(7))
+        # single-pass head: per-shard accumulator relative to the shard max,
+        # merged, finished (the label's shard subtracts its W row), summed
+        H = 7
+        W = torch.randn(V, H, generator=g, dtype=torch.float64)
+        rmax, rsum, amax = _stats(lg[:, a:b], a)
+        tgt = torch.tensor([float(lg[t, labels[t]]) if a <= labels[t] < b else 0.0 for t in range(T)])
+        acc = (torch.exp(lg[:, a:b].double() - rmax[:, None]) @ W[a:b]).float()
+        amax = merge_vocab_shards(rmax, rsum, amax, tgt, dist.group.WORLD, _cpu_rescale, dX=acc)
+        n = T
+        d = acc.double() / (n * rsum[:, None])
+        for t in range(T):
+            if a <= labels[t] < b:
+                d[t] -= W[labels[t]] / n
+        dist.all_reduce(d)
+        P = torch.softmax(lg.double(), dim=1)
+        P[torch.arange(T), labels] -= 1.0
+        want = P @ W / n
+        ok = ok and torch.allclose(d, want, rtol=1e-5, atol=1e-7)
         q.put((rank, bool(ok)))
+    except Exception as e:   # report instead of leaving the other rank waiting
+        q.put((rank, repr(e)))
     finally:
         dist.destroy_process_group()
 

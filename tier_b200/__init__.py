@@ -79,7 +79,9 @@ SIGNATURES = [
     ("tk_lmhead_stats", _I, [_P, _P, _I, _I, _I, _P, _I, _P, _P, _F, _I, _I, _P, _P, _P, _P, _P]),
     ("tk_lmhead_grad", _I, [_P, _P, _I, _I, _I, _P, _I, _P, _P, _I, _F, _I, _I, _P, _P, _P, _P]),
     ("tk_lmhead_loss", _I, [_P, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P]),
-    ("tk_lmhead_rescale", _I, [_P, _I, _P, _P, _P, _P]),
+    ("tk_lmhead_rescale", _I, [_P, _I, _P, _P, _P, _P, _I, _P]),
+    ("tk_lmhead_fused", _I, [_P, _P, _I, _I, _I, _P, _I, _P, _P, _F, _I, _I, _P, _P, _P, _P, _P, _P]),
+    ("tk_lmhead_finish", _I, [_P, _P, _I, _I, _I, _I, _P, _P, _I, _F, _P, _P, _P, _P]),
 ]
 
 _lib = None
@@ -217,9 +219,19 @@ class Context:
         _check(self.lib.tk_lmhead_loss(self.h, T, _ptr(labels), _ptr(mask), _ptr(rmax), _ptr(rsum), _ptr(amax),
                                        _ptr(tgt), _ptr(loss), _ptr(hits), _stream(stream)))
 
-    def lmhead_rescale(self, n, rmax_local, rsum_local, rmax_global, stream=None):
+    def lmhead_rescale(self, n, rmax_local, rsum_local, rmax_global, dX=None, H=0, stream=None):
         _check(self.lib.tk_lmhead_rescale(self.h, n, _ptr(rmax_local), _ptr(rsum_local), _ptr(rmax_global),
-                                          _stream(stream)))
+                                          _ptr(dX) if dX is not None else None, H, _stream(stream)))
+
+    def lmhead_fused(self, W, v0, V_shard, H, X, T, labels, mask, softcap, chunk, rmax, rsum, amax, tgt, dX,
+                     products=X3_REF, stream=None):
+        _check(self.lib.tk_lmhead_fused(self.h, _ptr(W), v0, V_shard, H, _ptr(X), T, _ptr(labels), _ptr(mask),
+                                        softcap, chunk, products, _ptr(rmax), _ptr(rsum), _ptr(amax), _ptr(tgt),
+                                        _ptr(dX), _stream(stream)))
+
+    def lmhead_finish(self, W, v0, V_shard, H, T, labels, mask, n_loss, softcap, rsum, tgt, dX, stream=None):
+        _check(self.lib.tk_lmhead_finish(self.h, _ptr(W), v0, V_shard, H, T, _ptr(labels), _ptr(mask), n_loss,
+                                         softcap, _ptr(rsum), _ptr(tgt), _ptr(dX), _stream(stream)))
 
 
 def make_weight(qtype: int, rows: int, cols: int, data, scale_log2: int = 0) -> Weight:

@@ -562,6 +562,90 @@ tk_status tk_lmhead_grad(tk_ctx* ctx, const uint16_t* W, int v0, int V_shard, in
     return TK_OK;
 }
 
+tk_status tk_lmhead_fused(tk_ctx* ctx, const uint16_t* W, int v0, int V_shard, int H, const float* X, int T,
+                          const int32_t* labels, const uint8_t* mask, float softcap, int chunk, int products,
+                          double* rmax, double* rsum, int32_t* amax, float* tgt, float* dX, void* stream) {
+    tk_status st = lm_check(ctx, W, V_shard, H, X, T, labels, mask, chunk, products, "tk_lmhead_fused");
+    if (st != TK_OK) return st;
+    if (!rmax || !rsum || !amax || !tgt || !dX) return fail(TK_ERR_INVALID, "tk_lmhead_fused: null state");
+    if (!aligned16(dX)) return fail(TK_ERR_INVALID, "tk_lmhead_fused: dX must be 16-byte aligned");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const int np = products == TK_X2 ? 2 : 3;
+    const int rows = T - 1;
+    const int ntiles = chunk / 256;
+    const size_t pstride = (size_t)rows * chunk;
+    const size_t need = align256((size_t)rows * H * 2 * np) + align256((size_t)T * 4) +
+                        align256((size_t)rows * ntiles * 4) * 3 + align256((size_t)rows * ntiles * 8) +
+                        align256(pstride * 4) + align256(pstride * 2) * 2 + align256((size_t)rows * 4);
+    st = ws_ensure(ctx, need, s);
+    if (st != TK_OK) return st;
+    Carve cv(ctx->ws);
+    uint16_t* xp;
+    int* rexp;
+    st = lm_split_x(ctx, cv, X, T, H, np, &xp, &rexp, s);
+    if (st != TK_OK) return st;
+    float* pmax = cv.take<float>((size_t)rows * ntiles);
+    int32_t* parg = cv.take<int32_t>((size_t)rows * ntiles);
+    float* ptgt = cv.take<float>((size_t)rows * ntiles);
+    double* psum = cv.take<double>((size_t)rows * ntiles);
+    float* Z = cv.take<float>(pstride);
+    uint16_t* P = cv.take<uint16_t>(pstride * 2);
+    float* alpha = cv.take<float>(rows);
+    for (int c0 = 0; c0 < V_shard; c0 += chunk) {
+        const int vc = V_shard - c0 < chunk ? V_shard - c0 : chunk;
+        // logits of the chunk: partial statistics + the logits themselves
+        GemmDesc g;
+        for (int p = 0; p < np; ++p) g.A[p] = xp + (size_t)p * rows * H;
+        g.B[0] = W + (size_t)c0 * H;
+        g.lda = H; g.ldb = H; g.b_mn = false;
+        g.M = rows; g.N = vc; g.K = H;
+        g.nprod = np;
+        for (int p = 0; p < np; ++p) { g.pa[p] = np - 1 - p; g.pb[p] = 0; }
+        g.D = reinterpret_cast<float*>(pmax);   // unused by this epilogue; must be valid & aligned
+        g.ldd = 4;
+        g.row_exp = rexp;
+        LseDesc e;
+        e.pmax = pmax; e.parg = parg; e.psum = psum; e.ptgt = ptgt;
+        e.labels = labels; e.v0 = v0 + c0; e.cap = softcap; e.ld_part = ntiles;
+        e.zout = Z; e.ldz = vc;
+        st = launch_gemm_lse(ctx, g, e, s);
+        if (st != TK_OK) return st;
+        st = launch_lse_merge(ctx, pmax, parg, psum, ptgt, ntiles, (vc + 255) / 256, rows, vc, v0 + c0, labels, mask,
+                              rmax, rsum, amax, tgt, s, alpha);
+        if (st != TK_OK) return st;
+        // P = exp(l - m_new) * softcap' in fp16 hi + lo
+        st = launch_lm_prob(ctx, Z, vc, rows, vc, rmax, mask, softcap, P, (long)rows * vc, vc, s);
+        if (st != TK_OK) return st;
+        // dXacc = alpha * dXacc + P . W_chunk
+        GemmDesc d;
+        d.A[0] = P;
+        d.A[1] = P + (size_t)rows * vc;
+        d.B[0] = W + (size_t)c0 * H;
+        d.lda = vc; d.ldb = H; d.b_mn = true;
+        d.M = rows; d.N = H; d.K = vc;
+        d.nprod = 2;
+        d.pa[0] = 1; d.pa[1] = 0; d.pb[0] = 0; d.pb[1] = 0;   // low part first
+        d.D = dX; d.ldd = H;
+        d.beta = c0 > 0;
+        d.row_alpha = alpha;
+        d.seg_kb = kSegKb;
+        st = launch_gemm(ctx, d, s);
+        if (st != TK_OK) return st;
+    }
+    return TK_OK;
+}
+
+tk_status tk_lmhead_finish(tk_ctx* ctx, const uint16_t* W, int v0, int V_shard, int H, int T, const int32_t* labels,
+                           const uint8_t* mask, int n_loss, float softcap, const double* rsum, const float* tgt,
+                           float* dX, void* stream) {
+    if (!ctx || !W || !labels || !mask || !rsum || !tgt || !dX) return fail(TK_ERR_INVALID, "tk_lmhead_finish: null argument");
+    if (T < 2 || H <= 0 || V_shard <= 0) return fail(TK_ERR_INVALID, "tk_lmhead_finish: bad shape");
+    if (n_loss <= 0) return launch_lm_finish(ctx, W, v0, V_shard, H, T, labels, mask, 1, softcap, rsum, tgt, dX,
+                                             static_cast<cudaStream_t>(stream));   // every row zero
+    return launch_lm_finish(ctx, W, v0, V_shard, H, T, labels, mask, n_loss, softcap, rsum, tgt, dX,
+                            static_cast<cudaStream_t>(stream));
+}
+
 tk_status tk_lmhead_loss(tk_ctx* ctx, int T, const int32_t* labels, const uint8_t* mask, const double* rmax,
                          const double* rsum, const int32_t* amax, const float* tgt, double* loss_sum, int32_t* hits,
                          void* stream) {
@@ -573,10 +657,11 @@ tk_status tk_lmhead_loss(tk_ctx* ctx, int T, const int32_t* labels, const uint8_
 }
 
 tk_status tk_lmhead_rescale(tk_ctx* ctx, int n, double* rmax_local, double* rsum_local, const double* rmax_global,
-                            void* stream) {
+                            float* dX, int H, void* stream) {
     if (!ctx || (n > 0 && (!rmax_local || !rsum_local || !rmax_global)))
         return fail(TK_ERR_INVALID, "tk_lmhead_rescale: null argument");
-    return launch_lm_rescale(ctx, n, rmax_local, rsum_local, rmax_global, static_cast<cudaStream_t>(stream));
+    if (dX && H <= 0) return fail(TK_ERR_INVALID, "tk_lmhead_rescale: H must be positive with dX");
+    return launch_lm_rescale(ctx, n, rmax_local, rsum_local, rmax_global, static_cast<cudaStream_t>(stream), dX, H);
 }
 
 }  // extern "C"

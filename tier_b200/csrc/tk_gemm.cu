@@ -79,6 +79,7 @@ struct __align__(64) GemmParams {
     long ldd;
     int beta;
     const int* row_exp;
+    const float* row_alpha;   // beta = 1: D = row_alpha[row] * D + A.B (null: alpha 1)
     int col_exp;
     int* status;
 };
@@ -294,6 +295,9 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
                 // direct split 1, whose earlier segments sit in the slab
                 const bool add_own = kb0 > kbs || (sp == 0 && p.beta);
                 const bool own_in_ws = direct && kb0 > kbs;
+                // per-row alpha on the caller's D: only where D is read for the
+                // first time in this launch (first segment of split 0, beta = 1)
+                const float al = (p.row_alpha && row_ok && sp == 0 && kb0 == kbs && p.beta) ? p.row_alpha[row] : 1.0f;
                 const bool add_d = add_own || direct;   // direct: D holds split 0's sum
 #pragma unroll 1
                 for (int c = 0; c < p.bn; c += 32) {
@@ -322,7 +326,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
                                                    __uint_as_float(r[4 * q + 2]) * f, __uint_as_float(r[4 * q + 3]) * f);
                             if (own_in_ws) { v.x += ow[q].x; v.y += ow[q].y; v.z += ow[q].z; v.w += ow[q].w; }
                             if (add_d) {
-                                v.x = od[q].x + v.x; v.y = od[q].y + v.y; v.z = od[q].z + v.z; v.w = od[q].w + v.w;
+                                v.x = fmaf(al, od[q].x, v.x); v.y = fmaf(al, od[q].y, v.y);
+                                v.z = fmaf(al, od[q].z, v.z); v.w = fmaf(al, od[q].w, v.w);
                             }
                             dp[q] = v;
                         }
@@ -332,7 +337,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
                             if (col0 + j < p.N) {
                                 float v = __uint_as_float(r[j]) * f;
                                 if (own_in_ws) v += wrow[col0 + j];
-                                if (add_d) v = drow[col0 + j] + v;
+                                if (add_d) v = fmaf(al, drow[col0 + j], v);
                                 drow[col0 + j] = v;
                             }
                         }
@@ -395,6 +400,12 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
                         v[j] = valid ? l : -INFINITY;
                         if (valid && l > cm) { cm = l; ci = col0 + j; }
                         if (col0 + j == label) tgt = l;
+                    }
+                    if (L.zout && row_ok && col0 + 32 <= p.N) {
+                        // the (softcapped) logits themselves, for the single-pass head
+                        float4* zp = reinterpret_cast<float4*>(L.zout + (size_t)row * L.ldz + col0);
+#pragma unroll
+                        for (int q = 0; q < 8; ++q) zp[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
                     }
                     if (cm > mx) {
                         sum *= exp((double)mx - (double)cm);
@@ -598,6 +609,7 @@ static tk_status build(const GemmDesc& g, tk_ctx* ctx, GemmParams& gp, int cg, i
     }
     gp.D = g.D; gp.ldd = g.ldd; gp.beta = g.beta;
     gp.row_exp = g.row_exp; gp.col_exp = g.col_exp;
+    gp.row_alpha = g.row_alpha;
     gp.status = ctx->status;
     (void)ctx;
     return TK_OK;

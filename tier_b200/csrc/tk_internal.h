@@ -99,6 +99,7 @@ struct GemmDesc {
     const int* row_exp = nullptr;
     int col_exp = 0;
     int seg_kb = 0;        // k-blocks (of 64) per fp32 accumulation segment; 0 = whole K
+    const float* row_alpha = nullptr;   // with beta = 1: D = row_alpha[row] * D + A.B
     float* split_ws = nullptr;   // fp32 [M, split_ld] slab; enables split-K when given
     long split_ld = 0;
 };
@@ -134,6 +135,7 @@ tk_status launch_gemm_q(tk_ctx* ctx, const GemmQDesc& g, cudaStream_t s);
 struct LseDesc {               // pass 1: per (row, 256-column tile) partial stats
     float* pmax; int32_t* parg; double* psum; float* ptgt;   // [T_rows, ntiles]
     const int32_t* labels; int v0; float cap; int ld_part;
+    float* zout = nullptr; long ldz = 0;   // optional: the softcapped logits [T_rows, ldz]
 };
 struct DlogitDesc {            // pass 2: dlogit planes
     const double* rmax; const double* rsum; const int32_t* labels; const uint8_t* mask;
@@ -147,11 +149,19 @@ tk_status launch_gemm_dlogit(tk_ctx* ctx, const GemmDesc& g, const DlogitDesc& e
 tk_status launch_lse_merge(tk_ctx* ctx, const float* pmax, const int32_t* parg, const double* psum,
                            const float* ptgt, int ld_part, int ntiles, int n_pred, int vc, int v0,
                            const int32_t* labels, const uint8_t* mask, double* rmax, double* rsum,
-                           int32_t* amax, float* tgt, cudaStream_t s);
+                           int32_t* amax, float* tgt, cudaStream_t s, float* alpha = nullptr);
+// Single-pass head: P[t, v] = exp(l - rmax[t]) * (1 - (l/cap)^2) as fp16 hi/lo planes.
+tk_status launch_lm_prob(tk_ctx* ctx, const float* Z, long ldz, int rows, int vc, const double* rmax,
+                         const uint8_t* mask, float cap, uint16_t* planes, long plane_stride, int ld, cudaStream_t s);
+// dX[t] = dX[t] / (n_loss * rsum[t]) - g_t * W[label - v0] / n_loss (label in this shard), 0 for rows
+// without loss; g_t = 1 - (tgt/cap)^2.
+tk_status launch_lm_finish(tk_ctx* ctx, const uint16_t* W, int v0, int V_shard, int H, int T, const int32_t* labels,
+                           const uint8_t* mask, int n_loss, float cap, const double* rsum, const float* tgt, float* dX,
+                           cudaStream_t s);
 tk_status launch_lm_loss(tk_ctx* ctx, int T, const int32_t* labels, const uint8_t* mask, const double* rmax,
                          const double* rsum, const int32_t* amax, const float* tgt, double* loss, int32_t* hits,
                          cudaStream_t s);
 tk_status launch_lm_rescale(tk_ctx* ctx, int n, double* rmax_l, double* rsum_l, const double* rmax_g,
-                            cudaStream_t s);
+                            cudaStream_t s, float* dX = nullptr, int H = 0);
 
 }  // namespace tk

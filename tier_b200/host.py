@@ -37,7 +37,7 @@ def shard_rows(n: int, world: int, rank: int, align: int = 1) -> tuple[int, int]
     return a, b
 
 
-def merge_vocab_shards(rmax, rsum, amax, tgt, group, rescale):
+def merge_vocab_shards(rmax, rsum, amax, tgt, group, rescale, dX=None):
     """Merge per-shard running CE state into the global one, in place for
     rmax / rsum / tgt; returns the merged argmax.  Shards are in vocab order
     (rank r holds a lower vocab range than rank r+1).
@@ -47,7 +47,9 @@ def merge_vocab_shards(rmax, rsum, amax, tgt, group, rescale):
       rmax:   all-reduce MAX.
       rsum:   each shard rescales its sum to the global max
               (rescale(rmax_local, rsum_local, rmax_global)), then all-reduce SUM.
-      tgt:    all-reduce SUM (only the shard holding the label has it non-zero)."""
+      tgt:    all-reduce SUM (only the shard holding the label has it non-zero).
+      dX:     (single-pass accumulator, optional) rescaled with rsum; the
+              caller all-reduces it after tk_lmhead_finish."""
     import torch.distributed as dist
     world = dist.get_world_size(group)
     allm = [torch.empty_like(rmax) for _ in range(world)]
@@ -58,7 +60,7 @@ def merge_vocab_shards(rmax, rsum, amax, tgt, group, rescale):
     merged = torch.stack(alla).gather(0, best[None]).squeeze(0).contiguous()
     gmax = rmax.clone()
     dist.all_reduce(gmax, op=dist.ReduceOp.MAX, group=group)
-    rescale(rmax, rsum, gmax)
+    rescale(rmax, rsum, gmax, dX)
     dist.all_reduce(rsum, group=group)
     dist.all_reduce(tgt, group=group)
     return merged
@@ -155,7 +157,7 @@ class LMHead:
                               rsum, amax, tgt, products=self.products)
         if self.group is not None:
             amax = merge_vocab_shards(rmax, rsum, amax, tgt, self.group,
-                                      lambda rl, sl, rg: self.ctx.lmhead_rescale(T - 1, rl, sl, rg))
+                                      lambda rl, sl, rg, d: self.ctx.lmhead_rescale(T - 1, rl, sl, rg))
         return rmax, rsum, amax, tgt
 
     def loss(self, T, labels, mask, rmax, rsum, amax, tgt):
@@ -182,6 +184,33 @@ class LMHead:
         rmax, rsum, amax, tgt = self.stats(X, labels, mask, softcap)
         loss, hits = self.loss(T, labels, mask, rmax, rsum, amax, tgt)
         dX = self.grad(X, labels, mask, n_loss, rmax, rsum, dX=dX, softcap=softcap)
+        return loss, n_loss, hits, amax, dX
+
+    def step_fused(self, X, labels, mask, softcap=0.0, n_loss=None):
+        """Single pass (one logits GEMM per chunk): returns (loss_sum, n_loss,
+        hits, amax, dX), the same quantities as `step`.  With a group, every
+        rank's accumulator is rescaled to the global max, finished against
+        the global sum, and the per-rank dX are all-reduced (SUM)."""
+        T, H = X.shape
+        dev = X.device
+        if n_loss is None:
+            n_loss = int(mask[: T - 1].count_nonzero().item())
+        rmax = torch.full((T - 1,), -1e30, dtype=torch.float64, device=dev)
+        rsum = torch.zeros(T - 1, dtype=torch.float64, device=dev)
+        amax = torch.full((T - 1,), -1, dtype=torch.int32, device=dev)
+        tgt = torch.zeros(T - 1, dtype=torch.float32, device=dev)
+        dX = torch.zeros(T, H, dtype=torch.float32, device=dev)
+        self.ctx.lmhead_fused(self.W, self.v0, self.V_shard, self.H, X, T, labels, mask, softcap, self.chunk, rmax,
+                              rsum, amax, tgt, dX, products=self.products)
+        if self.group is not None:
+            amax = merge_vocab_shards(rmax, rsum, amax, tgt, self.group,
+                                      lambda rl, sl, rg, d: self.ctx.lmhead_rescale(T - 1, rl, sl, rg, d, H),
+                                      dX=dX)
+        self.ctx.lmhead_finish(self.W, self.v0, self.V_shard, self.H, T, labels, mask, n_loss, softcap, rsum, tgt, dX)
+        if self.group is not None:
+            import torch.distributed as dist
+            dist.all_reduce(dX, group=self.group)
+        loss, hits = self.loss(T, labels, mask, rmax, rsum, amax, tgt)
         return loss, n_loss, hits, amax, dX
 
 
