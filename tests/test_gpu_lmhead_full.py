@@ -1,14 +1,15 @@
-"""Full-size LM head (V = 262144, H = 3840, T = 8192, chunk 16384): the GPU
-path runs every row; sampled rows are checked in fp64 on the host (vocab
-processed in chunks): per-row lse, target logit, argmax, loss contribution
-and the dX row, at the 1e-5 tolerance of the x3 path."""
+"""Full-size LM head (V = 262144, H = 3840, T = 8192, chunk 16384), two-pass
+and single-pass: the GPU path runs every row; sampled rows are checked in
+fp64 on the host (vocab processed in chunks): per-row lse, target logit,
+argmax, loss contribution and the dX row, at the 1e-5 tolerance."""
 import numpy as np
 import pytest
 
 pytestmark = pytest.mark.gpu
 
 
-def test_lmhead_full_size_sampled_rows(ctx):
+@pytest.mark.parametrize("single_pass", [False, True])
+def test_lmhead_full_size_sampled_rows(ctx, single_pass):
     import torch
     import tier_b200 as tk
     from tier_b200.host import LMHead
@@ -19,9 +20,15 @@ def test_lmhead_full_size_sampled_rows(ctx):
     labels = torch.randint(0, V, (T,), device="cuda", generator=g, dtype=torch.int32)
     mask = torch.ones(T, dtype=torch.uint8, device="cuda")
     head = LMHead(ctx, W, 0, chunk=chunk, products=tk.X3_REF)
-    rmax, rsum, amax, tgt = head.stats(X, labels, mask)
-    loss, hits = head.loss(T, labels, mask, rmax, rsum, amax, tgt)
-    dX = head.grad(X, labels, mask, T - 1, rmax, rsum)
+    if single_pass:
+        # the single pass leaves the same running state; rebuild it for the checks
+        loss, _, hits, amax, dX = head.step_fused(X, labels, mask)
+        rmax, rsum, amax2, tgt = head.stats(X, labels, mask)
+        assert torch.equal(amax, amax2)
+    else:
+        rmax, rsum, amax, tgt = head.stats(X, labels, mask)
+        loss, hits = head.loss(T, labels, mask, rmax, rsum, amax, tgt)
+        dX = head.grad(X, labels, mask, T - 1, rmax, rsum)
     torch.cuda.synchronize()
     ctx.sync_status()
 

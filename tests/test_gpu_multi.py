@@ -65,6 +65,12 @@ def _worker(rank, world, port, q):
         out["lm_loss"] = abs(loss.item() - loss1.item()) / abs(loss1.item())
         out["lm_dx"] = float((dXh - dXh1).norm() / dXh1.norm())
         out["lm_amax"] = bool(torch.equal(amax, amax1)) and hits.item() == hits1.item()
+        # single pass: accumulator rescaled to the global max, finished, summed
+        lossf, _, hitsf, amaxf, dXf = hs.step_fused(Xh, labels, mask)
+        torch.cuda.synchronize()
+        out["lmf_loss"] = abs(lossf.item() - loss1.item()) / abs(loss1.item())
+        out["lmf_dx"] = float((dXf - dXh1).norm() / dXh1.norm())
+        out["lmf_amax"] = bool(torch.equal(amaxf, amax1)) and hitsf.item() == hits1.item()
         ctx.close()
     except Exception as e:  # report, never hang the other rank
         out["error"] = repr(e)
@@ -91,3 +97,4 @@ def test_two_gpu_shards_match_single_gpu():
         assert "error" not in o, o
         assert o["lin_fwd"] < 1e-6 and o["lin_dx"] < 1e-5, o
         assert o["lm_loss"] < 1e-6 and o["lm_dx"] < 1e-5 and o["lm_amax"], o
+        assert o["lmf_loss"] < 1e-6 and o["lmf_dx"] < 1e-5 and o["lmf_amax"], o
