@@ -177,6 +177,31 @@ tk_status tk_weight_split_f32(tk_ctx *ctx, const float *W32, int rows, int cols,
 tk_status tk_split3(tk_ctx *ctx, const float *x, size_t n, uint16_t *h, uint16_t *m, uint16_t *l,
                     void *stream);
 
+/* ---- dX reduce-scatter over peer memory (multi-GPU, one process per GPU) -- */
+/* With W split by output rows over `world` GPUs, dX = sum_g dY_g . W_g.  A
+ * consumer that takes dX split by token rows (rank r: rows r*M/world ..
+ * (r+1)*M/world) needs a reduce-scatter.  tk_linear_dx_rs does it inside the
+ * dX GEMM: every finished tile is stored into its owner's receive buffer
+ * (peer memory over NVLink) while the remaining tiles compute; the owner adds
+ * the world contributions in rank order (deterministic).  No counterpart in
+ * the reference (it runs on one GPU; SURVEY-style row sharding is new).
+ *
+ * Set-up, once per context: tk_comm_init allocates this rank's buffer
+ * (4 KiB + 2 * recv_bytes; recv_bytes >= M * K * 4 for every later call) and
+ * writes its CUDA IPC handle (TK_IPC_HANDLE_BYTES) to handle_out; the caller
+ * exchanges the handles (e.g. an all-gather), passes all `world` of them in
+ * rank order to tk_comm_connect, then runs a barrier across the ranks.
+ * Every rank must make the same sequence of tk_linear_dx_rs calls. */
+enum { TK_IPC_HANDLE_BYTES = 64 };
+tk_status tk_comm_init(tk_ctx *ctx, int rank, int world, size_t recv_bytes, void *handle_out);
+tk_status tk_comm_connect(tk_ctx *ctx, const void *handles);
+/* dX_rows[M/world, ldd] = rows rank*M/world .. of sum over ranks of dY.W, dY
+ * [M, W->rows] (this rank's columns), as tk_linear_dx with beta = 0.
+ * M / world must be a multiple of 256.  Bounded device waits (2 s) report
+ * TK_ERR_TIMEOUT through tk_sync_status if a rank does not take part. */
+tk_status tk_linear_dx_rs(tk_ctx *ctx, const tk_weight *W, const void *dY, int dy_dtype, int M, int lddy,
+                          float *dX_rows, int ldd, int products, void *stream);
+
 /* ---- LM head + cross-entropy over a vocabulary shard --------------------- */
 /* The reference runs two passes over vocab chunks (tier/tier.cpp:3184-3266).
  * W: fp16 [V_shard, H] rows v0 .. v0+V_shard of the full head; X: fp32 [T, H]

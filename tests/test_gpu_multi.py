@@ -1,6 +1,8 @@
 """Row-sharded linear and vocab-sharded LM head across 2 GPUs (one process
-per GPU, NCCL): every rank's gathered / reduced result equals the single-GPU
-result within the path's tolerance.  Skipped with fewer than 2 GPUs."""
+per GPU, NCCL), and the dX reduce-scatter done inside the GEMM over peer
+memory: every rank's gathered / reduced / scattered result equals the
+single-GPU result within the path's tolerance.  Skipped with fewer than 2
+GPUs."""
 import os
 import socket
 
@@ -50,6 +52,24 @@ def _worker(rank, world, port, q):
         torch.cuda.synchronize()
         out["lin_fwd"] = float((Y - Y1).norm() / Y1.norm())
         out["lin_dx"] = float((dX - dX1).norm() / dX1.norm())
+        # dX reduce-scattered inside the GEMM over peer memory: this rank's
+        # token rows of the sum; three calls in a row cover both buffer
+        # parities and the acknowledgement path; fp32 dY (x3, several
+        # accumulation segments) and bf16 dY (one product, one segment)
+        Mr = 1024
+        lp.enable_reduce_scatter(Mr)
+        rows = Mr // world
+        errs = []
+        for it in range(3):
+            dYr = torch.from_numpy(rng.standard_normal((Mr, N)).astype(np.float32)).cuda()
+            if it == 2:
+                dYr = dYr.to(torch.bfloat16)
+            part = lp.dx_rs(dYr[:, a:b].contiguous())
+            want = full.dx(dYr)[rank * rows:(rank + 1) * rows]
+            torch.cuda.synchronize()
+            errs.append(float((part - want).norm() / want.norm()))
+        ctx.sync_status()
+        out["rs_dx"] = max(errs)
         # --- LM head, vocab split ---
         V, H, T = 4096, 256, 64
         W = (torch.randn(V, H, device="cuda", generator=g) * 0.02).half()
@@ -96,5 +116,6 @@ def test_two_gpu_shards_match_single_gpu():
     for r, o in res.items():
         assert "error" not in o, o
         assert o["lin_fwd"] < 1e-6 and o["lin_dx"] < 1e-5, o
+        assert o["rs_dx"] < 1e-5, o
         assert o["lm_loss"] < 1e-6 and o["lm_dx"] < 1e-5 and o["lm_amax"], o
         assert o["lmf_loss"] < 1e-6 and o["lmf_dx"] < 1e-5 and o["lmf_amax"], o

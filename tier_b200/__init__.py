@@ -35,6 +35,7 @@ DT_F32, DT_F16, DT_BF16 = 0, 1, 2
 # product sets
 X3_AUTO, X3_REF, X3_HHL, X2, X1 = 0, 1, 2, 3, 4
 QFUSED = 0x100   # OR into `products`: decode a quantized W inside the GEMM
+IPC_HANDLE_BYTES = 64   # TK_IPC_HANDLE_BYTES
 WFROZEN = 0x200  # OR into tk_gemv's qtype: W is never written by earlier kernels (early weight fetch)
 # kernel families for profiling
 PROF_GEMM, PROF_DEQUANT, PROF_SPLIT, PROF_GEMV, PROF_LMHEAD = range(5)
@@ -76,6 +77,9 @@ SIGNATURES = [
     ("tk_linear_fwd_noalloc", _I, [_P, ctypes.POINTER(Weight), _P, _I, _I, _I, _P, _I, _F, _I, _P]),
     ("tk_weight_split_f32", _I, [_P, _P, _I, _I, _P, ctypes.POINTER(_I), _P]),
     ("tk_split3", _I, [_P, _P, _SZ, _P, _P, _P, _P]),
+    ("tk_comm_init", _I, [_P, _I, _I, _SZ, _P]),
+    ("tk_comm_connect", _I, [_P, _P]),
+    ("tk_linear_dx_rs", _I, [_P, ctypes.POINTER(Weight), _P, _I, _I, _I, _P, _I, _I, _P]),
     ("tk_lmhead_stats", _I, [_P, _P, _I, _I, _I, _P, _I, _P, _P, _F, _I, _I, _P, _P, _P, _P, _P]),
     ("tk_lmhead_grad", _I, [_P, _P, _I, _I, _I, _P, _I, _P, _P, _I, _F, _I, _I, _P, _P, _P, _P]),
     ("tk_lmhead_loss", _I, [_P, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P]),
@@ -193,6 +197,25 @@ class Context:
 
     def linear_dx_acc(self, W: Weight, dY, M, dX, **kw):
         return self.linear_dx(W, dY, M, dX, beta=1.0, **kw)
+
+    # ---- reduce-scatter over peer memory (multi-GPU) ----
+    def comm_init(self, rank: int, world: int, recv_bytes: int) -> bytes:
+        """Allocate this rank's receive buffer; returns its IPC handle (64 bytes)."""
+        buf = ctypes.create_string_buffer(IPC_HANDLE_BYTES)
+        _check(self.lib.tk_comm_init(self.h, rank, world, recv_bytes, buf))
+        return buf.raw
+
+    def comm_connect(self, handles: bytes):
+        """Open the peers' buffers: `handles` = every rank's handle, in rank order."""
+        buf = ctypes.create_string_buffer(handles, len(handles))
+        _check(self.lib.tk_comm_connect(self.h, buf))
+
+    def linear_dx_rs(self, W: Weight, dY, M, dX_rows, dy_dtype=DT_F32, lddy=None, ldd=None, products=X3_AUTO,
+                     stream=None):
+        """This rank's token rows of sum over ranks of dY . W (tk_linear_dx_rs)."""
+        _check(self.lib.tk_linear_dx_rs(self.h, ctypes.byref(W), _ptr(dY), dy_dtype, M, lddy or W.rows, _ptr(dX_rows),
+                                        ldd or W.cols, products, _stream(stream)))
+        return dX_rows
 
     def weight_split_f32(self, W32, rows, cols, planes, stream=None) -> int:
         sc = _I(0)

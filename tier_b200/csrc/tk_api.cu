@@ -148,7 +148,7 @@ static tk_status check_weight(const tk_weight* W, const char* fn) {
 
 // Shared body of fwd (dx == false) and dX (dx == true).
 static tk_status linear(tk_ctx* ctx, const tk_weight* W, const void* A, int a_dtype, int M, int lda, float* D,
-                        int ldd, float beta, int products, cudaStream_t s, bool dx) {
+                        int ldd, float beta, int products, cudaStream_t s, bool dx, bool rs_scatter = false) {
     const char* fn = dx ? "tk_linear_dx" : "tk_linear_fwd";
     if (!ctx) return fail(TK_ERR_INVALID, std::string(fn) + ": null context");
     tk_status st = check_weight(W, fn);
@@ -163,7 +163,7 @@ static tk_status linear(tk_ctx* ctx, const tk_weight* W, const void* A, int a_dt
     if (a_dtype != TK_DT_F32 && a_dtype != TK_DT_F16 && a_dtype != TK_DT_BF16)
         return fail(TK_ERR_INVALID, std::string(fn) + ": activation dtype");
     if (!aligned16(D) || ldd % 4) return fail(TK_ERR_INVALID, std::string(fn) + ": output must be 16-byte aligned, ld % 4 == 0");
-    const bool want_fused = (products & TK_QFUSED) != 0;
+    const bool want_fused = (products & TK_QFUSED) != 0 && !rs_scatter;
     products &= ~TK_QFUSED;
     Plan pl;
     st = plan_products(W, a_dtype, products, pl);
@@ -189,10 +189,14 @@ static tk_status linear(tk_ctx* ctx, const tk_weight* W, const void* A, int a_dt
     probe.K = a_cols;
     probe.b_mn = dx;
     const long s_ld = (d_cols + 3) / 4 * 4;
-    const bool split = !fused && gemm_splits(ctx, probe) == 2;
+    const bool split = !fused && !rs_scatter && gemm_splits(ctx, probe) == 2;
+    // reduce-scatter with several accumulation segments: the earlier segments
+    // go to a local fp32 [M, d_cols] scratch, only the last to the owners
+    const bool rs_scratch = rs_scatter && pl.nprod > 1;
     const size_t need = align256(plane_elems * 2 * pl.x_planes) + align256((size_t)M * 4) +
                         (quant && !fused ? align256((size_t)N * K * 2) : 0) +
-                        (split ? align256((size_t)M * s_ld * 4) : 0);
+                        (split ? align256((size_t)M * s_ld * 4) : 0) +
+                        (rs_scratch ? align256((size_t)M * d_cols * 4) : 0);
     st = ws_ensure(ctx, need, s);
     if (st != TK_OK) return st;
     Carve cv(ctx->ws);
@@ -259,7 +263,21 @@ static tk_status linear(tk_ctx* ctx, const tk_weight* W, const void* A, int a_dt
         g.split_ws = cv.take<float>((size_t)M * s_ld);
         g.split_ld = s_ld;
     }
-    return launch_gemm(ctx, g, s);
+    if (!rs_scatter) return launch_gemm(ctx, g, s);
+    // reduce-scatter: D (the caller's [M/world, ldd] rows) receives the sum
+    // of the owners' slots; the GEMM itself writes [M, K] rows of stride K
+    RsDesc rs;
+    st = rs_begin(ctx, M, d_cols, rs, s);
+    if (st != TK_OK) return st;
+    float* out = D;
+    const long ldo = ldd;
+    g.D = rs_scratch ? cv.take<float>((size_t)M * d_cols) : out;   // unread for a single segment
+    g.ldd = d_cols;
+    g.beta = 0;
+    g.rs = &rs;
+    st = launch_gemm(ctx, g, s);
+    if (st != TK_OK) return st;
+    return rs_finish(ctx, rs, d_cols, out, ldo, s);
 }
 
 }  // namespace tk
@@ -308,6 +326,7 @@ void tk_destroy(tk_ctx* ctx) {
     if (ctx->ws) cudaFree(ctx->ws);
     if (ctx->status) cudaFree(ctx->status);
     if (ctx->flags) cudaFree(ctx->flags);
+    comm_destroy(ctx);
     for (cudaEvent_t e : ctx->prof.ev) cudaEventDestroy(e);
     delete ctx;
 }
@@ -644,6 +663,14 @@ tk_status tk_lmhead_finish(tk_ctx* ctx, const uint16_t* W, int v0, int V_shard, 
                                              static_cast<cudaStream_t>(stream));   // every row zero
     return launch_lm_finish(ctx, W, v0, V_shard, H, T, labels, mask, n_loss, softcap, rsum, tgt, dX,
                             static_cast<cudaStream_t>(stream));
+}
+
+tk_status tk_linear_dx_rs(tk_ctx* ctx, const tk_weight* W, const void* dY, int dy_dtype, int M, int lddy,
+                          float* dX_rows, int ldd, int products, void* stream) {
+    if (!ctx) return fail(TK_ERR_INVALID, "tk_linear_dx_rs: null context");
+    if (!ctx->comm) return fail(TK_ERR_INVALID, "tk_linear_dx_rs: tk_comm_init / tk_comm_connect first");
+    return linear(ctx, W, dY, dy_dtype, M, lddy, dX_rows, ldd, 0.0f, products, static_cast<cudaStream_t>(stream),
+                  true, true);
 }
 
 tk_status tk_lmhead_loss(tk_ctx* ctx, int T, const int32_t* labels, const uint8_t* mask, const double* rmax,

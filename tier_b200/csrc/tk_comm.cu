@@ -1,0 +1,225 @@
+// tk_comm.cu -- peer buffers over CUDA IPC and the reduce-scatter that the
+// dX GEMM performs through them (tk_linear_dx_rs).
+//
+// The reference all-reduces nothing (it runs on one GPU); sharding W by
+// output rows makes dX = sum over ranks of dY_g . W_g, and a consumer that
+// takes dX split by token rows (sequence-parallel) needs only its rows of
+// that sum: a reduce-scatter.  Instead of a GEMM followed by a collective,
+// the GEMM's epilogue stores every finished tile straight into the owning
+// rank's receive buffer (peer memory, NVLink), so the transfer overlaps the
+// remaining tiles' MMAs.  The owner then adds the world slots in rank order
+// (deterministic) into its output.
+//
+// Each rank's buffer (same layout on every rank):
+//   [0, 64)      done[2][8]  int: done[p][src] = epoch, written by rank src
+//   [256, 288)   ack[8]      int: ack[owner] = epoch, written by rank owner
+//   [512]        CTA counter of this rank's GEMM launch (local)
+//   [516]        block counter of this rank's reduce launch (local)
+//   [4096, ...)  recv[2][world][rpo][K] fp32, parity p = epoch & 1
+// A launch with epoch e writes recv[e & 1] of every owner; it first waits
+// until every owner acknowledged epoch e - 2 (the previous use of that
+// parity).  Every wait is bounded (2 s, status TK_ERR_TIMEOUT).
+#include "tk_device.cuh"
+#include "tk_internal.h"
+
+#include <cstring>
+
+struct tk_comm_state {
+    int rank = 0, world = 0;
+    uint8_t* buf = nullptr;
+    size_t recv_bytes = 0;                 // one parity: world * rpo * K * 4 (= M * K * 4)
+    uint8_t* peer[tk::TK_MAX_RANKS] = {};  // peer[rank] = buf
+    bool connected = false;
+    uint32_t epoch = 0;
+};
+
+namespace tk {
+
+constexpr size_t kHdr = 4096;
+constexpr size_t kDoneOff = 0, kAckOff = 256, kGemmCtr = 512, kRedCtr = 516;
+
+__device__ __forceinline__ int ld_acquire_sys(const int* p) {
+    int v;
+    asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_release_sys_c(int* p, int v) {
+    asm volatile("st.release.sys.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+// Bounded wait until *p >= want; false (and DEV_TIMEOUT) after 2 s.
+__device__ bool wait_ge(const int* p, int want, int* status) {
+    if (ld_acquire_sys(p) >= want) return true;
+    const uint64_t t0 = globaltimer();
+    while (ld_acquire_sys(p) < want) {
+        __nanosleep(200);
+        if (globaltimer() - t0 > kWaitLimitNs) {
+            raise_status(status, DEV_TIMEOUT);
+            return false;
+        }
+    }
+    return true;
+}
+
+__global__ void rs_wait_ack_kernel(const int* ack, int world, int need, int* status) {
+    if (threadIdx.x != 0) return;
+    for (int o = 0; o < world; ++o)
+        if (!wait_ge(ack + o, need, status)) return;
+}
+
+// out[r, c] = sum_src recv[src][r][c] (src in rank order); grid-stride over
+// float4s.  The last block to finish acknowledges the epoch to every rank.
+__global__ void rs_reduce_kernel(const int* done, const float* recv, int world, int rpo, int K, float* out,
+                                 long ldo, int epoch, int* red_ctr, int* const* peer_ack, int me, int* status) {
+    __shared__ int ok;
+    if (threadIdx.x == 0) {
+        int good = 1;
+        for (int src = 0; src < world && good; ++src) good = wait_ge(done + src, epoch, status);
+        ok = good;
+    }
+    __syncthreads();
+    if (ok) {
+        const size_t slot = (size_t)rpo * K;
+        const int k4 = K / 4;
+        const long n4 = (long)rpo * k4;
+        for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (long)gridDim.x * blockDim.x) {
+            const int r = (int)(i / k4), c = (int)(i - (long)r * k4) * 4;
+            float4 acc = *reinterpret_cast<const float4*>(recv + (size_t)r * K + c);
+            for (int src = 1; src < world; ++src) {
+                const float4 v = *reinterpret_cast<const float4*>(recv + src * slot + (size_t)r * K + c);
+                acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+            }
+            *reinterpret_cast<float4*>(out + (size_t)r * ldo + c) = acc;
+        }
+    }
+    // acknowledge only a completed reduction: without it the senders' next
+    // use of this parity times out instead of overwriting unread data
+    __syncthreads();
+    if (threadIdx.x == 0 && ok) {
+        __threadfence_system();
+        const int old = atomicAdd(red_ctr, 1);
+        if (old == (int)gridDim.x - 1) {
+            *red_ctr = 0;
+            __threadfence_system();
+            for (int o = 0; o < world; ++o) st_release_sys_c(peer_ack[o] + me, epoch);
+        }
+    }
+}
+
+static int* hdr_int(uint8_t* base, size_t off) { return reinterpret_cast<int*>(base + off); }
+
+tk_status rs_begin(tk_ctx* ctx, int M, int K, RsDesc& rs, cudaStream_t s) {
+    tk_comm_state* c = ctx->comm;
+    if (!c || !c->connected) return fail(TK_ERR_INVALID, "reduce-scatter: tk_comm_init / tk_comm_connect first");
+    const int W = c->world;
+    if (M % W || (M / W) % 256) return fail(TK_ERR_INVALID, "reduce-scatter: M / world must be a multiple of 256");
+    if (K % 4) return fail(TK_ERR_INVALID, "reduce-scatter: K must be a multiple of 4");
+    if ((size_t)M * K * 4 > c->recv_bytes) return fail(TK_ERR_INVALID, "reduce-scatter: M * K exceeds the comm buffer");
+    const int epoch = (int)++c->epoch;
+    const int par = epoch & 1;
+    const int rpo = M / W;
+    rs = RsDesc();
+    rs.world = W;
+    rs.rpo = rpo;
+    rs.epoch = epoch;
+    rs.counter = hdr_int(c->buf, kGemmCtr);
+    for (int o = 0; o < W; ++o) {
+        float* recv = reinterpret_cast<float*>(c->peer[o] + kHdr + (size_t)par * c->recv_bytes);
+        rs.dst[o] = recv + (size_t)c->rank * rpo * K;             // my slot in owner o's buffer
+        rs.done[o] = hdr_int(c->peer[o], kDoneOff) + par * 8 + c->rank;
+    }
+    // the parity this launch overwrites was last read for epoch - 2
+    rs_wait_ack_kernel<<<1, 32, 0, s>>>(hdr_int(c->buf, kAckOff), W, epoch - 2, ctx->status);
+    ctx->launches++;
+    return cuda_fail(cudaGetLastError(), "reduce-scatter ack wait launch");
+}
+
+tk_status rs_finish(tk_ctx* ctx, const RsDesc& rs, int K, float* out, long ldo, cudaStream_t s) {
+    tk_comm_state* c = ctx->comm;
+    const int par = rs.epoch & 1;
+    const float* recv = reinterpret_cast<const float*>(c->buf + kHdr + (size_t)par * c->recv_bytes);
+    // peer ack pointers live in device memory for the kernel: the header's
+    // tail holds them (written once at connect)
+    int* const* peer_ack = reinterpret_cast<int* const*>(c->buf + 1024);
+    const long n4 = (long)rs.rpo * (K / 4);
+    int blocks = (int)((n4 + 255) / 256);
+    if (blocks > 4 * ctx->num_sms) blocks = 4 * ctx->num_sms;
+    ProfScope ps(ctx, s, PK_GEMM);
+    rs_reduce_kernel<<<blocks, 256, 0, s>>>(hdr_int(c->buf, kDoneOff) + par * 8, recv, rs.world, rs.rpo, K, out, ldo,
+                                           rs.epoch, hdr_int(c->buf, kRedCtr), peer_ack, c->rank, ctx->status);
+    ctx->launches++;
+    return cuda_fail(cudaGetLastError(), "reduce-scatter reduce launch");
+}
+
+void comm_destroy(tk_ctx* ctx) {
+    tk_comm_state* c = ctx->comm;
+    if (!c) return;
+    for (int o = 0; o < c->world; ++o)
+        if (c->peer[o] && o != c->rank) cudaIpcCloseMemHandle(c->peer[o]);
+    if (c->buf) cudaFree(c->buf);
+    delete c;
+    ctx->comm = nullptr;
+}
+
+}  // namespace tk
+
+using namespace tk;
+
+extern "C" {
+
+tk_status tk_comm_init(tk_ctx* ctx, int rank, int world, size_t recv_bytes, void* handle_out) {
+    if (!ctx || !handle_out) return fail(TK_ERR_INVALID, "tk_comm_init: null argument");
+    if (world < 1 || world > TK_MAX_RANKS || rank < 0 || rank >= world)
+        return fail(TK_ERR_INVALID, "tk_comm_init: rank / world out of range (world <= 8)");
+    if (recv_bytes == 0 || recv_bytes % 256) return fail(TK_ERR_INVALID, "tk_comm_init: recv_bytes must be a positive multiple of 256");
+    cudaSetDevice(ctx->device);
+    comm_destroy(ctx);
+    tk_comm_state* c = new tk_comm_state();
+    c->rank = rank;
+    c->world = world;
+    c->recv_bytes = recv_bytes;
+    cudaError_t e = cudaMalloc(&c->buf, kHdr + 2 * recv_bytes);
+    if (e == cudaSuccess) e = cudaMemset(c->buf, 0, kHdr);
+    if (e != cudaSuccess) {
+        if (c->buf) cudaFree(c->buf);
+        delete c;
+        return cuda_fail(e, "tk_comm_init: buffer");
+    }
+    c->peer[rank] = c->buf;
+    cudaIpcMemHandle_t h;
+    e = cudaIpcGetMemHandle(&h, c->buf);
+    if (e != cudaSuccess) {
+        cudaFree(c->buf);
+        delete c;
+        return cuda_fail(e, "tk_comm_init: IPC handle");
+    }
+    memcpy(handle_out, &h, sizeof(h));
+    ctx->comm = c;
+    return TK_OK;
+}
+
+tk_status tk_comm_connect(tk_ctx* ctx, const void* handles) {
+    if (!ctx || !handles) return fail(TK_ERR_INVALID, "tk_comm_connect: null argument");
+    tk_comm_state* c = ctx->comm;
+    if (!c) return fail(TK_ERR_INVALID, "tk_comm_connect: tk_comm_init first");
+    cudaSetDevice(ctx->device);
+    const uint8_t* hb = static_cast<const uint8_t*>(handles);
+    for (int o = 0; o < c->world; ++o) {
+        if (o == c->rank) continue;
+        cudaIpcMemHandle_t h;
+        memcpy(&h, hb + (size_t)o * TK_IPC_HANDLE_BYTES, sizeof(h));
+        void* p = nullptr;
+        cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+        if (e != cudaSuccess)
+            return fail(TK_ERR_CUDA, "tk_comm_connect: open peer buffer " + std::to_string(o) + ": " + cudaGetErrorString(e));
+        c->peer[o] = static_cast<uint8_t*>(p);
+    }
+    // the reduce kernel reads the owners' ack addresses from device memory
+    int* acks[TK_MAX_RANKS] = {};
+    for (int o = 0; o < c->world; ++o) acks[o] = reinterpret_cast<int*>(c->peer[o] + kAckOff);
+    cudaError_t e = cudaMemcpy(c->buf + 1024, acks, sizeof(acks), cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) return cuda_fail(e, "tk_comm_connect: ack table");
+    c->connected = true;
+    return TK_OK;
+}
+
+}  // extern "C"

@@ -80,6 +80,12 @@ struct __align__(64) GemmParams {
     int beta;
     const int* row_exp;
     const float* row_alpha;   // beta = 1: D = row_alpha[row] * D + A.B (null: alpha 1)
+    // reduce-scatter over peer memory (rs_world > 0): the last segment of a
+    // tile row goes to the owner rank's receive slot instead of D
+    float* rs_dst[TK_MAX_RANKS];     // per owner: its receive slot for this rank (row 0 of the owner's range)
+    int* rs_done[TK_MAX_RANKS];      // per owner: done flag for this rank
+    int* rs_counter;                 // CTAs finished (local), reset by the last
+    int rs_world, rs_rpo, rs_epoch;
     int col_exp;
     int* status;
 };
@@ -93,6 +99,9 @@ __device__ __forceinline__ float exp2i(int e) {   // exact 2^e for e in [-126, 1
     return __uint_as_float((uint32_t)(e + 127) << 23);
 }
 
+__device__ __forceinline__ void st_release_sys(int* p, int v) {
+    asm volatile("st.release.sys.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
 __device__ __forceinline__ int ld_acquire_gpu(const int* p) {
     int v;
     asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
@@ -290,6 +299,14 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
                 float* dst = (sp == 0 || direct) ? p.D : p.sws;
                 const long ldst = (sp == 0 || direct) ? p.ldd : p.sws_ld;
                 float* drow = dst + (size_t)(row_ok ? row : 0) * ldst;
+                // where this segment's result is stored: D, or for the last
+                // segment of a reduce-scatter launch the owner's receive slot
+                // (peer memory over NVLink); earlier segments stay in D
+                float* srow = drow;
+                if (p.rs_world && last_seg && row_ok) {
+                    const int o = row / p.rs_rpo;
+                    srow = p.rs_dst[o] + (size_t)(row - o * p.rs_rpo) * p.ldd;
+                }
                 const float* wrow = p.sws ? p.sws + (size_t)(row_ok ? row : 0) * p.sws_ld : nullptr;
                 // partial of earlier segments of this split: in dst, except for a
                 // direct split 1, whose earlier segments sit in the slab
@@ -319,7 +336,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
                     tc_ld_32x32b_x32(taddr + c, r);
                     tc_wait_ld();
                     if (full_chunk) {
-                        float4* dp = reinterpret_cast<float4*>(drow + col0);
+                        float4* dp = reinterpret_cast<float4*>(srow + col0);
 #pragma unroll
                         for (int q = 0; q < 8; ++q) {
                             float4 v = make_float4(__uint_as_float(r[4 * q]) * f, __uint_as_float(r[4 * q + 1]) * f,
@@ -338,7 +355,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
                                 float v = __uint_as_float(r[j]) * f;
                                 if (own_in_ws) v += wrow[col0 + j];
                                 if (add_d) v = fmaf(al, drow[col0 + j], v);
-                                drow[col0 + j] = v;
+                                srow[col0 + j] = v;
                             }
                         }
                     }
@@ -490,9 +507,23 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         }
     }
 
+    if (EPI == EPI_STORE && p.rs_world) __threadfence_system();   // peer stores before the done flag
     tc_fence_before();
     __syncthreads();
     if constexpr (CG == 2) cluster_sync();   // the pair finishes together: no remote signal after exit
+    if constexpr (EPI == EPI_STORE) {
+        if (p.rs_world && threadIdx.x == 0) {
+            // every epilogue thread fenced its peer stores (system scope) before
+            // the barriers above; the last CTA of the launch tells each owner
+            __threadfence_system();
+            const int old = atomicAdd(p.rs_counter, 1);
+            if (old == (int)gridDim.x - 1) {
+                *p.rs_counter = 0;
+                __threadfence_system();
+                for (int o = 0; o < p.rs_world; ++o) st_release_sys(p.rs_done[o], p.rs_epoch);
+            }
+        }
+    }
     if (warp == 1) {
         tc_fence_after();
         if constexpr (CG == 2) tmem_dealloc_cg2(tmem_base, TMEM_COLS);
@@ -610,6 +641,14 @@ static tk_status build(const GemmDesc& g, tk_ctx* ctx, GemmParams& gp, int cg, i
     gp.D = g.D; gp.ldd = g.ldd; gp.beta = g.beta;
     gp.row_exp = g.row_exp; gp.col_exp = g.col_exp;
     gp.row_alpha = g.row_alpha;
+    gp.rs_world = 0;
+    if (g.rs) {
+        for (int i = 0; i < TK_MAX_RANKS; ++i) { gp.rs_dst[i] = g.rs->dst[i]; gp.rs_done[i] = g.rs->done[i]; }
+        gp.rs_counter = g.rs->counter;
+        gp.rs_world = g.rs->world;
+        gp.rs_rpo = g.rs->rpo;
+        gp.rs_epoch = g.rs->epoch;
+    }
     gp.status = ctx->status;
     (void)ctx;
     return TK_OK;

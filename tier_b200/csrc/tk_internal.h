@@ -27,6 +27,7 @@ struct tk_ctx {
     int flags_len = 0;
     uint32_t epoch = 0;          // stamps split-K flags per launch (no reset needed)
     tk_prof prof;
+    struct tk_comm_state* comm = nullptr;   // peer buffers for the reduce-scatter (tk_comm.cu)
 };
 
 namespace tk {
@@ -100,9 +101,30 @@ struct GemmDesc {
     int col_exp = 0;
     int seg_kb = 0;        // k-blocks (of 64) per fp32 accumulation segment; 0 = whole K
     const float* row_alpha = nullptr;   // with beta = 1: D = row_alpha[row] * D + A.B
+    const struct RsDesc* rs = nullptr;  // reduce-scatter the result over peer memory (tk_comm.cu)
     float* split_ws = nullptr;   // fp32 [M, split_ld] slab; enables split-K when given
     long split_ld = 0;
 };
+// Reduce-scatter target of a GEMM (rows split over `world` owners, `rpo` rows
+// each): the last segment of row r goes to dst[r / rpo] + (r % rpo) * ldd;
+// the launch's last CTA then stores `epoch` into done[o] of every owner.
+constexpr int TK_MAX_RANKS = 8;
+struct RsDesc {
+    float* dst[TK_MAX_RANKS] = {};
+    int* done[TK_MAX_RANKS] = {};
+    int* counter = nullptr;
+    int world = 0, rpo = 0, epoch = 0;
+};
+
+// ---- tk_comm.cu: peer buffers (CUDA IPC) and the reduce-scatter around a GEMM ----
+void comm_destroy(tk_ctx* ctx);
+// Before the GEMM: wait (bounded) until every owner has consumed the receive
+// buffer this launch will overwrite; fills `rs` for the GEMM and returns the epoch.
+tk_status rs_begin(tk_ctx* ctx, int M, int K, RsDesc& rs, cudaStream_t s);
+// After the GEMM: wait for every rank's done flag, sum the slots in rank
+// order into out[rpo, ldo], then acknowledge to every rank.
+tk_status rs_finish(tk_ctx* ctx, const RsDesc& rs, int K, float* out, long ldo, cudaStream_t s);
+
 // K splits launch_gemm would use for g given a split workspace (1 or 2).
 int gemm_splits(const tk_ctx* ctx, const GemmDesc& g);
 tk_status launch_gemm(tk_ctx* ctx, const GemmDesc& g, cudaStream_t s);

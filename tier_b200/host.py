@@ -111,6 +111,30 @@ class LinearPath:
             return Y
         return full
 
+    def enable_reduce_scatter(self, M_max: int):
+        """Set up the peer buffers for `dx_rs` (one collective exchange of
+        IPC handles, then a barrier); M_max bounds the token count."""
+        import torch.distributed as dist
+        world, rank = dist.get_world_size(self.group), dist.get_rank(self.group)
+        h = self.ctx.comm_init(rank, world, M_max * self.K * 4)
+        mine = torch.tensor(list(h), dtype=torch.uint8, device=torch.device("cuda", self.ctx.device))
+        allh = [torch.empty_like(mine) for _ in range(world)]
+        dist.all_gather(allh, mine, group=self.group)
+        self.ctx.comm_connect(bytes(torch.cat(allh).cpu().tolist()))
+        dist.barrier(group=self.group)
+        self.rs_world, self.rs_rank = world, rank
+
+    def dx_rs(self, dY: torch.Tensor, out: torch.Tensor | None = None, products: int = X3_AUTO) -> torch.Tensor:
+        """This rank's token rows (rank * M/world ...) of dX = sum_g dY_g . W_g,
+        reduce-scattered inside the dX GEMM over peer memory."""
+        M = dY.shape[0]
+        rows = M // self.rs_world
+        if out is None:
+            out = torch.empty(rows, self.K, device=dY.device, dtype=torch.float32)
+        self.ctx.linear_dx_rs(self.W, dY, M, out, dy_dtype=_DT[dY.dtype], lddy=dY.stride(0), ldd=out.stride(0),
+                              products=products)
+        return out
+
     def dx(self, dY: torch.Tensor, dX: torch.Tensor | None = None, beta: float = 0.0,
            products: int = X3_AUTO) -> torch.Tensor:
         """dX = dY . W (`linear_dx`; beta=1 is `linear_dx_acc`).  dY holds this
