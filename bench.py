@@ -207,6 +207,20 @@ def run_ours(args):
 
     chunks = args.dx_chunks if world > 1 else 1
     mc = M_TOK // chunks
+    dx_mode = args.dx_mode if world > 1 else "local"
+    dXr = None
+    if dx_mode in ("fused", "rs-nccl"):
+        dXr = torch.empty(M_TOK // world, K_IN, dtype=torch.float32, device=dev)
+    if dx_mode == "fused":
+        # peer buffers for the reduce-scatter inside the dX GEMM: exchange the
+        # IPC handles once, outside the timed region
+        import torch.distributed as dist
+        h = ctx.comm_init(rank, world, M_TOK * K_IN * 4)
+        mine = torch.tensor(list(h), dtype=torch.uint8, device=dev)
+        allh = [torch.empty_like(mine) for _ in range(world)]
+        dist.all_gather(allh, mine, group=group)
+        ctx.comm_connect(bytes(torch.cat(allh).cpu().tolist()))
+        dist.barrier(group=group)
 
     def step(Xin, dYin):
         ctx.linear(w, Xin, M_TOK, Y, x_dtype=tk.DT_BF16)
@@ -214,14 +228,20 @@ def run_ours(args):
             ctx.linear_dx(w, dYin, M_TOK, dX, dy_dtype=tk.DT_BF16)
             return
         import torch.distributed as dist
-        # NCCL runs on its own stream: the Y all-gather (if the consumer wants
-        # the full Y) and each dX chunk's all-reduce overlap the next GEMM.
         works = []
         if args.gather_y:
             works.append(dist.all_gather_into_tensor(Yfull, Y, group=group, async_op=True))
-        for c in range(chunks):
-            ctx.linear_dx(w, dYin[c * mc:(c + 1) * mc], mc, dX[c * mc:(c + 1) * mc], dy_dtype=tk.DT_BF16)
-            works.append(dist.all_reduce(dX[c * mc:(c + 1) * mc], group=group, async_op=True))
+        if dx_mode == "fused":
+            # one kernel: dX tiles go to their owner rank over NVLink as they finish
+            ctx.linear_dx_rs(w, dYin, M_TOK, dXr, dy_dtype=tk.DT_BF16)
+        elif dx_mode == "rs-nccl":
+            ctx.linear_dx(w, dYin, M_TOK, dX, dy_dtype=tk.DT_BF16)
+            works.append(dist.reduce_scatter_tensor(dXr, dX, group=group, async_op=True))
+        else:
+            # NCCL on its own stream: each dX chunk's all-reduce overlaps the next GEMM
+            for c in range(chunks):
+                ctx.linear_dx(w, dYin[c * mc:(c + 1) * mc], mc, dX[c * mc:(c + 1) * mc], dy_dtype=tk.DT_BF16)
+                works.append(dist.all_reduce(dX[c * mc:(c + 1) * mc], group=group, async_op=True))
         for wk in works:
             wk.wait()
 
@@ -281,7 +301,8 @@ def run_ours(args):
     Xh = Xb.pin_memory()
     dYh = dYb.pin_memory()
     Yh = torch.empty(M_TOK, n_loc, dtype=torch.float32).pin_memory()
-    dXh = torch.empty(M_TOK, K_IN, dtype=torch.float32).pin_memory()
+    dX_out = dXr if dXr is not None else dX        # this rank's dX: token-row shard or the full matrix
+    dXh = torch.empty(dX_out.shape, dtype=torch.float32).pin_memory()
     Xs = torch.empty_like(Xd)
     dYs = torch.empty_like(dYd)
 
@@ -290,7 +311,7 @@ def run_ours(args):
         dYs.copy_(dYh, non_blocking=True)
         step(Xs, dYs)
         Yh.copy_(Y, non_blocking=True)
-        dXh.copy_(dX, non_blocking=True)
+        dXh.copy_(dX_out, non_blocking=True)
 
     for _ in range(max(1, args.warmup // 2)):
         e2e_step()
@@ -332,7 +353,11 @@ def run_ours(args):
                        "x_dtype": "bf16",
                        "partition": (f"W rows split over {world} GPUs; Y " + ("all-gathered" if args.gather_y else
                                      "kept row-sharded (column-parallel: consumed where produced)") +
-                                     f"; dX all-reduced in {chunks} M-chunks overlapped with the GEMMs")
+                                     {"fused": "; dX reduce-scattered by token rows inside the dX GEMM "
+                                               "(tiles stored into the owner GPU's memory over NVLink)",
+                                      "rs-nccl": "; dX reduce-scattered by token rows (NCCL after the GEMM)",
+                                      "allreduce": f"; dX all-reduced in {chunks} M-chunks overlapped with the GEMMs"
+                                      }[dx_mode])
                        if world > 1 else "1 GPU",
                        "l2": "working set per step ~0.5 GB > 126 MB L2 (no explicit flush)"},
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": tf_burst, "unit": "TFLOP/s",
@@ -544,7 +569,10 @@ def main():
     ap.add_argument("--ref-seconds", type=float, default=10.0, help="CPU baseline sample size (seconds)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--gather-y", action="store_true", help="multi-GPU: all-gather the full Y every step")
-    ap.add_argument("--dx-chunks", type=int, default=4, help="multi-GPU: dX GEMM / all-reduce pipeline chunks")
+    ap.add_argument("--dx-chunks", type=int, default=4, help="multi-GPU allreduce mode: dX GEMM / all-reduce chunks")
+    ap.add_argument("--dx-mode", default="fused", choices=["fused", "rs-nccl", "allreduce"],
+                    help="multi-GPU dX: reduce-scatter by token rows inside the GEMM over NVLink (fused), "
+                         "GEMM then NCCL reduce-scatter (rs-nccl), or chunked NCCL all-reduce of the full dX")
     ap.add_argument("--c4-two-pass", action="store_true", help="c4: the reference's two passes")
     ap.add_argument("--config", default="c2", choices=["c1", "c2", "c3", "c4"],
                     help="c2 (default, the headline) or a secondary configuration on one GPU")

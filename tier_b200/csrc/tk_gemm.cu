@@ -56,7 +56,9 @@ struct Geo {
     static constexpr int A_BYTES = BM * BK * 2;            // 16 KB
     static constexpr int B_BYTES = B_ROWS * BK * 2;        // 32 KB (CG 1) or 16 KB (CG 2)
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-    static constexpr size_t SMEM = (size_t)STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+    // + per epilogue warp a 32 x 36 fp32 transpose stage (peer stores)
+    static constexpr size_t STAGE_T = 4 * 32 * 36 * 4;
+    static constexpr size_t SMEM = (size_t)STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/ + STAGE_T;
 };
 
 enum { EPI_STORE = 0, EPI_LSE = 1, EPI_DLOGIT = 2 };
@@ -122,6 +124,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     uint64_t* tfull = empty + STAGES;
     uint64_t* tempty = tfull + 2;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+    float* tstage = reinterpret_cast<float*>(sB + STAGES * G::B_BYTES + 256);   // 16-byte aligned
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t rank = CG == 2 ? cluster_ctarank() : 0;
@@ -303,10 +306,15 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
                 // segment of a reduce-scatter launch the owner's receive slot
                 // (peer memory over NVLink); earlier segments stay in D
                 float* srow = drow;
-                if (p.rs_world && last_seg && row_ok) {
+                const bool rs_store = p.rs_world && last_seg;
+                if (rs_store && row_ok) {
                     const int o = row / p.rs_rpo;
                     srow = p.rs_dst[o] + (size_t)(row - o * p.rs_rpo) * p.ldd;
                 }
+                // peer stores go through a per-warp transpose so that each store
+                // instruction writes whole 128-byte row segments over NVLink
+                float4* stg = reinterpret_cast<float4*>(tstage + (size_t)(warp - 2) * 32 * 36);
+                const int row_w0 = (mb * CG + (int)rank) * BM + quarter * 32;   // row of lane 0
                 const float* wrow = p.sws ? p.sws + (size_t)(row_ok ? row : 0) * p.sws_ld : nullptr;
                 // partial of earlier segments of this split: in dst, except for a
                 // direct split 1, whose earlier segments sit in the slab
@@ -320,6 +328,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
                 for (int c = 0; c < p.bn; c += 32) {
                     const int col0 = col_base + c;
                     const bool full_chunk = row_ok && col0 + 32 <= p.N;
+                    const bool t_store = rs_store && col0 + 32 <= p.N;   // warp-uniform
                     // issue this chunk's global reads before the TMEM read and
                     // before any store, so the 8 (or 16) loads overlap instead
                     // of each waiting behind the previous store
@@ -335,7 +344,30 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
                     uint32_t r[32];
                     tc_ld_32x32b_x32(taddr + c, r);
                     tc_wait_ld();
-                    if (full_chunk) {
+                    if (t_store) {
+#pragma unroll
+                        for (int q = 0; q < 8; ++q) {
+                            float4 v = make_float4(__uint_as_float(r[4 * q]) * f, __uint_as_float(r[4 * q + 1]) * f,
+                                                   __uint_as_float(r[4 * q + 2]) * f, __uint_as_float(r[4 * q + 3]) * f);
+                            if (add_d && full_chunk) {
+                                v.x = fmaf(al, od[q].x, v.x); v.y = fmaf(al, od[q].y, v.y);
+                                v.z = fmaf(al, od[q].z, v.z); v.w = fmaf(al, od[q].w, v.w);
+                            }
+                            stg[lane * 9 + q] = v;        // row `lane`, stride 36 floats
+                        }
+                        __syncwarp();
+#pragma unroll
+                        for (int k = 0; k < 8; ++k) {     // 4 rows x 8 float4 per instruction
+                            const int rr = (lane >> 3) + 4 * k, cq = lane & 7;
+                            const int rg = row_w0 + rr;
+                            if (rg < p.M) {
+                                const int o = rg / p.rs_rpo;
+                                float* dr = p.rs_dst[o] + (size_t)(rg - o * p.rs_rpo) * p.ldd + col0;
+                                reinterpret_cast<float4*>(dr)[cq] = stg[rr * 9 + cq];
+                            }
+                        }
+                        __syncwarp();
+                    } else if (full_chunk) {
                         float4* dp = reinterpret_cast<float4*>(srow + col0);
 #pragma unroll
                         for (int q = 0; q < 8; ++q) {
