@@ -510,6 +510,112 @@ def run_c3(args):
                       "clocks": clk}))
 
 
+def _c5_blocks(qt, n, k, g):
+    """Seeded random blocks of type qt [n rows, K = k] on the GPU with finite,
+    small fp16 scales (d, dmin): synthetic weights of the 40-layer sweep."""
+    import torch
+    import tier_b200 as tk
+    rb = tk.row_bytes(qt, k)
+    B = torch.randint(0, 256, (n, rb), dtype=torch.uint8, device="cuda", generator=g)
+    if qt == tk.Q8_0:
+        v = B.view(n, k // 32, 34)
+        d = (torch.rand(n, k // 32, device="cuda", generator=g) * 3e-4 + 5e-5).half()
+        v[:, :, 0:2] = d.view(torch.uint8).view(n, k // 32, 2)
+    else:
+        sb = 144 if qt == tk.Q4_K else 176
+        v = B.view(n, k // 256, sb)
+        dd = (torch.rand(n, k // 256, 2, device="cuda", generator=g) * 2e-3 + 1e-4).half()
+        v[:, :, 0:4] = dd.view(torch.uint8).view(n, k // 256, 4)
+    return B
+
+
+def run_c5(args):
+    """C5: 40 layers x the 7 projections of a 12B-class layer (hidden 5120,
+    q 4096, k/v 1024, o, SwiGLU 14336), every layer its own weights (so every
+    read comes from HBM), in q8_0, the Q4_K_S recipe (Q4_K; Q5_K for v_proj of
+    layers 0-3 and down_proj of layers < 40/8), or fp32 weights split into fp16
+    hi/lo.  M >= 512: forward + dX of every projection (fp32 activations, x3
+    products); M <= 16 (decode): the forward GEMV of every projection (frozen
+    weights).  One JSON line per (weights, M)."""
+    import torch
+    import tier_b200 as tk
+    from tier_b200.host import LinearPath
+    ctx = tk.Context(0)
+    H, I, L = 5120, 14336, 40
+    shapes = [(4096, H), (1024, H), (1024, H), (H, 4096), (I, H), (I, H), (H, I)]
+    names = ["q", "k", "v", "o", "gate", "up", "down"]
+    hbm, tf_burst = peaks()[0], peaks()[1]
+    kinds = args.c5_kinds.split(",")
+    Ms = [int(m) for m in args.c5_m.split(",")]
+    snk = sum(n * k for n, k in shapes)
+    for kind in kinds:
+        g = torch.Generator(device="cuda").manual_seed(4)
+        layers, wbytes = [], 0
+        for l in range(L):
+            ws = []
+            for j, (n, k) in enumerate(shapes):
+                if kind == "fp16x3":
+                    W32 = torch.randn(n, k, device="cuda", generator=g) * 0.02
+                    lp = LinearPath.from_f32_split(ctx, W32)
+                    del W32
+                    ws.append((lp.W, tk.F16X2, lp.data))
+                    wbytes += n * k * 4
+                else:
+                    q5 = (names[j] == "v" and l < 4) or (names[j] == "down" and l < L // 8)
+                    qt = tk.Q8_0 if kind == "q8_0" else (tk.Q5_K if q5 else tk.Q4_K)
+                    B = _c5_blocks(qt, n, k, g)
+                    ws.append((tk.make_weight(qt, n, k, B), qt, B))
+                    wbytes += B.numel()
+            layers.append(ws)
+        torch.cuda.synchronize()
+        for M in Ms:
+            xs = {k: torch.randn(M, k, device="cuda", generator=g) for k in {k for _, k in shapes}}
+            ys = {n: torch.empty(M, n, device="cuda") for n in {n for n, _ in shapes}}
+            decode = M <= 16
+            if not decode:
+                dys = {n: torch.randn(M, n, device="cuda", generator=g) for n in {n for n, _ in shapes}}
+                dxs = {k: torch.empty(M, k, device="cuda") for k in {k for _, k in shapes}}
+
+            def fn():
+                for ws in layers:
+                    for (w, qt, data), (n, k) in zip(ws, shapes):
+                        if decode and qt != tk.F16X2:
+                            ctx.gemv(qt | tk.WFROZEN, data, n, k, xs[k], ys[n], M=M)
+                        elif decode:
+                            ctx.linear(w, xs[k], M, ys[n])
+                        else:
+                            ctx.linear(w, xs[k], M, ys[n])
+                            ctx.linear_dx(w, dys[n], M, dxs[k])
+
+            steps = 1 if M >= 4096 else max(1, min(args.steps, 5))
+            t_ms, k_ms, k_n, clk = _timed(ctx, fn, steps, 1, tk.PROF_GEMV if (decode and kind != "fp16x3")
+                                          else tk.PROF_GEMM)
+            ms = t_ms / steps
+            line = {"metric": "C5 40-layer sweep", "kind": kind, "M": M, "ms_per_step": ms, "steps": steps,
+                    "n_gpus": 1, "weight_bytes": wbytes, "clocks": clk,
+                    "config": {"workload": f"C5 40 layers x 7 projections (12B-class), {kind} weights, M={M}, " +
+                               ("forward GEMV (decode)" if decode else "forward + dX, fp32 activations, x3 products")}}
+            if decode:
+                gbs = wbytes / (ms * 1e-3) / 1e9
+                line.update({"value": gbs, "unit": "GB/s", "higher_is_better": True,
+                             "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s",
+                                          "frac": gbs / hbm, "note": "whole step, weight bytes / step time"}})
+            else:
+                useful = 2 * 2.0 * M * snk * L
+                gemm_exec = 3 * useful / (k_ms / steps * 1e-3) / 1e12
+                line.update({"value": useful / (ms * 1e-3) / 1e12, "unit": "TFLOP/s (fp32-equivalent useful)",
+                             "higher_is_better": True, "executed_tflops": 3 * useful / (ms * 1e-3) / 1e12,
+                             "roofline": {"bound": "tensor", "achieved": gemm_exec, "peak": tf_burst,
+                                          "unit": "TFLOP/s", "frac": gemm_exec / tf_burst,
+                                          "kernel": "gemm_tc_kernel (executed products)"}})
+            print(json.dumps(line), flush=True)
+            del xs, ys
+            if not decode:
+                del dys, dxs
+        del layers
+        torch.cuda.empty_cache()
+
+
 def run_c4(args):
     """C4: chunked-vocab LM head + CE: W fp16 [262144, 3840], hidden fp32
     [8192, 3840], labels uniform, chunk 16384.  Default: the single pass
@@ -574,12 +680,14 @@ def main():
                     help="multi-GPU dX: reduce-scatter by token rows inside the GEMM over NVLink (fused), "
                          "GEMM then NCCL reduce-scatter (rs-nccl), or chunked NCCL all-reduce of the full dX")
     ap.add_argument("--c4-two-pass", action="store_true", help="c4: the reference's two passes")
-    ap.add_argument("--config", default="c2", choices=["c1", "c2", "c3", "c4"],
+    ap.add_argument("--c5-kinds", default="q8_0,q4_k_s,fp16x3", help="c5: weight kinds")
+    ap.add_argument("--c5-m", default="1,16,512,4096,16384", help="c5: token counts")
+    ap.add_argument("--config", default="c2", choices=["c1", "c2", "c3", "c4", "c5"],
                     help="c2 (default, the headline) or a secondary configuration on one GPU")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "ours" and args.config != "c2":
-        return {"c1": run_c1, "c3": run_c3, "c4": run_c4}[args.config](args)
+        return {"c1": run_c1, "c3": run_c3, "c4": run_c4, "c5": run_c5}[args.config](args)
     if args.impl == "reference":
         run_reference(args)
     else:

@@ -124,6 +124,14 @@ size_t tk_row_bytes(int qtype, int cols);
 tk_status tk_dequant(tk_ctx *ctx, int qtype, const void *blocks, size_t row_bytes,
                      int r0, int nrows, int cols, int out_dtype, void *out, void *stream);
 
+/* ---- quantizer ------------------------------------------------------------ */
+/* out rows (row_bytes apart) = the blocks of x [rows, cols] (fp32, or bf16
+ * widened exactly) in Q8_0, Q4_K, Q5_K or Q6_K, byte for byte what the
+ * reference's CPU quantizer writes (q_row, tier/quant.h:201-204: q8_0_row,
+ * qk_minmax_row, q6_k_row; run per matrix by quant_main, tier/tier.cpp:2698-2746). */
+tk_status tk_quantize(tk_ctx *ctx, int qtype, const void *x, int x_dtype, int rows, int cols, int ldx,
+                      void *out, size_t row_bytes, void *stream);
+
 /* ---- decode GEMV (M = 1..16) -------------------------------------------- */
 /* y[m, n] = sum_k W(n, k) * x[m, k] for m < M, n < N, fp32 x and y.
  * qtype: TK_Q8_0, TK_Q4_K, TK_Q5_K, TK_Q6_K, TK_Q4_0, TK_F16, TK_BF16, TK_F32,

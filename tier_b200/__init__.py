@@ -77,6 +77,7 @@ SIGNATURES = [
     ("tk_linear_fwd_noalloc", _I, [_P, ctypes.POINTER(Weight), _P, _I, _I, _I, _P, _I, _F, _I, _P]),
     ("tk_weight_split_f32", _I, [_P, _P, _I, _I, _P, ctypes.POINTER(_I), _P]),
     ("tk_split3", _I, [_P, _P, _SZ, _P, _P, _P, _P]),
+    ("tk_quantize", _I, [_P, _I, _P, _I, _I, _I, _I, _P, _SZ, _P]),
     ("tk_comm_init", _I, [_P, _I, _I, _SZ, _P]),
     ("tk_comm_connect", _I, [_P, _P]),
     ("tk_linear_dx_rs", _I, [_P, ctypes.POINTER(Weight), _P, _I, _I, _I, _P, _I, _I, _P]),
@@ -197,6 +198,13 @@ class Context:
 
     def linear_dx_acc(self, W: Weight, dY, M, dX, **kw):
         return self.linear_dx(W, dY, M, dX, beta=1.0, **kw)
+
+    def quantize(self, qtype, x, rows, cols, out, x_dtype=DT_F32, ldx=None, row_bytes_=None, stream=None):
+        """out (uint8 [rows, row_bytes]) = x quantized to qtype, byte-exact with the reference's q_row."""
+        rb = row_bytes_ if row_bytes_ is not None else row_bytes(qtype, cols)
+        _check(self.lib.tk_quantize(self.h, qtype, _ptr(x), x_dtype, rows, cols, ldx or cols, _ptr(out), rb,
+                                    _stream(stream)))
+        return out
 
     # ---- reduce-scatter over peer memory (multi-GPU) ----
     def comm_init(self, rank: int, world: int, recv_bytes: int) -> bytes:

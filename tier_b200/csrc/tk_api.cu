@@ -665,6 +665,33 @@ tk_status tk_lmhead_finish(tk_ctx* ctx, const uint16_t* W, int v0, int V_shard, 
                             static_cast<cudaStream_t>(stream));
 }
 
+tk_status tk_quantize(tk_ctx* ctx, int qtype, const void* x, int x_dtype, int rows, int cols, int ldx, void* out,
+                      size_t row_bytes, void* stream) {
+    if (!ctx || !x || !out) return fail(TK_ERR_INVALID, "tk_quantize: null argument");
+    if (qtype != TK_Q8_0 && qtype != TK_Q4_K && qtype != TK_Q5_K && qtype != TK_Q6_K)
+        return fail(TK_ERR_UNSUPPORTED, "tk_quantize: the reference quantizes to Q8_0, Q4_K, Q5_K and Q6_K only");
+    if (rows < 0 || cols <= 0 || ldx < cols) return fail(TK_ERR_INVALID, "tk_quantize: bad shape");
+    if (rows == 0) return TK_OK;
+    const size_t need_rb = tk_row_bytes(qtype, cols);
+    if (need_rb == 0) return fail(TK_ERR_INVALID, "tk_quantize: cols is not a multiple of the block size");
+    if (row_bytes < need_rb) return fail(TK_ERR_INVALID, "tk_quantize: row_bytes too small");
+    if (x_dtype != TK_DT_F32 && x_dtype != TK_DT_BF16) return fail(TK_ERR_INVALID, "tk_quantize: x must be fp32 or bf16");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const float* xf = static_cast<const float*>(x);
+    long ldf = ldx;
+    if (x_dtype == TK_DT_BF16) {
+        // bf16 sources (safetensors, as quant_main reads them) widen exactly to fp32 first
+        tk_status st = ws_ensure(ctx, align256((size_t)rows * cols * 4), s);
+        if (st != TK_OK) return st;
+        float* w = static_cast<float*>(ctx->ws);
+        st = launch_bf16_to_f32(ctx, static_cast<const uint16_t*>(x), ldx, rows, cols, w, s);
+        if (st != TK_OK) return st;
+        xf = w;
+        ldf = cols;
+    }
+    return launch_quantize(ctx, qtype, xf, ldf, rows, cols, static_cast<uint8_t*>(out), row_bytes, s);
+}
+
 tk_status tk_linear_dx_rs(tk_ctx* ctx, const tk_weight* W, const void* dY, int dy_dtype, int M, int lddy,
                           float* dX_rows, int ldd, int products, void* stream) {
     if (!ctx) return fail(TK_ERR_INVALID, "tk_linear_dx_rs: null context");

@@ -116,6 +116,12 @@ struct RsDesc {
     int world = 0, rpo = 0, epoch = 0;
 };
 
+// ---- tk_quant.cu: quantizers byte-exact with the reference's CPU ones ----
+tk_status launch_quantize(tk_ctx* ctx, int qtype, const float* x, long ldx, int rows, int cols, uint8_t* out,
+                          size_t rb, cudaStream_t s);
+tk_status launch_bf16_to_f32(tk_ctx* ctx, const uint16_t* src, long lds, int rows, int cols, float* dst,
+                             cudaStream_t s);
+
 // ---- tk_comm.cu: peer buffers (CUDA IPC) and the reduce-scatter around a GEMM ----
 void comm_destroy(tk_ctx* ctx);
 // Before the GEMM: wait (bounded) until every owner has consumed the receive
