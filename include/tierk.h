@@ -132,6 +132,32 @@ tk_status tk_dequant(tk_ctx *ctx, int qtype, const void *blocks, size_t row_byte
 tk_status tk_quantize(tk_ctx *ctx, int qtype, const void *x, int x_dtype, int rows, int cols, int ldx,
                       void *out, size_t row_bytes, void *stream);
 
+/* ---- `.tq` quantized-base files ------------------------------------------ */
+/* Reader: the reference's tq_load (tier/tier.cpp:274-292) -- header
+ * "TQB1 <hb> <n>", "#key value" lines, one "<name> <type> <rows> <cols>
+ * <offset> <bytes> [err]" line per matrix, 4096-aligned block data.  Entries
+ * keep the file's order.  tk_tq_read copies entry i to host memory or (with
+ * dst_on_device) to device memory through a pinned 32 MiB stage. */
+typedef struct tk_tq tk_tq;
+tk_status tk_tq_open(const char *path, tk_tq **out);
+void tk_tq_close(tk_tq *tq);
+int tk_tq_count(const tk_tq *tq);
+int tk_tq_find(const tk_tq *tq, const char *name);          /* index, or -1 */
+tk_status tk_tq_entry(const tk_tq *tq, int i, const char **name, int *qtype, int *rows, int *cols,
+                      uint64_t *offset, uint64_t *bytes, double *err);
+tk_status tk_tq_read(const tk_tq *tq, int i, void *dst, int dst_on_device, void *stream);
+/* Writer: the layout of quant_main (tier/tier.cpp:2698-2746) and write_tq
+ * (tier/quant.py:60-105): data[i] (host or device pointers) with the header
+ * above; `meta` holds "#key value" lines (nullable); errs nullable (writes -1).
+ * Writes <path>.part, then renames it to <path>. */
+tk_status tk_tq_write(const char *path, int n, const char *const *names, const int *qtypes,
+                      const int *rows, const int *cols, const void *const *data, const double *errs,
+                      const char *meta);
+/* Type names of the format (tier/quant.h:25-31): "Q4_K" <-> TK_Q4_K etc.;
+ * -1 / NULL when unknown. */
+int tk_qtype_from_name(const char *name);
+const char *tk_qtype_name(int qtype);
+
 /* ---- decode GEMV (M = 1..16) -------------------------------------------- */
 /* y[m, n] = sum_k W(n, k) * x[m, k] for m < M, n < N, fp32 x and y.
  * qtype: TK_Q8_0, TK_Q4_K, TK_Q5_K, TK_Q6_K, TK_Q4_0, TK_F16, TK_BF16, TK_F32,

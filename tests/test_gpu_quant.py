@@ -93,3 +93,27 @@ def test_quantize_bf16_source_and_round_trip(ctx, oracle, name):
     rel = np.linalg.norm(back - xf) / np.linalg.norm(xf)
     # measured on N(0, 0.02) rows: Q4_K 7.1 %, Q5_K 3.6 %, Q6_K 1.8 % relative RMS
     assert rel < {8: 0.01, 12: 0.09, 13: 0.045, 14: 0.025}[qt], rel
+
+
+def test_quantize_to_tq_round_trip(ctx, tmp_path):
+    """GPU quantizer -> .tq writer -> reader into device memory: the bytes come
+    back unchanged, match the golden quantizer bytes, and each matrix's err is
+    its relative RMS dequantization error."""
+    import torch
+    import tier_b200 as tk
+    from tier_b200.tq import TQFile, quantize_to_tq
+    g = np.load(GOLDEN)
+    x = dev(g["x"])
+    names = list(TYPES)
+    errs = quantize_to_tq(ctx, tmp_path / "m.tq", [(f"w.{n}", x) for n in names], [TYPES[n] for n in names],
+                          meta="#from tierlm test\n")
+    with TQFile(tmp_path / "m.tq") as f:
+        for i, n in enumerate(names):
+            e = f.entries[i]
+            assert (e.name, e.qtype, e.rows, e.cols) == (f"w.{n}", TYPES[n], 4, 1024)
+            back = f.read(i, device="cuda")
+            assert np.array_equal(back.cpu().numpy(), g[f"{n}_bytes"])
+            deq = torch.empty(4, 1024, device="cuda")
+            ctx.dequant(TYPES[n], back, 4, 1024, deq)
+            want = float(np.sqrt(((deq.cpu().numpy().astype(np.float64) - g["x"]) ** 2).sum() / (g["x"].astype(np.float64) ** 2).sum()))
+            assert abs(e.err - want) < 1e-6 and abs(errs[i] - want) < 1e-9

@@ -78,6 +78,19 @@ SIGNATURES = [
     ("tk_weight_split_f32", _I, [_P, _P, _I, _I, _P, ctypes.POINTER(_I), _P]),
     ("tk_split3", _I, [_P, _P, _SZ, _P, _P, _P, _P]),
     ("tk_quantize", _I, [_P, _I, _P, _I, _I, _I, _I, _P, _SZ, _P]),
+    ("tk_tq_open", _I, [ctypes.c_char_p, ctypes.POINTER(_P)]),
+    ("tk_tq_close", None, [_P]),
+    ("tk_tq_count", _I, [_P]),
+    ("tk_tq_find", _I, [_P, ctypes.c_char_p]),
+    ("tk_tq_entry", _I, [_P, _I, ctypes.POINTER(ctypes.c_char_p), ctypes.POINTER(_I), ctypes.POINTER(_I),
+                         ctypes.POINTER(_I), ctypes.POINTER(ctypes.c_uint64), ctypes.POINTER(ctypes.c_uint64),
+                         ctypes.POINTER(ctypes.c_double)]),
+    ("tk_tq_read", _I, [_P, _I, _P, _I, _P]),
+    ("tk_tq_write", _I, [ctypes.c_char_p, _I, ctypes.POINTER(ctypes.c_char_p), ctypes.POINTER(_I),
+                         ctypes.POINTER(_I), ctypes.POINTER(_I), ctypes.POINTER(_P), ctypes.POINTER(ctypes.c_double),
+                         ctypes.c_char_p]),
+    ("tk_qtype_from_name", _I, [ctypes.c_char_p]),
+    ("tk_qtype_name", ctypes.c_char_p, [_I]),
     ("tk_comm_init", _I, [_P, _I, _I, _SZ, _P]),
     ("tk_comm_connect", _I, [_P, _P]),
     ("tk_linear_dx_rs", _I, [_P, ctypes.POINTER(Weight), _P, _I, _I, _I, _P, _I, _I, _P]),
