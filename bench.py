@@ -213,13 +213,27 @@ def run_ours(args):
         dXr = torch.empty(M_TOK // world, K_IN, dtype=torch.float32, device=dev)
     if dx_mode == "fused":
         # peer buffers for the reduce-scatter inside the dX GEMM: exchange the
-        # IPC handles once, outside the timed region
+        # IPC handles once, outside the timed region.  If any rank cannot map
+        # its peers, every rank falls back to GEMM + NCCL reduce-scatter.
         import torch.distributed as dist
-        h = ctx.comm_init(rank, world, M_TOK * K_IN * 4)
+        ok = torch.ones(1, dtype=torch.int32, device=dev)
+        h = b"\0" * tk.IPC_HANDLE_BYTES
+        try:
+            h = ctx.comm_init(rank, world, M_TOK * K_IN * 4)
+        except tk.TierkError:
+            ok.zero_()
         mine = torch.tensor(list(h), dtype=torch.uint8, device=dev)
         allh = [torch.empty_like(mine) for _ in range(world)]
         dist.all_gather(allh, mine, group=group)
-        ctx.comm_connect(bytes(torch.cat(allh).cpu().tolist()))
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN, group=group)
+        if int(ok.item()):
+            try:
+                ctx.comm_connect(bytes(torch.cat(allh).cpu().tolist()))
+            except tk.TierkError:
+                ok.zero_()
+            dist.all_reduce(ok, op=dist.ReduceOp.MIN, group=group)
+        if not int(ok.item()):
+            dx_mode = "rs-nccl"
         dist.barrier(group=group)
 
     def step(Xin, dYin):
