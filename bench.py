@@ -420,33 +420,40 @@ def _timed(ctx, fn, steps, warmup, kind):
     return t_ms, k_ms, k_n, clocks.stop()
 
 
+C1_TYPES = {"q8_0": 8, "q4_k": 12, "q5_k": 13, "q6_k": 14}
+
+
 def run_c1(args):
     """C1: q8_0 decode GEMV W[4096, 4096], M = 1, rotating over distinct
     weight copies (>= 4x the 126 MB L2) so every launch reads HBM.  The
     launches are captured in one CUDA graph and the graph is replayed, so the
-    timing measures back-to-back kernels, not the host's launch rate."""
+    timing measures back-to-back kernels, not the host's launch rate.
+    --c1-type / --c1-shape / --c1-m run the same measurement for the other
+    block types and the decode shapes of the 40-layer sweep."""
     import numpy as np
     import torch
     import tier_b200 as tk
-    from gen import q8_0_blocks
+    from gen import blocks_for
     ctx = tk.Context(0)
-    N = K = 4096
+    qt = C1_TYPES[args.c1_type]
+    N, K = (int(v) for v in args.c1_shape.lower().split("x"))
+    Ms = [int(m) for m in args.c1_m.split(",")]
     rng = np.random.default_rng(0)
     out = {}
-    for M in (1, 4, 16):
-        b = q8_0_blocks(rng, N, K)
+    for M in Ms:
+        b = blocks_for(rng, qt, N, K)
         wbytes = b.nbytes
         copies = int(np.ceil(4 * 126e6 / wbytes))
         W = torch.from_numpy(b).cuda()
         pool = [W.clone() for _ in range(copies)]
         x = torch.from_numpy(rng.standard_normal((M, K)).astype(np.float32)).cuda()
         y = torch.empty(M, N, device="cuda")
-        ctx.gemv(tk.Q8_0, pool[0], N, K, x, y, M=M)            # module load / attributes outside capture
+        ctx.gemv(qt, pool[0], N, K, x, y, M=M)                 # module load / attributes outside capture
         torch.cuda.synchronize()
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g):
             for w in pool:
-                ctx.gemv(tk.Q8_0, w, N, K, x, y, M=M)
+                ctx.gemv(qt, w, N, K, x, y, M=M)
         for _ in range(3):
             g.replay()
         torch.cuda.synchronize()
@@ -469,13 +476,17 @@ def run_c1(args):
         out[M] = (per_launch, gbs, copies, clk)
         del pool, g
     hbm = peaks()[0]
-    per_launch, gbs, copies, clk = out[1]
-    print(json.dumps({"metric": "decode GEMV HBM GB/s (q8_0 4096x4096, M=1)", "value": gbs, "unit": "GB/s",
+    m0 = Ms[0]
+    per_launch, gbs, copies, clk = out[m0]
+    shape = f"{args.c1_type} {N}x{K}"
+    print(json.dumps({"metric": f"decode GEMV HBM GB/s ({shape}, M={m0})", "value": gbs, "unit": "GB/s",
                       "n_gpus": 1, "steps": args.steps, "higher_is_better": True,
                       "us_per_launch": per_launch * 1e3,
                       "by_M": {m: {"us_per_launch": v[0] * 1e3, "GB_s": v[1]} for m, v in out.items()},
-                      "config": {"workload": "C1 q8_0 GEMV 4096x4096", "rotating_copies": copies,
-                                 "bytes_per_launch_M1": 17825792 + 4 * 4096 * 2, "timing": "CUDA graph replay"},
+                      "config": {"workload": f"{'C1' if shape == 'q8_0 4096x4096' else 'decode'} GEMV {shape}",
+                                 "rotating_copies": copies,
+                                 "bytes_per_launch": tk.row_bytes(qt, K) * N + 4 * (K + N) * m0,
+                                 "timing": "CUDA graph replay"},
                       "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s",
                                    "frac": gbs / hbm}, "clocks": clk}))
 
@@ -535,6 +546,10 @@ def _c5_blocks(qt, n, k, g):
         v = B.view(n, k // 32, 34)
         d = (torch.rand(n, k // 32, device="cuda", generator=g) * 3e-4 + 5e-5).half()
         v[:, :, 0:2] = d.view(torch.uint8).view(n, k // 32, 2)
+    elif qt == tk.Q6_K:
+        v = B.view(n, k // 256, 210)
+        d = (torch.rand(n, k // 256, device="cuda", generator=g) * 2e-4 + 1e-5).half()
+        v[:, :, 208:210] = d.view(torch.uint8).view(n, k // 256, 2)
     else:
         sb = 144 if qt == tk.Q4_K else 176
         v = B.view(n, k // 256, sb)
@@ -547,8 +562,9 @@ def run_c5(args):
     """C5: 40 layers x the 7 projections of a 12B-class layer (hidden 5120,
     q 4096, k/v 1024, o, SwiGLU 14336), every layer its own weights (so every
     read comes from HBM), in q8_0, the Q4_K_S recipe (Q4_K; Q5_K for v_proj of
-    layers 0-3 and down_proj of layers < 40/8), or fp32 weights split into fp16
-    hi/lo.  M >= 512: forward + dX of every projection (fp32 activations, x3
+    layers 0-3 and down_proj of layers < 40/8), the Q4_K_M recipe (Q4_K; Q6_K
+    for the v_proj / down_proj layers quant_main gives more bits), or fp32
+    weights split into fp16 hi/lo.  M >= 512: forward + dX of every projection (fp32 activations, x3
     products); M <= 16 (decode): the forward GEMV of every projection (frozen
     weights).  One JSON line per (weights, M)."""
     import torch
@@ -562,6 +578,13 @@ def run_c5(args):
     kinds = args.c5_kinds.split(",")
     Ms = [int(m) for m in args.c5_m.split(",")]
     snk = sum(n * k for n, k in shapes)
+    from tier_b200.tq import recipe_types
+    slots = ["q_proj", "k_proj", "v_proj", "o_proj", "gate_proj", "up_proj", "down_proj"]
+    rtypes = {}
+    for kind in kinds:
+        if kind in ("q4_k_s", "q4_k_m"):
+            for l, slot, qt in recipe_types(kind.upper(), [slots] * L):
+                rtypes[(kind, l, slots.index(slot))] = qt
     for kind in kinds:
         g = torch.Generator(device="cuda").manual_seed(4)
         layers, wbytes = [], 0
@@ -575,8 +598,7 @@ def run_c5(args):
                     ws.append((lp.W, tk.F16X2, lp.data))
                     wbytes += n * k * 4
                 else:
-                    q5 = (names[j] == "v" and l < 4) or (names[j] == "down" and l < L // 8)
-                    qt = tk.Q8_0 if kind == "q8_0" else (tk.Q5_K if q5 else tk.Q4_K)
+                    qt = tk.Q8_0 if kind == "q8_0" else rtypes[(kind, l, j)]
                     B = _c5_blocks(qt, n, k, g)
                     ws.append((tk.make_weight(qt, n, k, B), qt, B))
                     wbytes += B.numel()
@@ -693,6 +715,9 @@ def main():
     ap.add_argument("--dx-mode", default="fused", choices=["fused", "rs-nccl", "allreduce"],
                     help="multi-GPU dX: reduce-scatter by token rows inside the GEMM over NVLink (fused), "
                          "GEMM then NCCL reduce-scatter (rs-nccl), or chunked NCCL all-reduce of the full dX")
+    ap.add_argument("--c1-type", default="q8_0", choices=sorted(C1_TYPES), help="c1: weight block type")
+    ap.add_argument("--c1-shape", default="4096x4096", help="c1: N x K of the weight")
+    ap.add_argument("--c1-m", default="1,4,16", help="c1: token counts (the first is the headline)")
     ap.add_argument("--c4-two-pass", action="store_true", help="c4: the reference's two passes")
     ap.add_argument("--c5-kinds", default="q8_0,q4_k_s,fp16x3", help="c5: weight kinds")
     ap.add_argument("--c5-m", default="1,16,512,4096,16384", help="c5: token counts")

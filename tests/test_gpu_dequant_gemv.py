@@ -64,7 +64,9 @@ def test_dequant_large_rows_and_offset(ctx, oracle, qtype):
 @pytest.mark.parametrize("qtype,N,K", [(8, 4096, 4096), (12, 1024, 4096), (13, 512, 5120), (1, 768, 3840),
                                         (30, 256, 2048), (0, 256, 1024), (14, 256, 2048), (2, 256, 2048),
                                         # fewer rows than SMs, ragged slots, shared-memory ring reuse
-                                        (8, 100, 256), (8, 32768, 1024), (12, 20000, 2048), (13, 9000, 1280)])
+                                        (8, 100, 256), (8, 32768, 1024), (12, 20000, 2048), (13, 9000, 1280),
+                                        # Q6_K: one chunk, 7 chunks of 2048, and 16-byte-unaligned rows (scalar kernel)
+                                        (14, 4096, 4096), (14, 3000, 14336), (14, 700, 5120)])
 @pytest.mark.parametrize("M", [1, 3, 16])
 def test_gemv_vs_f64(ctx, oracle, qtype, N, K, M):
     import torch
@@ -95,7 +97,7 @@ def test_gemv_c1_matches_reference_order_closely(ctx, oracle):
     assert np.abs(got[:256] - ref_order).max() / np.abs(ref_order).max() < 1e-5
 
 
-@pytest.mark.parametrize("qtype", [8, 12])
+@pytest.mark.parametrize("qtype", [8, 12, 14])
 def test_gemv_frozen_chain(ctx, oracle, qtype):
     """TK_WFROZEN lets a GEMV fetch its (never written) weight before the
     previous kernel ends, but x is still read after it: a chain whose x is

@@ -1,36 +1,36 @@
 // tk_gemv5.cu -- decode GEMV on the tensor cores (mma.sync m16n8k16, fp16 in,
-// fp32 accumulate) for Q8_0 / Q4_K / Q5_K rows and M <= 8 tokens.
+// fp32 accumulate) for Q8_0 / Q4_K / Q5_K / Q6_K rows and M <= 8 tokens.
 //
 // y[m, n] = sum_k W(n, k) x[m, k].  The path is HBM-bound; the point of the
 // tensor cores here is to take the multiply-adds off the issue slots, which
 // the scalar kernel (tk_gemv4.cu) fills before HBM does.
 //
-//  * Two blocks per SM, each owning a contiguous range of rows (any count,
-//    so the bytes per SM differ by at most one row); rows are processed in
-//    groups of 16 (one MMA A tile; rows past the range are never loaded and
-//    their results are dropped).  A producer warp streams (group, K-chunk)
-//    slots through a shared-memory ring: one cp.async.bulk per row, into
-//    rows padded to a stride of 32 mod 128 bytes so the fragment loads below
-//    are bank-conflict-free.  With two blocks per SM, the next kernel's
-//    blocks start (programmatic dependent launch) while this one drains.
-//  * Eight consumer warps split every slot's K range (Q8_0: block pairs,
+//  * One block per SM, owning a contiguous range of rows (any count, so the
+//    bytes per SM differ by at most one row); rows are processed in groups of
+//    16 (one MMA A tile; rows past the range are never loaded and their
+//    results are dropped).  A producer warp streams (group, K-chunk) slots
+//    through a shared-memory ring: one cp.async.bulk per row, into rows
+//    padded to a stride of 32 mod 128 bytes so the 64-bit fragment loads
+//    below are bank-conflict-free.
+//  * Sixteen consumer warps split every slot's K range (Q8_0: block pairs,
 //    K-quants: super-blocks) and keep fp32 partial sums in registers; at the
 //    end of a group they are summed over the warps in a fixed order
 //    (deterministic), one named barrier per group.
 //  * W fragment: the MMA's k index is permuted the same way for A and B.
-//    Thread q takes the quants 8q .. 8q+7 of each 32-element block: 8q .. 8q+3
-//    are k 2q, 2q+1, 2q+8, 2q+9 of the block's first 16-element window, and
-//    8q+4 .. 8q+7 those of the second.  A row's A operand per window is one
-//    32-bit word of quants: a byte permute with the fp16 magic 0x64 gives
-//    1024 + u, an exact f16x2 subtraction gives the quant, and one 16-byte
-//    x load serves both windows.  Quants of every type here are integers of
-//    at most 8 bits: exact in fp16.
+//    Q8_0 / Q4_K / Q5_K: thread q takes the quants 8q .. 8q+7 of each
+//    32-element block: 8q .. 8q+3 are k 2q, 2q+1, 2q+8, 2q+9 of the block's
+//    first 16-element window, and 8q+4 .. 8q+7 those of the second.  Q6_K has
+//    a scale per 16 elements, so each window is one 16-element sub-block and
+//    thread q takes its elements 4q .. 4q+3.  A row's A operand per window is
+//    one 32-bit word of quants: a byte permute with the fp16 magic 0x64 gives
+//    1024 + u, an exact f16x2 subtraction gives the quant.  Quants of every
+//    type here are integers of at most 8 bits: exact in fp16.
 //  * x: each 32-element block of each token is scaled by a power of two (its
 //    max into [2^14, 2^15)) and split into fp16 hi + lo (x = hi + lo to about
-//    2^-22 relative); two MMAs (hi, lo) per window, and the block's fp32
-//    result is multiplied by the block scale and by d (Q8_0) or by d*sc, with
-//    -dmin*m times the fp32 block sum of x (K-quants).  Agreement with fp64
-//    is ~1e-6 relative; the reference's decode tolerance is 2e-3.
+//    2^-22 relative); two MMAs (hi, lo) per window, and the window's fp32
+//    result is multiplied by the block scale and by d (Q8_0), d*sc with
+//    -dmin*m times the fp32 block sum of x (Q4_K, Q5_K) or d*sc (Q6_K).
+//    Agreement with fp64 is ~1e-6 relative; the decode tolerance is 2e-3.
 //  * Programmatic dependent launch as in tk_gemv4.cu.
 #include "tk_device.cuh"
 #include "tk_internal.h"
@@ -88,6 +88,18 @@ __device__ __forceinline__ uint4 g_lds128(uint32_t a) {
     asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a));
     return v;
 }
+// 32-bit shared load at an address that is 4-byte aligned (odd == false) or
+// 2 mod 4 (odd == true: two aligned loads and a funnel shift).  Q6_K
+// super-blocks are 210 bytes, so every other one starts at 2 mod 4.
+__device__ __forceinline__ uint32_t g_lds32_a(uint32_t a, bool odd) {
+    if (!odd) return g_lds32(a);
+    return __funnelshift_r(g_lds32(a - 2u), g_lds32(a + 2u), 16);
+}
+__device__ __forceinline__ uint32_t g_lds16(uint32_t a) {
+    uint16_t v;
+    asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(a));
+    return v;
+}
 __device__ __forceinline__ uint32_t hsub2(uint32_t a, uint32_t b) {
     uint32_t r;
     asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
@@ -130,7 +142,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1) gemv_mma_kernel(const __grid_co
     float* xsc = reinterpret_cast<float*>(xl + (size_t)a.M * a.XS);   // [nblk][8]: 2^-e per block and token
     float* xsum = xsc + (size_t)nblk * 8;                                // [nblk][8]: fp32 block sums (K-quants)
     float* part = xsum + (size_t)nblk * 8;                               // [2][CW][16][8]
-    float* tab = part + 2 * GM_CW * 16 * 8;                              // [CW][16 rows][8 sub][2] (K-quants)
+    float* tab = part + 2 * GM_CW * 16 * 8;   // per warp [16 rows][8 sub][2] (Q4_K, Q5_K) or [16 rows][16] (Q6_K)
     uint64_t* full = reinterpret_cast<uint64_t*>(tab + GM_CW * 256);
     uint64_t* empty = full + a.nslots;
 
@@ -235,6 +247,8 @@ __global__ void __launch_bounds__(GM_THREADS, 1) gemv_mma_kernel(const __grid_co
     const int tok = g < a.M ? g : 0;
     const uint32_t xh_t = smem_u32(xh + (size_t)tok * a.XS) + 16u * q;   // x[8q .. 8q+7] of each block
     const uint32_t xl_t = smem_u32(xl + (size_t)tok * a.XS) + 16u * q;
+    const uint32_t xh6_t = smem_u32(xh + (size_t)tok * a.XS) + 8u * q;   // Q6_K: x[4q .. 4q+3] of each window
+    const uint32_t xl6_t = smem_u32(xl + (size_t)tok * a.XS) + 8u * q;
     const uint32_t xsc_q = smem_u32(xsc) + 8u * q;      // + blk * 32: tokens 2q, 2q+1
     const uint32_t xsum_q = smem_u32(xsum) + 8u * q;
     const uint32_t ring_u = smem_u32(ring);
@@ -299,6 +313,76 @@ __global__ void __launch_bounds__(GM_THREADS, 1) gemv_mma_kernel(const __grid_co
                             acc[2] = fmaf(d1 * sc.x, cb[2], acc[2]);
                             acc[3] = fmaf(d1 * sc.y, cb[3], acc[3]);
                         }
+                    }
+                } else if constexpr (T == QT_Q6_K) {
+                    // super-block (tier/quant.h:88-90): ql[128] low nibbles, qh[64]
+                    // 2-bit high parts, sc[16] int8 per 16 elements, d fp16 at 208.
+                    // Element e of half a (e < 128): ql byte 64a + (e & 63), nibble
+                    // e >> 6; qh byte 128 + 32a + (e & 31), bits 2 (e >> 5).
+                    const int nsb = a.KC / 256;
+                    for (int sbi = warp; sbi < nsb; sbi += GM_CW) {
+                        const uint32_t sA = rA + 210u * sbi, sB = rB + 210u * sbi;
+                        const bool odd = (sbi & 1) != 0;
+                        // d * sc of sub-blocks 4q .. 4q+3 for rows g and g+8 -> per-warp table [16 rows][16]
+                        {
+                            const uint32_t wA = g_lds32_a(sA + 192u + 4u * q, odd);
+                            const uint32_t wB = g_lds32_a(sB + 192u + 4u * q, odd);
+                            const float dA = __half2float(__ushort_as_half((uint16_t)g_lds16(sA + 208u)));
+                            const float dB = __half2float(__ushort_as_half((uint16_t)g_lds16(sB + 208u)));
+                            asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(tab_w + 64u * g + 16u * q),
+                                         "f"(dA * (float)(int8_t)(wA & 0xff)), "f"(dA * (float)(int8_t)((wA >> 8) & 0xff)),
+                                         "f"(dA * (float)(int8_t)((wA >> 16) & 0xff)), "f"(dA * (float)(int8_t)(wA >> 24))
+                                         : "memory");
+                            asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(tab_w + 64u * (g + 8) + 16u * q),
+                                         "f"(dB * (float)(int8_t)(wB & 0xff)), "f"(dB * (float)(int8_t)((wB >> 8) & 0xff)),
+                                         "f"(dB * (float)(int8_t)((wB >> 16) & 0xff)), "f"(dB * (float)(int8_t)(wB >> 24))
+                                         : "memory");
+                            __syncwarp();
+                        }
+                        const int sb_elem = kc0 + 256 * sbi;
+                        const uint32_t h1056 = 0x64206420u;          // f16x2 (1056, 1056): 1024 + u - 1056 = q - 32
+#pragma unroll 1
+                        for (int ha = 0; ha < 2; ++ha) {              // 128-element half
+                            // d * sc of this half's sub-blocks 8ha .. 8ha+7 (index 2 gq + w)
+                            const float4 tA0 = g_lds128f(tab_w + 64u * g + 32u * ha);
+                            const float4 tA1 = g_lds128f(tab_w + 64u * g + 32u * ha + 16u);
+                            const float4 tB0 = g_lds128f(tab_w + 64u * (g + 8) + 32u * ha);
+                            const float4 tB1 = g_lds128f(tab_w + 64u * (g + 8) + 32u * ha + 16u);
+                            const float scA[8] = {tA0.x, tA0.y, tA0.z, tA0.w, tA1.x, tA1.y, tA1.z, tA1.w};
+                            const float scB[8] = {tB0.x, tB0.y, tB0.z, tB0.w, tB1.x, tB1.y, tB1.z, tB1.w};
+#pragma unroll
+                            for (int w = 0; w < 2; ++w) {             // 16-element window of each 32-block
+                                const uint32_t o = 64u * ha + 16u * w + 4u * q;
+                                const uint32_t ho = 128u + 32u * ha + 16u * w + 4u * q;
+                                const uint32_t l0A = g_lds32_a(sA + o, odd), l1A = g_lds32_a(sA + o + 32u, odd);
+                                const uint32_t l0B = g_lds32_a(sB + o, odd), l1B = g_lds32_a(sB + o + 32u, odd);
+                                const uint32_t hA = g_lds32_a(sA + ho, odd), hB = g_lds32_a(sB + ho, odd);
+#pragma unroll
+                                for (int gq = 0; gq < 4; ++gq) {      // 32-block gq of the half
+                                    const uint32_t lA = gq & 1 ? l1A : l0A, lB = gq & 1 ? l1B : l0B;
+                                    const uint32_t qA = ((lA >> (4 * (gq >> 1))) & 0x0F0F0F0Fu) |
+                                                        (((hA >> (2 * gq)) & 0x03030303u) << 4);
+                                    const uint32_t qB = ((lB >> (4 * (gq >> 1))) & 0x0F0F0F0Fu) |
+                                                        (((hB >> (2 * gq)) & 0x03030303u) << 4);
+                                    uint32_t a0, a1, a2, a3;
+                                    bytes_h2(qA, h1056, a0, a2);
+                                    bytes_h2(qB, h1056, a1, a3);
+                                    const int e0 = sb_elem + 128 * ha + 32 * gq + 16 * w;
+                                    const uint2 bh = g_lds64(xh6_t + 2u * (uint32_t)e0);
+                                    const uint2 bl = g_lds64(xl6_t + 2u * (uint32_t)e0);
+                                    float cb[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+                                    mma16816(cb, a0, a1, a2, a3, bh.x, bh.y);
+                                    mma16816(cb, a0, a1, a2, a3, bl.x, bl.y);
+                                    const float2 xs = g_lds64f(xsc_q + 32u * (uint32_t)(e0 >> 5));
+                                    const float sa = scA[2 * gq + w], sb = scB[2 * gq + w];
+                                    acc[0] = fmaf(sa * xs.x, cb[0], acc[0]);
+                                    acc[1] = fmaf(sa * xs.y, cb[1], acc[1]);
+                                    acc[2] = fmaf(sb * xs.x, cb[2], acc[2]);
+                                    acc[3] = fmaf(sb * xs.y, cb[3], acc[3]);
+                                }
+                            }
+                        }
+                        __syncwarp();     // table reads done before the next super-block overwrites it
                     }
                 } else {
                     constexpr uint32_t SB = T == QT_Q4_K ? 144u : 176u;
@@ -422,7 +506,7 @@ struct GmPlan {
 };
 
 
-static uint32_t gm_block_bytes(int t) { return t == QT_Q8_0 ? 34u : t == QT_Q4_K ? 144u : 176u; }
+static uint32_t gm_block_bytes(int t) { return t == QT_Q8_0 ? 34u : t == QT_Q4_K ? 144u : t == QT_Q5_K ? 176u : 210u; }
 static int gm_block_elems(int t) { return t == QT_Q8_0 ? 32 : 256; }
 
 static bool gm_plan(int t, int N, int K, int M, int grid, GmPlan& p) {
@@ -443,6 +527,7 @@ static bool gm_plan(int t, int N, int K, int M, int grid, GmPlan& p) {
         if (units % nc) continue;
         const int KC = K / nc;
         const uint32_t kcb = (uint32_t)((size_t)KC / gm_block_elems(t) * gm_block_bytes(t));
+        if (kcb % 16u) continue;                 // bulk copies: 16-byte sizes and source offsets (Q6_K)
         uint32_t RS = (kcb + 15u) & ~15u;
         while (RS % 128u != 32u) RS += 16u;
         if (16u * (size_t)RS > slot_max) continue;
@@ -466,7 +551,7 @@ static bool gm_plan(int t, int N, int K, int M, int grid, GmPlan& p) {
 }
 
 bool gemv_mma_ok(int t, size_t rb, int K, int M) {
-    if (t != QT_Q8_0 && t != QT_Q4_K && t != QT_Q5_K) return false;
+    if (t != QT_Q8_0 && t != QT_Q4_K && t != QT_Q5_K && t != QT_Q6_K) return false;
     if (M < 1 || M > 8 || rb % 16 || K % 256) return false;
     GmPlan p;
     return gm_plan(t, 148 * 64, K, M, 148, p);
@@ -514,6 +599,7 @@ tk_status launch_gemv_mma(tk_ctx* ctx, int t, const void* Wv, size_t rb, int N, 
     if (t == QT_Q8_0) return go_mma<QT_Q8_0>(ctx, W, rb, N, K, M, x, ldx, y, ldy, frozen, s);
     if (t == QT_Q4_K) return go_mma<QT_Q4_K>(ctx, W, rb, N, K, M, x, ldx, y, ldy, frozen, s);
     if (t == QT_Q5_K) return go_mma<QT_Q5_K>(ctx, W, rb, N, K, M, x, ldx, y, ldy, frozen, s);
+    if (t == QT_Q6_K) return go_mma<QT_Q6_K>(ctx, W, rb, N, K, M, x, ldx, y, ldy, frozen, s);
     return fail(TK_ERR_UNSUPPORTED, "gemv mma: type");
 }
 
