@@ -66,8 +66,10 @@ def test_dequant_large_rows_and_offset(ctx, oracle, qtype):
                                         # fewer rows than SMs, ragged slots, shared-memory ring reuse
                                         (8, 100, 256), (8, 32768, 1024), (12, 20000, 2048), (13, 9000, 1280),
                                         # Q6_K: one chunk, 7 chunks of 2048, and 16-byte-unaligned rows (scalar kernel)
-                                        (14, 4096, 4096), (14, 3000, 14336), (14, 700, 5120)])
-@pytest.mark.parametrize("M", [1, 3, 16])
+                                        (14, 4096, 4096), (14, 3000, 14336), (14, 700, 5120),
+                                        # several K-chunks per row group and few slots per ring
+                                        (8, 5120, 14336), (12, 5120, 14336)])
+@pytest.mark.parametrize("M", [1, 2, 3, 16])
 def test_gemv_vs_f64(ctx, oracle, qtype, N, K, M):
     import torch
     rng = np.random.default_rng(qtype * 31 + M)

@@ -219,6 +219,9 @@ static int popcount_chunks(int M) {
 tk_status launch_gemv(tk_ctx* ctx, int t, const void* Wv, size_t rb, int N, int K, const float* x, int ldx, int M,
                       float* y, int ldy, cudaStream_t s, bool frozen) {
     if (N == 0 || M == 0) return TK_OK;
+    // Integer tensor-core kernel (tk_gemv6.cu) for one or two tokens.
+    if (M <= 2 && gemv_imma_ok(t, rb, K, M) && (reinterpret_cast<uintptr_t>(Wv) & 15) == 0)
+        return launch_gemv_imma(ctx, t, Wv, rb, N, K, x, ldx, M, y, ldy, frozen, s);
     // Tensor-core kernel (tk_gemv5.cu) for Q8_0 / Q4_K / Q5_K when x fits in
     // shared memory: token chunks of up to 8.
     if (gemv_mma_ok(t, rb, K, 1) && (reinterpret_cast<uintptr_t>(Wv) & 15) == 0) {

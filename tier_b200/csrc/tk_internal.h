@@ -74,6 +74,9 @@ tk_status launch_gemv_stream(tk_ctx* ctx, int qtype, const void* W, size_t rb, i
 bool gemv_mma_ok(int qtype, size_t rb, int K, int M);
 tk_status launch_gemv_mma(tk_ctx* ctx, int qtype, const void* W, size_t rb, int N, int K, const float* x, int ldx,
                           int M, float* y, int ldy, bool frozen, cudaStream_t s);
+bool gemv_imma_ok(int qtype, size_t rb, int K, int M);
+tk_status launch_gemv_imma(tk_ctx* ctx, int qtype, const void* W, size_t rb, int N, int K, const float* x, int ldx,
+                           int M, float* y, int ldy, bool frozen, cudaStream_t s);
 
 // ---- tk_gemv.cu ----
 bool gemv_supported(int qtype);
