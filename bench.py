@@ -238,8 +238,10 @@ def run_ours(args):
 
     def step(Xin, dYin):
         ctx.linear(w, Xin, M_TOK, Y, x_dtype=tk.DT_BF16)
+        # the dX GEMM reuses the forward's fp16 expansion of W (same frozen
+        # weight, same step): one dequant per step
         if world == 1:
-            ctx.linear_dx(w, dYin, M_TOK, dX, dy_dtype=tk.DT_BF16)
+            ctx.linear_dx(w, dYin, M_TOK, dX, dy_dtype=tk.DT_BF16, products=tk.WREUSE)
             return
         import torch.distributed as dist
         works = []
@@ -247,14 +249,15 @@ def run_ours(args):
             works.append(dist.all_gather_into_tensor(Yfull, Y, group=group, async_op=True))
         if dx_mode == "fused":
             # one kernel: dX tiles go to their owner rank over NVLink as they finish
-            ctx.linear_dx_rs(w, dYin, M_TOK, dXr, dy_dtype=tk.DT_BF16)
+            ctx.linear_dx_rs(w, dYin, M_TOK, dXr, dy_dtype=tk.DT_BF16, products=tk.WREUSE)
         elif dx_mode == "rs-nccl":
-            ctx.linear_dx(w, dYin, M_TOK, dX, dy_dtype=tk.DT_BF16)
+            ctx.linear_dx(w, dYin, M_TOK, dX, dy_dtype=tk.DT_BF16, products=tk.WREUSE)
             works.append(dist.reduce_scatter_tensor(dXr, dX, group=group, async_op=True))
         else:
             # NCCL on its own stream: each dX chunk's all-reduce overlaps the next GEMM
             for c in range(chunks):
-                ctx.linear_dx(w, dYin[c * mc:(c + 1) * mc], mc, dX[c * mc:(c + 1) * mc], dy_dtype=tk.DT_BF16)
+                ctx.linear_dx(w, dYin[c * mc:(c + 1) * mc], mc, dX[c * mc:(c + 1) * mc], dy_dtype=tk.DT_BF16,
+                              products=tk.WREUSE)
                 works.append(dist.all_reduce(dX[c * mc:(c + 1) * mc], group=group, async_op=True))
         for wk in works:
             wk.wait()
@@ -365,6 +368,7 @@ def run_ours(args):
             "data": "synthetic (seeded, tests/gen.py)",
             "config": {"workload": "C2 Q4_K 14336x4096, M=4096 tokens, fwd + dX per step",
                        "x_dtype": "bf16",
+                       "dequant": "W expanded to fp16 once per step by the forward; the dX GEMM reuses it (TK_WREUSE)",
                        "partition": (f"W rows split over {world} GPUs; Y " + ("all-gathered" if args.gather_y else
                                      "kept row-sharded (column-parallel: consumed where produced)") +
                                      {"fused": "; dX reduce-scattered by token rows inside the dX GEMM "

@@ -73,6 +73,15 @@ enum { TK_X3_AUTO = 0, TK_X3_REF = 1, TK_X3_HHL = 2, TK_X2 = 3, TK_X1 = 4 };
  * decode is repeated for every 256-row tile of M, so it is slower than the
  * default at every M measured on B200 so far. */
 enum { TK_QFUSED = 0x100 };
+/* OR-able flag for `products` of tk_linear_fwd / tk_linear_dx with a
+ * block-quantized weight: W's bytes have not changed since the previous
+ * linear call on this context that expanded it (a frozen weight's forward
+ * followed by its dX), so that call's fp16 expansion, kept at the start of
+ * the workspace, may be used without dequantizing again.  Reused only when
+ * the previous workspace user was a linear call on the same data pointer and
+ * shape; otherwise W is dequantized as usual.  Calls on different streams
+ * must be ordered by the caller. */
+enum { TK_WREUSE = 0x400 };
 /* OR-ed into tk_gemv's qtype: W is frozen (see tk_gemv). */
 enum { TK_WFROZEN = 0x200 };
 

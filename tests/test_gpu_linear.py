@@ -240,3 +240,49 @@ def test_split_k_shapes(ctx, M, N, K, prods):
     assert np.array_equal(d1, host(dX))
     assert rel_fro(d1, f64(dY) @ f64(W)) < tol
     ctx.sync_status()
+
+
+@pytest.mark.gpu
+def test_wreuse_same_bits_and_one_dequant(ctx):
+    """TK_WREUSE: the dX call after the forward on the same frozen quantized W
+    uses the forward's fp16 expansion (one dequant fewer) and gives the same
+    bits as a dX call that dequantizes; a different weight or another
+    workspace user in between forces a fresh dequant."""
+    import torch
+    import tier_b200 as tk
+    rng = np.random.default_rng(21)
+    N, K, M = 768, 1024, 384
+    b1, b2 = blocks_for(rng, tk.Q4_K, N, K), blocks_for(rng, tk.Q4_K, N, K)
+    w1 = tk.make_weight(tk.Q4_K, N, K, dev(b1))
+    w2 = tk.make_weight(tk.Q4_K, N, K, dev(b2))
+    X = dev(rng.standard_normal((M, K)).astype(np.float32)).to(torch.bfloat16)
+    dY = dev(rng.standard_normal((M, N)).astype(np.float32)).to(torch.bfloat16)
+    Y = torch.empty(M, N, device="cuda")
+    want = torch.empty(M, K, device="cuda")
+    ctx.linear_dx(w1, dY, M, want, dy_dtype=tk.DT_BF16)
+    ref = host(want)
+
+    got = torch.empty(M, K, device="cuda")
+    ctx.linear(w1, X, M, Y, x_dtype=tk.DT_BF16)
+    n0 = ctx.launches()
+    ctx.linear_dx(w1, dY, M, got, dy_dtype=tk.DT_BF16, products=tk.WREUSE)
+    reused = ctx.launches() - n0
+    ctx.linear_dx(w1, dY, M, want, dy_dtype=tk.DT_BF16)
+    fresh = ctx.launches() - n0 - reused
+    assert np.array_equal(host(got), ref)
+    assert reused == fresh - 1                       # the dequant was skipped
+
+    # another weight in between: the flag must not pick up w2's expansion
+    ctx.linear(w1, X, M, Y, x_dtype=tk.DT_BF16)
+    ctx.linear(w2, X, M, Y, x_dtype=tk.DT_BF16)
+    got.fill_(float("nan"))
+    ctx.linear_dx(w1, dY, M, got, dy_dtype=tk.DT_BF16, products=tk.WREUSE)
+    assert np.array_equal(host(got), ref)
+
+    # the workspace grows (reallocated) in between
+    ctx.linear(w1, X, M, Y, x_dtype=tk.DT_BF16)
+    ctx.reserve(ctx.lib.tk_workspace_bytes(ctx.h) + (1 << 20))
+    got.fill_(float("nan"))
+    ctx.linear_dx(w1, dY, M, got, dy_dtype=tk.DT_BF16, products=tk.WREUSE)
+    assert np.array_equal(host(got), ref)
+    ctx.sync_status()

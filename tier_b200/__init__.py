@@ -37,6 +37,7 @@ X3_AUTO, X3_REF, X3_HHL, X2, X1 = 0, 1, 2, 3, 4
 QFUSED = 0x100   # OR into `products`: decode a quantized W inside the GEMM
 IPC_HANDLE_BYTES = 64   # TK_IPC_HANDLE_BYTES
 WFROZEN = 0x200  # OR into tk_gemv's qtype: W is never written by earlier kernels (early weight fetch)
+WREUSE = 0x400   # OR into linear products: reuse the previous call's fp16 expansion of the same (unchanged) W
 # kernel families for profiling
 PROF_GEMM, PROF_DEQUANT, PROF_SPLIT, PROF_GEMV, PROF_LMHEAD = range(5)
 

@@ -22,6 +22,7 @@ tk_status cuda_fail(cudaError_t e, const char* what) {
 }
 
 tk_status ws_ensure(tk_ctx* ctx, size_t bytes, cudaStream_t stream) {
+    ctx->wexp_valid = false;     // the caller is about to carve the workspace
     if (bytes <= ctx->ws_bytes) return TK_OK;
     // Work queued on any stream may still use the old buffer.
     cudaError_t e = cudaDeviceSynchronize();
@@ -164,7 +165,8 @@ static tk_status linear(tk_ctx* ctx, const tk_weight* W, const void* A, int a_dt
         return fail(TK_ERR_INVALID, std::string(fn) + ": activation dtype");
     if (!aligned16(D) || ldd % 4) return fail(TK_ERR_INVALID, std::string(fn) + ": output must be 16-byte aligned, ld % 4 == 0");
     const bool want_fused = (products & TK_QFUSED) != 0 && !rs_scatter;
-    products &= ~TK_QFUSED;
+    const bool want_reuse = (products & TK_WREUSE) != 0;
+    products &= ~(TK_QFUSED | TK_WREUSE);
     Plan pl;
     st = plan_products(W, a_dtype, products, pl);
     if (st != TK_OK) return st;
@@ -197,9 +199,17 @@ static tk_status linear(tk_ctx* ctx, const tk_weight* W, const void* A, int a_dt
                         (quant && !fused ? align256((size_t)N * K * 2) : 0) +
                         (split ? align256((size_t)M * s_ld * 4) : 0) +
                         (rs_scratch ? align256((size_t)M * d_cols * 4) : 0);
+    // The fp16 expansion of a quantized W sits at the start of the workspace,
+    // so a later call on the same weight (TK_WREUSE) finds it there.
+    const bool expand = quant && !fused;
+    const bool reuse = expand && want_reuse && ctx->wexp_valid && ctx->wexp_data == W->data &&
+                       ctx->wexp_qtype == W->qtype && ctx->wexp_rows == N && ctx->wexp_cols == K &&
+                       ctx->wexp_rb == W->row_bytes;
+    const void* ws_before = ctx->ws;
     st = ws_ensure(ctx, need, s);
     if (st != TK_OK) return st;
     Carve cv(ctx->ws);
+    uint16_t* wf = expand ? cv.take<uint16_t>((size_t)N * K) : nullptr;
     // plane p of the split activation at pbase + p * M * a_cols (16-byte aligned: a_cols % 8 == 0)
     uint16_t* pbase = cv.take<uint16_t>(plane_elems * pl.x_planes);
     int* row_exp = cv.take<int>(M);
@@ -228,9 +238,16 @@ static tk_status linear(tk_ctx* ctx, const tk_weight* W, const void* A, int a_dt
     }
     const uint16_t* wplanes[2] = {nullptr, nullptr};
     if (quant) {
-        uint16_t* wf = cv.take<uint16_t>((size_t)N * K);
-        st = launch_dequant(ctx, W->qtype, W->data, W->row_bytes, 0, N, K, TK_DT_F16, wf, s);
-        if (st != TK_OK) return st;
+        if (!(reuse && ctx->ws == ws_before)) {
+            st = launch_dequant(ctx, W->qtype, W->data, W->row_bytes, 0, N, K, TK_DT_F16, wf, s);
+            if (st != TK_OK) return st;
+        }
+        ctx->wexp_valid = true;
+        ctx->wexp_data = W->data;
+        ctx->wexp_qtype = W->qtype;
+        ctx->wexp_rows = N;
+        ctx->wexp_cols = K;
+        ctx->wexp_rb = W->row_bytes;
         wplanes[0] = wf;
     } else {
         wplanes[0] = static_cast<const uint16_t*>(W->data);

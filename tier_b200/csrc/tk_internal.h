@@ -28,6 +28,12 @@ struct tk_ctx {
     uint32_t epoch = 0;          // stamps split-K flags per launch (no reset needed)
     tk_prof prof;
     struct tk_comm_state* comm = nullptr;   // peer buffers for the reduce-scatter (tk_comm.cu)
+    // fp16 expansion of a quantized weight left at the start of ws by the
+    // last linear call (TK_WREUSE); any other workspace user clears it
+    bool wexp_valid = false;
+    const void* wexp_data = nullptr;
+    int wexp_qtype = 0, wexp_rows = 0, wexp_cols = 0;
+    size_t wexp_rb = 0;
 };
 
 namespace tk {
