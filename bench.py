@@ -45,7 +45,7 @@ def peaks():
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
         d = json.loads(p.read_text())
-        return d["hbm_gbs"], d["bf16_tflops"], d.get("bf16_tflops_sustained"), "measured"
+        return d["hbm_gbs"], d["bf16_tflops"], d.get("bf16_tflops_sustained") or d["bf16_tflops"], "measured"
     return 6650.0, 1590.0, 1400.0, "fallback"
 
 
@@ -378,10 +378,13 @@ def run_ours(args):
                                       }[dx_mode])
                        if world > 1 else "1 GPU",
                        "l2": "working set per step ~0.5 GB > 126 MB L2 (no explicit flush)"},
-            "roofline": {"bound": "tensor", "achieved": achieved, "peak": tf_burst, "unit": "TFLOP/s",
-                         "frac": achieved / tf_burst, "traffic": traffic,
-                         "kernel": "gemm_tc_kernel", "peak_source": f"{src} bf16 burst (MEASURED_PEAKS.json)",
-                         "sustained_peak": tf_sus},
+            # the timed steps run back to back after >= 1 s of load, at the 1 kW
+            # power cap (clocks below): the sustained GEMM figure is the peak
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": tf_sus, "unit": "TFLOP/s",
+                         "frac": achieved / tf_sus, "traffic": traffic,
+                         "kernel": "gemm_tc_kernel",
+                         "peak_source": f"{src} bf16 sustained (MEASURED_PEAKS.json; steps run at the power cap)",
+                         "burst_peak": tf_burst, "frac_of_burst": achieved / tf_burst},
             "kernels_ms_per_step": {"gemm": gemm_ms / args.steps, "dequant": deq_ms / args.steps,
                                     "act_split": spl_ms / args.steps},
             "e2e": {"value": e2e_val, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
