@@ -174,6 +174,9 @@ const char *tk_qtype_name(int qtype);
  * earlier on the stream writes W (frozen weights), so the Q8_0 / Q4_K / Q5_K
  * kernel may start fetching W before the preceding kernel has finished
  * (x is still read only after it); without the flag nothing is read early.
+ * For 3..16 tokens with a Q8_0 / Q4_K / Q5_K weight, x is first turned into
+ * per-chunk records in the context workspace (calls on one context are
+ * stream-ordered, as for the linear entry points).
  * Replaces gemv_q (tier/tier.cpp:300-306) and gemv<T> (tier/tier.cpp:2261-2268)
  * as dispatched by chat_lin (tier/tier.cpp:2351-2378). */
 tk_status tk_gemv(tk_ctx *ctx, int qtype, const void *W, size_t row_bytes, int N, int K,

@@ -121,3 +121,25 @@ def test_gemv_frozen_chain(ctx, oracle, qtype):
     for a, b in zip(*outs):
         assert np.array_equal(a, b)
     ctx.sync_status()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("qtype,N,K", [(8, 4096, 5120), (12, 3000, 14336), (13, 700, 4096), (8, 100, 2048)])
+@pytest.mark.parametrize("M", [5, 8, 9, 13])
+def test_gemv_tokens_3_to_16(ctx, oracle, qtype, N, K, M):
+    """3..16 tokens: one launch reading W once (x records streamed with the
+    weight), both token halves, ragged row groups."""
+    import torch
+    rng = np.random.default_rng(qtype * 7 + M)
+    b = blocks_for(rng, qtype, N, K)
+    x = rng.standard_normal((M, K)).astype(np.float32)
+    x[1] *= 1e-3                                  # per-token scaling
+    y = torch.full((M, N), float("nan"), dtype=torch.float32, device="cuda")
+    n0 = ctx.launches()
+    ctx.gemv(qtype, dev(b), N, K, dev(x), y, M=M)
+    assert ctx.launches() - n0 == 2               # x records + one GEMV
+    got = host(y)
+    ref = oracle.qgemm_f64(b, qtype, N, K, x)
+    assert rel_fro(got, ref) < 1e-5
+    assert rel_fro(got[1], ref[1]) < 1e-5
+    ctx.sync_status()

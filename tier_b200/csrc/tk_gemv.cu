@@ -222,6 +222,12 @@ tk_status launch_gemv(tk_ctx* ctx, int t, const void* Wv, size_t rb, int N, int 
     // Integer tensor-core kernel (tk_gemv6.cu) for one or two tokens.
     if (M <= 2 && gemv_imma_ok(t, rb, K, M) && (reinterpret_cast<uintptr_t>(Wv) & 15) == 0)
         return launch_gemv_imma(ctx, t, Wv, rb, N, K, x, ldx, M, y, ldy, frozen, s);
+    // 3..16 tokens reading W once, x records streamed with the weight
+    // (tk_gemv7.cu); 3 or 4 tokens whose x fits shared memory stay on the fp16
+    // kernel below (one launch, measured faster there).
+    const bool aligned = (reinterpret_cast<uintptr_t>(Wv) & 15) == 0;
+    if (M >= 3 && aligned && !(M <= 4 && gemv_mma_ok(t, rb, K, M)) && gemv_wide_ok(t, rb, K, M))
+        return launch_gemv_wide(ctx, t, Wv, rb, N, K, x, ldx, M, y, ldy, s);
     // Tensor-core kernel (tk_gemv5.cu) for Q8_0 / Q4_K / Q5_K when x fits in
     // shared memory: token chunks of up to 8.
     if (gemv_mma_ok(t, rb, K, 1) && (reinterpret_cast<uintptr_t>(Wv) & 15) == 0) {
