@@ -226,8 +226,22 @@ tk_status launch_gemv(tk_ctx* ctx, int t, const void* Wv, size_t rb, int N, int 
     // (tk_gemv7.cu); 3 or 4 tokens whose x fits shared memory stay on the fp16
     // kernel below (one launch, measured faster there).
     const bool aligned = (reinterpret_cast<uintptr_t>(Wv) & 15) == 0;
-    if (M >= 3 && aligned && !(M <= 4 && gemv_mma_ok(t, rb, K, M)) && gemv_wide_ok(t, rb, K, M))
-        return launch_gemv_wide(ctx, t, Wv, rb, N, K, x, ldx, M, y, ldy, s);
+    if (M >= 3 && aligned && !(M <= 4 && gemv_mma_ok(t, rb, K, M))) {
+        if (gemv_wide_ok(t, rb, K, M)) return launch_gemv_wide(ctx, t, Wv, rb, N, K, x, ldx, M, y, ldy, s);
+        if (M > 8 && gemv_wide_ok(t, rb, K, 8)) {
+            // 16-token records do not fit next to the weight ring (Q6_K): token
+            // halves, W read twice; a remainder of 1-2 tokens takes the M <= 2 path
+            for (int m0 = 0; m0 < M; m0 += 8) {
+                const int c = M - m0 < 8 ? M - m0 : 8;
+                tk_status st = c >= 3 ? launch_gemv_wide(ctx, t, Wv, rb, N, K, x + (size_t)m0 * ldx, ldx, c,
+                                                         y + (size_t)m0 * ldy, ldy, s)
+                                      : launch_gemv(ctx, t, Wv, rb, N, K, x + (size_t)m0 * ldx, ldx, c,
+                                                    y + (size_t)m0 * ldy, ldy, s, frozen);
+                if (st != TK_OK) return st;
+            }
+            return TK_OK;
+        }
+    }
     // Tensor-core kernel (tk_gemv5.cu) for Q8_0 / Q4_K / Q5_K when x fits in
     // shared memory: token chunks of up to 8.
     if (gemv_mma_ok(t, rb, K, 1) && (reinterpret_cast<uintptr_t>(Wv) & 15) == 0) {

@@ -1,5 +1,5 @@
 // tk_gemv7.cu -- decode GEMV for 3..16 tokens on the integer tensor cores
-// (mma.sync s8 x s8 -> s32) for Q8_0 / Q4_K / Q5_K rows, reading W once.
+// (mma.sync s8 x s8 -> s32) for Q8_0 / Q4_K / Q5_K / Q6_K rows, reading W once.
 //
 // x of 16 tokens at K = 14336 does not fit shared memory next to a weight
 // ring, so x travels with the weight instead:
@@ -23,7 +23,8 @@
 //    the team sums its warps' partials in a fixed order.
 //  * Per unit and plane: Q8_0 one m16n8k32 MMA per block, times d; Q4_K / Q5_K
 //    one per 32-element sub-block, times its 6-bit sc in int32, minus m times
-//    the block's x sum, then d and dmin in fp32.
+//    the block's x sum, then d and dmin in fp32; Q6_K one m16n8k16 MMA per
+//    16-element sub-block, times its int8 sc, then d.
 // Agreement with fp64 is ~1e-7 relative.  x must be finite.
 #include "tk_device.cuh"
 #include "tk_internal.h"
@@ -92,6 +93,20 @@ __device__ __forceinline__ void wmma32z(int (&d)[4], uint32_t a0, uint32_t a1, u
         "{%10, %10, %10, %10};"
         : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(z));
+}
+// D = A (16 x 16, s8) * B (16 x 8, s8), s32, accumulator input zero
+__device__ __forceinline__ void wmma16z(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t b0) {
+    const int z = 0;
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.s32.s8.s8.s32 {%0, %1, %2, %3}, {%4, %5}, {%6}, {%7, %7, %7, %7};"
+        : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+        : "r"(a0), "r"(a1), "r"(b0), "r"(z));
+}
+// 32-bit load at an address that is 4-byte aligned or (odd) 2 mod 4 (Q6_K
+// super-blocks are 210 bytes)
+__device__ __forceinline__ uint32_t w_lds32_a(uint32_t a, bool odd) {
+    if (!odd) return w_lds32(a);
+    return __funnelshift_r(w_lds32(a - 2u), w_lds32(a + 2u), 16);
 }
 // int -> float, exact for |v| < 2^22: v added to the mantissa of 1.5 * 2^23
 __device__ __forceinline__ float w_i2f22(int v) { return __int_as_float(v + 0x4B400000) - 12582912.0f; }
@@ -290,6 +305,57 @@ __global__ void __launch_bounds__(GW_THREADS, 1) gemv_wide_kernel(const __grid_c
                             acc[2] = fmaf(sc.x, fmaf(dBo, w_i2f22(co[2]), dBe * w_i2f22(ce[2])), acc[2]);
                             acc[3] = fmaf(sc.y, fmaf(dBo, w_i2f22(co[3]), dBe * w_i2f22(ce[3])), acc[3]);
                         }
+                    } else if constexpr (T == QT_Q6_K) {
+                        // Q6_K (tier/quant.h:88-90): unit u is elements 64j .. 64j+63 of
+                        // super-block u / 4, i.e. 16-element sub-blocks 4j+t (t < 4), one
+                        // m16n8k16 MMA each; thread q takes elements 4q .. 4q+3 of each.
+                        // In half ha = j / 2: ql bytes 64ha + 16t + 4q (nibble j & 1), qh
+                        // bytes 128 + 32ha + 16 (t & 1) + 4q (bits 2 (2 (j & 1) + t / 2)).
+                        const int j = u & 3, sbi = u >> 2, ha = j >> 1, nb = j & 1;
+                        const uint32_t sA = rA + 210u * (uint32_t)sbi, sB = rB + 210u * (uint32_t)sbi;
+                        const bool odd = (sbi & 1) != 0;
+                        const uint32_t scwA = w_lds32_a(sA + 192u + 4u * j, odd), scwB = w_lds32_a(sB + 192u + 4u * j, odd);
+                        const float dA = w_h2f(w_lds16(sA + 208u)), dB = w_h2f(w_lds16(sB + 208u));
+                        uint32_t vA[4], vB[4];
+                        {
+                            const uint32_t hA0 = w_lds32_a(sA + 128u + 32u * ha + 4u * q, odd);
+                            const uint32_t hA1 = w_lds32_a(sA + 128u + 32u * ha + 16u + 4u * q, odd);
+                            const uint32_t hB0 = w_lds32_a(sB + 128u + 32u * ha + 4u * q, odd);
+                            const uint32_t hB1 = w_lds32_a(sB + 128u + 32u * ha + 16u + 4u * q, odd);
+#pragma unroll
+                            for (int t = 0; t < 4; ++t) {
+                                const uint32_t o = 64u * ha + 16u * t + 4u * q;
+                                const int sh = 2 * (2 * nb + (t >> 1));
+                                const uint32_t uA = ((w_lds32_a(sA + o, odd) >> (4 * nb)) & 0x0F0F0F0Fu) |
+                                                    ((((t & 1) ? hA1 : hA0) >> sh) & 0x03030303u) << 4;
+                                const uint32_t uB = ((w_lds32_a(sB + o, odd) >> (4 * nb)) & 0x0F0F0F0Fu) |
+                                                    ((((t & 1) ? hB1 : hB0) >> sh) & 0x03030303u) << 4;
+                                // bytes u - 32 (u < 64): no borrow crosses a byte
+                                vA[t] = ((uA | 0x80808080u) - 0x20202020u) ^ 0x80808080u;
+                                vB[t] = ((uB | 0x80808080u) - 0x20202020u) ^ 0x80808080u;
+                            }
+                        }
+#pragma unroll
+                        for (int p = 0; p < 3; ++p) {
+                            // + 16 t: thread q's x bytes 4q .. 4q+3 of sub-block t
+                            const uint32_t xr = rec + (uint32_t)(p * TOKS) * GW_XROW + xb_row - 4u * q + eo;
+                            int I1[4] = {0, 0, 0, 0};
+#pragma unroll
+                            for (int t = 0; t < 4; ++t) {
+                                int cc[4];
+                                wmma16z(cc, vA[t], vB[t], w_lds32(xr + 16u * t));
+                                const int sa = (int)(scwA << (24 - 8 * t)) >> 24, sb = (int)(scwB << (24 - 8 * t)) >> 24;
+                                I1[0] += sa * cc[0];
+                                I1[1] += sa * cc[1];
+                                I1[2] += sb * cc[2];
+                                I1[3] += sb * cc[3];
+                            }
+                            const float2 sc = w_lds64f(rec + cs_col + (uint32_t)(p * TOKS) * 4u);
+                            acc[0] = fmaf(sc.x, dA * __int2float_rn(I1[0]), acc[0]);
+                            acc[1] = fmaf(sc.y, dA * __int2float_rn(I1[1]), acc[1]);
+                            acc[2] = fmaf(sc.x, dB * __int2float_rn(I1[2]), acc[2]);
+                            acc[3] = fmaf(sc.y, dB * __int2float_rn(I1[3]), acc[3]);
+                        }
                     } else {
                         // Q4_K / Q5_K: unit u is sub-blocks 2j, 2j+1 of super-block u / 4
                         // (tier/quant.h:83-87; sc / m packing tier/quant.h:47-48)
@@ -386,7 +452,7 @@ struct GwPlan {
     size_t smem;
 };
 
-static uint32_t gw_block_bytes(int t) { return t == QT_Q8_0 ? 34u : t == QT_Q4_K ? 144u : 176u; }
+static uint32_t gw_block_bytes(int t) { return t == QT_Q8_0 ? 34u : t == QT_Q4_K ? 144u : t == QT_Q5_K ? 176u : 210u; }
 static int gw_block_elems(int t) { return t == QT_Q8_0 ? 32 : 256; }
 
 // The fewest K-chunks (largest copies) that give two slots, with at least
@@ -408,7 +474,7 @@ static bool gw_plan(int t, int N, int K, size_t rb, int M, int grid, GwPlan& p) 
             const uint32_t kcb = (uint32_t)((size_t)KC / gw_block_elems(t) * gw_block_bytes(t));
             if (kcb % 16u) continue;
             uint32_t RS = (kcb + 15u) & ~15u;
-            while (RS % 128u != 32u) RS += 16u;
+            while (RS % 128u != (t == QT_Q6_K ? 16u : 32u)) RS += 16u;    // 32-bit (Q6_K) or 64-bit fragment loads
             const uint32_t CS = (nc == 1 && rb == kcb) ? ((4u * kcb + 127u) & ~127u) + 32u : 0u;
             const size_t wpart = CS ? 4u * (size_t)CS : 16u * (size_t)RS;
             const uint32_t xoff = (uint32_t)((wpart + 127) & ~size_t(127));
@@ -437,7 +503,7 @@ static bool gw_plan(int t, int N, int K, size_t rb, int M, int grid, GwPlan& p) 
 }
 
 bool gemv_wide_ok(int t, size_t rb, int K, int M) {
-    if (t != QT_Q8_0 && t != QT_Q4_K && t != QT_Q5_K) return false;
+    if (t != QT_Q8_0 && t != QT_Q4_K && t != QT_Q5_K && t != QT_Q6_K) return false;
     if (M < 3 || M > 16 || rb % 16 || K % 256) return false;
     GwPlan p;
     return gw_plan(t, 148 * 64, K, rb, M, 148, p);
@@ -498,10 +564,12 @@ tk_status launch_gemv_wide(tk_ctx* ctx, int t, const void* Wv, size_t rb, int N,
         if (t == QT_Q8_0) return go_wide<QT_Q8_0, 1>(ctx, W, rb, N, K, M, xr, y, ldy, s);
         if (t == QT_Q4_K) return go_wide<QT_Q4_K, 1>(ctx, W, rb, N, K, M, xr, y, ldy, s);
         if (t == QT_Q5_K) return go_wide<QT_Q5_K, 1>(ctx, W, rb, N, K, M, xr, y, ldy, s);
+        if (t == QT_Q6_K) return go_wide<QT_Q6_K, 1>(ctx, W, rb, N, K, M, xr, y, ldy, s);
     } else {
         if (t == QT_Q8_0) return go_wide<QT_Q8_0, 2>(ctx, W, rb, N, K, M, xr, y, ldy, s);
         if (t == QT_Q4_K) return go_wide<QT_Q4_K, 2>(ctx, W, rb, N, K, M, xr, y, ldy, s);
         if (t == QT_Q5_K) return go_wide<QT_Q5_K, 2>(ctx, W, rb, N, K, M, xr, y, ldy, s);
+        if (t == QT_Q6_K) return go_wide<QT_Q6_K, 2>(ctx, W, rb, N, K, M, xr, y, ldy, s);
     }
     return fail(TK_ERR_UNSUPPORTED, "gemv wide: type");
 }
