@@ -458,6 +458,36 @@ def run_ours(args):
 
 # ---------------------------------------------------------------------------
 # Secondary configurations (not the driver's headline line): --config c1|c3|c4
+def _timed_graph(fn, steps):
+    """One step captured as a CUDA graph (how a serving engine issues a decode
+    step: no host launch cost per kernel), replayed `steps` times."""
+    import torch
+    fn()                                   # workspace growth and attributes outside the capture
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        fn()
+    for _ in range(3):
+        g.replay()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    while time.perf_counter() - t0 < 0.5:
+        g.replay()
+        torch.cuda.synchronize()
+    clocks = Clocks(torch.cuda.current_device())
+    clocks.start()
+    time.sleep(0.25)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record()
+    for _ in range(steps):
+        g.replay()
+    ev1.record()
+    torch.cuda.synchronize()
+    t_ms = ev0.elapsed_time(ev1)
+    del g
+    return t_ms, clocks.stop()
+
+
 def _timed(ctx, fn, steps, warmup, kind):
     import torch
     for _ in range(warmup):
@@ -687,13 +717,23 @@ def run_c5(args):
                             ctx.linear_dx(w, dys[n], M, dxs[k])
 
             steps = 1 if M >= 4096 else max(1, min(args.steps, 5))
-            t_ms, k_ms, k_n, clk = _timed(ctx, fn, steps, 1, tk.PROF_GEMV if (decode and kind != "fp16x3")
-                                          else tk.PROF_GEMM)
+            # quantized decode (GEMVs only) replays as one CUDA graph; the fp16-x3 weights
+            # decode through tk_linear_fwd, whose split-K stamps advance per launch, so
+            # those steps launch eagerly
+            graph = decode and kind != "fp16x3"
+            if graph:
+                steps = max(steps, 20)
+                t_ms, clk = _timed_graph(fn, steps)
+                k_ms = None
+            else:
+                t_ms, k_ms, k_n, clk = _timed(ctx, fn, steps, 1, tk.PROF_GEMV if decode else tk.PROF_GEMM)
             ms = t_ms / steps
             line = {"metric": "C5 40-layer sweep", "kind": kind, "M": M, "ms_per_step": ms, "steps": steps,
                     "n_gpus": 1, "weight_bytes": wbytes, "clocks": clk,
                     "config": {"workload": f"C5 40 layers x 7 projections (12B-class), {kind} weights, M={M}, " +
-                               ("forward GEMV (decode)" if decode else "forward + dX, fp32 activations, x3 products")}}
+                               (("forward GEMV (decode), a step's launches replayed as one CUDA graph" if graph
+                                 else "forward (decode) through tk_linear_fwd, eager launches")
+                                if decode else "forward + dX, fp32 activations, x3 products")}}
             if decode:
                 gbs = wbytes / (ms * 1e-3) / 1e9
                 line.update({"value": gbs, "unit": "GB/s", "higher_is_better": True,
