@@ -93,3 +93,52 @@ def test_vocab_merge_and_row_split_gloo():
     for p in procs:
         p.join(timeout=60)
     assert res == {0: True, 1: True}
+
+
+class _HostGemv:
+    """Stands in for the device context on CPU: gemv on an fp32 weight."""
+
+    def gemv(self, qtype, W, N, K, x, y, M=1, ldx=None, ldy=None, row_bytes_=None, stream=None):
+        y[:M, :N] = x[:M, :K] @ W.view(N, K).T
+        return y
+
+
+def _decode_worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from tier_b200 import F32
+        from tier_b200.host import LinearPath, shard_rows
+        g = torch.Generator().manual_seed(3)
+        ok = True
+        for N, M in ((64, 3), (65, 16)):                   # equal and unequal row shards
+            K = 40
+            W = torch.randn(N, K, generator=g)
+            x = torch.randn(M, K, generator=g)
+            a, b = shard_rows(N, world, rank)
+            lp = LinearPath(_HostGemv(), F32, b - a, K, W[a:b].contiguous(), group=dist.group.WORLD,
+                            n_total=N, row0=a)
+            y = lp.decode(x)
+            ok = ok and y.shape == (M, N) and torch.allclose(y, x @ W.T, rtol=1e-5, atol=1e-5)
+            out = torch.empty(M, N)
+            ok = ok and lp.decode(x, y=out) is out and torch.allclose(out, x @ W.T, rtol=1e-5, atol=1e-5)
+        q.put((rank, bool(ok)))
+    except Exception as e:   # report instead of leaving the other rank waiting
+        q.put((rank, repr(e)))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_row_sharded_decode_gather_gloo():
+    """Decode on row shards: each rank's y columns land in the gathered
+    [M, N_total] in rank order, for equal and unequal shards."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_decode_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=120) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+    assert res == {0: True, 1: True}

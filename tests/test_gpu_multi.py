@@ -1,5 +1,5 @@
-"""Row-sharded linear and vocab-sharded LM head across 2 GPUs (one process
-per GPU, NCCL), and the dX reduce-scatter done inside the GEMM over peer
+"""Row-sharded linear and decode and vocab-sharded LM head across 2 GPUs (one
+process per GPU, NCCL), and the dX reduce-scatter done inside the GEMM over peer
 memory: every rank's gathered / reduced / scattered result equals the
 single-GPU result within the path's tolerance.  Skipped with fewer than 2
 GPUs."""
@@ -52,6 +52,14 @@ def _worker(rank, world, port, q):
         torch.cuda.synchronize()
         out["lin_fwd"] = float((Y - Y1).norm() / Y1.norm())
         out["lin_dx"] = float((dX - dX1).norm() / dX1.norm())
+        # decode on the row shards (1, 2 and 12 tokens), y shards all-gathered
+        derr = []
+        for Md in (1, 2, 12):
+            xd = torch.from_numpy(rng.standard_normal((Md, K)).astype(np.float32)).cuda()
+            yd, yd1 = lp.decode(xd), full.decode(xd)
+            torch.cuda.synchronize()
+            derr.append(float((yd - yd1).norm() / yd1.norm()))
+        out["decode"] = max(derr)
         # dX reduce-scattered inside the GEMM over peer memory: this rank's
         # token rows of the sum; three calls in a row cover both buffer
         # parities and the acknowledgement path; fp32 dY (x3, several
@@ -116,6 +124,7 @@ def test_two_gpu_shards_match_single_gpu():
     for r, o in res.items():
         assert "error" not in o, o
         assert o["lin_fwd"] < 1e-6 and o["lin_dx"] < 1e-5, o
+        assert o["decode"] < 1e-5, o
         assert o["rs_dx"] < 1e-5, o
         assert o["lm_loss"] < 1e-6 and o["lm_dx"] < 1e-5 and o["lm_amax"], o
         assert o["lmf_loss"] < 1e-6 and o["lmf_dx"] < 1e-5 and o["lmf_amax"], o

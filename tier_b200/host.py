@@ -11,7 +11,9 @@ Sharding (weights split by output rows, vocab split by rows of the head):
   * linear fwd: rank g owns W[N_g, K]; Y[:, N_g] is computed locally and, if
     the caller wants the full Y, all-gathered.
   * linear dX: rank g computes dY[:, N_g] . W[N_g, :] and the partial dX are
-    all-reduced (SUM).
+    all-reduced (SUM), or reduce-scattered by token rows inside the GEMM.
+  * decode (chat_lin, 1..16 tokens): rank g runs the GEMV on its rows and the
+    y shards are all-gathered into [M, N_total].
   * LM head: rank g owns head rows [v0_g, v0_g + V_g).  After the local pass
     1 the running states are merged with all-reduce MAX of rmax, a local
     rescale, all-reduce SUM of rsum and of the target logit (only the owning
@@ -22,7 +24,7 @@ from __future__ import annotations
 
 import torch
 
-from . import (BF16, DT_BF16, DT_F16, DT_F32, F16, F16X2, X2, X3_AUTO, X3_REF, Context, Weight, make_weight,
+from . import (BF16, DT_BF16, DT_F16, DT_F32, F16, F16X2, WFROZEN, X2, X3_AUTO, X3_REF, Context, Weight, make_weight,
                row_bytes)
 
 _DT = {torch.float32: DT_F32, torch.float16: DT_F16, torch.bfloat16: DT_BF16}
@@ -109,6 +111,40 @@ class LinearPath:
             else:
                 Y.copy_(full)
             return Y
+        return full
+
+    def decode(self, x: torch.Tensor, y: torch.Tensor | None = None, frozen: bool = True,
+               gather: bool = True) -> torch.Tensor:
+        """y = x . W^T for 1..16 tokens x [M, K] fp32 on the decode GEMV
+        (`chat_lin`, tier/tier.cpp:2351-2378).  Block-quantized and dense
+        weights; `frozen`: W is never rewritten (early weight fetch).  With a
+        group and gather=True the rows' y shards are all-gathered into the
+        full [M, N_total] (one collective; shorter shards are padded)."""
+        M = x.shape[0]
+        qt = self.W.qtype | (WFROZEN if frozen else 0)
+        local = y if (y is not None and self.group is None) else torch.empty(M, self.N, device=x.device,
+                                                                               dtype=torch.float32)
+        self.ctx.gemv(qt, self.data, self.N, self.K, x, local, M=M, ldx=x.stride(0), ldy=local.stride(0),
+                      row_bytes_=self.W.row_bytes)
+        if self.group is None or not gather:
+            return local
+        import torch.distributed as dist
+        world = dist.get_world_size(self.group)
+        sizes = [torch.zeros(1, dtype=torch.int64, device=x.device) for _ in range(world)]
+        dist.all_gather(sizes, torch.tensor([self.N], dtype=torch.int64, device=x.device), group=self.group)
+        ns = [int(t.item()) for t in sizes]
+        nmax = max(ns)
+        if self.N == nmax:
+            send = local.contiguous()
+        else:                                    # collectives want equal sizes: pad the short shard
+            send = torch.zeros(M, nmax, device=x.device, dtype=torch.float32)
+            send[:, : self.N] = local
+        buf = torch.empty(world * M, nmax, device=x.device, dtype=torch.float32)
+        dist.all_gather_into_tensor(buf, send, group=self.group)
+        full = torch.cat([buf[r * M:(r + 1) * M, : ns[r]] for r in range(world)], dim=1)
+        if y is not None:
+            y.copy_(full)
+            return y
         return full
 
     def enable_reduce_scatter(self, M_max: int):
