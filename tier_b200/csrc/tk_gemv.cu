@@ -242,8 +242,8 @@ tk_status launch_gemv(tk_ctx* ctx, int t, const void* Wv, size_t rb, int N, int 
             return TK_OK;
         }
     }
-    // Tensor-core kernel (tk_gemv5.cu) for Q8_0 / Q4_K / Q5_K when x fits in
-    // shared memory: token chunks of up to 8.
+    // fp16 tensor-core kernel (tk_gemv5.cu) for Q8_0 / Q4_K / Q5_K / Q6_K when
+    // x fits in shared memory: token chunks of up to 8.
     if (gemv_mma_ok(t, rb, K, 1) && (reinterpret_cast<uintptr_t>(Wv) & 15) == 0) {
         int m0 = 0;
         while (m0 < M) {

@@ -1,5 +1,9 @@
 // tk_gemv5.cu -- decode GEMV on the tensor cores (mma.sync m16n8k16, fp16 in,
-// fp32 accumulate) for Q8_0 / Q4_K / Q5_K / Q6_K rows and M <= 8 tokens.
+// fp32 accumulate) for Q8_0 / Q4_K / Q5_K / Q6_K rows and M <= 8 tokens with x
+// resident in shared memory.  The dispatcher (tk_gemv.cu) sends 1-2 tokens to
+// the integer kernel (tk_gemv6.cu) and most 5..16-token cases to the one that
+// streams x with the weight (tk_gemv7.cu); this one takes 3-4 tokens whose x
+// fits and the shapes those kernels do not plan for.
 //
 // y[m, n] = sum_k W(n, k) x[m, k].  The path is HBM-bound; the point of the
 // tensor cores here is to take the multiply-adds off the issue slots, which
