@@ -238,6 +238,7 @@ __global__ void __launch_bounds__(GV_THREADS, 2) gemv_sk_kernel(const __grid_con
         // ---------------- producer ----------------
         if (lane == 0) {
             bool ok = true;
+            int issued = 0;
             for (int st = 0; st < nst && ok; ++st) {
                 const int slot = st % a.nslots;
                 if (st >= a.nslots && !mbar_wait(&empty[slot], (uint32_t)((st / a.nslots) - 1) & 1u, a.status)) {
@@ -249,11 +250,13 @@ __global__ void __launch_bounds__(GV_THREADS, 2) gemv_sk_kernel(const __grid_con
                 const uint32_t bytes = (uint32_t)((size_t)nr * a.rb);
                 mbar_arrive_expect_tx(&full[slot], bytes);
                 bulk_load(ring + (size_t)slot * a.slot_bytes, a.W + (size_t)r0 * a.rb, bytes, &full[slot]);
+                issued = st + 1;
             }
             if (!ok) {
-                // copies still in flight land before the block exits (bounded)
-                const int first = nst > a.nslots ? nst - a.nslots : 0;
-                for (int st = first; st < nst; ++st)
+                // copies still in flight land before the block exits (bounded): the
+                // last nslots uses issued (earlier ones were consumed before reuse)
+                const int first = issued > a.nslots ? issued - a.nslots : 0;
+                for (int st = first; st < issued; ++st)
                     (void)mbar_wait(&full[st % a.nslots], (uint32_t)(st / a.nslots) & 1u, a.status);
             }
         }

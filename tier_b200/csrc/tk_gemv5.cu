@@ -170,7 +170,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1) gemv_mma_kernel(const __grid_co
     if (warp == GM_CW) {
         // ---------------- producer: one bulk copy per row of each slot ----------------
         bool ok = true;
-        int slot = 0;
+        int slot = 0, issued = 0;
         for (int s = 0; s < nslot_total; ++s) {
             const int grp = s / a.nchunks, c = s - grp * a.nchunks;
             const int row0 = r_begin + grp * 16;
@@ -185,12 +185,14 @@ __global__ void __launch_bounds__(GM_THREADS, 1) gemv_mma_kernel(const __grid_co
             if (lane < nv)
                 bulk_load(ring + (size_t)slot * slot_bytes + (size_t)lane * a.RS,
                           a.W + (size_t)(row0 + lane) * a.rb + (size_t)c * a.kcb, a.kcb, &full[slot]);
+            issued = s + 1;
             if (++slot == a.nslots) slot = 0;
         }
         if (!ok && lane == 0) {
-            // copies already issued land before the block exits (bounded)
-            const int first = nslot_total > a.nslots ? nslot_total - a.nslots : 0;
-            for (int s = first; s < nslot_total; ++s)
+            // copies already issued land before the block exits (bounded): the
+            // last nslots uses issued (earlier ones were consumed before reuse)
+            const int first = issued > a.nslots ? issued - a.nslots : 0;
+            for (int s = first; s < issued; ++s)
                 (void)mbar_wait(&full[s % a.nslots], (uint32_t)(s / a.nslots) & 1u, a.status);
         }
         return;

@@ -214,7 +214,7 @@ __global__ void __launch_bounds__(GW_THREADS, 1) gemv_wide_kernel(const __grid_c
     if (warp == GW_CW) {
         // ---------------- producer: weight rows + the chunk's x records per slot ----------------
         bool ok = true;
-        int slot = 0;
+        int slot = 0, issued = 0;
         const uint32_t xbytes = (uint32_t)(a.KC / 256) * REC;
         for (int s = 0; s < nslot_total; ++s) {
             const int grp = s / a.nchunks, c = s - grp * a.nchunks;
@@ -239,12 +239,14 @@ __global__ void __launch_bounds__(GW_THREADS, 1) gemv_wide_kernel(const __grid_c
                           &full[slot]);
             }
             if (lane == 31) bulk_load(sb + a.xoff, a.xr + (size_t)c * xbytes, xbytes, &full[slot]);
+            issued = s + 1;
             if (++slot == a.nslots) slot = 0;
         }
         if (!ok && lane == 0) {
-            // copies already issued land before the block exits (bounded)
-            const int first = nslot_total > a.nslots ? nslot_total - a.nslots : 0;
-            for (int s = first; s < nslot_total; ++s)
+            // copies already issued land before the block exits (bounded): the
+            // last nslots uses issued (earlier ones were consumed before reuse)
+            const int first = issued > a.nslots ? issued - a.nslots : 0;
+            for (int s = first; s < issued; ++s)
                 (void)mbar_wait(&full[s % a.nslots], (uint32_t)(s / a.nslots) & 1u, a.status);
         }
         return;
