@@ -146,3 +146,25 @@ def test_gemv_tokens_3_to_16(ctx, oracle, qtype, N, K, M):
     assert rel_fro(got, ref) < 1e-5
     assert rel_fro(got[1], ref[1]) < 1e-5
     ctx.sync_status()
+
+
+@pytest.mark.parametrize("qtype", [8, 12])
+@pytest.mark.parametrize("M", [1, 2, 3, 9])
+@pytest.mark.parametrize("bad", [float("nan"), float("inf")])
+def test_gemv_nonfinite_x(ctx, oracle, qtype, M, bad):
+    """A NaN or inf in one token's x makes that token's y non-finite, as the
+    reference's fp32 sum does; the other tokens are unaffected."""
+    import torch
+    rng = np.random.default_rng(17 + M)
+    N, K = 600, 4096
+    b = blocks_for(rng, qtype, N, K)
+    x = rng.standard_normal((M, K)).astype(np.float32)
+    x[M - 1, 1234] = bad
+    y = torch.empty((M, N), dtype=torch.float32, device="cuda")
+    ctx.gemv(qtype, dev(b), N, K, dev(x), y, M=M)
+    got = host(y)
+    assert not np.isfinite(got[M - 1]).any()
+    if M > 1:
+        ref = oracle.qgemm_f64(b, qtype, N, K, x[: M - 1])
+        assert rel_fro(got[: M - 1], ref) < 1e-5
+    ctx.sync_status()

@@ -213,13 +213,18 @@ __global__ void __launch_bounds__(GI_THREADS, 1) gemv_imma_kernel(const __grid_c
                          fmaxf(fmaxf(fabsf(v1.x), fabsf(v1.y)), fmaxf(fabsf(v1.z), fabsf(v1.w))));
 #pragma unroll
         for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        // a non-finite x element makes the chunk's scale NaN, so y comes out
+        // non-finite as the reference's fp32 sum does; its planes are zero
+        const bool nonfin = __any_sync(0xffffffffu, !(isfinite(v0.x) && isfinite(v0.y) && isfinite(v0.z) &&
+                                                      isfinite(v0.w) && isfinite(v1.x) && isfinite(v1.y) &&
+                                                      isfinite(v1.z) && isfinite(v1.w)));
         int s = 0;
         if (mx > 0.0f) {
             // mx in [2^(E-127), 2^(E-126)): mx * 2^s in [2^21, 2^22); s >= -106 for finite mx
             s = 148 - (int)((__float_as_uint(mx) >> 23) & 0xffu);
             if (s > 127) s = 127;
         }
-        const float up = __uint_as_float((uint32_t)(127 + s) << 23);
+        const float up = nonfin ? 0.0f : __uint_as_float((uint32_t)(127 + s) << 23);
         const float f[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
         uint32_t w0[2] = {0u, 0u}, w1[2] = {0u, 0u}, w2[2] = {0u, 0u};
         int s0 = 0, s1 = 0, s2 = 0;
@@ -241,7 +246,7 @@ __global__ void __launch_bounds__(GI_THREADS, 1) gemv_imma_kernel(const __grid_c
         *reinterpret_cast<uint2*>(xrow) = make_uint2(w0[0], w0[1]);
         *reinterpret_cast<uint2*>(xrow + a.XQ) = make_uint2(w1[0], w1[1]);
         *reinterpret_cast<uint2*>(xrow + 2 * a.XQ) = make_uint2(w2[0], w2[1]);
-        if (lane < 3) cs[c * 8 + 3 * m + lane] = ldexpf(1.0f, 16 - 8 * lane - s);
+        if (lane < 3) cs[c * 8 + 3 * m + lane] = nonfin ? __uint_as_float(0x7fc00000u) : ldexpf(1.0f, 16 - 8 * lane - s);
         if constexpr (T == QT_Q4_K || T == QT_Q5_K) {
             // x sums of each 32-element block (4 lanes), split S = hi * 128 + lo
 #pragma unroll

@@ -130,6 +130,7 @@ __global__ void __launch_bounds__(256) gw_xrec_kernel(const float* __restrict__ 
     int16_t* xs = reinterpret_cast<int16_t*>(r + (size_t)rows * (GW_XROW + 4));
     uint32_t w0[2] = {0u, 0u}, w1[2] = {0u, 0u}, w2[2] = {0u, 0u};
     int s0 = 0, s1 = 0, s2 = 0, s = 0;
+    bool nonfin = false;
     if (m < M) {
         const float4* src = reinterpret_cast<const float4*>(x + (size_t)m * ldx + c * 256 + 8 * lane);
         const float4 v0 = __ldg(src), v1 = __ldg(src + 1);
@@ -137,12 +138,16 @@ __global__ void __launch_bounds__(256) gw_xrec_kernel(const float* __restrict__ 
                          fmaxf(fmaxf(fabsf(v1.x), fabsf(v1.y)), fmaxf(fabsf(v1.z), fabsf(v1.w))));
 #pragma unroll
         for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        // a non-finite x element makes the chunk's scale NaN, so y comes out
+        // non-finite as the reference's fp32 sum does; its planes are zero
+        nonfin = __any_sync(0xffffffffu, !(isfinite(v0.x) && isfinite(v0.y) && isfinite(v0.z) && isfinite(v0.w) &&
+                                           isfinite(v1.x) && isfinite(v1.y) && isfinite(v1.z) && isfinite(v1.w)));
         if (mx > 0.0f) {
             // mx in [2^(E-127), 2^(E-126)): mx * 2^s in [2^21, 2^22); s >= -106 for finite mx
             s = 148 - (int)((__float_as_uint(mx) >> 23) & 0xffu);
             if (s > 127) s = 127;
         }
-        const float up = __uint_as_float((uint32_t)(127 + s) << 23);
+        const float up = nonfin ? 0.0f : __uint_as_float((uint32_t)(127 + s) << 23);
         const float f[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
@@ -162,7 +167,7 @@ __global__ void __launch_bounds__(256) gw_xrec_kernel(const float* __restrict__ 
     *reinterpret_cast<uint2*>(r + (size_t)(0 * toks + m) * GW_XROW + 8 * lane) = make_uint2(w0[0], w0[1]);
     *reinterpret_cast<uint2*>(r + (size_t)(1 * toks + m) * GW_XROW + 8 * lane) = make_uint2(w1[0], w1[1]);
     *reinterpret_cast<uint2*>(r + (size_t)(2 * toks + m) * GW_XROW + 8 * lane) = make_uint2(w2[0], w2[1]);
-    if (lane < 3) scl[lane * toks + m] = m < M ? ldexpf(1.0f, 16 - 8 * lane - s) : 0.0f;
+    if (lane < 3) scl[lane * toks + m] = m >= M ? 0.0f : nonfin ? __uint_as_float(0x7fc00000u) : ldexpf(1.0f, 16 - 8 * lane - s);
     // x sums of each 32-element block (4 lanes)
 #pragma unroll
     for (int o = 1; o <= 2; o <<= 1) {
