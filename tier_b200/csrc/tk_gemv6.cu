@@ -27,7 +27,8 @@
 //    barrier and fixed-order reduction overlap the other team's MMAs.  At the
 //    end of a row group the three plane columns of each token are summed with
 //    two warp shuffles.
-// The result agrees with fp64 to ~1e-7 relative.  x must be finite.
+// The result agrees with fp64 to ~1e-7 relative.  A non-finite x element makes
+// its token's y non-finite (the chunk's scale is NaN).
 #include "tk_device.cuh"
 #include "tk_internal.h"
 

@@ -25,7 +25,8 @@
 //    one per 32-element sub-block, times its 6-bit sc in int32, minus m times
 //    the block's x sum, then d and dmin in fp32; Q6_K one m16n8k16 MMA per
 //    16-element sub-block, times its int8 sc, then d.
-// Agreement with fp64 is ~1e-7 relative.  x must be finite.
+// Agreement with fp64 is ~1e-7 relative.  A non-finite x element makes its
+// token's y non-finite (the chunk's scale is NaN).
 #include "tk_device.cuh"
 #include "tk_internal.h"
 
