@@ -705,12 +705,31 @@ def run_c5(args):
                 dys = {n: torch.randn(M, n, device="cuda", generator=g) for n in {n for n, _ in shapes}}
                 dxs = {k: torch.empty(M, k, device="cuda") for k in {k for _, k in shapes}}
 
+            # decode: the projections that read the same x (q/k/v, gate/up) go in one
+            # tk_gemv_multi launch when their block types match
+            yp = [torch.empty(M, n, device="cuda") for n, _ in shapes] if decode else None
+
             def fn():
                 for ws in layers:
+                    if decode and kind != "fp16x3":
+                        for grp in ((0, 1, 2), (3,), (4, 5), (6,)):
+                            runs = []
+                            for j in grp:
+                                if runs and ws[runs[-1][-1]][1] == ws[j][1]:
+                                    runs[-1].append(j)
+                                else:
+                                    runs.append([j])
+                            for run in runs:
+                                qt, k = ws[run[0]][1], shapes[run[0]][1]
+                                if len(run) == 1:
+                                    j = run[0]
+                                    ctx.gemv(qt | tk.WFROZEN, ws[j][2], shapes[j][0], k, xs[k], yp[j], M=M)
+                                else:
+                                    ctx.gemv_multi(qt | tk.WFROZEN, [ws[j][2] for j in run], [shapes[j][0] for j in run],
+                                                   [yp[j] for j in run], k, xs[k], M=M)
+                        continue
                     for (w, qt, data), (n, k) in zip(ws, shapes):
-                        if decode and qt != tk.F16X2:
-                            ctx.gemv(qt | tk.WFROZEN, data, n, k, xs[k], ys[n], M=M)
-                        elif decode:
+                        if decode:
                             ctx.linear(w, xs[k], M, ys[n])
                         else:
                             ctx.linear(w, xs[k], M, ys[n])
@@ -731,7 +750,8 @@ def run_c5(args):
             line = {"metric": "C5 40-layer sweep", "kind": kind, "M": M, "ms_per_step": ms, "steps": steps,
                     "n_gpus": 1, "weight_bytes": wbytes, "clocks": clk,
                     "config": {"workload": f"C5 40 layers x 7 projections (12B-class), {kind} weights, M={M}, " +
-                               (("forward GEMV (decode), a step's launches replayed as one CUDA graph" if graph
+                               (("forward GEMV (decode; q/k/v and gate/up of one type share a tk_gemv_multi "
+                                 "launch), a step's launches replayed as one CUDA graph" if graph
                                  else "forward (decode) through tk_linear_fwd, eager launches")
                                 if decode else "forward + dX, fp32 activations, x3 products")}}
             if decode:

@@ -181,6 +181,18 @@ const char *tk_qtype_name(int qtype);
  * as dispatched by chat_lin (tier/tier.cpp:2351-2378). */
 tk_status tk_gemv(tk_ctx *ctx, int qtype, const void *W, size_t row_bytes, int N, int K,
                   const float *x, int ldx, int M, float *y, int ldy, void *stream);
+/* Several frozen weights that share one x, in one launch (no counterpart in
+ * the reference, which calls gemv_q once per projection): for i < nseg,
+ * y_i[m, n] = sum_k W_i(n, k) x[m, k], n < rows[i], with y_i at y[i] and row
+ * stride ldy[i].  All W_i have the same qtype (TK_WFROZEN may be OR-ed in),
+ * K and row_bytes -- a decoder layer's q/k/v, or gate/up.  x is staged once
+ * and the per-launch fixed cost is paid once.  With 1-2 tokens and a Q8_0 /
+ * Q4_K / Q5_K / Q6_K weight the rows run in one integer-MMA launch; otherwise
+ * each W_i goes through tk_gemv in turn (same results). */
+enum { TK_GEMV_MAXSEG = 4 };
+tk_status tk_gemv_multi(tk_ctx *ctx, int qtype, int nseg, const void *const *W, const int *rows,
+                        float *const *y, const int *ldy, size_t row_bytes, int K, const float *x,
+                        int ldx, int M, void *stream);
 
 /* ---- linear layers (tensor cores) --------------------------------------- */
 /* Y[M, N] = X[M, K] . W^T (+ Y if beta == 1).  X dtype per x_dtype with row

@@ -168,3 +168,27 @@ def test_gemv_nonfinite_x(ctx, oracle, qtype, M, bad):
         ref = oracle.qgemm_f64(b, qtype, N, K, x[: M - 1])
         assert rel_fro(got[: M - 1], ref) < 1e-5
     ctx.sync_status()
+
+
+@pytest.mark.parametrize("qtype", [8, 12, 14])
+@pytest.mark.parametrize("M", [1, 2, 5])
+def test_gemv_multi_segments(ctx, oracle, qtype, M):
+    """tk_gemv_multi: weights sharing x (q/k/v-like row counts, boundaries
+    inside row groups and SM ranges) give each weight's own GEMV result; 5
+    tokens take the per-weight path."""
+    import torch
+    import tier_b200 as tk
+    rng = np.random.default_rng(40 + qtype + M)
+    K = 4096
+    rows = [700, 130, 129]
+    bs = [blocks_for(rng, qtype, n, K) for n in rows]
+    x = rng.standard_normal((M, K)).astype(np.float32)
+    ys = [torch.full((M, n), float("nan"), device="cuda") for n in rows]
+    n0 = ctx.launches()
+    ctx.gemv_multi(qtype | tk.WFROZEN, [dev(b) for b in bs], rows, ys, K, dev(x), M=M)
+    if M <= 2:
+        assert ctx.launches() - n0 == 1
+    for b, n, y in zip(bs, rows, ys):
+        ref = oracle.qgemm_f64(b, qtype, n, K, x)
+        assert rel_fro(host(y), ref) < 1e-5
+    ctx.sync_status()

@@ -73,6 +73,7 @@ SIGNATURES = [
     ("tk_row_bytes", _SZ, [_I, _I]),
     ("tk_dequant", _I, [_P, _I, _P, _SZ, _I, _I, _I, _I, _P, _P]),
     ("tk_gemv", _I, [_P, _I, _P, _SZ, _I, _I, _P, _I, _I, _P, _I, _P]),
+    ("tk_gemv_multi", _I, [_P, _I, _I, _P, _P, _P, _P, _SZ, _I, _P, _I, _I, _P]),
     ("tk_linear_fwd", _I, [_P, ctypes.POINTER(Weight), _P, _I, _I, _I, _P, _I, _F, _I, _P]),
     ("tk_linear_dx", _I, [_P, ctypes.POINTER(Weight), _P, _I, _I, _I, _P, _I, _F, _I, _P]),
     ("tk_linear_fwd_noalloc", _I, [_P, ctypes.POINTER(Weight), _P, _I, _I, _I, _P, _I, _F, _I, _P]),
@@ -197,6 +198,19 @@ class Context:
         _check(self.lib.tk_gemv(self.h, qtype, _ptr(W), rb, N, K, _ptr(x), ldx or K, M, _ptr(y), ldy or N,
                                 _stream(stream)))
         return y
+
+    def gemv_multi(self, qtype, Ws, rows, ys, K, x, M=1, ldx=None, row_bytes_=None, stream=None):
+        """ys[i][:M, :rows[i]] = x . Ws[i]^T for weights that share x (tk_gemv_multi):
+        one launch for a layer's q/k/v or gate/up."""
+        n = len(Ws)
+        rb = row_bytes_ if row_bytes_ is not None else row_bytes(qtype & ~WFROZEN, K)
+        wp = (ctypes.c_void_p * n)(*[w.data_ptr() for w in Ws])
+        rp = (ctypes.c_int * n)(*rows)
+        yp = (ctypes.c_void_p * n)(*[y.data_ptr() for y in ys])
+        lp = (ctypes.c_int * n)(*[y.stride(0) for y in ys])
+        _check(self.lib.tk_gemv_multi(self.h, qtype, n, wp, rp, yp, lp, rb, K, _ptr(x), ldx or K, M,
+                                      _stream(stream)))
+        return ys
 
     def linear(self, W: Weight, X, M, Y, x_dtype=DT_F32, ldx=None, ldy=None, beta=0.0, products=X3_AUTO,
                stream=None):

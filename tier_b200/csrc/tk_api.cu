@@ -449,6 +449,34 @@ tk_status tk_gemv(tk_ctx* ctx, int qtype, const void* W, size_t row_bytes, int N
     return launch_gemv(ctx, qtype, W, row_bytes, N, K, x, ldx, M, y, ldy, static_cast<cudaStream_t>(stream), frozen);
 }
 
+tk_status tk_gemv_multi(tk_ctx* ctx, int qtype, int nseg, const void* const* W, const int* rows, float* const* y,
+                        const int* ldy, size_t row_bytes, int K, const float* x, int ldx, int M, void* stream) {
+    if (!ctx) return fail(TK_ERR_INVALID, "tk_gemv_multi: null context");
+    if (nseg < 1 || nseg > TK_GEMV_MAXSEG || !W || !rows || !y || !ldy)
+        return fail(TK_ERR_INVALID, "tk_gemv_multi: nseg must be 1..TK_GEMV_MAXSEG with W, rows, y, ldy given");
+    long total = 0;
+    bool aligned = true;
+    for (int i = 0; i < nseg; ++i) {
+        if (!W[i] || !y[i] || rows[i] <= 0 || ldy[i] < rows[i])
+            return fail(TK_ERR_INVALID, "tk_gemv_multi: segment " + std::to_string(i) + ": null pointer or bad rows/ldy");
+        total += rows[i];
+        aligned = aligned && aligned16(W[i]);
+    }
+    if (total > (1L << 30)) return fail(TK_ERR_INVALID, "tk_gemv_multi: too many rows");
+    const bool frozen = (qtype & TK_WFROZEN) != 0;
+    const int t = qtype & ~TK_WFROZEN;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (M >= 1 && M <= 2 && aligned && row_bytes % 16 == 0 && K > 0 && K % 256 == 0 && x && ldx >= K &&
+        ldx % 4 == 0 && aligned16(x) && tk_row_bytes(t, K) != 0 && row_bytes >= tk_row_bytes(t, K) &&
+        gemv_imma_multi_ok(t, row_bytes, K, M))
+        return launch_gemv_imma_multi(ctx, t, nseg, W, rows, y, ldy, row_bytes, K, x, ldx, M, frozen, s);
+    for (int i = 0; i < nseg; ++i) {
+        tk_status st = tk_gemv(ctx, qtype, W[i], row_bytes, rows[i], K, x, ldx, M, y[i], ldy[i], stream);
+        if (st != TK_OK) return st;
+    }
+    return TK_OK;
+}
+
 tk_status tk_linear_fwd(tk_ctx* ctx, const tk_weight* W, const void* X, int x_dtype, int M, int ldx, float* Y, int ldy,
                         float beta, int products, void* stream) {
     return linear(ctx, W, X, x_dtype, M, ldx, Y, ldy, beta, products, static_cast<cudaStream_t>(stream), false);

@@ -57,7 +57,22 @@ struct GiArgs {
     int XQ;           // x plane row stride in bytes
     int frozen;
     int* status;
+    // several weights sharing x (tk_gemv_multi): rows [seg_end[i-1], seg_end[i])
+    // are rows of Ws[i] with outputs ys[i]; nseg == 1 uses W, y, ldy
+    int nseg;
+    int seg_end[TK_GEMV_MAXSEG];
+    const uint8_t* Ws[TK_GEMV_MAXSEG];
+    float* ys[TK_GEMV_MAXSEG];
+    int ldys[TK_GEMV_MAXSEG];
 };
+
+// segment of a row of the concatenated weights and the row within it
+__device__ __forceinline__ int gi_seg(const GiArgs& a, int row, int& local) {
+    int sg = 0;
+    while (sg + 1 < a.nseg && row >= a.seg_end[sg]) ++sg;
+    local = row - (sg ? a.seg_end[sg - 1] : 0);
+    return sg;
+}
 
 __device__ __forceinline__ uint32_t i_lds16(uint32_t a) {
     uint16_t v;
@@ -182,8 +197,14 @@ __global__ void __launch_bounds__(GI_THREADS, 1) gemv_imma_kernel(const __grid_c
                               a.W + (size_t)(row0 + 4 * lane) * a.rb, (uint32_t)nr * a.kcb, &full[slot]);
                 }
             } else if (lane < nv) {
-                bulk_load(ring + (size_t)slot * slot_bytes + (size_t)lane * a.RS,
-                          a.W + (size_t)(row0 + lane) * a.rb + (size_t)c * a.kcb, a.kcb, &full[slot]);
+                const uint8_t* src = a.W + (size_t)(row0 + lane) * a.rb;
+                if (a.nseg > 1) {
+                    int lr;
+                    const int sg = gi_seg(a, row0 + lane, lr);
+                    src = a.Ws[sg] + (size_t)lr * a.rb;
+                }
+                bulk_load(ring + (size_t)slot * slot_bytes + (size_t)lane * a.RS, src + (size_t)c * a.kcb, a.kcb,
+                          &full[slot]);
             }
             issued = s + 1;
         }
@@ -496,7 +517,13 @@ __global__ void __launch_bounds__(GI_THREADS, 1) gemv_imma_kernel(const __grid_c
                 float sum = 0.0f;
 #pragma unroll
                 for (int w = 0; w < TWn; ++w) sum += pb[w * 128 + r * 8 + m];
-                a.y[(size_t)m * a.ldy + row] = sum;
+                if (a.nseg > 1) {
+                    int lr;
+                    const int sg = gi_seg(a, row, lr);
+                    a.ys[sg][(size_t)m * a.ldys[sg] + lr] = sum;
+                } else {
+                    a.y[(size_t)m * a.ldy + row] = sum;
+                }
             }
         }
         // the team's next group writes the other partial buffer; the team
@@ -516,7 +543,10 @@ static int gi_block_elems(int t) { return t == QT_Q8_0 ? 32 : 256; }
 
 // Plan for a given team count and number of K-chunks: false if the x planes
 // and two slots per team ring (one if `one_ok`) do not fit.
-static bool gi_plan_for(int t, int N, int K, size_t rb, int M, int grid, int teams, int nc, bool one_ok, GiPlan& p) {
+// `whole`: a group's 16 rows are contiguous in one weight (one matrix, not
+// segments), so a whole-row slot can be four 4-row copies.
+static bool gi_plan_for(int t, int N, int K, size_t rb, int M, int grid, int teams, int nc, bool one_ok, bool whole,
+                        GiPlan& p) {
     if (K % 256 || M < 1 || M > 2 || (K / 256) % nc) return false;
     const int rows_blk = (N + grid - 1) / grid;
     const int ngroups = (rows_blk + 15) / 16;
@@ -532,7 +562,7 @@ static bool gi_plan_for(int t, int N, int K, size_t rb, int M, int grid, int tea
     uint32_t RS = (kcb + 15u) & ~15u;
     while (RS % 128u != rs_mod) RS += 16u;
     // whole rows with no gap between them: four copies of 4 rows per slot
-    const uint32_t CS = (nc == 1 && rb == kcb) ? ((4u * kcb + 127u) & ~127u) + 32u : 0u;
+    const uint32_t CS = (whole && nc == 1 && rb == kcb) ? ((4u * kcb + 127u) & ~127u) + 32u : 0u;
     const size_t slot = CS ? 4u * (size_t)CS : 16u * (size_t)RS;
     int nsl = (int)((GI_SMEM_MAX - fixed) / slot) / teams;
     if (nsl > GI_MAXSLOTS / teams) nsl = GI_MAXSLOTS / teams;
@@ -554,12 +584,12 @@ static bool gi_plan_for(int t, int N, int K, size_t rb, int M, int grid, int tea
 // Whole rows (one K-chunk) when they fit, with two consumer teams and two
 // slots per team, else one; otherwise one team and the fewest K-chunks that
 // give two slots.  Fewer, larger bulk copies stream faster.
-static bool gi_plan(int t, int N, int K, size_t rb, int M, int grid, GiPlan& p) {
-    if (gi_plan_for(t, N, K, rb, M, grid, 2, 1, false, p)) return true;
-    if (gi_plan_for(t, N, K, rb, M, grid, 2, 1, true, p)) return true;
+static bool gi_plan(int t, int N, int K, size_t rb, int M, int grid, GiPlan& p, bool whole = true) {
+    if (gi_plan_for(t, N, K, rb, M, grid, 2, 1, false, whole, p)) return true;
+    if (gi_plan_for(t, N, K, rb, M, grid, 2, 1, true, whole, p)) return true;
     const int units = K / 256;
     for (int nc = 2; nc <= units; ++nc)
-        if (gi_plan_for(t, N, K, rb, M, grid, 1, nc, false, p)) return true;
+        if (gi_plan_for(t, N, K, rb, M, grid, 1, nc, false, whole, p)) return true;
     return false;
 }
 
@@ -570,12 +600,21 @@ bool gemv_imma_ok(int t, size_t rb, int K, int M) {
     return gi_plan(t, 148 * 64, K, rb, M, 148, p);
 }
 
+struct GiSegs {
+    int n;
+    const void* const* W;
+    const int* rows;
+    float* const* y;
+    const int* ldy;
+};
+
 template <int T>
 static tk_status go_imma(tk_ctx* ctx, const uint8_t* W, size_t rb, int N, int K, int M, const float* x, int ldx,
-                         float* y, int ldy, bool frozen, cudaStream_t s) {
+                         float* y, int ldy, bool frozen, cudaStream_t s, const GiSegs* seg = nullptr) {
     const int grid = ctx->num_sms < N ? ctx->num_sms : N;
     GiPlan p;
-    if (!gi_plan(T, N, K, rb, M, grid, p)) return fail(TK_ERR_UNSUPPORTED, "gemv imma: shape does not fit shared memory");
+    if (!gi_plan(T, N, K, rb, M, grid, p, seg == nullptr))
+        return fail(TK_ERR_UNSUPPORTED, "gemv imma: shape does not fit shared memory");
     auto kern = gemv_imma_kernel<T>;
     static bool attr_set = false;   // per instantiation
     if (!attr_set) {
@@ -588,6 +627,18 @@ static tk_status go_imma(tk_ctx* ctx, const uint8_t* W, size_t rb, int N, int K,
     a.KC = p.KC; a.nchunks = p.nchunks; a.kcb = p.kcb; a.RS = p.RS; a.CS = p.CS; a.nslots = p.nslots; a.teams = p.teams; a.XQ = p.XQ;
     a.frozen = frozen;
     a.status = ctx->status;
+    a.nseg = 1;
+    if (seg) {
+        a.nseg = seg->n;
+        int end = 0;
+        for (int i = 0; i < seg->n; ++i) {
+            end += seg->rows[i];
+            a.seg_end[i] = end;
+            a.Ws[i] = static_cast<const uint8_t*>(seg->W[i]);
+            a.ys[i] = seg->y[i];
+            a.ldys[i] = seg->ldy[i];
+        }
+    }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid, 1, 1);
     cfg.blockDim = dim3(GI_THREADS, 1, 1);
@@ -612,6 +663,27 @@ tk_status launch_gemv_imma(tk_ctx* ctx, int t, const void* Wv, size_t rb, int N,
     if (t == QT_Q4_K) return go_imma<QT_Q4_K>(ctx, W, rb, N, K, M, x, ldx, y, ldy, frozen, s);
     if (t == QT_Q5_K) return go_imma<QT_Q5_K>(ctx, W, rb, N, K, M, x, ldx, y, ldy, frozen, s);
     if (t == QT_Q6_K) return go_imma<QT_Q6_K>(ctx, W, rb, N, K, M, x, ldx, y, ldy, frozen, s);
+    return fail(TK_ERR_UNSUPPORTED, "gemv imma: type");
+}
+
+bool gemv_imma_multi_ok(int t, size_t rb, int K, int M) {
+    if (t != QT_Q8_0 && t != QT_Q4_K && t != QT_Q5_K && t != QT_Q6_K) return false;
+    if (M < 1 || M > 2 || rb % 16 || K % 256) return false;
+    GiPlan p;
+    return gi_plan(t, 148 * 64, K, rb, M, 148, p, false);
+}
+
+tk_status launch_gemv_imma_multi(tk_ctx* ctx, int t, int nseg, const void* const* W, const int* rows, float* const* y,
+                                 const int* ldy, size_t rb, int K, const float* x, int ldx, int M, bool frozen,
+                                 cudaStream_t s) {
+    int N = 0;
+    for (int i = 0; i < nseg; ++i) N += rows[i];
+    const GiSegs seg{nseg, W, rows, y, ldy};
+    const uint8_t* W0 = static_cast<const uint8_t*>(W[0]);
+    if (t == QT_Q8_0) return go_imma<QT_Q8_0>(ctx, W0, rb, N, K, M, x, ldx, y[0], ldy[0], frozen, s, &seg);
+    if (t == QT_Q4_K) return go_imma<QT_Q4_K>(ctx, W0, rb, N, K, M, x, ldx, y[0], ldy[0], frozen, s, &seg);
+    if (t == QT_Q5_K) return go_imma<QT_Q5_K>(ctx, W0, rb, N, K, M, x, ldx, y[0], ldy[0], frozen, s, &seg);
+    if (t == QT_Q6_K) return go_imma<QT_Q6_K>(ctx, W0, rb, N, K, M, x, ldx, y[0], ldy[0], frozen, s, &seg);
     return fail(TK_ERR_UNSUPPORTED, "gemv imma: type");
 }
 

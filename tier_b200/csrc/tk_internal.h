@@ -81,6 +81,10 @@ bool gemv_mma_ok(int qtype, size_t rb, int K, int M);
 tk_status launch_gemv_mma(tk_ctx* ctx, int qtype, const void* W, size_t rb, int N, int K, const float* x, int ldx,
                           int M, float* y, int ldy, bool frozen, cudaStream_t s);
 bool gemv_imma_ok(int qtype, size_t rb, int K, int M);
+bool gemv_imma_multi_ok(int qtype, size_t rb, int K, int M);
+tk_status launch_gemv_imma_multi(tk_ctx* ctx, int qtype, int nseg, const void* const* W, const int* rows,
+                                 float* const* y, const int* ldy, size_t rb, int K, const float* x, int ldx, int M,
+                                 bool frozen, cudaStream_t s);
 bool gemv_wide_ok(int qtype, size_t rb, int K, int M);
 tk_status launch_gemv_wide(tk_ctx* ctx, int qtype, const void* W, size_t rb, int N, int K, const float* x, int ldx,
                            int M, float* y, int ldy, cudaStream_t s);
