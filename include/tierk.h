@@ -242,7 +242,7 @@ tk_status tk_split3(tk_ctx *ctx, const float *x, size_t n, uint16_t *h, uint16_t
  * dX GEMM: every finished tile is stored into its owner's receive buffer
  * (peer memory over NVLink) while the remaining tiles compute; the owner adds
  * the world contributions in rank order (deterministic).  No counterpart in
- * the reference (it runs on one GPU; SURVEY-style row sharding is new).
+ * the reference (it runs on one GPU; sharding W by output rows is new here).
  *
  * Set-up, once per context: tk_comm_init allocates this rank's buffer
  * (4 KiB + 2 * recv_bytes; recv_bytes >= M * K * 4 for every later call) and
