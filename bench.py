@@ -147,16 +147,19 @@ def run_reference(args):
 
 
 def calibrate_rows(eng, Wq, X, dY, threads, target_s):
-    """Rows of the workload that take about target_s on the host: a 16-row
-    probe (dominated by fixed costs) sizes a ~1 s probe, which sizes the run."""
+    """Rows of the workload that take about target_s on the host.  The
+    per-row cost falls as fixed costs amortise, so probes grow (at most 8x at
+    a time) until one takes a quarter of the target; the run is sized from it."""
     rows = 16
-    for goal in (1.0, target_s):
+    while True:
         t0 = time.perf_counter()
         eng.qgemm_fwd(Wq, 12, 0, rows, K_IN, X, threads)
         eng.qgemm_dx(Wq, 12, 0, rows, K_IN, dY[:, :rows], threads)
         dt = max(time.perf_counter() - t0, 1e-3)
-        rows = max(16, min(N_OUT, int(rows * min(goal, target_s) / dt) // 16 * 16))
-    return rows
+        want = max(16, min(N_OUT, int(rows * target_s / dt) // 16 * 16))
+        if dt >= target_s / 4 or rows == N_OUT:
+            return want
+        rows = max(16, min(N_OUT, want, rows * 8))
 
 
 def cpu_baseline(Wq, X, dY, seconds):
