@@ -51,6 +51,20 @@ def test_null_context_is_rejected_not_crashed(lib):
     assert b"null context" in lib.tk_last_error_string()
     st = lib.tk_gemv(None, 8, None, 34, 1, 32, None, 32, 1, None, 1, None)
     assert st == 1
+    st = lib.tk_gemv_multi(None, 8, 2, None, None, None, None, 34, 32, None, 32, 1, None)
+    assert st == 1 and b"null context" in lib.tk_last_error_string()
+
+
+def test_flag_values_match_header():
+    """The Python flag constants equal the header's enums."""
+    import tier_b200 as tk
+    text = (ROOT / "include" / "tierk.h").read_text()
+    for name, value in (("TK_QFUSED", tk.QFUSED), ("TK_WFROZEN", tk.WFROZEN), ("TK_WREUSE", tk.WREUSE),
+                        ("TK_IPC_HANDLE_BYTES", tk.IPC_HANDLE_BYTES)):
+        m = re.search(rf"\b{name}\s*=\s*(0x[0-9a-fA-F]+|\d+)", text)
+        assert m and int(m.group(1), 0) == value, name
+    flags = [tk.QFUSED, tk.WREUSE]                  # OR-ed into `products` with the product set (0..4)
+    assert all(f & 0xff == 0 for f in flags) and tk.QFUSED & tk.WREUSE == 0
 
 
 def test_init_without_gpu_reports_error(lib):
