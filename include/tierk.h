@@ -47,6 +47,9 @@ enum {
     TK_F32 = 0, TK_F16 = 1, TK_Q4_0 = 2, TK_Q4_1 = 3, TK_Q5_0 = 6, TK_Q5_1 = 7,
     TK_Q8_0 = 8, TK_Q2_K = 10, TK_Q3_K = 11, TK_Q4_K = 12, TK_Q5_K = 13,
     TK_Q6_K = 14, TK_BF16 = 30,
+    /* types whose levels come from a 16-entry list or from base-3 digits */
+    TK_IQ4_NL = 20, TK_IQ4_XS = 23, TK_TQ1_0 = 34, TK_TQ2_0 = 35, TK_MXFP4 = 39,
+    TK_NF4 = 200, TK_FP4 = 201,
     /* fp32 weight stored as two fp16 planes hi = f16(W*2^s), lo = f16(W*2^s - hi);
        plane lo starts rows*row_bytes bytes after plane hi (see tk_weight_split_f32) */
     TK_F16X2 = 100
@@ -129,7 +132,8 @@ size_t tk_row_bytes(int qtype, int cols);
 /* out[r, c] = value of element c of row r0+r, for r < nrows, as fp32, fp16
  * (round-to-nearest-even of the fp32 value) or bf16.  Bit-exact with
  * q_val / tier_fp16(q_val).  Replaces dq_launch / dq_k (tier/tier.cpp:294-298).
- * Supported qtype: all TK_* block types except TK_F16X2. */
+ * Supported qtype: all TK_* block types except TK_F16X2 (the reference's
+ * IQ1/IQ2/IQ3 grid types are not among them). */
 tk_status tk_dequant(tk_ctx *ctx, int qtype, const void *blocks, size_t row_bytes,
                      int r0, int nrows, int cols, int out_dtype, void *out, void *stream);
 
@@ -169,7 +173,8 @@ const char *tk_qtype_name(int qtype);
 
 /* ---- decode GEMV (M = 1..16) -------------------------------------------- */
 /* y[m, n] = sum_k W(n, k) * x[m, k] for m < M, n < N, fp32 x and y.
- * qtype: TK_Q8_0, TK_Q4_K, TK_Q5_K, TK_Q6_K, TK_Q4_0, TK_F16, TK_BF16, TK_F32,
+ * qtype: any type tk_dequant takes (the reference's gemv_q decodes every type
+ * through q_val; Q8_0 / Q4_K / Q5_K / Q6_K have the fast kernels),
  * optionally OR TK_WFROZEN: the caller guarantees that no kernel enqueued
  * earlier on the stream writes W (frozen weights), so the Q8_0 / Q4_K / Q5_K
  * kernel may start fetching W before the preceding kernel has finished

@@ -7,7 +7,9 @@
  * checker or the timed CPU baseline.
  *
  * It restates, in plain C, the reference's arithmetic for the path:
- *   - block formats and scalar dequant       tier/quant.h:20-121 (q_val)
+ *   - block formats and scalar dequant       tier/quant.h:20-121 (q_val): the
+ *     legacy and K-quant types plus IQ4_NL, IQ4_XS, MXFP4, NF4, FP4, TQ1_0,
+ *     TQ2_0; not the IQ1/IQ2/IQ3 grid types
  *   - fp16 <-> fp32 software conversion      tier/quant.h:37-42, tier/gpu_compat.h:151-190
  *   - decode GEMV summation order            tier/tier.cpp:300-306 (gemv_q), 2261-2268 (gemv<T>)
  *   - x3 activation split                    tier/tier.cpp:869-870 (split3_fp_k)
@@ -30,7 +32,9 @@
 enum {
     TKO_F32 = 0, TKO_F16 = 1, TKO_Q4_0 = 2, TKO_Q4_1 = 3, TKO_Q5_0 = 6, TKO_Q5_1 = 7,
     TKO_Q8_0 = 8, TKO_Q2_K = 10, TKO_Q3_K = 11, TKO_Q4_K = 12, TKO_Q5_K = 13,
-    TKO_Q6_K = 14, TKO_BF16 = 30
+    TKO_Q6_K = 14, TKO_BF16 = 30,
+    TKO_IQ4_NL = 20, TKO_IQ4_XS = 23, TKO_TQ1_0 = 34, TKO_TQ2_0 = 35, TKO_MXFP4 = 39,
+    TKO_NF4 = 200, TKO_FP4 = 201
 };
 
 /* (elements per block, bytes per block) -- tier/quant.h:25-29 */
@@ -51,6 +55,13 @@ int tko_block_geom(int type, int *elems, int *bytes)
     case TKO_Q4_K: e = 256; b = 144; break;
     case TKO_Q5_K: e = 256; b = 176; break;
     case TKO_Q6_K: e = 256; b = 210; break;
+    case TKO_IQ4_NL: e = 32; b = 18; break;
+    case TKO_MXFP4: e = 32;  b = 17;  break;
+    case TKO_NF4:  e = 64;  b = 36;  break;
+    case TKO_FP4:  e = 64;  b = 36;  break;
+    case TKO_IQ4_XS: e = 256; b = 136; break;
+    case TKO_TQ1_0: e = 256; b = 54; break;
+    case TKO_TQ2_0: e = 256; b = 66; break;
     default: return 0;
     }
     if (elems) *elems = e;
@@ -146,8 +157,46 @@ static void k_scale_min(int j, const uint8_t *s, int *sc, int *mn)
 
 /* One weight value, bit-exact with tier/quant.h:59-121 (q_val) for the
  * non-table block types. Each product and difference rounds to fp32. */
+/* 16-level lists of the table types (tier/quant.h:51-57; tier/quant_tables.h
+ * qt_kv_iq4, qt_kv_mxfp4): IQ4 non-linear levels, MXFP4 doubled e2m1 levels,
+ * QLoRA NormalFloat4 quantiles, bitsandbytes FP4 magnitudes / 12. */
+static const int kv_iq4[16] = {-127, -104, -83, -65, -49, -35, -22, -10, 1, 13, 25, 38, 53, 69, 89, 113};
+static const int kv_mxfp4[16] = {0, 1, 2, 3, 4, 6, 8, 12, 0, -1, -2, -3, -4, -6, -8, -12};
+static const float kv_nf4[16] = {
+    -1.0f, -0.6961928009986877f, -0.5250730514526367f, -0.39491748809814453f, -0.28444138169288635f,
+    -0.18477343022823334f, -0.09105003625154495f, 0.0f, 0.07958029955625534f, 0.16093020141124725f,
+    0.24611230194568634f, 0.33791524171829224f, 0.44070982933044434f, 0.5626170039176941f,
+    0.7229568362236023f, 1.0f};
+static float fp4_level(int v)
+{
+    static const float m[8] = {0.0f, 0.0625f, 8.0f, 12.0f, 4.0f, 6.0f, 2.0f, 3.0f};
+    float a = m[v % 8] / 12.0f;
+    return v >= 8 ? -a : a;
+}
+
+/* element i of a 32-element block of 16 nibble bytes: low nibbles first, then high */
+static int nib32(const uint8_t *qs, int i) { return (qs[i % 16] >> (i < 16 ? 0 : 4)) & 15; }
+
 float tko_q_val(const uint8_t *row, int type, int col)
 {
+    switch (type) {
+    case TKO_IQ4_NL: { /* [d f16][16 B]: d * kv_iq4[q] (tier/quant.h:69) */
+        const uint8_t *b = row + (size_t)(col / 32) * 18;
+        return blk_d(b) * (float)kv_iq4[nib32(b + 2, col % 32)];
+    }
+    case TKO_MXFP4: { /* [e][16 B]: 2^(e-128) * kv_mxfp4[q] (tier/quant.h:70-71) */
+        const uint8_t *b = row + (size_t)(col / 32) * 17;
+        float scale = ldexpf(1.0f, (int)b[0] - 128);   /* exact, subnormal for e < 2 */
+        return scale * (float)kv_mxfp4[nib32(b + 1, col % 32)];
+    }
+    case TKO_NF4: case TKO_FP4: { /* [absmax f32][32 B], element 2k high nibble, 2k+1 low (tier/quant.h:72-73) */
+        const uint8_t *b = row + (size_t)(col / 64) * 36;
+        int i = col % 64, y = b[4 + i / 2], q = (i % 2) ? (y & 15) : (y >> 4);
+        float a = bits_f32(ld32(b));
+        return (type == TKO_NF4 ? kv_nf4[q] : fp4_level(q)) * a;
+    }
+    default: break;
+    }
     switch (type) {
     case TKO_F32:  return bits_f32(ld32(row + (size_t)col * 4));
     case TKO_F16:  return tko_h2f(ld16(row + (size_t)col * 2));
@@ -237,6 +286,31 @@ float tko_q_val(const uint8_t *row, int type, int col)
         int q = (int)(int8_t)(uint8_t)(ql | (qh << 4)) - 32;
         float a = blk_d(b + 208) * (float)(int8_t)b[192 + i / 16];
         return a * (float)q;
+    }
+    case TKO_IQ4_XS: { /* [d f16][sh u16][sl 4 B][qs 128 B]: (d*sc) * kv_iq4[q] (tier/quant.h:91-93) */
+        const uint8_t *b = row + (size_t)(col / 256) * 136;
+        int j = i / 32;
+        int lo = (b[4 + j / 2] >> (j % 2 ? 4 : 0)) & 15, hi = (ld16(b + 2) >> (2 * j)) & 3;
+        int sc = lo + 16 * hi - 32;
+        float a = blk_d(b) * (float)sc;
+        return a * (float)kv_iq4[nib32(b + 8 + 16 * j, i % 32)];
+    }
+    case TKO_TQ2_0: { /* [qs 64 B][d f16]: four 2-bit codes per byte, d*(c-1) (tier/quant.h:116) */
+        const uint8_t *b = row + (size_t)(col / 256) * 66;
+        int c = (b[(i / 128) * 32 + i % 32] >> (2 * ((i % 128) / 32))) & 3;
+        return blk_d(b + 64) * (float)(c - 1);
+    }
+    case TKO_TQ1_0: { /* [qs 48 B][qh 4 B][d f16]: base-3 digits, d*(c-1) (tier/quant.h:117-119) */
+        const uint8_t *b = row + (size_t)(col / 256) * 54;
+        int byte, n;
+        if (i < 160) { byte = i % 32; n = i / 32; }
+        else if (i < 240) { byte = 32 + (i - 160) % 16; n = (i - 160) / 16; }
+        else { byte = 48 + (i - 240) % 4; n = (i - 240) / 4; }
+        unsigned p = 1;
+        for (int k = 0; k < n; ++k) p *= 3;
+        unsigned x = (b[byte] * p) % 256;
+        int c = (int)((x * 3) / 256);
+        return blk_d(b + 52) * (float)(c - 1);
     }
     default: break;
     }

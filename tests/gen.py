@@ -71,7 +71,24 @@ def random_blocks(rng, qtype, rows, cols, scale_offsets, block_bytes, block_elem
 
 
 SCALE_OFFSETS = {2: [0], 3: [0, 2], 6: [0], 7: [0, 2], 8: [0], 10: [80, 82], 11: [108], 12: [0, 2], 13: [0, 2],
-                 14: [208]}
+                 14: [208], 20: [0], 23: [0], 34: [52], 35: [64]}
+
+
+def mxfp4_blocks(rng, rows, cols):
+    """MXFP4 (tier/quant.h:70-71): E8M0 scale bytes 118..124 (2^-10..2^-4) so
+    the products stay well inside fp32 and fp16, random nibbles."""
+    nb = rows * cols // 32
+    b = rng.integers(0, 256, size=(nb, 17), dtype=np.uint8)
+    b[:, 0] = rng.integers(118, 125, size=nb, dtype=np.uint8)
+    return b.reshape(rows, -1)
+
+
+def absmax_blocks(rng, rows, cols):
+    """NF4 / FP4 (tier/quant.h:72-73): fp32 absmax per 64 elements, random nibbles."""
+    nb = rows * cols // 64
+    b = rng.integers(0, 256, size=(nb, 36), dtype=np.uint8)
+    b[:, 0:4] = np.abs(rng.standard_normal(nb) * 0.05).astype(np.float32).view(np.uint8).reshape(nb, 4)
+    return b.reshape(rows, -1)
 
 
 def blocks_for(rng, qtype, rows, cols):
@@ -90,6 +107,10 @@ def blocks_for(rng, qtype, rows, cols):
         return (x.view(np.uint32) >> 16).astype(np.uint16).view(np.uint8)
     if qtype == 0:
         return (rng.standard_normal((rows, cols)) * 0.02).astype(np.float32).view(np.uint8)
+    if qtype == 39:
+        return mxfp4_blocks(rng, rows, cols)
+    if qtype in (200, 201):
+        return absmax_blocks(rng, rows, cols)
     return random_blocks(rng, qtype, rows, cols, SCALE_OFFSETS[qtype], bb, be)
 
 

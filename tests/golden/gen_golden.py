@@ -12,7 +12,9 @@ Sources of truth recorded per fixture:
                        bit-for-bit against the reference's quant.h q_val built
                        in place (oracle/_ref/libtkref.so), plus the fp16-storage
                        values tier_fp16(q_val) the training path stores
-                       (tier/tier.cpp:294-296).
+                       (tier/tier.cpp:294-296).  NF4 and FP4 are tierlm's own
+                       types (no gguf-py type): their values come from the
+                       reference's quant.h alone.
   quantize_golden.npz  reference q_row bytes (tier/quant.h:201-204) for
                        Q8_0/Q4_K/Q5_K/Q6_K on seeded rows; Q8_0 also equals
                        gguf-py's quantizer (tier/check_quant.py:114).
@@ -66,7 +68,19 @@ TYPES = [
     (12, "Q4_K", 256, 144, [0, 2]),
     (13, "Q5_K", 256, 176, [0, 2]),
     (14, "Q6_K", 256, 210, [208]),
+    # table-level types (tier/quant.h:69-73, 91-93, 116-119); appended so the
+    # random stream of the types above is unchanged
+    (20, "IQ4_NL", 32, 18, [0]),
+    (23, "IQ4_XS", 256, 136, [0]),
+    (34, "TQ1_0", 256, 54, [52]),
+    (35, "TQ2_0", 256, 66, [64]),
+    (39, "MXFP4", 32, 17, []),
+    # tierlm's own 64-element types (tier/quant.h:23, 72-73): no gguf-py type,
+    # pinned to the reference's quant.h alone; fp32 absmax at byte 0
+    (200, "NF4", 64, 36, "f32"),
+    (201, "FP4", 64, 36, "f32"),
 ]
+GGUF_ONLY_REF = {"NF4", "FP4"}
 ROWS, COLS = 4, 512
 
 
@@ -75,7 +89,7 @@ def gen_dequant(ref):
     rng = np.random.default_rng(7)
     out = {}
     for code, name, be, bb, halfs in TYPES:
-        gt = getattr(constants.GGMLQuantizationType, name)
+        gt = getattr(constants.GGMLQuantizationType, name, None)
         if be == 1:
             if name == "F32":
                 x = rng.standard_normal(ROWS * COLS).astype(np.float32)
@@ -90,24 +104,32 @@ def gen_dequant(ref):
         else:
             nb = ROWS * COLS // be
             b = rng.integers(0, 256, size=(nb, bb), dtype=np.uint8)
-            for o in halfs:
-                h = (rng.standard_normal(nb) * 0.02).astype(np.float16).view(np.uint8).reshape(nb, 2)
-                b[:, o:o + 2] = h
+            if halfs == "f32":
+                a = np.abs(rng.standard_normal(nb) * 0.05).astype(np.float32).view(np.uint8).reshape(nb, 4)
+                b[:, 0:4] = a
+            else:
+                for o in halfs:
+                    h = (rng.standard_normal(nb) * 0.02).astype(np.float16).view(np.uint8).reshape(nb, 2)
+                    b[:, o:o + 2] = h
             b = b.reshape(ROWS, -1).copy()
-        want = quants.dequantize(b.reshape(-1), gt).reshape(ROWS, COLS).astype(np.float32)
         rb = ref.ref_row_bytes(code, COLS)
         assert rb == b.shape[1], (name, rb, b.shape)
         got = np.zeros((ROWS, COLS), np.float32)
         ref.ref_dequant(ptr(b), ctypes.c_size_t(rb), code, 0, ROWS, COLS, 0, ptr(got))
-        if not np.array_equal(got.view(np.uint32), want.view(np.uint32)):
-            sys.exit(f"{name}: reference quant.h disagrees with gguf-py -- not writing fixtures")
+        if name in GGUF_ONLY_REF:
+            want = got
+        else:
+            want = quants.dequantize(b.reshape(-1), gt).reshape(ROWS, COLS).astype(np.float32)
+            if not np.array_equal(got.view(np.uint32), want.view(np.uint32)):
+                sys.exit(f"{name}: reference quant.h disagrees with gguf-py -- not writing fixtures")
         f16 = np.zeros((ROWS, COLS), np.uint16)
         ref.ref_dequant(ptr(b), ctypes.c_size_t(rb), code, 0, ROWS, COLS, 1, ptr(f16))
         out[f"{name}_blocks"] = b
         out[f"{name}_f32"] = want
         out[f"{name}_f16"] = f16
         out[f"{name}_type"] = np.int32(code)
-        print(f"{name:6s} dequant: gguf-py == reference quant.h (bit-exact), {ROWS}x{COLS}")
+        src = "reference quant.h" if name in GGUF_ONLY_REF else "gguf-py == reference quant.h (bit-exact)"
+        print(f"{name:6s} dequant: {src}, {ROWS}x{COLS}")
     np.savez_compressed(HERE / "dequant_golden.npz", **out)
 
 

@@ -26,10 +26,14 @@ TK_OK, TK_ERR_INVALID, TK_ERR_UNSUPPORTED, TK_ERR_CUDA, TK_ERR_NOMEM, TK_ERR_TIM
 # block types = the reference's QT_* codes (tier/quant.h:20-23)
 F32, F16, Q4_0, Q4_1, Q5_0, Q5_1, Q8_0 = 0, 1, 2, 3, 6, 7, 8
 Q2_K, Q3_K, Q4_K, Q5_K, Q6_K, BF16, F16X2 = 10, 11, 12, 13, 14, 30, 100
+IQ4_NL, IQ4_XS, TQ1_0, TQ2_0, MXFP4, NF4, FP4 = 20, 23, 34, 35, 39, 200, 201
 QTYPES = {"F32": F32, "F16": F16, "BF16": BF16, "Q4_0": Q4_0, "Q4_1": Q4_1, "Q5_0": Q5_0, "Q5_1": Q5_1,
-          "Q8_0": Q8_0, "Q2_K": Q2_K, "Q3_K": Q3_K, "Q4_K": Q4_K, "Q5_K": Q5_K, "Q6_K": Q6_K}
+          "Q8_0": Q8_0, "Q2_K": Q2_K, "Q3_K": Q3_K, "Q4_K": Q4_K, "Q5_K": Q5_K, "Q6_K": Q6_K,
+          "IQ4_NL": IQ4_NL, "IQ4_XS": IQ4_XS, "TQ1_0": TQ1_0, "TQ2_0": TQ2_0, "MXFP4": MXFP4, "NF4": NF4, "FP4": FP4}
 BLOCK = {F32: (1, 4), F16: (1, 2), BF16: (1, 2), Q4_0: (32, 18), Q4_1: (32, 20), Q5_0: (32, 22), Q5_1: (32, 24),
-         Q8_0: (32, 34), Q2_K: (256, 84), Q3_K: (256, 110), Q4_K: (256, 144), Q5_K: (256, 176), Q6_K: (256, 210)}
+         Q8_0: (32, 34), Q2_K: (256, 84), Q3_K: (256, 110), Q4_K: (256, 144), Q5_K: (256, 176), Q6_K: (256, 210),
+         IQ4_NL: (32, 18), IQ4_XS: (256, 136), TQ1_0: (256, 54), TQ2_0: (256, 66), MXFP4: (32, 17),
+         NF4: (64, 36), FP4: (64, 36)}
 # activation dtypes
 DT_F32, DT_F16, DT_BF16 = 0, 1, 2
 # product sets

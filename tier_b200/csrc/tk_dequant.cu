@@ -17,7 +17,7 @@ int block_elems(int t) {
         case QT_F32: case QT_F16: case QT_BF16: return 1;
         case QT_Q4_0: case QT_Q4_1: case QT_Q5_0: case QT_Q5_1: case QT_Q8_0: return 32;
         case QT_Q2_K: case QT_Q3_K: case QT_Q4_K: case QT_Q5_K: case QT_Q6_K: return 256;
-        default: return 0;
+        default: return tkq::elems(t);
     }
 }
 int block_bytes(int t) {
@@ -34,7 +34,7 @@ int block_bytes(int t) {
         case QT_Q4_K: return 144;
         case QT_Q5_K: return 176;
         case QT_Q6_K: return 210;
-        default: return 0;
+        default: return tkq::bytes(t);
     }
 }
 bool dequant_supported(int t) { return block_elems(t) > 0; }
@@ -200,6 +200,13 @@ tk_status launch_dequant(tk_ctx* ctx, int t, const void* W, size_t rb, int r0, i
         case QT_Q4_K: dq_dispatch_out<QT_Q4_K>(out_dtype, grid, block, s, w, rb, r0, nrows, cols, out); break;
         case QT_Q5_K: dq_dispatch_out<QT_Q5_K>(out_dtype, grid, block, s, w, rb, r0, nrows, cols, out); break;
         case QT_Q6_K: dq_dispatch_out<QT_Q6_K>(out_dtype, grid, block, s, w, rb, r0, nrows, cols, out); break;
+        case QT_IQ4_NL: dq_dispatch_out<QT_IQ4_NL>(out_dtype, grid, block, s, w, rb, r0, nrows, cols, out); break;
+        case QT_IQ4_XS: dq_dispatch_out<QT_IQ4_XS>(out_dtype, grid, block, s, w, rb, r0, nrows, cols, out); break;
+        case QT_MXFP4: dq_dispatch_out<QT_MXFP4>(out_dtype, grid, block, s, w, rb, r0, nrows, cols, out); break;
+        case QT_NF4: dq_dispatch_out<QT_NF4>(out_dtype, grid, block, s, w, rb, r0, nrows, cols, out); break;
+        case QT_FP4: dq_dispatch_out<QT_FP4>(out_dtype, grid, block, s, w, rb, r0, nrows, cols, out); break;
+        case QT_TQ1_0: dq_dispatch_out<QT_TQ1_0>(out_dtype, grid, block, s, w, rb, r0, nrows, cols, out); break;
+        case QT_TQ2_0: dq_dispatch_out<QT_TQ2_0>(out_dtype, grid, block, s, w, rb, r0, nrows, cols, out); break;
         default: return fail(TK_ERR_UNSUPPORTED, "tk_dequant: unsupported block type " + std::to_string(t));
     }
     ctx->launches++;

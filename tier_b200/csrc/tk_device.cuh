@@ -1,10 +1,13 @@
 // tk_device.cuh -- sm_100a device primitives shared by the tierk kernels:
 // mbarrier / TMA / tcgen05 wrappers with bounded waits, the device status
-// word, and bit-exact block dequant (restating tier/quant.h:37-121).
+// word, and bit-exact block dequant (restating tier/quant.h:37-121; the
+// table-level types in tk_qtypes.h).
 #pragma once
 #include <cstdint>
 #include <cuda_fp16.h>
 #include <cuda_bf16.h>
+
+#include "tk_qtypes.h"
 
 namespace tk {
 
@@ -253,7 +256,9 @@ __device__ __forceinline__ uint16_t f2bf_bits(float v) { return __bfloat16_as_us
 // ---------------------------------------------------------------------------
 enum : int {
     QT_F32 = 0, QT_F16 = 1, QT_Q4_0 = 2, QT_Q4_1 = 3, QT_Q5_0 = 6, QT_Q5_1 = 7, QT_Q8_0 = 8, QT_Q2_K = 10,
-    QT_Q3_K = 11, QT_Q4_K = 12, QT_Q5_K = 13, QT_Q6_K = 14, QT_BF16 = 30
+    QT_Q3_K = 11, QT_Q4_K = 12, QT_Q5_K = 13, QT_Q6_K = 14, QT_BF16 = 30,
+    QT_IQ4_NL = tkq::IQ4_NL, QT_IQ4_XS = tkq::IQ4_XS, QT_TQ1_0 = tkq::TQ1_0, QT_TQ2_0 = tkq::TQ2_0,
+    QT_MXFP4 = tkq::MXFP4, QT_NF4 = tkq::NF4, QT_FP4 = tkq::FP4
 };
 
 __device__ __forceinline__ uint16_t ld_u16(const uint8_t* p) { return (uint16_t)(p[0] | (p[1] << 8)); }
@@ -275,6 +280,7 @@ __device__ __forceinline__ void kq_scale_min(int j, const uint8_t* s, int& sc, i
 
 // Scalar value of element `col` of a block row.
 __device__ __forceinline__ float qval(const uint8_t* row, int type, int col) {
+    if (tkq::elems(type)) return tkq::value(row, type, col);   // IQ4_NL, IQ4_XS, MXFP4, NF4, FP4, TQ1_0, TQ2_0
     switch (type) {
         case QT_F32: return __uint_as_float(ld_u32(row + (size_t)col * 4));
         case QT_F16: return h2f_bits(ld_u16(row + (size_t)col * 2));

@@ -173,10 +173,9 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32) gemv_direct_kernel(const uint
     }
 }
 
-bool gemv_supported(int t) {
-    return t == QT_Q8_0 || t == QT_Q4_0 || t == QT_Q4_K || t == QT_Q5_K || t == QT_Q6_K || t == QT_F16 ||
-           t == QT_BF16 || t == QT_F32;
-}
+// Every block type of the dequant: the reference's gemv_q decodes any type
+// through q_val; the types without a dedicated kernel take gemv_direct_kernel.
+bool gemv_supported(int t) { return dequant_supported(t); }
 
 template <int T, int M>
 static void gemv_go(int blocks, cudaStream_t s, const uint8_t* W, size_t rb, int N, int K, const float* x, int ldx,
@@ -283,6 +282,18 @@ tk_status launch_gemv(tk_ctx* ctx, int t, const void* Wv, size_t rb, int N, int 
         case QT_F16: gemv_m<QT_F16>(M, blocks, s, W, rb, N, K, x, ldx, y, ldy); break;
         case QT_BF16: gemv_m<QT_BF16>(M, blocks, s, W, rb, N, K, x, ldx, y, ldy); break;
         case QT_F32: gemv_m<QT_F32>(M, blocks, s, W, rb, N, K, x, ldx, y, ldy); break;
+        case QT_Q4_1: gemv_m<QT_Q4_1>(M, blocks, s, W, rb, N, K, x, ldx, y, ldy); break;
+        case QT_Q5_0: gemv_m<QT_Q5_0>(M, blocks, s, W, rb, N, K, x, ldx, y, ldy); break;
+        case QT_Q5_1: gemv_m<QT_Q5_1>(M, blocks, s, W, rb, N, K, x, ldx, y, ldy); break;
+        case QT_Q2_K: gemv_m<QT_Q2_K>(M, blocks, s, W, rb, N, K, x, ldx, y, ldy); break;
+        case QT_Q3_K: gemv_m<QT_Q3_K>(M, blocks, s, W, rb, N, K, x, ldx, y, ldy); break;
+        case QT_IQ4_NL: gemv_m<QT_IQ4_NL>(M, blocks, s, W, rb, N, K, x, ldx, y, ldy); break;
+        case QT_IQ4_XS: gemv_m<QT_IQ4_XS>(M, blocks, s, W, rb, N, K, x, ldx, y, ldy); break;
+        case QT_MXFP4: gemv_m<QT_MXFP4>(M, blocks, s, W, rb, N, K, x, ldx, y, ldy); break;
+        case QT_NF4: gemv_m<QT_NF4>(M, blocks, s, W, rb, N, K, x, ldx, y, ldy); break;
+        case QT_FP4: gemv_m<QT_FP4>(M, blocks, s, W, rb, N, K, x, ldx, y, ldy); break;
+        case QT_TQ1_0: gemv_m<QT_TQ1_0>(M, blocks, s, W, rb, N, K, x, ldx, y, ldy); break;
+        case QT_TQ2_0: gemv_m<QT_TQ2_0>(M, blocks, s, W, rb, N, K, x, ldx, y, ldy); break;
         default: return fail(TK_ERR_UNSUPPORTED, "tk_gemv: unsupported weight type " + std::to_string(t));
     }
     ctx->launches += popcount_chunks(M);
