@@ -50,6 +50,9 @@ enum {
     /* types whose levels come from a 16-entry list or from base-3 digits */
     TK_IQ4_NL = 20, TK_IQ4_XS = 23, TK_TQ1_0 = 34, TK_TQ2_0 = 35, TK_MXFP4 = 39,
     TK_NF4 = 200, TK_FP4 = 201,
+    /* lattice types: need the tables of tk_set_iq_grids */
+    TK_IQ2_XXS = 16, TK_IQ2_XS = 17, TK_IQ3_XXS = 18, TK_IQ1_S = 19, TK_IQ3_S = 21, TK_IQ2_S = 22,
+    TK_IQ1_M = 29,
     /* fp32 weight stored as two fp16 planes hi = f16(W*2^s), lo = f16(W*2^s - hi);
        plane lo starts rows*row_bytes bytes after plane hi (see tk_weight_split_f32) */
     TK_F16X2 = 100
@@ -132,10 +135,29 @@ size_t tk_row_bytes(int qtype, int cols);
 /* out[r, c] = value of element c of row r0+r, for r < nrows, as fp32, fp16
  * (round-to-nearest-even of the fp32 value) or bf16.  Bit-exact with
  * q_val / tier_fp16(q_val).  Replaces dq_launch / dq_k (tier/tier.cpp:294-298).
- * Supported qtype: all TK_* block types except TK_F16X2 (the reference's
- * IQ1/IQ2/IQ3 grid types are not among them). */
+ * Supported qtype: all TK_* block types except TK_F16X2 -- the reference's 27;
+ * the lattice types once tk_set_iq_grids has run on the context. */
 tk_status tk_dequant(tk_ctx *ctx, int qtype, const void *blocks, size_t row_bytes,
                      int r0, int nrows, int cols, int out_dtype, void *out, void *stream);
+
+/* ---- IQ1 / IQ2 / IQ3 lattice tables --------------------------------------- */
+/* TK_IQ2_XXS, TK_IQ2_XS, TK_IQ2_S, TK_IQ3_XXS, TK_IQ3_S, TK_IQ1_S and TK_IQ1_M
+ * look groups of 8 (4) values up in fixed lattice tables: the format's data,
+ * tier/quant_tables.h qt_iq2xxs_grid ... qt_iq1s_grid (gguf-py's IQ*.grid hold
+ * the same numbers).  The library does not carry them: the caller registers
+ * its copies (host pointers, int8 entries) once per context; until then these
+ * types return TK_ERR_UNSUPPORTED from every entry point.  The sign table
+ * (qt_ksigns) follows from a rule and is built here.  The call synchronizes
+ * the device before and after the copy. */
+typedef struct tk_iq_grids {
+    const int8_t *iq2xxs;   /* [256][8]   qt_iq2xxs_grid */
+    const int8_t *iq2xs;    /* [512][8]   qt_iq2xs_grid  */
+    const int8_t *iq2s;     /* [1024][8]  qt_iq2s_grid   */
+    const int8_t *iq3xxs;   /* [256][4]   qt_iq3xxs_grid */
+    const int8_t *iq3s;     /* [512][4]   qt_iq3s_grid   */
+    const int8_t *iq1s;     /* [2048][8]  qt_iq1s_grid (IQ1_S and IQ1_M) */
+} tk_iq_grids;
+tk_status tk_set_iq_grids(tk_ctx *ctx, const tk_iq_grids *grids);
 
 /* ---- quantizer ------------------------------------------------------------ */
 /* out rows (row_bytes apart) = the blocks of x [rows, cols] (fp32, or bf16

@@ -48,6 +48,20 @@ class Oracle:
         L.tko_f2bf.restype = ctypes.c_uint16
         L.tko_f2bf.argtypes = [ctypes.c_float]
         self.L = L
+        self.iq_grids = None
+        try:
+            self.set_iq_grids()
+        except ImportError:
+            pass            # no gguf-py: the IQ1/IQ2/IQ3 lattice types decode to NaN
+
+    def set_iq_grids(self, grids: dict | None = None):
+        """Register the lattice tables (int8, keyed as tier_b200.IQ_GRID_SHAPES);
+        None takes them from gguf-py's IQ*.grid (the numbers of
+        tier/quant_tables.h)."""
+        from tier_b200 import IQ_GRID_SHAPES, iq_grids_from_gguf
+        grids = iq_grids_from_gguf() if grids is None else grids
+        self.iq_grids = [np.ascontiguousarray(grids[n], dtype=np.int8) for n, _, _ in IQ_GRID_SHAPES]
+        self.L.tko_set_iq_grids(*[_p(a) for a in self.iq_grids])
 
     def row_bytes(self, qtype: int, cols: int) -> int:
         return int(self.L.tko_row_bytes(qtype, cols))

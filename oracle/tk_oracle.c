@@ -9,7 +9,7 @@
  * It restates, in plain C, the reference's arithmetic for the path:
  *   - block formats and scalar dequant       tier/quant.h:20-121 (q_val): the
  *     legacy and K-quant types plus IQ4_NL, IQ4_XS, MXFP4, NF4, FP4, TQ1_0,
- *     TQ2_0; not the IQ1/IQ2/IQ3 grid types
+ *     TQ2_0 and the IQ1/IQ2/IQ3 lattice types (tables registered by the caller)
  *   - fp16 <-> fp32 software conversion      tier/quant.h:37-42, tier/gpu_compat.h:151-190
  *   - decode GEMV summation order            tier/tier.cpp:300-306 (gemv_q), 2261-2268 (gemv<T>)
  *   - x3 activation split                    tier/tier.cpp:869-870 (split3_fp_k)
@@ -34,7 +34,9 @@ enum {
     TKO_Q8_0 = 8, TKO_Q2_K = 10, TKO_Q3_K = 11, TKO_Q4_K = 12, TKO_Q5_K = 13,
     TKO_Q6_K = 14, TKO_BF16 = 30,
     TKO_IQ4_NL = 20, TKO_IQ4_XS = 23, TKO_TQ1_0 = 34, TKO_TQ2_0 = 35, TKO_MXFP4 = 39,
-    TKO_NF4 = 200, TKO_FP4 = 201
+    TKO_NF4 = 200, TKO_FP4 = 201,
+    TKO_IQ2_XXS = 16, TKO_IQ2_XS = 17, TKO_IQ3_XXS = 18, TKO_IQ1_S = 19, TKO_IQ3_S = 21, TKO_IQ2_S = 22,
+    TKO_IQ1_M = 29
 };
 
 /* (elements per block, bytes per block) -- tier/quant.h:25-29 */
@@ -62,6 +64,13 @@ int tko_block_geom(int type, int *elems, int *bytes)
     case TKO_IQ4_XS: e = 256; b = 136; break;
     case TKO_TQ1_0: e = 256; b = 54; break;
     case TKO_TQ2_0: e = 256; b = 66; break;
+    case TKO_IQ2_XXS: e = 256; b = 66; break;
+    case TKO_IQ2_XS: e = 256; b = 74; break;
+    case TKO_IQ2_S: e = 256; b = 82; break;
+    case TKO_IQ3_XXS: e = 256; b = 98; break;
+    case TKO_IQ3_S: e = 256; b = 110; break;
+    case TKO_IQ1_S: e = 256; b = 50; break;
+    case TKO_IQ1_M: e = 256; b = 56; break;
     default: return 0;
     }
     if (elems) *elems = e;
@@ -174,12 +183,96 @@ static float fp4_level(int v)
     return v >= 8 ? -a : a;
 }
 
+/* Lattice tables of the IQ1/IQ2/IQ3 types (tier/quant_tables.h), registered
+ * by the caller (tko_set_iq_grids; the tests pass gguf-py's IQ*.grid).  The
+ * grid types decode to NaN until then. */
+static const int8_t *g_iq2xxs, *g_iq2xs, *g_iq2s, *g_iq3xxs, *g_iq3s, *g_iq1s;
+void tko_set_iq_grids(const int8_t *iq2xxs, const int8_t *iq2xs, const int8_t *iq2s, const int8_t *iq3xxs,
+                      const int8_t *iq3s, const int8_t *iq1s)
+{
+    g_iq2xxs = iq2xxs; g_iq2xs = iq2xs; g_iq2s = iq2s; g_iq3xxs = iq3xxs; g_iq3s = iq3s; g_iq1s = iq1s;
+}
+/* qt_ksigns[j]: the 7 sign bits j plus an eighth that makes the parity even */
+static unsigned ksign(unsigned j)
+{
+    unsigned p = 0;
+    for (unsigned t = j; t; t >>= 1) p ^= t & 1;
+    return j | (p << 7);
+}
+static float with_sign(float v, unsigned bits, int e) { return (bits >> e) & 1 ? v * -1.0f : v; }
+/* d * (0.5 + s) * f: the IQ2/IQ3_XXS block scale, left to right as q_val */
+static float half_step(float d, unsigned s, float f) { float t = d * (0.5f + (float)s); return t * f; }
+
+static float grid_q_val(const uint8_t *row, int type, int col)
+{
+    int i = col % 256, e = i % 8;
+    if (!g_iq1s) return NAN;
+    switch (type) {
+    case TKO_IQ2_XXS: { /* tier/quant.h:94-96 */
+        const uint8_t *b = row + (size_t)(col / 256) * 66, *grp = b + 2 + 8 * (i / 32);
+        int k = (i % 32) / 8;
+        uint32_t aux = ld32(grp + 4);
+        float db = half_step(blk_d(b), aux >> 28, 0.25f);
+        return with_sign(db * (float)g_iq2xxs[grp[k] * 8 + e], ksign((aux >> (7 * k)) & 127), e);
+    }
+    case TKO_IQ2_XS: { /* tier/quant.h:97-99 */
+        const uint8_t *b = row + (size_t)(col / 256) * 74;
+        unsigned q = ld16(b + 2 + 2 * (i / 8)), s = i / 16;
+        float db = half_step(blk_d(b), (b[66 + s / 2] >> (s % 2 ? 4 : 0)) & 15, 0.25f);
+        return with_sign(db * (float)g_iq2xs[(q % 512) * 8 + e], ksign(q >> 9), e);
+    }
+    case TKO_IQ2_S: { /* tier/quant.h:100-102 */
+        const uint8_t *b = row + (size_t)(col / 256) * 82;
+        int k = i / 8, s = i / 16;
+        float db = half_step(blk_d(b), (b[74 + s / 2] >> (s % 2 ? 4 : 0)) & 15, 0.25f);
+        int gi = b[2 + k] + 256 * ((b[66 + k / 4] >> (2 * (k % 4))) & 3);
+        return with_sign(db * (float)g_iq2s[gi * 8 + e], b[34 + k], e);
+    }
+    case TKO_IQ3_XXS: { /* tier/quant.h:103-105 */
+        const uint8_t *b = row + (size_t)(col / 256) * 98;
+        uint32_t aux = ld32(b + 66 + 4 * (i / 32));
+        float db = half_step(blk_d(b), aux >> 28, 0.5f);
+        return with_sign(db * (float)g_iq3xxs[b[2 + i / 4] * 4 + i % 4], ksign((aux >> (7 * ((i % 32) / 8))) & 127), e);
+    }
+    case TKO_IQ3_S: { /* tier/quant.h:106-108 */
+        const uint8_t *b = row + (size_t)(col / 256) * 110;
+        int g = i / 32, k = i / 4;
+        float db = blk_d(b) * (float)(1 + 2 * ((b[106 + g / 2] >> (g % 2 ? 4 : 0)) & 15));
+        int gi = b[2 + k] + 256 * ((b[66 + k / 8] >> (k % 8)) & 1);
+        return with_sign(db * (float)g_iq3s[gi * 4 + i % 4], b[74 + i / 8], e);
+    }
+    case TKO_IQ1_S: { /* tier/quant.h:109-111 */
+        const uint8_t *b = row + (size_t)(col / 256) * 50;
+        int k = i / 8;
+        unsigned qh = ld16(b + 34 + 2 * (i / 32));
+        float dl = blk_d(b) * (float)(2 * ((qh >> 12) & 7) + 1);
+        float dt = (qh & 0x8000) ? -0.125f : 0.125f;
+        int gi = b[2 + k] + 256 * ((qh >> (3 * (k % 4))) & 7);
+        return dl * ((float)g_iq1s[gi * 8 + e] + dt);
+    }
+    case TKO_IQ1_M: { /* tier/quant.h:112-115 */
+        const uint8_t *b = row + (size_t)(col / 256) * 56, *sc = b + 48;
+        int k = i / 8, s = i / 16;
+        unsigned dh = 0;
+        for (int w = 0; w < 4; ++w) dh |= (unsigned)(ld16(sc + 2 * w) >> 12) << (4 * w);
+        float dl = tko_h2f((uint16_t)dh) * (float)(2 * ((ld16(sc + 2 * (s / 4)) >> (3 * (s % 4))) & 7) + 1);
+        int nib = (b[32 + k / 2] >> (k % 2 ? 4 : 0)) & 15;
+        float dt = (nib & 8) ? -0.125f : 0.125f;
+        return dl * ((float)g_iq1s[(b[k] + 256 * (nib & 7)) * 8 + e] + dt);
+    }
+    default: return 0.0f;
+    }
+}
+
 /* element i of a 32-element block of 16 nibble bytes: low nibbles first, then high */
 static int nib32(const uint8_t *qs, int i) { return (qs[i % 16] >> (i < 16 ? 0 : 4)) & 15; }
 
 float tko_q_val(const uint8_t *row, int type, int col)
 {
     switch (type) {
+    case TKO_IQ2_XXS: case TKO_IQ2_XS: case TKO_IQ2_S: case TKO_IQ3_XXS: case TKO_IQ3_S:
+    case TKO_IQ1_S: case TKO_IQ1_M:
+        return grid_q_val(row, type, col);
     case TKO_IQ4_NL: { /* [d f16][16 B]: d * kv_iq4[q] (tier/quant.h:69) */
         const uint8_t *b = row + (size_t)(col / 32) * 18;
         return blk_d(b) * (float)kv_iq4[nib32(b + 2, col % 32)];

@@ -71,7 +71,21 @@ def random_blocks(rng, qtype, rows, cols, scale_offsets, block_bytes, block_elem
 
 
 SCALE_OFFSETS = {2: [0], 3: [0, 2], 6: [0], 7: [0, 2], 8: [0], 10: [80, 82], 11: [108], 12: [0, 2], 13: [0, 2],
-                 14: [208], 20: [0], 23: [0], 34: [52], 35: [64]}
+                 14: [208], 20: [0], 23: [0], 34: [52], 35: [64], 16: [0], 17: [0], 22: [0], 18: [0], 21: [0],
+                 19: [0]}
+
+
+def iq1_m_blocks(rng, rows, cols):
+    """IQ1_M (tier/quant.h:112-115): the fp16 block scale spread over the top
+    nibbles of the four scale words (nibble k in word k)."""
+    nb = rows * cols // 256
+    b = rng.integers(0, 256, size=(nb, 56), dtype=np.uint8)
+    h = (rng.standard_normal(nb) * 0.02).astype(np.float16).view(np.uint16)
+    sc = b[:, 48:56].copy().view(np.uint16).reshape(nb, 4)
+    for k in range(4):
+        sc[:, k] = (sc[:, k] & 0x0FFF) | (((h >> (4 * k)) & 0xF) << 12)
+    b[:, 48:56] = sc.view(np.uint8).reshape(nb, 8)
+    return b.reshape(rows, -1)
 
 
 def mxfp4_blocks(rng, rows, cols):
@@ -111,6 +125,8 @@ def blocks_for(rng, qtype, rows, cols):
         return mxfp4_blocks(rng, rows, cols)
     if qtype in (200, 201):
         return absmax_blocks(rng, rows, cols)
+    if qtype == 29:
+        return iq1_m_blocks(rng, rows, cols)
     return random_blocks(rng, qtype, rows, cols, SCALE_OFFSETS[qtype], bb, be)
 
 

@@ -79,6 +79,14 @@ TYPES = [
     # pinned to the reference's quant.h alone; fp32 absmax at byte 0
     (200, "NF4", 64, 36, "f32"),
     (201, "FP4", 64, 36, "f32"),
+    # lattice types (tier/quant.h:94-115; tables tier/quant_tables.h)
+    (16, "IQ2_XXS", 256, 66, [0]),
+    (17, "IQ2_XS", 256, 74, [0]),
+    (22, "IQ2_S", 256, 82, [0]),
+    (18, "IQ3_XXS", 256, 98, [0]),
+    (21, "IQ3_S", 256, 110, [0]),
+    (19, "IQ1_S", 256, 50, [0]),
+    (29, "IQ1_M", 256, 56, "iq1m"),
 ]
 GGUF_ONLY_REF = {"NF4", "FP4"}
 ROWS, COLS = 4, 512
@@ -107,6 +115,14 @@ def gen_dequant(ref):
             if halfs == "f32":
                 a = np.abs(rng.standard_normal(nb) * 0.05).astype(np.float32).view(np.uint8).reshape(nb, 4)
                 b[:, 0:4] = a
+            elif halfs == "iq1m":
+                # the fp16 block scale lives in the top nibbles of the four
+                # scale words (tier/quant.h:113; tier/check_quant.py:40-45)
+                h = (rng.standard_normal(nb) * 0.02).astype(np.float16).view(np.uint16)
+                sc = b[:, 48:56].copy().view(np.uint16).reshape(nb, 4)
+                for k in range(4):
+                    sc[:, k] = (sc[:, k] & 0x0FFF) | (((h >> (4 * k)) & 0xF) << 12)
+                b[:, 48:56] = sc.view(np.uint8).reshape(nb, 8)
             else:
                 for o in halfs:
                     h = (rng.standard_normal(nb) * 0.02).astype(np.float16).view(np.uint8).reshape(nb, 2)

@@ -38,7 +38,9 @@ def test_binding_covers_header():
 
 
 def test_row_bytes_matches_oracle(lib, oracle):
-    for t in (0, 1, 2, 3, 6, 7, 8, 10, 11, 12, 13, 14, 30):
+    import tier_b200 as tk
+    assert len(tk.QTYPES) == 27                     # every type of tier/quant.h:25-31
+    for t in sorted(tk.QTYPES.values()):
         for cols in (256, 4096, 5120, 14336):
             assert lib.tk_row_bytes(t, cols) == oracle.row_bytes(t, cols), (t, cols)
     assert lib.tk_row_bytes(12, 100) == 0          # not a block multiple
@@ -53,6 +55,20 @@ def test_null_context_is_rejected_not_crashed(lib):
     assert st == 1
     st = lib.tk_gemv_multi(None, 8, 2, None, None, None, None, 34, 32, None, 32, 1, None)
     assert st == 1 and b"null context" in lib.tk_last_error_string()
+    st = lib.tk_set_iq_grids(None, None)
+    assert st == 1 and b"null context" in lib.tk_last_error_string()
+
+
+def test_qtype_values_and_names_match_header(lib):
+    """Every TK_<type> enum of the header equals the Python constant, and the
+    library's name table maps the same names to the same codes."""
+    import tier_b200 as tk
+    text = (ROOT / "include" / "tierk.h").read_text()
+    for name, code in tk.QTYPES.items():
+        m = re.search(rf"\bTK_{name}\s*=\s*(\d+)", text)
+        assert m and int(m.group(1)) == code, name
+        assert lib.tk_qtype_from_name(name.encode()) == code, name
+        assert lib.tk_qtype_name(code) == name.encode(), name
 
 
 def test_flag_values_match_header():

@@ -30,6 +30,9 @@ def test_dequant_golden_bit_exact(ctx, name):
     b = DQ[f"{name}_blocks"]
     t = int(DQ[f"{name}_type"])
     R, C = DQ[f"{name}_f32"].shape
+    if name.startswith(("IQ1", "IQ2", "IQ3")):
+        pytest.importorskip("gguf")
+        ctx.set_iq_grids()          # lattice tables from gguf-py (= tier/quant_tables.h)
     bd = dev(b)
     o32 = torch.empty(R, C, dtype=torch.float32, device="cuda")
     ctx.dequant(t, bd, R, C, o32, out_dtype=tk.DT_F32)

@@ -1,6 +1,8 @@
 """GPU parity of the block types that have no dedicated decode kernel: the
-legacy Q4_1 / Q5_0 / Q5_1 / Q2_K / Q3_K and the table-level IQ4_NL, IQ4_XS,
-TQ1_0, TQ2_0, MXFP4, NF4, FP4 (tier/quant.h:59-121).  The reference's gemv_q
+legacy Q4_1 / Q5_0 / Q5_1 / Q2_K / Q3_K, the table-level IQ4_NL, IQ4_XS,
+TQ1_0, TQ2_0, MXFP4, NF4, FP4 and the lattice IQ2_XXS, IQ2_XS, IQ2_S,
+IQ3_XXS, IQ3_S, IQ1_S, IQ1_M (tier/quant.h:59-121; lattice tables registered
+from gguf-py, the numbers of tier/quant_tables.h).  The reference's gemv_q
 (tier/tier.cpp:300-306) and dq_k (294-298) decode every type through q_val;
 here the same types go through the generic dequant / GEMV kernels, and the
 linear path expands them to fp16 for the tensor-core GEMM.
@@ -18,6 +20,15 @@ pytestmark = pytest.mark.gpu
 
 LEGACY = [3, 6, 7, 10, 11]
 TABLE = [20, 23, 34, 35, 39, 200, 201]
+GRID = [16, 17, 22, 18, 21, 19, 29]
+
+
+@pytest.fixture
+def gctx(ctx):
+    """The session context with the lattice tables registered."""
+    pytest.importorskip("gguf")
+    ctx.set_iq_grids()
+    return ctx
 
 
 def dev(a):
@@ -31,8 +42,9 @@ def host(t):
     return t.cpu().numpy()
 
 
-@pytest.mark.parametrize("qtype", TABLE)
-def test_dequant_rows_offset_all_dtypes(ctx, oracle, qtype):
+@pytest.mark.parametrize("qtype", TABLE + GRID)
+def test_dequant_rows_offset_all_dtypes(gctx, oracle, qtype):
+    ctx = gctx
     import torch
     import tier_b200 as tk
     rng = np.random.default_rng(300 + qtype)
@@ -51,9 +63,10 @@ def test_dequant_rows_offset_all_dtypes(ctx, oracle, qtype):
     ctx.sync_status()
 
 
-@pytest.mark.parametrize("qtype", LEGACY + TABLE)
+@pytest.mark.parametrize("qtype", LEGACY + TABLE + GRID)
 @pytest.mark.parametrize("M", [1, 3, 16])
-def test_gemv_every_type(ctx, oracle, qtype, M):
+def test_gemv_every_type(gctx, oracle, qtype, M):
+    ctx = gctx
     import torch
     rng = np.random.default_rng(400 + qtype * 7 + M)
     N, K = 300, 2048
@@ -79,8 +92,9 @@ def test_gemv_multi_falls_back_per_segment(ctx, oracle, qtype):
     ctx.sync_status()
 
 
-@pytest.mark.parametrize("qtype", [20, 23, 34, 39, 201, 10])
-def test_linear_fwd_dx(ctx, oracle, qtype):
+@pytest.mark.parametrize("qtype", [20, 23, 34, 39, 201, 10, 16, 21, 29])
+def test_linear_fwd_dx(gctx, oracle, qtype):
+    ctx = gctx
     import torch
     import tier_b200 as tk
     rng = np.random.default_rng(600 + qtype)
@@ -97,3 +111,30 @@ def test_linear_fwd_dx(ctx, oracle, qtype):
     ctx.linear_dx(w, dYb.cuda(), M, dX, dy_dtype=tk.DT_BF16)
     assert rel_fro(host(dX), dYb.float().numpy().astype(np.float64) @ Wf) < 2e-3
     ctx.sync_status()
+
+
+def test_grid_types_need_registered_tables():
+    """A fresh context rejects the lattice types on the host (no launch) until
+    tk_set_iq_grids has run; then the same call decodes bit-exactly."""
+    import torch
+    import tier_b200 as tk
+    pytest.importorskip("gguf")
+    from oracle.oracle import Oracle
+    c = tk.Context(0)
+    try:
+        rng = np.random.default_rng(900)
+        b = blocks_for(rng, 16, 8, 512)
+        out = torch.empty(8, 512, dtype=torch.float32, device="cuda")
+        with pytest.raises(tk.TierkError) as e:
+            c.dequant(16, dev(b), 8, 512, out)
+        assert e.value.status == tk.TK_ERR_UNSUPPORTED and "tk_set_iq_grids" in str(e.value)
+        y = torch.empty(1, 8, dtype=torch.float32, device="cuda")
+        with pytest.raises(tk.TierkError):
+            c.gemv(16, dev(b), 8, 512, dev(np.ones((1, 512), np.float32)), y)
+        c.set_iq_grids()
+        c.dequant(16, dev(b), 8, 512, out)
+        assert np.array_equal(host(out).view(np.uint32), Oracle().dequant(b, 16, 8, 512).view(np.uint32))
+        c.sync_status()
+    finally:
+        torch.cuda.synchronize()
+        c.close()

@@ -27,13 +27,19 @@ TK_OK, TK_ERR_INVALID, TK_ERR_UNSUPPORTED, TK_ERR_CUDA, TK_ERR_NOMEM, TK_ERR_TIM
 F32, F16, Q4_0, Q4_1, Q5_0, Q5_1, Q8_0 = 0, 1, 2, 3, 6, 7, 8
 Q2_K, Q3_K, Q4_K, Q5_K, Q6_K, BF16, F16X2 = 10, 11, 12, 13, 14, 30, 100
 IQ4_NL, IQ4_XS, TQ1_0, TQ2_0, MXFP4, NF4, FP4 = 20, 23, 34, 35, 39, 200, 201
+# lattice types: decode after Context.set_iq_grids
+IQ2_XXS, IQ2_XS, IQ3_XXS, IQ1_S, IQ3_S, IQ2_S, IQ1_M = 16, 17, 18, 19, 21, 22, 29
 QTYPES = {"F32": F32, "F16": F16, "BF16": BF16, "Q4_0": Q4_0, "Q4_1": Q4_1, "Q5_0": Q5_0, "Q5_1": Q5_1,
           "Q8_0": Q8_0, "Q2_K": Q2_K, "Q3_K": Q3_K, "Q4_K": Q4_K, "Q5_K": Q5_K, "Q6_K": Q6_K,
-          "IQ4_NL": IQ4_NL, "IQ4_XS": IQ4_XS, "TQ1_0": TQ1_0, "TQ2_0": TQ2_0, "MXFP4": MXFP4, "NF4": NF4, "FP4": FP4}
+          "IQ4_NL": IQ4_NL, "IQ4_XS": IQ4_XS, "TQ1_0": TQ1_0, "TQ2_0": TQ2_0, "MXFP4": MXFP4, "NF4": NF4, "FP4": FP4,
+          "IQ2_XXS": IQ2_XXS, "IQ2_XS": IQ2_XS, "IQ2_S": IQ2_S, "IQ3_XXS": IQ3_XXS, "IQ3_S": IQ3_S, "IQ1_S": IQ1_S,
+          "IQ1_M": IQ1_M}
 BLOCK = {F32: (1, 4), F16: (1, 2), BF16: (1, 2), Q4_0: (32, 18), Q4_1: (32, 20), Q5_0: (32, 22), Q5_1: (32, 24),
          Q8_0: (32, 34), Q2_K: (256, 84), Q3_K: (256, 110), Q4_K: (256, 144), Q5_K: (256, 176), Q6_K: (256, 210),
          IQ4_NL: (32, 18), IQ4_XS: (256, 136), TQ1_0: (256, 54), TQ2_0: (256, 66), MXFP4: (32, 17),
-         NF4: (64, 36), FP4: (64, 36)}
+         NF4: (64, 36), FP4: (64, 36),
+         IQ2_XXS: (256, 66), IQ2_XS: (256, 74), IQ2_S: (256, 82), IQ3_XXS: (256, 98), IQ3_S: (256, 110),
+         IQ1_S: (256, 50), IQ1_M: (256, 56)}
 # activation dtypes
 DT_F32, DT_F16, DT_BF16 = 0, 1, 2
 # product sets
@@ -58,6 +64,30 @@ class Weight(ctypes.Structure):
                 ("scale_log2", ctypes.c_int), ("row_bytes", ctypes.c_size_t), ("data", ctypes.c_void_p)]
 
 
+class IqGrids(ctypes.Structure):
+    """tk_iq_grids: host pointers to the six lattice tables (int8)."""
+    _fields_ = [(n, ctypes.c_void_p) for n in ("iq2xxs", "iq2xs", "iq2s", "iq3xxs", "iq3s", "iq1s")]
+
+
+# (name, rows, cols) of each table, in tk_iq_grids order
+IQ_GRID_SHAPES = [("iq2xxs", 256, 8), ("iq2xs", 512, 8), ("iq2s", 1024, 8), ("iq3xxs", 256, 4), ("iq3s", 512, 4),
+                  ("iq1s", 2048, 8)]
+
+
+def iq_grids_from_gguf() -> dict:
+    """The lattice tables as int8 arrays, taken from gguf-py's IQ*.grid (the
+    numbers of tier/quant_tables.h).  Needs the gguf package."""
+    import numpy as np
+    from gguf import quants
+    out = {}
+    for (name, rows, cols), cls in zip(IQ_GRID_SHAPES, ("IQ2_XXS", "IQ2_XS", "IQ2_S", "IQ3_XXS", "IQ3_S", "IQ1_S")):
+        q = getattr(quants, cls)
+        q.init_grid()
+        g = np.asarray(q.grid, dtype=np.float64).reshape(rows, cols)
+        out[name] = np.ascontiguousarray(g.astype(np.int8))
+    return out
+
+
 _P = ctypes.c_void_p
 _I = ctypes.c_int
 _SZ = ctypes.c_size_t
@@ -75,6 +105,7 @@ SIGNATURES = [
     ("tk_profile", _I, [_P, _I]),
     ("tk_profile_read", _I, [_P, _I, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_uint64)]),
     ("tk_row_bytes", _SZ, [_I, _I]),
+    ("tk_set_iq_grids", _I, [_P, ctypes.POINTER(IqGrids)]),
     ("tk_dequant", _I, [_P, _I, _P, _SZ, _I, _I, _I, _I, _P, _P]),
     ("tk_gemv", _I, [_P, _I, _P, _SZ, _I, _I, _P, _I, _I, _P, _I, _P]),
     ("tk_gemv_multi", _I, [_P, _I, _I, _P, _P, _P, _P, _SZ, _I, _P, _I, _I, _P]),
@@ -191,6 +222,21 @@ class Context:
         _check(self.lib.tk_reserve(self.h, nbytes))
 
     # ---- operations (torch tensors in, device pointers to the C ABI) ----
+    def set_iq_grids(self, grids: dict | None = None):
+        """Register the IQ1/IQ2/IQ3 lattice tables (tk_set_iq_grids): a dict of
+        int8 arrays keyed as IQ_GRID_SHAPES, or None for iq_grids_from_gguf()."""
+        import numpy as np
+        grids = iq_grids_from_gguf() if grids is None else grids
+        keep = []
+        s = IqGrids()
+        for name, rows, cols in IQ_GRID_SHAPES:
+            a = np.ascontiguousarray(grids[name], dtype=np.int8)
+            if a.shape != (rows, cols):
+                raise ValueError(f"{name}: expected shape {(rows, cols)}, got {a.shape}")
+            keep.append(a)
+            setattr(s, name, a.ctypes.data)
+        _check(self.lib.tk_set_iq_grids(self.h, ctypes.byref(s)))
+
     def dequant(self, qtype, blocks, rows, cols, out, r0=0, out_dtype=DT_F32, row_bytes_=None, stream=None):
         rb = row_bytes_ if row_bytes_ is not None else row_bytes(qtype, cols)
         _check(self.lib.tk_dequant(self.h, qtype, _ptr(blocks), rb, r0, rows, cols, out_dtype, _ptr(out),

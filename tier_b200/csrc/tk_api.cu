@@ -4,6 +4,7 @@
 #include <cmath>
 #include <cstring>
 #include <string>
+#include <vector>
 #include "tk_device.cuh"
 #include "tk_internal.h"
 
@@ -343,6 +344,7 @@ void tk_destroy(tk_ctx* ctx) {
     if (ctx->ws) cudaFree(ctx->ws);
     if (ctx->status) cudaFree(ctx->status);
     if (ctx->flags) cudaFree(ctx->flags);
+    if (ctx->iq_tab) cudaFree(ctx->iq_tab);
     comm_destroy(ctx);
     for (cudaEvent_t e : ctx->prof.ev) cudaEventDestroy(e);
     delete ctx;
@@ -399,6 +401,32 @@ tk_status tk_sync_status(tk_ctx* ctx, void* stream) {
         return fail(TK_ERR_DEVICE, "a kernel reported invalid input (code " + std::to_string(code) + ")");
     }
     return TK_OK;
+}
+
+tk_status tk_set_iq_grids(tk_ctx* ctx, const tk_iq_grids* g) {
+    if (!ctx) return fail(TK_ERR_INVALID, "tk_set_iq_grids: null context");
+    if (!g || !g->iq2xxs || !g->iq2xs || !g->iq2s || !g->iq3xxs || !g->iq3s || !g->iq1s)
+        return fail(TK_ERR_INVALID, "tk_set_iq_grids: every table pointer is required");
+    std::vector<int8_t> h(tkq::GRID_BYTES);
+    memcpy(h.data() + tkq::GRID_IQ2XXS, g->iq2xxs, 256 * 8);
+    memcpy(h.data() + tkq::GRID_IQ2XS, g->iq2xs, 512 * 8);
+    memcpy(h.data() + tkq::GRID_IQ2S, g->iq2s, 1024 * 8);
+    memcpy(h.data() + tkq::GRID_IQ3XXS, g->iq3xxs, 256 * 4);
+    memcpy(h.data() + tkq::GRID_IQ3S, g->iq3s, 512 * 4);
+    memcpy(h.data() + tkq::GRID_IQ1S, g->iq1s, 2048 * 8);
+    for (int i = 0; i < 128; ++i) h[tkq::GRID_SIGNS + i] = (int8_t)tkq::sign_byte(i);
+    cudaError_t e = cudaDeviceSynchronize();   // no kernel may be reading the old table
+    if (e != cudaSuccess) return cuda_fail(e, "tk_set_iq_grids: synchronize");
+    if (!ctx->iq_tab) {
+        e = cudaMalloc(&ctx->iq_tab, tkq::GRID_BYTES);
+        if (e != cudaSuccess) {
+            ctx->iq_tab = nullptr;
+            return cuda_fail(e, "tk_set_iq_grids: allocate");
+        }
+    }
+    e = cudaMemcpy(ctx->iq_tab, h.data(), tkq::GRID_BYTES, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    return e == cudaSuccess ? TK_OK : cuda_fail(e, "tk_set_iq_grids: copy");
 }
 
 size_t tk_row_bytes(int qtype, int cols) {

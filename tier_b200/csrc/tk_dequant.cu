@@ -17,7 +17,7 @@ int block_elems(int t) {
         case QT_F32: case QT_F16: case QT_BF16: return 1;
         case QT_Q4_0: case QT_Q4_1: case QT_Q5_0: case QT_Q5_1: case QT_Q8_0: return 32;
         case QT_Q2_K: case QT_Q3_K: case QT_Q4_K: case QT_Q5_K: case QT_Q6_K: return 256;
-        default: return tkq::elems(t);
+        default: return tkq::is_grid(t) ? 256 : tkq::elems(t);
     }
 }
 int block_bytes(int t) {
@@ -34,7 +34,7 @@ int block_bytes(int t) {
         case QT_Q4_K: return 144;
         case QT_Q5_K: return 176;
         case QT_Q6_K: return 210;
-        default: return tkq::bytes(t);
+        default: return tkq::is_grid(t) ? tkq::grid_bytes(t) : tkq::bytes(t);
     }
 }
 bool dequant_supported(int t) { return block_elems(t) > 0; }
@@ -152,6 +152,33 @@ __global__ void __launch_bounds__(256) dequant_sub_f16_kernel(const uint8_t* __r
     }
 }
 
+// Lattice types (tk_qgrid.h): as dequant_kernel, the table buffer in global
+// memory (34 KB, L1/L2-resident after the first touches).
+template <int T, int OUT>
+__global__ void __launch_bounds__(DQ_THREADS) dequant_grid_kernel(const uint8_t* __restrict__ W, size_t rb, int r0,
+                                                                  int nrows, int cols, void* __restrict__ out,
+                                                                  const int8_t* __restrict__ tab) {
+    const int gpr = cols >> 3;
+    for (int r = blockIdx.y; r < nrows; r += gridDim.y) {
+        const uint8_t* row = W + (size_t)(r0 + r) * rb;
+        const size_t orow = (size_t)r * cols;
+        for (int g = blockIdx.x * DQ_THREADS + threadIdx.x; g < gpr; g += gridDim.x * DQ_THREADS) {
+            float v[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) v[j] = tkq::grid_value(row, T, g * 8 + j, tab);
+            store8<OUT>(out, orow + (size_t)g * 8, v);
+        }
+    }
+}
+
+template <int T>
+static void dq_grid_out(int out_dtype, dim3 g, dim3 b, cudaStream_t s, const uint8_t* W, size_t rb, int r0,
+                        int nrows, int cols, void* out, const int8_t* tab) {
+    if (out_dtype == TK_DT_F32) dequant_grid_kernel<T, TK_DT_F32><<<g, b, 0, s>>>(W, rb, r0, nrows, cols, out, tab);
+    else if (out_dtype == TK_DT_F16) dequant_grid_kernel<T, TK_DT_F16><<<g, b, 0, s>>>(W, rb, r0, nrows, cols, out, tab);
+    else dequant_grid_kernel<T, TK_DT_BF16><<<g, b, 0, s>>>(W, rb, r0, nrows, cols, out, tab);
+}
+
 template <int T>
 static void dq_dispatch_out(int out_dtype, dim3 g, dim3 b, cudaStream_t s, const uint8_t* W, size_t rb, int r0,
                             int nrows, int cols, void* out) {
@@ -180,6 +207,29 @@ tk_status launch_dequant(tk_ctx* ctx, int t, const void* W, size_t rb, int r0, i
         return cuda_fail(cudaGetLastError(), "dequant launch");
     }
     const int gpr = cols / 8;
+    if (tkq::is_grid(t)) {
+        if (!ctx->iq_tab)
+            return fail(TK_ERR_UNSUPPORTED, "tk_dequant: type " + std::to_string(t) +
+                                                " needs the IQ grid tables (tk_set_iq_grids)");
+        const int gx = (gpr + DQ_THREADS - 1) / DQ_THREADS;
+        const int gy_cap = (ctx->num_sms * 16 + gx - 1) / gx;
+        const int gy = nrows < gy_cap ? nrows : (gy_cap < 65535 ? gy_cap : 65535);
+        const dim3 grid((unsigned)gx, (unsigned)gy), block(DQ_THREADS);
+        const uint8_t* w = static_cast<const uint8_t*>(W);
+        const int8_t* tab = ctx->iq_tab;
+        ProfScope ps(ctx, s, PK_DEQUANT);
+        switch (t) {
+            case tkq::IQ2_XXS: dq_grid_out<tkq::IQ2_XXS>(out_dtype, grid, block, s, w, rb, r0, nrows, cols, out, tab); break;
+            case tkq::IQ2_XS: dq_grid_out<tkq::IQ2_XS>(out_dtype, grid, block, s, w, rb, r0, nrows, cols, out, tab); break;
+            case tkq::IQ2_S: dq_grid_out<tkq::IQ2_S>(out_dtype, grid, block, s, w, rb, r0, nrows, cols, out, tab); break;
+            case tkq::IQ3_XXS: dq_grid_out<tkq::IQ3_XXS>(out_dtype, grid, block, s, w, rb, r0, nrows, cols, out, tab); break;
+            case tkq::IQ3_S: dq_grid_out<tkq::IQ3_S>(out_dtype, grid, block, s, w, rb, r0, nrows, cols, out, tab); break;
+            case tkq::IQ1_S: dq_grid_out<tkq::IQ1_S>(out_dtype, grid, block, s, w, rb, r0, nrows, cols, out, tab); break;
+            default: dq_grid_out<tkq::IQ1_M>(out_dtype, grid, block, s, w, rb, r0, nrows, cols, out, tab); break;
+        }
+        ctx->launches++;
+        return cuda_fail(cudaGetLastError(), "dequant launch");
+    }
     const int gx = (gpr + DQ_THREADS * DQ_UNROLL - 1) / (DQ_THREADS * DQ_UNROLL);
     const int gy_cap = (ctx->num_sms * 16 + gx - 1) / gx;      // ~16 blocks per SM in flight
     const int gy = nrows < gy_cap ? nrows : (gy_cap < 65535 ? gy_cap : 65535);

@@ -7,6 +7,7 @@
 #include <cuda_fp16.h>
 #include <cuda_bf16.h>
 
+#include "tk_qgrid.h"
 #include "tk_qtypes.h"
 
 namespace tk {

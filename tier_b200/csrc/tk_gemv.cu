@@ -173,6 +173,47 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32) gemv_direct_kernel(const uint
     }
 }
 
+// Lattice types (tk_qgrid.h): as gemv_direct_kernel, the registered table
+// buffer passed in.
+template <int T, int M>
+__global__ void __launch_bounds__(GEMV_WARPS * 32) gemv_grid_kernel(const uint8_t* __restrict__ W, size_t rb, int N,
+                                                                    int K, const float* __restrict__ x, int ldx,
+                                                                    float* __restrict__ y, int ldy,
+                                                                    const int8_t* __restrict__ tab) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nwarps = gridDim.x * GEMV_WARPS;
+    for (int n = blockIdx.x * GEMV_WARPS + warp; n < N; n += nwarps) {
+        const uint8_t* row = W + (size_t)n * rb;
+        float acc[M];
+#pragma unroll
+        for (int m = 0; m < M; ++m) acc[m] = 0.0f;
+        for (int c = lane * 8; c < K; c += 256) {
+            float v[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) v[j] = tkq::grid_value(row, T, c + j, tab);
+            fma8<M>(acc, v, x, ldx, c);
+        }
+        warp_store<M>(acc, y, ldy, n, lane);
+    }
+}
+
+template <int T>
+static void gemv_grid_m(int M, int blocks, cudaStream_t s, const uint8_t* W, size_t rb, int N, int K, const float* x,
+                        int ldx, float* y, int ldy, const int8_t* tab) {
+    int m0 = 0;
+    while (m0 < M) {
+        const int r = M - m0;
+        const float* xs = x + (size_t)m0 * ldx;
+        float* ys = y + (size_t)m0 * ldy;
+        const dim3 g(blocks), b(GEMV_WARPS * 32);
+        if (r >= 16) { gemv_grid_kernel<T, 16><<<g, b, 0, s>>>(W, rb, N, K, xs, ldx, ys, ldy, tab); m0 += 16; }
+        else if (r >= 8) { gemv_grid_kernel<T, 8><<<g, b, 0, s>>>(W, rb, N, K, xs, ldx, ys, ldy, tab); m0 += 8; }
+        else if (r >= 4) { gemv_grid_kernel<T, 4><<<g, b, 0, s>>>(W, rb, N, K, xs, ldx, ys, ldy, tab); m0 += 4; }
+        else if (r >= 2) { gemv_grid_kernel<T, 2><<<g, b, 0, s>>>(W, rb, N, K, xs, ldx, ys, ldy, tab); m0 += 2; }
+        else { gemv_grid_kernel<T, 1><<<g, b, 0, s>>>(W, rb, N, K, xs, ldx, ys, ldy, tab); m0 += 1; }
+    }
+}
+
 // Every block type of the dequant: the reference's gemv_q decodes any type
 // through q_val; the types without a dedicated kernel take gemv_direct_kernel.
 bool gemv_supported(int t) { return dequant_supported(t); }
@@ -272,6 +313,24 @@ tk_status launch_gemv(tk_ctx* ctx, int t, const void* Wv, size_t rb, int N, int 
     const uint8_t* W = static_cast<const uint8_t*>(Wv);
     const int rows_per_block = GEMV_WARPS;
     int blocks = (N + rows_per_block - 1) / rows_per_block;
+    if (tkq::is_grid(t)) {
+        if (!ctx->iq_tab)
+            return fail(TK_ERR_UNSUPPORTED, "tk_gemv: type " + std::to_string(t) +
+                                                " needs the IQ grid tables (tk_set_iq_grids)");
+        const int8_t* tab = ctx->iq_tab;
+        ProfScope ps(ctx, s, PK_GEMV);
+        switch (t) {
+            case tkq::IQ2_XXS: gemv_grid_m<tkq::IQ2_XXS>(M, blocks, s, W, rb, N, K, x, ldx, y, ldy, tab); break;
+            case tkq::IQ2_XS: gemv_grid_m<tkq::IQ2_XS>(M, blocks, s, W, rb, N, K, x, ldx, y, ldy, tab); break;
+            case tkq::IQ2_S: gemv_grid_m<tkq::IQ2_S>(M, blocks, s, W, rb, N, K, x, ldx, y, ldy, tab); break;
+            case tkq::IQ3_XXS: gemv_grid_m<tkq::IQ3_XXS>(M, blocks, s, W, rb, N, K, x, ldx, y, ldy, tab); break;
+            case tkq::IQ3_S: gemv_grid_m<tkq::IQ3_S>(M, blocks, s, W, rb, N, K, x, ldx, y, ldy, tab); break;
+            case tkq::IQ1_S: gemv_grid_m<tkq::IQ1_S>(M, blocks, s, W, rb, N, K, x, ldx, y, ldy, tab); break;
+            default: gemv_grid_m<tkq::IQ1_M>(M, blocks, s, W, rb, N, K, x, ldx, y, ldy, tab); break;
+        }
+        ctx->launches += popcount_chunks(M);
+        return cuda_fail(cudaGetLastError(), "gemv launch");
+    }
     ProfScope ps(ctx, s, PK_GEMV);
     switch (t) {
         case QT_Q8_0: gemv_m<QT_Q8_0>(M, blocks, s, W, rb, N, K, x, ldx, y, ldy); break;

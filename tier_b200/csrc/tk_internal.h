@@ -34,6 +34,9 @@ struct tk_ctx {
     const void* wexp_data = nullptr;
     int wexp_qtype = 0, wexp_rows = 0, wexp_cols = 0;
     size_t wexp_rb = 0;
+    // IQ1/IQ2/IQ3 lattice tables registered by tk_set_iq_grids (device,
+    // tkq::GRID_BYTES, layout in tk_qgrid.h); null until then
+    int8_t* iq_tab = nullptr;
 };
 
 namespace tk {
