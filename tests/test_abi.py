@@ -97,3 +97,31 @@ def test_product_sets_and_types_exposed():
     import tier_b200 as tk
     assert (tk.X3_AUTO, tk.X3_REF, tk.X3_HHL, tk.X2, tk.X1) == (0, 1, 2, 3, 4)
     assert tk.Q8_0 == 8 and tk.Q4_K == 12 and tk.Q5_K == 13   # tier/quant.h:20-23
+
+
+def test_plain_c_caller(lib, tmp_path):
+    """include/tierk.h compiles as strict C99 and a C program linked to
+    libtierk.so gets the same answers as the Python binding (no GPU needed)."""
+    import shutil
+    import tier_b200 as tk
+    if not shutil.which("gcc"):
+        pytest.skip("gcc not available")
+    exe = tmp_path / "abi_consumer"
+    so_dir = ROOT / "tier_b200"
+    r = subprocess.run(["gcc", "-std=c99", "-pedantic", "-Wall", "-Wextra", "-Werror", "-I", str(ROOT / "include"),
+                        str(ROOT / "tests" / "abi_consumer.c"), "-L", str(so_dir), "-ltierk",
+                        f"-Wl,-rpath,{so_dir}", "-o", str(exe)], capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+    r = subprocess.run([str(exe)], capture_output=True, text=True, timeout=120)
+    assert r.returncode == 0, r.stderr
+    lines = r.stdout.split("\n")
+    rows = [ln.split() for ln in lines if ln.startswith("type ")]
+    assert len(rows) == 27
+    for _, code, name, rb, back in rows:
+        assert tk.QTYPES[name] == int(code) == int(back)
+        assert int(rb) == tk.row_bytes(int(code), 4096)
+    assert "null_ctx 1 1" in lines and "null_grids 1" in lines
+    init = next(ln for ln in lines if ln.startswith("init "))
+    import torch
+    if not torch.cuda.is_available():
+        assert init != "init 0 1" and init.endswith(" 1")     # an error status, no context
