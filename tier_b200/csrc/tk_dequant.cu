@@ -1,6 +1,7 @@
 // tk_dequant.cu -- HBM-bound elementwise kernels of the path:
 //   * block dequant to fp32/fp16/bf16, bit-exact with q_val
-//     (tier/quant.h:59-121) and dq_k (tier/tier.cpp:294-298);
+//     (tier/quant.h:59-121) and dq_k (tier/tier.cpp:294-298), for all 27
+//     block types (the lattice types read the tables of tk_set_iq_grids);
 //   * activation split/convert into fp16 planes for the tensor-core GEMM
 //     (the reference's split3_fp_k, tier/tier.cpp:869-870, plus an exact
 //     per-row power-of-two scale that keeps the low parts out of the fp16

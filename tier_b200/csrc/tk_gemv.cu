@@ -9,7 +9,11 @@
 // decodes 8-element groups from shared memory with the bit-exact dequant and
 // accumulates fp32 dot products for all M tokens.  Lane partial sums are
 // reduced with a shuffle tree, as the reference does.  fp16/bf16/fp32 rows
-// are read directly with 16-byte vector loads.
+// are read directly with 16-byte vector loads.  Every other block type (the
+// legacy and remaining K-quants, the table-level types of tk_qtypes.h, the
+// lattice types of tk_qgrid.h) decodes per element straight from global
+// memory, as gemv_q does for every type.  The dedicated kernels for Q8_0 /
+// Q4_K / Q5_K / Q6_K live in tk_gemv4-7.cu; launch_gemv picks among them.
 #include "tk_device.cuh"
 #include "tk_internal.h"
 
