@@ -107,3 +107,26 @@ def test_recipe_types():
     assert [q for _, q in v] == [tk.Q5_K] * 4 + [tk.Q4_K] * 4 and [l for l, _ in v][:4] == [0, 2, 4, 6]
     with pytest.raises(ValueError):
         recipe_types("Q3_K", layers)
+
+
+def test_every_block_type_round_trips(tmp_path):
+    """One matrix of each of the 27 types of tier/quant.h:25-31: the writer
+    records its name and the reader returns the same geometry and bytes."""
+    import tier_b200 as tk
+    from tier_b200.tq import TQFile, write_tq
+    rng = np.random.default_rng(27)
+    items = []
+    for name, code in sorted(tk.QTYPES.items(), key=lambda kv: kv[1]):
+        rows, cols = 3, 512
+        b = rng.integers(0, 256, size=(rows, tk.row_bytes(code, cols)), dtype=np.uint8)
+        items.append((f"m.{name.lower()}", code, rows, cols, b))
+    write_tq(tmp_path / "all.tq", items, "#from tierlm test\n")
+    with TQFile(tmp_path / "all.tq") as f:
+        assert len(f.entries) == 27
+        for i, (nm, code, rows, cols, b) in enumerate(items):
+            e = f.entries[i]
+            assert (e.name, e.qtype, e.rows, e.cols) == (nm, code, rows, cols)
+            assert e.offset % 4096 == 0
+            assert f.read(i).tobytes() == b.tobytes()
+    text = (tmp_path / "all.tq").read_bytes().split(b"\n")
+    assert any(b" IQ1_M " in ln for ln in text) and any(b" MXFP4 " in ln for ln in text)
