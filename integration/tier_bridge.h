@@ -1,0 +1,77 @@
+// tier_bridge.h -- the glue a maintainer adds to tierlm's engine (tier/tier.cpp)
+// so that its frozen-weight linear path runs on libtierk.so.  It is included
+// once, just before `linear` (tier/tier.cpp:1202).  Everything it names from
+// the engine is declared before that point; the chat part is a template, so
+// the ChatMat fields resolve where chat_lin (tier/tier.cpp:2351) uses it.
+//
+// Routed to libtierk:
+//   * linear / linear_dx / linear_dx_acc (tier/tier.cpp:1202-1238) for fp16
+//     weights in the fp16-x3 mode (g_fp16w, g_bf3, g_use_fp16_x3).  The
+//     reference runs fp3gemm's three cuBLASLt GEMMs (tier/tier.cpp:922-943);
+//     here that is one tk_linear_fwd / tk_linear_dx with TK_X3_REF, i.e. the
+//     same products W.xl + W.xm + W.xh in one tcgen05 GEMM.
+//   * chat_lin's quantized branch (tier/tier.cpp:2356-2360): gemv_q for one
+//     token and dq_launch + chat_linear_ld slabs beyond it become tk_gemv for
+//     up to 16 tokens and tk_linear_fwd above that.  Resident weights
+//     (m.dev) are frozen, so they take TK_WFROZEN.
+// Everything else (row splits shared with the CPU, bf16 and fp32 weights, the
+// fallbacks) keeps the reference's own path: each function returns false and
+// the caller continues as before.  A failed libtierk call also returns false
+// after printing the library's message, so the reference path stays the
+// safety net.
+#pragma once
+#include <cstdio>
+
+#include "tierk.h"
+
+static tk_ctx* g_tk = nullptr;
+
+// One context per process, on the device current at the first call (the
+// engine uses one GPU per process).
+static bool tk_bridge_ready() {
+    static int state = -1;
+    if (state < 0) {
+        int dev = 0;
+        state = (cudaGetDevice(&dev) == cudaSuccess && tk_init(dev, &g_tk) == TK_OK) ? 1 : 0;
+        if (!state) fprintf(stderr, "libtierk: %s (reference path kept)\n", tk_last_error_string());
+    }
+    return state == 1;
+}
+
+static bool tk_bridge_ok(tk_status st) {
+    if (st == TK_OK) return true;
+    fprintf(stderr, "libtierk: %s (reference path used)\n", tk_last_error_string());
+    return false;
+}
+
+// The fp16-x3 weights of the training path: W[N, K] fp16 on the device.
+static bool tk_bridge_fp16_x3(const float* W) {
+    return !g_split.count(W) && g_fp16w.count(W) && g_bf16w.count(W) && g_bf3 && g_use_fp16_x3;
+}
+
+// out[M, N] = x[M, K] . W^T (linear, beta 0).
+static bool tk_bridge_fwd(const float* x, const float* W, float* out, int M, int K, int N) {
+    if (!tk_bridge_fp16_x3(W) || !tk_bridge_ready()) return false;
+    tk_weight w{TK_F16, N, K, 0, (size_t)K * 2, W};
+    return tk_bridge_ok(tk_linear_fwd(g_tk, &w, x, TK_DT_F32, M, K, out, N, 0.0f, TK_X3_REF, nullptr));
+}
+
+// dX[M, K] (=|+=) dY[M, N] . W (linear_dx with beta 0, linear_dx_acc with beta 1).
+static bool tk_bridge_dx(const float* dY, const float* W, float* dX, int M, int K, int N, float beta) {
+    if (!tk_bridge_fp16_x3(W) || !tk_bridge_ready()) return false;
+    tk_weight w{TK_F16, N, K, 0, (size_t)K * 2, W};
+    return tk_bridge_ok(tk_linear_dx(g_tk, &w, dY, TK_DT_F32, M, N, dX, K, beta, TK_X3_REF, nullptr));
+}
+
+// chat_lin, quantized weight m (block type m.qt, m.rows x m.cols, m.rb bytes
+// per row) at W: y[M, m.rows] = x[M, m.cols] . W^T on the chat stream.
+template <class ChatMatT>
+static bool tk_bridge_chat(const ChatMatT& m, const void* W, const float* x, float* y, int M, cudaStream_t s) {
+    if (!m.qt || !tk_bridge_ready()) return false;
+    if (M <= 16) {
+        const int qt = m.qt | (m.dev ? TK_WFROZEN : 0);
+        return tk_bridge_ok(tk_gemv(g_tk, qt, W, m.rb, m.rows, m.cols, x, m.cols, M, y, m.rows, s));
+    }
+    tk_weight w{m.qt, m.rows, m.cols, 0, m.rb, W};
+    return tk_bridge_ok(tk_linear_fwd(g_tk, &w, x, TK_DT_F32, M, m.cols, y, m.rows, 0.0f, TK_X3_AUTO, s));
+}

@@ -1,0 +1,49 @@
+"""Engine integration, checked by building it: integration/build_patched_tier.py
+adds the libtierk hooks (integration/tier_bridge.h) to the reference engine's
+linear / linear_dx / linear_dx_acc (tier/tier.cpp:1202-1238) and chat_lin
+(tier/tier.cpp:2351-2378), then compiles and links it with the reference's
+own nvcc line.  The test needs the reference tree (skipped without it); the
+binary is not run (it needs model files)."""
+import os
+import shutil
+import subprocess
+import sys
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parent.parent
+sys.path.insert(0, str(ROOT / "integration"))
+
+
+def test_patch_hooks_each_call_site_once():
+    from build_patched_tier import patch
+    src = ("static void linear(hipblasHandle_t h, const float* x, const float* W, float* out, int M, int K, int N){ a; }\n"
+           "static void linear_dx(hipblasHandle_t h, const float* dY, const float* W, float* dX, int M, int K, int N){ b; }\n"
+           "static void linear_dx_acc(hipblasHandle_t h, const float* dY, const float* W, float* dX, int M, int K, int N)"
+           "{ c; }\nstatic void chat_lin(ChatMat& m, const float* x, float* y, int M){ if(m.qt){ q; } else { r; } }\n")
+    out = patch(src)
+    assert out.count('#include "tier_bridge.h"') == 1
+    assert "if(tk_bridge_fwd(x,W,out,M,K,N)) return; a;" in out
+    assert "if(tk_bridge_dx(dY,W,dX,M,K,N,0.0f)) return; b;" in out
+    assert "if(tk_bridge_dx(dY,W,dX,M,K,N,1.0f)) return; c;" in out
+    assert "if(m.qt && tk_bridge_chat(m,W,x,y,M,g_chat_cs)){ } else if(m.qt){ q; }" in out
+    with pytest.raises(SystemExit):
+        patch(src.replace("linear_dx_acc", "other"))
+
+
+def test_patched_engine_builds_and_binds_libtierk():
+    from build_patched_tier import build, default_ref
+    ref = default_ref()
+    if not (ref / "tier.cpp").exists():
+        pytest.skip("reference tree not present")
+    if not (Path(os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")).exists() or shutil.which("nvcc")):
+        pytest.skip("nvcc not available")
+    from tier_b200 import build as tkbuild
+    tkbuild.build()
+    exe = build(ref)
+    syms = subprocess.run(["nm", "-D", "--undefined-only", str(exe)], capture_output=True, text=True).stdout
+    for name in ("tk_init", "tk_linear_fwd", "tk_linear_dx", "tk_gemv"):
+        assert f" {name}\n" in syms, name
+    deps = subprocess.run(["ldd", str(exe)], capture_output=True, text=True).stdout
+    assert "libtierk.so" in deps
