@@ -1,4 +1,4 @@
-"""Host-side sharding logic on CPU with gloo, world size 2: the row split
+"""Host-side sharding logic on CPU with gloo, world sizes 2 and 3: the row split
 used by the linear path, the vocab-shard merge of the running
 cross-entropy state (max, rescaled sum, target, argmax with the reference's
 lowest-index tie rule), and the single-pass head's dX accumulator merge
@@ -82,17 +82,19 @@ def _worker(rank, world, port, q):
         dist.destroy_process_group()
 
 
-def test_vocab_merge_and_row_split_gloo():
+@pytest.mark.parametrize("world", [2, 3])
+def test_vocab_merge_and_row_split_gloo(world):
+    """world 3 splits the 1000-entry vocabulary unevenly (8-aligned shards)."""
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
     for p in procs:
         p.start()
     res = dict(q.get(timeout=120) for _ in procs)
     for p in procs:
         p.join(timeout=60)
-    assert res == {0: True, 1: True}
+    assert res == {r: True for r in range(world)}
 
 
 class _HostGemv:
