@@ -346,6 +346,14 @@ tk_status tk_lmhead_loss(tk_ctx *ctx, int T, const int32_t *labels, const uint8_
  * rmax_local = rmax_global, for rows t < n (run between an all-reduce MAX of
  * rmax and an all-reduce SUM of rsum); with dX (nullable, [n, H]) the
  * single-pass accumulator rows are scaled by the same factor. */
+/* Vocabulary chunk for the LM head: the reference's lm_chunk rule
+ * (tier/tier.cpp:2015-2017) -- device_bytes / 36 / (6*hidden + 8*max(seq,1))
+ * rows, clamped to [1024, vocab rounded up] -- rounded down to a multiple of
+ * 256 (the reference rounds to 128; these kernels take 256-row tiles).
+ * device_bytes = 0 (memory not known) gives 8192, as the reference.  Host
+ * only, no context. */
+int tk_lmhead_chunk(size_t device_bytes, int hidden, int seq, int vocab);
+
 tk_status tk_lmhead_rescale(tk_ctx *ctx, int n, double *rmax_local, double *rsum_local,
                             const double *rmax_global, float *dX, int H, void *stream);
 

@@ -125,3 +125,24 @@ def test_plain_c_caller(lib, tmp_path):
     import torch
     if not torch.cuda.is_available():
         assert init != "init 0 1" and init.endswith(" 1")     # an error status, no context
+
+
+def test_lmhead_chunk_follows_the_reference_rule(lib):
+    """tk_lmhead_chunk = tier/tier.cpp:2015-2017 (total memory / 36 / (6H + 8T),
+    clamped to [1024, V]) rounded down to 256 rows instead of 128."""
+    import tier_b200 as tk
+
+    def ref_rule(total, H, T, V):             # the reference's arithmetic, then our 256 rounding
+        if total == 0:
+            return 8192
+        c = total // 36 // (H * 6 + max(T, 1) * 8)
+        c = c // 128 * 128
+        return max(1024, min(c // 256 * 256, (V + 255) // 256 * 256))
+
+    b200 = 183359 * 2 ** 20
+    assert tk.lmhead_chunk(b200, 3840, 8192, 262144) == 60160        # C4's shape on a B200's 183,359 MiB
+    for total in (0, 2 ** 30, 24 * 2 ** 30, 80 * 2 ** 30, b200):
+        for H, T, V in ((3840, 8192, 262144), (5120, 4096, 152064), (2048, 1, 32000), (4096, 65536, 1000)):
+            got = tk.lmhead_chunk(total, H, T, V)
+            assert got == ref_rule(total, H, T, V), (total, H, T, V)
+            assert got % 256 == 0 or total == 0

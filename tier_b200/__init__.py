@@ -106,6 +106,7 @@ SIGNATURES = [
     ("tk_profile_read", _I, [_P, _I, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_uint64)]),
     ("tk_row_bytes", _SZ, [_I, _I]),
     ("tk_set_iq_grids", _I, [_P, ctypes.POINTER(IqGrids)]),
+    ("tk_lmhead_chunk", _I, [_SZ, _I, _I, _I]),
     ("tk_dequant", _I, [_P, _I, _P, _SZ, _I, _I, _I, _I, _P, _P]),
     ("tk_gemv", _I, [_P, _I, _P, _SZ, _I, _I, _P, _I, _I, _P, _I, _P]),
     ("tk_gemv_multi", _I, [_P, _I, _I, _P, _P, _P, _P, _SZ, _I, _P, _I, _I, _P]),
@@ -163,6 +164,12 @@ def load(path: str | os.PathLike | None = None) -> ctypes.CDLL:
 def row_bytes(qtype: int, cols: int) -> int:
     be, bb = BLOCK[qtype]
     return cols // be * bb
+
+
+def lmhead_chunk(device_bytes: int, hidden: int, seq: int, vocab: int) -> int:
+    """tk_lmhead_chunk: the reference's lm_chunk rule (tier/tier.cpp:2015-2017)
+    with chunks in multiples of 256; device_bytes is the GPU's total memory."""
+    return int(load().tk_lmhead_chunk(device_bytes, hidden, seq, vocab))
 
 
 def _check(st: int):

@@ -429,6 +429,17 @@ tk_status tk_set_iq_grids(tk_ctx* ctx, const tk_iq_grids* g) {
     return e == cudaSuccess ? TK_OK : cuda_fail(e, "tk_set_iq_grids: copy");
 }
 
+int tk_lmhead_chunk(size_t device_bytes, int hidden, int seq, int vocab) {
+    if (device_bytes == 0) return 8192;
+    const size_t per = (size_t)(hidden > 0 ? hidden : 0) * 6 + (size_t)(seq > 1 ? seq : 1) * 8;
+    size_t c = device_bytes / 36 / per;
+    c = c / 256 * 256;
+    const size_t vmax = ((size_t)(vocab > 0 ? vocab : 0) + 255) / 256 * 256;
+    if (c > vmax) c = vmax;
+    if (c < 1024) c = 1024;
+    return c > (size_t)INT32_MAX / 256 * 256 ? INT32_MAX / 256 * 256 : (int)c;
+}
+
 size_t tk_row_bytes(int qtype, int cols) {
     const int be = block_elems(qtype), bb = block_bytes(qtype);
     if (be <= 0 || cols < 0 || cols % be) return 0;
