@@ -98,11 +98,20 @@ def test_vocab_merge_and_row_split_gloo(world):
 
 
 class _HostGemv:
-    """Stands in for the device context on CPU: gemv on an fp32 weight."""
+    """Stands in for the device context on CPU: gemv and linear on an fp32
+    weight (linear finds the weight tensor by its data pointer)."""
+
+    def __init__(self):
+        self.weights = {}
 
     def gemv(self, qtype, W, N, K, x, y, M=1, ldx=None, ldy=None, row_bytes_=None, stream=None):
         y[:M, :N] = x[:M, :K] @ W.view(N, K).T
         return y
+
+    def linear(self, w, X, M, Y, x_dtype=0, ldx=None, ldy=None, beta=0.0, products=0, stream=None):
+        W = self.weights[w.data].view(w.rows, w.cols)
+        Y[:M, : w.rows] = (beta * Y[:M, : w.rows] if beta else 0) + X[:M] @ W.T
+        return Y
 
 
 def _decode_worker(rank, world, port, q):
@@ -113,17 +122,25 @@ def _decode_worker(rank, world, port, q):
         from tier_b200.host import LinearPath, shard_rows
         g = torch.Generator().manual_seed(3)
         ok = True
-        for N, M in ((64, 3), (65, 16)):                   # equal and unequal row shards
+        for N, M in ((64, 3), (65, 16), (14336, 2)):       # equal and unequal row shards
             K = 40
             W = torch.randn(N, K, generator=g)
             x = torch.randn(M, K, generator=g)
-            a, b = shard_rows(N, world, rank)
-            lp = LinearPath(_HostGemv(), F32, b - a, K, W[a:b].contiguous(), group=dist.group.WORLD,
-                            n_total=N, row0=a)
+            a, b = shard_rows(N, world, rank, align=256 if N > 1000 else 1)
+            host = _HostGemv()
+            Ws = W[a:b].contiguous()
+            host.weights[Ws.data_ptr()] = Ws
+            lp = LinearPath(host, F32, b - a, K, Ws, group=dist.group.WORLD, n_total=N, row0=a)
+            want = x @ W.T
             y = lp.decode(x)
-            ok = ok and y.shape == (M, N) and torch.allclose(y, x @ W.T, rtol=1e-5, atol=1e-5)
+            ok = ok and y.shape == (M, N) and torch.allclose(y, want, rtol=1e-5, atol=1e-5)
             out = torch.empty(M, N)
-            ok = ok and lp.decode(x, y=out) is out and torch.allclose(out, x @ W.T, rtol=1e-5, atol=1e-5)
+            ok = ok and lp.decode(x, y=out) is out and torch.allclose(out, want, rtol=1e-5, atol=1e-5)
+            # forward (`linear`): the same gather of unequal column shards
+            Y = lp.forward(x)
+            ok = ok and Y.shape == (M, N) and torch.allclose(Y, want, rtol=1e-5, atol=1e-5)
+            Y2 = torch.ones(M, N)
+            ok = ok and lp.forward(x, Y=Y2, beta=1.0) is Y2 and torch.allclose(Y2, want + 1, rtol=1e-5, atol=1e-5)
         q.put((rank, bool(ok)))
     except Exception as e:   # report instead of leaving the other rank waiting
         q.put((rank, repr(e)))
@@ -131,16 +148,18 @@ def _decode_worker(rank, world, port, q):
         dist.destroy_process_group()
 
 
-def test_row_sharded_decode_gather_gloo():
-    """Decode on row shards: each rank's y columns land in the gathered
-    [M, N_total] in rank order, for equal and unequal shards."""
+@pytest.mark.parametrize("world", [2, 3])
+def test_row_sharded_gather_gloo(world):
+    """Decode and forward on row shards: each rank's columns land in the
+    gathered [M, N_total] in rank order, for equal and unequal shards
+    (14336 rows over 3 ranks in 256-row units: 18 / 18 / 20 units)."""
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_decode_worker, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_decode_worker, args=(r, world, port, q)) for r in range(world)]
     for p in procs:
         p.start()
     res = dict(q.get(timeout=120) for _ in procs)
     for p in procs:
         p.join(timeout=60)
-    assert res == {0: True, 1: True}
+    assert res == {r: True for r in range(world)}

@@ -68,6 +68,28 @@ def merge_vocab_shards(rmax, rsum, amax, tgt, group, rescale, dX=None):
     return merged
 
 
+def gather_cols(local: torch.Tensor, group) -> torch.Tensor:
+    """All-gather the column shards local [M, n_rank] of every rank, in rank
+    order, into [M, sum n_rank].  Shards may differ in width (row splits that
+    do not divide evenly): collectives want equal sizes, so short shards are
+    padded to the widest and the padding is dropped after the exchange."""
+    import torch.distributed as dist
+    world = dist.get_world_size(group)
+    M, n = local.shape
+    sizes = [torch.zeros(1, dtype=torch.int64, device=local.device) for _ in range(world)]
+    dist.all_gather(sizes, torch.tensor([n], dtype=torch.int64, device=local.device), group=group)
+    ns = [int(t.item()) for t in sizes]
+    nmax = max(ns)
+    if n == nmax:
+        send = local.contiguous()
+    else:
+        send = torch.zeros(M, nmax, device=local.device, dtype=local.dtype)
+        send[:, :n] = local
+    buf = torch.empty(world * M, nmax, device=local.device, dtype=local.dtype)
+    dist.all_gather_into_tensor(buf, send, group=group)
+    return torch.cat([buf[r * M:(r + 1) * M, : ns[r]] for r in range(world)], dim=1)
+
+
 class LinearPath:
     """One frozen projection W[N, K] (block-quantized, fp16, or fp32 split into
     fp16 hi/lo) on this rank's device, optionally row-sharded across `group`."""
@@ -94,17 +116,13 @@ class LinearPath:
         """Y = X . W^T (the reference's `linear`).  With a group and gather=True
         the output shards are all-gathered into the full [M, N_total]."""
         M = X.shape[0]
-        local = Y if (Y is not None and self.group is None) else torch.empty(M, self.N, device=X.device,
-                                                                               dtype=torch.float32)
-        self.ctx.linear(self.W, X, M, local, x_dtype=_DT[X.dtype], ldx=X.stride(0), ldy=local.stride(0), beta=beta,
-                        products=products)
+        direct = Y is not None and self.group is None      # the GEMM writes (beta: accumulates into) Y itself
+        local = Y if direct else torch.empty(M, self.N, device=X.device, dtype=torch.float32)
+        self.ctx.linear(self.W, X, M, local, x_dtype=_DT[X.dtype], ldx=X.stride(0), ldy=local.stride(0),
+                        beta=beta if direct else 0.0, products=products)
         if self.group is None or not gather:
             return local
-        import torch.distributed as dist
-        world = dist.get_world_size(self.group)
-        parts = [torch.empty(M, self.N, device=X.device, dtype=torch.float32) for _ in range(world)]
-        dist.all_gather(parts, local, group=self.group)
-        full = torch.cat(parts, dim=1)
+        full = gather_cols(local, self.group)
         if Y is not None:
             if beta:
                 Y += full
@@ -128,20 +146,7 @@ class LinearPath:
                       row_bytes_=self.W.row_bytes)
         if self.group is None or not gather:
             return local
-        import torch.distributed as dist
-        world = dist.get_world_size(self.group)
-        sizes = [torch.zeros(1, dtype=torch.int64, device=x.device) for _ in range(world)]
-        dist.all_gather(sizes, torch.tensor([self.N], dtype=torch.int64, device=x.device), group=self.group)
-        ns = [int(t.item()) for t in sizes]
-        nmax = max(ns)
-        if self.N == nmax:
-            send = local.contiguous()
-        else:                                    # collectives want equal sizes: pad the short shard
-            send = torch.zeros(M, nmax, device=x.device, dtype=torch.float32)
-            send[:, : self.N] = local
-        buf = torch.empty(world * M, nmax, device=x.device, dtype=torch.float32)
-        dist.all_gather_into_tensor(buf, send, group=self.group)
-        full = torch.cat([buf[r * M:(r + 1) * M, : ns[r]] for r in range(world)], dim=1)
+        full = gather_cols(local, self.group)
         if y is not None:
             y.copy_(full)
             return y
