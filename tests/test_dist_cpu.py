@@ -163,3 +163,49 @@ def test_row_sharded_gather_gloo(world):
     for p in procs:
         p.join(timeout=60)
     assert res == {r: True for r in range(world)}
+
+
+class _HostHead:
+    """Device context stand-in for LMHead.grad: each rank's pass 2 adds
+    (rank + 1) to every dX entry, as a real partial gradient would add."""
+
+    def __init__(self, rank):
+        self.rank = rank
+
+    def lmhead_grad(self, W, v0, V_shard, H, X, T, labels, mask, n_loss, softcap, chunk, rmax, rsum, dX,
+                    products=0):
+        dX += float(self.rank + 1)
+
+
+def _head_worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from tier_b200.host import LMHead
+        head = LMHead.__new__(LMHead)
+        head.ctx, head.W, head.v0, head.V_shard, head.H = _HostHead(rank), None, 0, 8, 4
+        head.chunk, head.products, head.group = 256, 0, dist.group.WORLD
+        X = torch.zeros(5, 4)
+        dX = torch.full((5, 4), 10.0)                       # an existing gradient to accumulate into
+        out = head.grad(X, None, None, 4, None, None, dX=dX)
+        want = 10.0 + sum(r + 1 for r in range(world))       # 10 once, plus every rank's part
+        q.put((rank, bool(out is dX and torch.all(dX == want))))
+    except Exception as e:
+        q.put((rank, repr(e)))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_lmhead_grad_accumulates_once_gloo():
+    """LMHead.grad with a group adds the all-reduced parts to dX without
+    summing dX's previous contents across ranks."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_head_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=120) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+    assert res == {0: True, 1: True}

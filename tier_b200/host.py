@@ -232,14 +232,19 @@ class LMHead:
         return loss, hits
 
     def grad(self, X, labels, mask, n_loss, rmax, rsum, dX=None, softcap=0.0):
+        """dX += this head's input gradient (pass 2).  With a group, each rank's
+        part goes into a zeroed buffer that is all-reduced before it is added,
+        so a dX that already holds a gradient is not summed across ranks."""
         T, H = X.shape
         if dX is None:
             dX = torch.zeros(T, H, dtype=torch.float32, device=X.device)
+        part = dX if self.group is None else torch.zeros(T, H, dtype=torch.float32, device=X.device)
         self.ctx.lmhead_grad(self.W, self.v0, self.V_shard, self.H, X, T, labels, mask, n_loss, softcap, self.chunk,
-                             rmax, rsum, dX, products=self.products)
+                             rmax, rsum, part, products=self.products)
         if self.group is not None:
             import torch.distributed as dist
-            dist.all_reduce(dX, group=self.group)
+            dist.all_reduce(part, group=self.group)
+            dX += part
         return dX
 
     def step(self, X, labels, mask, softcap=0.0, dX=None):
@@ -279,4 +284,4 @@ class LMHead:
         return loss, n_loss, hits, amax, dX
 
 
-__all__ = ["LinearPath", "LMHead", "shard_rows", "merge_vocab_shards"]
+__all__ = ["LinearPath", "LMHead", "shard_rows", "merge_vocab_shards", "gather_cols"]
