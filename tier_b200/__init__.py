@@ -360,4 +360,5 @@ def make_weight(qtype: int, rows: int, cols: int, data, scale_log2: int = 0) -> 
 
 from .host import LinearPath, LMHead  # noqa: E402  (host-side mirror of the reference's operators)
 
-__all__ = ["Context", "Weight", "make_weight", "load", "row_bytes", "LinearPath", "LMHead", "TierkError"]
+__all__ = ["Context", "Weight", "make_weight", "load", "row_bytes", "lmhead_chunk", "IqGrids", "IQ_GRID_SHAPES",
+           "iq_grids_from_gguf", "LinearPath", "LMHead", "TierkError"]
