@@ -169,8 +169,11 @@ def quantize_to_tq(ctx, path: str, tensors, qtypes, meta: str | None = None):
     items, errs, se, sq = [], [], 0.0, 0.0
     for (name, x), qt in zip(tensors, qtypes):
         rows, cols = x.shape
+        if x.stride(1) != 1:                 # the quantizer reads rows of cols contiguous elements
+            x = x.contiguous()
         blocks = torch.empty(rows, row_bytes(qt, cols), dtype=torch.uint8, device=x.device)
-        ctx.quantize(qt, x, rows, cols, blocks, x_dtype=DT_BF16 if x.dtype == torch.bfloat16 else DT_F32)
+        ctx.quantize(qt, x, rows, cols, blocks, x_dtype=DT_BF16 if x.dtype == torch.bfloat16 else DT_F32,
+                     ldx=x.stride(0))
         back = torch.empty(rows, cols, dtype=torch.float32, device=x.device)
         ctx.dequant(qt, blocks, rows, cols, back)
         xf = x.float()
