@@ -24,8 +24,7 @@ from __future__ import annotations
 
 import torch
 
-from . import (BF16, DT_BF16, DT_F16, DT_F32, F16, F16X2, WFROZEN, X2, X3_AUTO, X3_REF, Context, Weight, make_weight,
-               row_bytes)
+from . import DT_BF16, DT_F16, DT_F32, F16X2, WFROZEN, X3_AUTO, X3_REF, Context, Weight, make_weight
 
 _DT = {torch.float32: DT_F32, torch.float16: DT_F16, torch.bfloat16: DT_BF16}
 
