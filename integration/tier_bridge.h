@@ -13,7 +13,10 @@
 //   * chat_lin's quantized branch (tier/tier.cpp:2356-2360): gemv_q for one
 //     token and dq_launch + chat_linear_ld slabs beyond it become tk_gemv for
 //     up to 16 tokens and tk_linear_fwd above that.  Resident weights
-//     (m.dev) are frozen, so they take TK_WFROZEN.
+//     (m.dev) are frozen, so they take TK_WFROZEN.  Above 16 tokens the
+//     tensor-core path rounds the expanded weight to fp16 (about 2e-4
+//     relative), where the reference's chat path expands it to fp32; the
+//     GEMV agrees with fp64 to ~1e-7.
 // Everything else (row splits shared with the CPU, bf16 and fp32 weights, the
 // fallbacks) keeps the reference's own path: each function returns false and
 // the caller continues as before.  A failed libtierk call also returns false
