@@ -170,6 +170,15 @@ class RefOracle:
         self.L.ref_split3_fp16(_p(x), _p(h), _p(m), _p(l), ctypes.c_size_t(n))
         return h, m, l
 
+    def lse_chunk(self, lg, rmax, rsum, amax, tgt, tokens, mask, v0):
+        """lse_chunk_kernel itself (tier/tier.cpp:750-759) over rmax.size rows,
+        blocks of 256 emulated threads; updates the state arrays in place."""
+        n_pred = rmax.size
+        T, vc = lg.shape
+        self.L.ref_lse_chunk(_p(np.ascontiguousarray(lg, np.float32)), _p(rmax), _p(rsum), _p(amax), _p(tgt),
+                             _p(np.ascontiguousarray(tokens, np.int32)), _p(np.ascontiguousarray(mask, np.uint8)),
+                             n_pred, vc, v0)
+
     def qgemm_fwd(self, blocks, qtype, n0, nrows, K, X, threads):
         """CPU baseline: Y[M, nrows] via q_val row expansion + fp32 dots."""
         b = np.ascontiguousarray(blocks, dtype=np.uint8)

@@ -14,6 +14,9 @@
 //   ref_split3_fp16              tier/tier.cpp:869-870 (split3_fp_k, extracted)
 //   ref_dlogit                   tier/tier.cpp:736-748 (dlogit_kernel, extracted)
 //   ref_softcap                  tier/tier.cpp:728 (softcap_kernel, extracted)
+//   ref_lse_chunk                tier/tier.cpp:750-759 (lse_chunk_kernel, extracted;
+//                                each block runs as 256 host threads with a
+//                                barrier for __syncthreads, as launched at 3219)
 //   ref_cpu_qgemm_fwd / _dx      CPU baseline: q_val row expansion + the
 //                                cpu_gemm_fwd / cpu_gemm_dx loop structure
 //                                (tier/tier.cpp:1049-1099) over fp32 rows,
@@ -27,11 +30,27 @@
 #include <vector>
 #include <algorithm>
 #include <functional>
+#include <mutex>
+#include <condition_variable>
 
 // ---- emulated CUDA launch environment for the extracted kernel bodies ----
 namespace refsim {
 struct dim { unsigned x = 0, y = 0, z = 0; };
 static thread_local dim threadIdx, blockIdx, blockDim;
+// __syncthreads for one block run as blockDim.x host threads (one block at a
+// time, so a kernel's __shared__ arrays can be function statics)
+struct Barrier {
+    std::mutex m;
+    std::condition_variable cv;
+    unsigned n = 0, waiting = 0, gen = 0;
+    void wait() {
+        std::unique_lock<std::mutex> lk(m);
+        const unsigned g = gen;
+        if (++waiting == n) { waiting = 0; ++gen; cv.notify_all(); return; }
+        cv.wait(lk, [&] { return gen != g; });
+    }
+};
+static Barrier block_barrier;
 }
 using refsim::threadIdx;
 using refsim::blockIdx;
@@ -39,6 +58,8 @@ using refsim::blockDim;
 #define __host__
 #define __device__
 #define __global__
+#define __shared__ static
+#define __syncthreads() refsim::block_barrier.wait()
 typedef unsigned short ref_u16;
 #include "ref_kernels.inc"   // generated: tier_fp16 + split3_fp_k + dlogit_kernel + softcap_kernel
 
@@ -81,6 +102,24 @@ void ref_dlogit(const float* lg, const double* rmax, const double* rsum, const i
     for (size_t i = 0; i < n; ++i) {
         blockIdx.x = (unsigned)(i / 256); threadIdx.x = (unsigned)(i % 256);
         dlogit_kernel(lg, rmax, rsum, tokens, dl, seq_len, vc, v0, n_loss, mask, cap);
+    }
+}
+
+// lse_chunk_kernel<<<n_pred, 256>>> (tier/tier.cpp:3219): blocks one after
+// another, each as 256 threads.
+void ref_lse_chunk(const float* lg, double* rmax, double* rsum, int* amax, float* tgt, const int32_t* tokens,
+                   const unsigned char* mask, int n_pred, int vc, int v0)
+{
+    const unsigned nt = 256;
+    refsim::block_barrier.n = nt;
+    for (int b = 0; b < n_pred; ++b) {
+        std::vector<std::thread> th;
+        for (unsigned i = 0; i < nt; ++i)
+            th.emplace_back([=] {
+                blockDim.x = nt; blockIdx.x = (unsigned)b; threadIdx.x = i;
+                lse_chunk_kernel(lg, rmax, rsum, amax, tgt, tokens, mask, vc, v0);
+            });
+        for (auto& t : th) t.join();
     }
 }
 

@@ -493,8 +493,17 @@ void tko_lse_chunk(const float *lg, double *rmax, double *rsum, int *amax, float
         int bi = 0x7fffffff;
         for (int v = 0; v < vc; ++v)
             if (row[v] > bm || (row[v] == bm && v < bi)) { bm = row[v]; bi = v; }
-        double s = 0.0;
-        for (int v = 0; v < vc; ++v) s += exp((double)row[v] - (double)bm);
+        /* the kernel's order: 256 threads each sum v = tid, tid+256, ...; then
+         * a halving tree over the 256 partials (tier/tier.cpp:755-756) */
+        double sd[256];
+        for (int i = 0; i < 256; ++i) {
+            double s = 0.0;
+            for (int v = i; v < vc; v += 256) s += exp((double)row[v] - (double)bm);
+            sd[i] = s;
+        }
+        for (int o = 128; o > 0; o >>= 1)
+            for (int i = 0; i < o; ++i) sd[i] += sd[i + o];
+        double s = sd[0];
         double om = rmax[t], nm = fmax(om, (double)bm);
         if ((double)bm > om) amax[t] = v0 + bi;
         rsum[t] = rsum[t] * exp(om - nm) + s * exp((double)bm - nm);

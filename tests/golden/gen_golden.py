@@ -22,6 +22,11 @@ Sources of truth recorded per fixture:
                        from the extracted kernel body, on seeded and edge values.
   dlogit_golden.npz    reference dlogit_kernel (tier/tier.cpp:736-748) on a
                        small seeded chunk, with and without softcap.
+  lse_golden.npz       reference lse_chunk_kernel (tier/tier.cpp:750-759), each
+                       block run as 256 host threads with a barrier for
+                       __syncthreads: running max / Σexp / argmax / target
+                       merged into a seeded prior state, with a masked row, an
+                       argmax tie and labels on both sides of the chunk.
 
 usage: python tests/golden/gen_golden.py   (from the repository root)
 """
@@ -209,12 +214,36 @@ def gen_dlogit(ref):
     print("dlogit: 2 cases")
 
 
+def gen_lse(ref):
+    rng = np.random.default_rng(13)
+    out = {}
+    for k, (T, vc, v0) in enumerate(((9, 700, 256), (6, 256, 0), (5, 100, 1024))):
+        lg = (rng.standard_normal((T, vc)) * 4).astype(np.float32)
+        lg[2, 10] = lg[2, vc - 3] = lg[2].max() + 1.0        # tie: the lower index wins
+        tokens = rng.integers(v0 - 40, v0 + vc + 40, size=T).astype(np.int32)
+        mask = np.ones(T, np.uint8)
+        mask[3] = 0
+        rmax = rng.uniform(-1, 3, T - 1)
+        rsum = rng.uniform(10, 100, T - 1)
+        amax = np.full(T - 1, 7, np.int32)
+        tgt = np.full(T - 1, -5.0, np.float32)
+        st = {"rmax": rmax, "rsum": rsum, "amax": amax, "tgt": tgt}
+        for n, a in st.items():
+            out[f"c{k}_{n}0"] = a.copy()
+        ref.ref_lse_chunk(ptr(lg), ptr(rmax), ptr(rsum), ptr(amax), ptr(tgt), ptr(tokens), ptr(mask), T - 1, vc, v0)
+        out.update({f"c{k}_lg": lg, f"c{k}_tokens": tokens, f"c{k}_mask": mask, f"c{k}_v0": np.int32(v0),
+                    f"c{k}_rmax": rmax, f"c{k}_rsum": rsum, f"c{k}_amax": amax, f"c{k}_tgt": tgt})
+    np.savez_compressed(HERE / "lse_golden.npz", **out)
+    print("lse_chunk: 3 cases")
+
+
 def main():
     ref = load_ref()
     gen_dequant(ref)
     gen_quantize(ref)
     gen_split3(ref)
     gen_dlogit(ref)
+    gen_lse(ref)
 
 
 if __name__ == "__main__":

@@ -135,3 +135,40 @@ def test_reference_build_agrees_with_oracle(oracle):
         a = oracle.dequant(b, t, 8, 2048)
         r = ref.dequant(b, t, 8, 2048)
         assert np.array_equal(a.view(np.uint32), r.view(np.uint32))
+
+
+LSE = np.load(GOLDEN / "lse_golden.npz")
+
+
+@pytest.mark.parametrize("k", [0, 1, 2])
+def test_lse_chunk_matches_reference_kernel(oracle, k):
+    """The oracle's lse_chunk restates lse_chunk_kernel (tier/tier.cpp:750-759)
+    in its order -- 256 thread-strided fp64 partial sums and a halving tree --
+    and reproduces the golden outputs of the kernel body run on 256 host
+    threads: bit for bit in the running max, Σexp, argmax (ties to the lower
+    index) and target logit, a masked row left untouched."""
+    c = f"c{k}_"
+    state = [LSE[c + n + "0"].copy() for n in ("rmax", "rsum", "amax", "tgt")]
+    oracle.lse_chunk(LSE[c + "lg"], *state, LSE[c + "tokens"], LSE[c + "mask"], int(LSE[c + "v0"]))
+    for n, got in zip(("rmax", "rsum", "amax", "tgt"), state):
+        assert np.array_equal(got.view(np.uint8), LSE[c + n].view(np.uint8)), n
+    assert state[2][3] == LSE[c + "amax0"][3]            # mask[3] == 0: row 3 keeps its prior state
+
+
+def test_lse_chunk_oracle_agrees_with_reference_live(oracle):
+    from oracle.oracle import RefOracle
+    if not RefOracle.available():
+        pytest.skip("oracle/_ref not built (reference tree absent)")
+    ref = RefOracle()
+    rng = np.random.default_rng(21)
+    for T, vc, v0 in ((12, 1333, 0), (4, 7, 300), (3, 4096, 8192)):
+        lg = (rng.standard_normal((T, vc)) * 6).astype(np.float32)
+        tokens = rng.integers(v0 - 10, v0 + vc + 10, size=T).astype(np.int32)
+        mask = (rng.uniform(size=T) > 0.2).astype(np.uint8)
+        st = [rng.uniform(-2, 8, T - 1), rng.uniform(1, 50, T - 1), np.full(T - 1, -1, np.int32),
+              np.zeros(T - 1, np.float32)]
+        a, b = [x.copy() for x in st], [x.copy() for x in st]
+        oracle.lse_chunk(lg, *a, tokens, mask, v0)
+        ref.lse_chunk(lg, *b, tokens, mask, v0)
+        for x, y in zip(a, b):
+            assert np.array_equal(x.view(np.uint8), y.view(np.uint8)), (T, vc, v0)
