@@ -47,3 +47,23 @@ def test_patched_engine_builds_and_binds_libtierk():
         assert f" {name}\n" in syms, name
     deps = subprocess.run(["ldd", str(exe)], capture_output=True, text=True).stdout
     assert "libtierk.so" in deps
+
+
+def test_bridge_routing_and_call_arguments(tmp_path):
+    """integration/tier_bridge.h with stand-ins for the engine's globals and
+    recording stubs for the library (tests/bridge_check.cpp): which weights go
+    to libtierk, the argument order of each call (leading dimensions, beta,
+    product set, stream, TK_WFROZEN only for resident weights), and the
+    fall-back to the reference path when a call fails."""
+    if not shutil.which("g++"):
+        pytest.skip("g++ not available")
+    exe = tmp_path / "bridge_check"
+    r = subprocess.run(["g++", "-std=c++17", "-Wall", "-Wextra", "-Werror", "-I", str(ROOT / "include"),
+                        "-I", str(ROOT / "integration"), str(ROOT / "tests" / "bridge_check.cpp"), "-o", str(exe)],
+                       capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+    r = subprocess.run([str(exe)], capture_output=True, text=True, timeout=60)
+    assert r.returncode == 0, r.stderr
+    lines = [ln.split() for ln in r.stdout.splitlines() if ln.strip()]
+    assert len(lines) == 12
+    assert all(v == "1" for _, v in lines), [n for n, v in lines if v != "1"]
