@@ -70,25 +70,32 @@ def patch(src: str) -> str:
     return src[:q.start()] + "if(m.qt && tk_bridge_chat(m,W,x,y,M,g_chat_cs)){ } else if(m.qt){" + src[q.end():]
 
 
-def build(ref: Path) -> Path:
+def build(ref: Path, hooked: bool = True) -> Path:
+    """Build the engine into oracle/_ref/: tier_tk (hooked, linked to
+    libtierk.so) or, with hooked=False, tier_ref (the reference unchanged,
+    compiled from tier.cpp where it lies with the same command line)."""
     tier = ref / "tier.cpp"
     if not tier.exists():
         raise SystemExit(f"{tier} not found")
     lib = ROOT / "tier_b200" / "libtierk.so"
-    if not lib.exists():
+    if hooked and not lib.exists():
         raise SystemExit("libtierk.so not built: python -m tier_b200.build")
     OUT_DIR.mkdir(parents=True, exist_ok=True)
-    patched = OUT_DIR / "tier_tk.cpp"
-    patched.write_text(patch(tier.read_text()))
-    exe = OUT_DIR / "tier_tk"
+    if hooked:
+        src = OUT_DIR / "tier_tk.cpp"
+        src.write_text(patch(tier.read_text()))
+        exe = OUT_DIR / "tier_tk"
+    else:
+        src, exe = tier, OUT_DIR / "tier_ref"
     cmd = [NVCC, "-x", "cu", "-DTIER_CUDA", "-std=c++17", "-O1", "-Xcompiler", "-pthread -Wno-unused-result",
            "-diag-suppress", "177,1650", "-I", str(ref), "-I", str(ROOT / "include"), "-I", str(ROOT / "integration"),
-           "-gencode", "arch=compute_100,code=sm_100", str(patched), "-o", str(exe), "-lcublas", "-lcublasLt",
-           "-L", str(lib.parent), "-ltierk", "-Xlinker", f"-rpath={lib.parent}"]
+           "-gencode", "arch=compute_100,code=sm_100", str(src), "-o", str(exe), "-lcublas", "-lcublasLt"]
+    if hooked:
+        cmd += ["-L", str(lib.parent), "-ltierk", "-Xlinker", f"-rpath={lib.parent}"]
     r = subprocess.run(cmd, capture_output=True, text=True)
     if r.returncode:
         sys.stderr.write(r.stdout[-4000:] + r.stderr[-4000:])
-        raise SystemExit("patched engine did not build")
+        raise SystemExit("engine did not build")
     return exe
 
 

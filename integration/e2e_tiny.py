@@ -1,0 +1,103 @@
+#!/usr/bin/env python3
+"""End-to-end check of the hooked engine: tierlm's own training step run by
+the reference engine unchanged (oracle/_ref/tier_ref) and by the engine with
+its linear path on libtierk (oracle/_ref/tier_tk), on the same tiny model and
+tokens; the two step losses must agree.
+
+  prepare   (where the reference tree is, no GPU needed) writes
+            oracle/_ref/tiny/: a random-init 2-layer Llama (hidden 256,
+            vocab 2048) saved as bf16 safetensors by transformers, its
+            tier_arch.txt written by the reference's own arch.py, and
+            seq_len int32 token ids; then builds both engines.
+  run       (on a GPU) runs one training step of each engine with --bf3
+            (the fp16-x3 linear path the bridge routes) and --log, and
+            prints both losses as one JSON line; exit 1 if they differ by
+            more than the tolerance.
+
+The model is random, so its loss is near ln(vocab) and the engine's start-up
+check that stops a model it computes wrongly would fire:
+TIER_NO_SELFCHECK=1 turns that check off for this synthetic model.
+
+usage: python integration/e2e_tiny.py prepare [REF_DIR]
+       python integration/e2e_tiny.py run [--tol 1e-3]
+"""
+from __future__ import annotations
+
+import json
+import os
+import re
+import subprocess
+import sys
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parents[1]
+sys.path.insert(0, str(ROOT / "integration"))
+from build_patched_tier import OUT_DIR, build, default_ref  # noqa: E402
+
+TINY = OUT_DIR / "tiny"
+SEQ = 128
+LAYERS = 2
+
+
+def make_model(out: Path, ref: Path) -> None:
+    import numpy as np
+    import torch
+    from transformers import LlamaConfig, LlamaForCausalLM
+    torch.manual_seed(0)
+    cfg = LlamaConfig(vocab_size=2048, hidden_size=256, intermediate_size=512, num_hidden_layers=LAYERS,
+                      num_attention_heads=4, num_key_value_heads=2, max_position_embeddings=512, rms_norm_eps=1e-6,
+                      rope_theta=10000.0, tie_word_embeddings=False, bos_token_id=1, eos_token_id=2)
+    LlamaForCausalLM(cfg).to(torch.bfloat16).save_pretrained(str(out), safe_serialization=True)
+    r = subprocess.run([sys.executable, str(ref / "arch.py"), str(out)], capture_output=True, text=True)
+    if r.returncode != 0 or not (out / "tier_arch.txt").exists():
+        raise SystemExit("arch.py did not describe the model:\n" + r.stdout + r.stderr)
+    rng = np.random.default_rng(0)
+    rng.integers(3, cfg.vocab_size, size=SEQ, dtype=np.int32).tofile(out / "tokens.bin")
+
+
+def prepare(ref: Path) -> None:
+    TINY.mkdir(parents=True, exist_ok=True)
+    make_model(TINY, ref)
+    build(ref, hooked=False)
+    build(ref, hooked=True)
+    print(TINY)
+
+
+def step_loss(engine: Path, work: Path, timeout: int = 600) -> float:
+    """One training step on the tiny model; the loss from the step log."""
+    work.mkdir(parents=True, exist_ok=True)
+    log = work / "step.log"
+    for f in (log, work / "adam.bin", work / "tier1.bin"):
+        if f.exists():
+            f.unlink()
+    env = dict(os.environ, TIER_NO_SELFCHECK="1")
+    cmd = [str(engine), str(TINY / "model.safetensors"), str(TINY / "tokens.bin"), str(SEQ), str(work / "adam.bin"),
+           str(work / "tier1.bin"), "1e-5", str(LAYERS), "1", "--bf3", "--log", str(log)]
+    r = subprocess.run(cmd, capture_output=True, text=True, timeout=timeout, env=env, cwd=str(work))
+    (work / "stdout.txt").write_text(r.stdout + "\n--- stderr ---\n" + r.stderr)
+    if r.returncode != 0 or not log.exists():
+        raise SystemExit(f"{engine.name} failed (rc {r.returncode}); see {work / 'stdout.txt'}")
+    m = re.search(r"===== step \d+ .*? loss ([-0-9.eE+]+)", log.read_text())
+    if not m:
+        raise SystemExit(f"{engine.name}: no step loss in {log}")
+    return float(m.group(1))
+
+
+def run(tol: float) -> int:
+    ref_loss = step_loss(OUT_DIR / "tier_ref", TINY / "run_ref")
+    tk_loss = step_loss(OUT_DIR / "tier_tk", TINY / "run_tk")
+    diff = abs(tk_loss - ref_loss)
+    print(json.dumps({"check": "tiny llama, one --bf3 training step", "loss_reference": ref_loss,
+                      "loss_libtierk": tk_loss, "abs_diff": diff, "tol": tol}))
+    return 0 if diff <= tol else 1
+
+
+if __name__ == "__main__":
+    if len(sys.argv) > 1 and sys.argv[1] == "prepare":
+        prepare(Path(sys.argv[2]) if len(sys.argv) > 2 else default_ref())
+    elif len(sys.argv) > 1 and sys.argv[1] == "run":
+        tol = float(sys.argv[sys.argv.index("--tol") + 1]) if "--tol" in sys.argv else 1e-3
+        sys.exit(run(tol))
+    else:
+        print(__doc__)
+        sys.exit(2)

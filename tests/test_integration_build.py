@@ -67,3 +67,20 @@ def test_bridge_routing_and_call_arguments(tmp_path):
     lines = [ln.split() for ln in r.stdout.splitlines() if ln.strip()]
     assert len(lines) == 12
     assert all(v == "1" for _, v in lines), [n for n, v in lines if v != "1"]
+
+
+def test_tiny_model_is_accepted_by_the_reference_arch_tool(tmp_path):
+    """integration/e2e_tiny.py's model: a random 2-layer Llama that the
+    reference's own arch.py describes (tier_arch.txt), plus the token file the
+    engine's training mode reads (seq_len int32 ids)."""
+    from build_patched_tier import default_ref
+    ref = default_ref()
+    if not (ref / "arch.py").exists():
+        pytest.skip("reference tree not present")
+    pytest.importorskip("transformers")
+    from e2e_tiny import SEQ, make_model
+    make_model(tmp_path, ref)
+    desc = (tmp_path / "tier_arch.txt").read_text()
+    for key in ("family llama", "hidden 256", "inter 512", "heads 4", "vocab 2048", "head lm_head.weight"):
+        assert key in desc, key
+    assert (tmp_path / "tokens.bin").stat().st_size == 4 * SEQ
