@@ -238,8 +238,11 @@ tk_status tk_linear_dx(tk_ctx *ctx, const tk_weight *W, const void *dY, int dy_d
 /* tk_linear_fwd for callers that cannot allocate device memory -- an engine
  * that budgets all VRAM through its own arena, or code that must not call
  * cudaMalloc once running.  No counterpart in the reference.  Same arguments
- * and results as tk_linear_fwd, restricted to TK_F16 / TK_F16X2 weights; it
- * calls no cudaMalloc/cudaFree and never touches the context workspace.  Its
+ * as tk_linear_fwd, restricted to TK_F16 / TK_F16X2 weights (TK_QFUSED and
+ * TK_WREUSE are ignored); it calls no cudaMalloc/cudaFree and never touches
+ * the context workspace.  It never splits K, so its result equals
+ * tk_linear_fwd's bit for bit wherever tk_linear_fwd runs one K split (always
+ * for K < 2048) and within the product set's tolerance elsewhere.  Its
  * scratch is a static 24 MiB device array inside libtierk.so (held on every
  * GPU that loads the library until exit): 2 * parts * M * round8(K) + 4 * M
  * bytes (each term rounded up to 256) must fit, else TK_ERR_INVALID.  The
@@ -342,10 +345,6 @@ tk_status tk_lmhead_loss(tk_ctx *ctx, int T, const int32_t *labels, const uint8_
                          const double *rmax, const double *rsum, const int32_t *amax,
                          const float *tgt, double *loss_sum, int32_t *hits, void *stream);
 
-/* Vocab-sharded merge helper: rsum *= exp(rmax_local - rmax_global) and
- * rmax_local = rmax_global, for rows t < n (run between an all-reduce MAX of
- * rmax and an all-reduce SUM of rsum); with dX (nullable, [n, H]) the
- * single-pass accumulator rows are scaled by the same factor. */
 /* Vocabulary chunk for the LM head: the reference's lm_chunk rule
  * (tier/tier.cpp:2015-2017) -- device_bytes / 36 / (6*hidden + 8*max(seq,1))
  * rows, clamped to [1024, vocab rounded up] -- rounded down to a multiple of
@@ -354,6 +353,10 @@ tk_status tk_lmhead_loss(tk_ctx *ctx, int T, const int32_t *labels, const uint8_
  * only, no context. */
 int tk_lmhead_chunk(size_t device_bytes, int hidden, int seq, int vocab);
 
+/* Vocab-sharded merge helper: rsum *= exp(rmax_local - rmax_global) and
+ * rmax_local = rmax_global, for rows t < n (run between an all-reduce MAX of
+ * rmax and an all-reduce SUM of rsum); with dX (nullable, [n, H]) the
+ * single-pass accumulator rows are scaled by the same factor. */
 tk_status tk_lmhead_rescale(tk_ctx *ctx, int n, double *rmax_local, double *rsum_local,
                             const double *rmax_global, float *dX, int H, void *stream);
 

@@ -1,0 +1,195 @@
+"""Parity at the shapes the benchmark numbers are quoted on.
+
+Every case runs the product path through the C ABI at full size and checks
+  * the whole output against an fp64 matmul of the same operands on the GPU
+    (cuBLAS DGEMM as the checker: every tile of the timed schedule is seen), and
+  * sampled rows against a host fp64 matmul of the oracle's dequantization
+    (oracle/tk_oracle.c, pinned to the reference's q_val), which does not
+    depend on any GPU library.
+
+Cases:
+  C2  Q4_K W[14336, 4096], bf16 X[4096, 4096] and dY[4096, 14336], forward
+      then dX with TK_WREUSE (the bench's step): rel-Frobenius <= 2e-3 against
+      the exact q_val weight (the stated bound of the bf16 quant GEMM).
+  C3  the seven projections of one 12B-class layer at M = 4096 with fp32 X:
+      TK_X3_HHL on fp32 W split into fp16 hi/lo (<= 1e-5 against fp32 W) and
+      TK_X3_REF on fp16 W (the reference's fp3gemm, <= 1e-5 against that W).
+  C5  one layer of the 40-layer sweep per weight kind (q8_0; Q4_K_S recipe's
+      layer 0 = Q4_K + Q5_K; Q4_K_M recipe's layer 0 = Q4_K + Q6_K) at
+      M = 4096, fp32 X through the x3 split: <= 1e-5 against the fp16 expansion
+      of q_val that the GEMM consumes (tier/tier.cpp:294-296 rounds it so).
+  split3  tk_split3 against the reference kernel's own outputs
+      (tests/golden/split3_golden.npz, split3_fp_k tier/tier.cpp:869-870).
+"""
+import numpy as np
+import pytest
+
+from conftest import GOLDEN
+from gen import blocks_for, q4_k_blocks, rel_fro
+
+pytestmark = pytest.mark.gpu
+
+H, I = 5120, 14336
+C3_SHAPES = [(4096, H), (1024, H), (1024, H), (H, 4096), (I, H), (I, H), (H, I)]   # q k v o gate up down
+C3_NAMES = ["q", "k", "v", "o", "gate", "up", "down"]
+
+
+def _fp64_ref(A, B_t):
+    """A[M, K] . B_t^T in fp64 on the GPU (B_t is [N, K])."""
+    import torch
+    return A.double() @ B_t.double().T
+
+
+def _fp64_ref_dx(dY, W):
+    return dY.double() @ W.double()
+
+
+def _rel(got, want):
+    import torch
+    d = (got.double() - want).norm()
+    return float(d / want.norm().clamp_min(1e-300))
+
+
+def _rows_rel(got_rows, want_rows):
+    return max(rel_fro(g, w) for g, w in zip(got_rows, want_rows))
+
+
+def test_split3_matches_reference_kernel_on_gpu(ctx):
+    """tk_split3 is bit-identical to split3_fp_k's outputs recorded from the
+    reference's kernel body (including the fixture's zeros, signed zeros,
+    subnormals and large values)."""
+    import torch
+    g = np.load(GOLDEN / "split3_golden.npz")
+    x = torch.from_numpy(g["x"]).cuda()
+    n = x.numel()
+    h, m, l = (torch.empty(n, dtype=torch.float16, device="cuda") for _ in range(3))
+    ctx.split3(x, h, m, l)
+    torch.cuda.synchronize()
+    for got, key in ((h, "h"), (m, "m"), (l, "l")):
+        assert np.array_equal(got.cpu().view(torch.int16).numpy().view(np.uint16), g[key]), key
+    # a second call with an odd length and an offset start (unaligned vector path)
+    x2 = x[3:3 + 1001]
+    h2, m2, l2 = (torch.empty(1001, dtype=torch.float16, device="cuda") for _ in range(3))
+    ctx.split3(x2, h2, m2, l2)
+    torch.cuda.synchronize()
+    assert np.array_equal(h2.cpu().view(torch.int16).numpy().view(np.uint16), g["h"][3:1004])
+    assert np.array_equal(l2.cpu().view(torch.int16).numpy().view(np.uint16), g["l"][3:1004])
+    ctx.sync_status()
+
+
+def test_c2_full_size_fwd_dx(ctx, oracle):
+    """The headline step at its own shape: Q4_K 14336x4096, M = 4096, bf16."""
+    import torch
+    import tier_b200 as tk
+    M, N, K = 4096, 14336, 4096
+    rng = np.random.default_rng(1)
+    Wq = q4_k_blocks(rng, N, K)
+    X = torch.from_numpy(rng.standard_normal((M, K), dtype=np.float32)).to(torch.bfloat16)
+    dY = torch.from_numpy(rng.standard_normal((M, N), dtype=np.float32)).to(torch.bfloat16)
+    Wf = oracle.dequant(Wq, tk.Q4_K, N, K, 0)                 # exact q_val, fp32
+    w = tk.make_weight(tk.Q4_K, N, K, torch.from_numpy(Wq).cuda())
+    Xd, dYd = X.cuda(), dY.cuda()
+    Y = torch.empty(M, N, device="cuda")
+    dX = torch.empty(M, K, device="cuda")
+    for _ in range(2):            # the second step reuses the first's expansion state, as the bench does
+        ctx.linear(w, Xd, M, Y, x_dtype=tk.DT_BF16)
+        ctx.linear_dx(w, dYd, M, dX, dy_dtype=tk.DT_BF16, products=tk.WREUSE)
+    torch.cuda.synchronize()
+    ctx.sync_status()
+    Wg = torch.from_numpy(Wf).cuda()
+    ey = _rel(Y, _fp64_ref(Xd, Wg))
+    edx = _rel(dX, _fp64_ref_dx(dYd, Wg))
+    assert ey < 2e-3 and edx < 2e-3, (ey, edx)
+    # no tile may be off even when the whole is close: per-row relative error
+    ry = ((Y.double() - _fp64_ref(Xd, Wg)).norm(dim=1) / _fp64_ref(Xd, Wg).norm(dim=1)).max().item()
+    assert ry < 5e-3, ry
+    # host fp64 of the oracle's dequantization on sampled rows (first, last, tile edges)
+    rows = [0, 127, 128, 255, 256, 2047, 4095]
+    Xf = X.float().numpy().astype(np.float64)
+    dYf = dY.float().numpy().astype(np.float64)
+    Wf64 = Wf.astype(np.float64)
+    Yh = Y.cpu().numpy()
+    dXh = dX.cpu().numpy()
+    assert _rows_rel([Yh[r] for r in rows], [Xf[r] @ Wf64.T for r in rows]) < 2e-3
+    assert _rows_rel([dXh[r] for r in rows], [dYf[r] @ Wf64 for r in rows]) < 2e-3
+    # sampled columns of Y cross every M tile: Y[:, n] = X . W[n]
+    cols = [0, 255, 256, 7167, 14335]
+    assert _rows_rel([Yh[:, c] for c in cols], [Xf @ Wf64[c] for c in cols]) < 2e-3
+
+
+@pytest.mark.parametrize("mode", ["hhl", "ref"])
+def test_c3_layer_full_size(ctx, mode):
+    """All seven projections of the 12B-class layer at M = 4096, fwd + dX."""
+    import torch
+    import tier_b200 as tk
+    from tier_b200.host import LinearPath
+    M = 4096
+    g = torch.Generator(device="cuda").manual_seed(2)
+    worst = {}
+    for name, (n, k) in zip(C3_NAMES, C3_SHAPES):
+        W32 = torch.randn(n, k, device="cuda", generator=g) * 0.02
+        X = torch.randn(M, k, device="cuda", generator=g)
+        dY = torch.randn(M, n, device="cuda", generator=g)
+        if mode == "hhl":
+            lp = LinearPath.from_f32_split(ctx, W32)
+            w, Wref, prod = lp.W, W32, tk.X3_HHL
+        else:
+            W16 = W32.half()
+            w, Wref, prod = tk.make_weight(tk.F16, n, k, W16), W16, tk.X3_REF
+        Y = torch.empty(M, n, device="cuda")
+        dX = torch.empty(M, k, device="cuda")
+        ctx.linear(w, X, M, Y, products=prod)
+        ctx.linear_dx(w, dY, M, dX, products=prod)
+        torch.cuda.synchronize()
+        ctx.sync_status()
+        ey = _rel(Y, _fp64_ref(X, Wref))
+        edx = _rel(dX, _fp64_ref_dx(dY, Wref))
+        worst[name] = (ey, edx)
+        # host fp64 on two sampled rows
+        Wh = Wref.double().cpu().numpy()
+        for r in (1, M - 1):
+            assert rel_fro(Y[r].cpu().numpy(), X[r].double().cpu().numpy() @ Wh.T) < 1e-5, (name, r)
+            assert rel_fro(dX[r].cpu().numpy(), dY[r].double().cpu().numpy() @ Wh) < 1e-5, (name, r)
+        del W32, X, dY, Y, dX
+    bad = {k: v for k, v in worst.items() if max(v) >= 1e-5}
+    assert not bad, bad
+
+
+def _c5_layer0_types(kind):
+    import tier_b200 as tk
+    from tier_b200.tq import recipe_types
+    if kind == "q8_0":
+        return [tk.Q8_0] * 7
+    slots = ["q_proj", "k_proj", "v_proj", "o_proj", "gate_proj", "up_proj", "down_proj"]
+    t = {(l, s): qt for l, s, qt in recipe_types(kind.upper(), [slots] * 40)}
+    return [t[(0, s)] for s in slots]
+
+
+@pytest.mark.parametrize("kind", ["q8_0", "q4_k_s", "q4_k_m"])
+def test_c5_layer_full_size(ctx, oracle, kind):
+    """One sweep layer per weight kind at M = 4096: fp32 X split in three
+    (the reference's fp3gemm products) over the bit-exact fp16 expansion."""
+    import torch
+    import tier_b200 as tk
+    M = 4096
+    types = _c5_layer0_types(kind)
+    if kind != "q8_0":
+        assert tk.Q4_K in types and (tk.Q5_K in types or tk.Q6_K in types)
+    rng = np.random.default_rng(4)
+    g = torch.Generator(device="cuda").manual_seed(4)
+    for name, (n, k), qt in zip(C3_NAMES, C3_SHAPES, types):
+        b = blocks_for(rng, qt, n, k)
+        W16 = torch.from_numpy(oracle.dequant(b, qt, n, k, 1).view(np.float16)).cuda()   # tier_fp16(q_val)
+        w = tk.make_weight(qt, n, k, torch.from_numpy(b).cuda())
+        X = torch.randn(M, k, device="cuda", generator=g)
+        dY = torch.randn(M, n, device="cuda", generator=g)
+        Y = torch.empty(M, n, device="cuda")
+        dX = torch.empty(M, k, device="cuda")
+        ctx.linear(w, X, M, Y)
+        ctx.linear_dx(w, dY, M, dX, products=tk.WREUSE)
+        torch.cuda.synchronize()
+        ctx.sync_status()
+        ey = _rel(Y, _fp64_ref(X, W16))
+        edx = _rel(dX, _fp64_ref_dx(dY, W16))
+        assert ey < 1e-5 and edx < 1e-5, (kind, name, qt, ey, edx)
+        del W16, X, dY, Y, dX

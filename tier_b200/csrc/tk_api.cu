@@ -81,17 +81,6 @@ struct Carve {
     }
 };
 
-// k-blocks (64 each) per fp32 accumulation segment for the split product sets.
-// The error of the tensor-core fp32 accumulation grows with the segment
-// length, not with K (measured relative error vs fp64 on B200, x3 REF / HHL:
-// 8 -> 1.2e-6 / 1.7e-6, 16 -> 2.4e-6 / 3.5e-6, 32 -> 4.5e-6 / 7.1e-6), while
-// each segment costs one fp32 read-modify-write of the tile.  16 keeps a 3x
-// margin under the 1e-5 bound.
-#ifndef TK_SEG_KB
-#define TK_SEG_KB 16
-#endif
-constexpr int kSegKb = TK_SEG_KB;
-
 static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
 // Planes / products for one linear call.

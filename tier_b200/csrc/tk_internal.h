@@ -41,6 +41,17 @@ struct tk_ctx {
 
 namespace tk {
 
+// k-blocks (64 each) per fp32 accumulation segment for the split product sets.
+// The error of the tensor-core fp32 accumulation grows with the segment
+// length, not with K (measured relative error vs fp64 on B200, x3 REF / HHL:
+// 8 -> 1.2e-6 / 1.7e-6, 16 -> 2.4e-6 / 3.5e-6, 32 -> 4.5e-6 / 7.1e-6), while
+// each segment costs one fp32 read-modify-write of the tile.  16 keeps a 3x
+// margin under the 1e-5 bound.
+#ifndef TK_SEG_KB
+#define TK_SEG_KB 16
+#endif
+constexpr int kSegKb = TK_SEG_KB;
+
 // Kernel families for tk_profile_read (TK_PROF_* in tierk.h).
 enum ProfKind { PK_GEMM = 0, PK_DEQUANT = 1, PK_SPLIT = 2, PK_GEMV = 3, PK_LMHEAD = 4, PK_COUNT = 5 };
 int prof_begin(tk_ctx* ctx, cudaStream_t s);

@@ -72,7 +72,9 @@ static tk_status noalloc_fwd(tk_ctx* ctx, const tk_weight* W, const void* X, int
     if ((reinterpret_cast<uintptr_t>(Y) & 15) || ldy % 4)
         return fail(TK_ERR_INVALID, std::string(fn) + ": output must be 16-byte aligned, ld % 4 == 0");
 
-    // product set: same meaning as tk_linear_fwd
+    // product set: same meaning as tk_linear_fwd.  TK_QFUSED and TK_WREUSE
+    // only concern quantized weights, which this entry point does not take.
+    products &= ~(TK_QFUSED | TK_WREUSE);
     const bool wx2 = W->qtype == TK_F16X2;
     int mode = products == TK_X3_AUTO ? (wx2 ? TK_X3_HHL : (x_dtype == TK_DT_F32 ? TK_X3_REF : TK_X1)) : products;
     int planes = 1, nprod = 1, pa[3] = {0, 0, 0}, pb[3] = {0, 0, 0};
@@ -116,7 +118,8 @@ static tk_status noalloc_fwd(tk_ctx* ctx, const tk_weight* W, const void* X, int
     g.beta = beta != 0.0f;
     g.row_exp = row_exp;
     g.col_exp = wx2 ? W->scale_log2 : 0;
-    g.seg_kb = nprod > 1 ? 8 : 0;   // same fp32 accumulation segments as tk_linear_fwd
+    g.seg_kb = nprod > 1 ? kSegKb : 0;   // the accumulation segments tk_linear_fwd uses
+    // no split-K workspace (g.split_ws stays null): K is never split here
     return launch_gemm(ctx, g, s);
 }
 
