@@ -15,9 +15,11 @@ which is all-reduced in M-chunks overlapped with the next chunk's GEMM.
 Total work is fixed (strong scaling); value = total FLOP / max-over-ranks time.
 
 --impl reference: the reference's CPU implementation of the same operation
-(its quant.h q_val dequant compiled from its sources in oracle/_ref, with the
-cpu_gemm_fwd/cpu_gemm_dx loop structure), timed on this host's cores on a
-bounded sample of the workload (a slice of weight rows), rank 0 only.
+(the engine's own cpu_gemm_fwd / cpu_gemm_dx and thread pool, extracted and
+compiled from its sources into oracle/_ref, over its quant.h q_val rows
+rounded to bf16), timed on this host's cores on a bounded sample of the
+workload (a slice of weight rows), rank 0 only; gguf-py + numpy (the
+reference test's oracle) is timed beside it.
 
 Data: synthetic, seeded (tests/gen.py); no dataset exists for this path.
 """
@@ -109,74 +111,143 @@ def make_inputs(seed=1):
 
 
 # ---------------------------------------------------------------------------
+class RefCPU:
+    """The reference's CPU path for one sampled slice of the C2 step.
+
+    engine (kind "reference"): the reference engine's own CPU GEMMs,
+      cpu_gemm_fwd / cpu_gemm_dx with the thread pool they run on
+      (tier/tier.cpp:1015-1099, AVX2 FMA over bf16 weight rows), extracted and
+      compiled from the reference's sources into oracle/_ref/libtkref.so, fed
+      the reference's q_val expansion (tier/quant.h:59-121) of the sampled
+      weight rows rounded to bf16 -- the expansion is inside every step.
+    numpy (the reference test's oracle, tier/check_quant.py:71): gguf-py's
+      quants.dequantize of the sampled rows, then numpy float32 matmuls (BLAS
+      threads = all cores)."""
+
+    def __init__(self, threads):
+        from oracle.oracle import RefOracle
+        self.threads = threads
+        self.eng = RefOracle()
+        self.eng.engine_pool(threads)
+
+    @staticmethod
+    def available() -> bool:
+        from oracle.oracle import RefOracle
+        return RefOracle.available()
+
+    def prepare(self, Wq, X, dY, rows):
+        import numpy as np
+        self.rows = rows
+        self.Wq = Wq
+        self.X = X
+        self.dY = np.ascontiguousarray(dY[:, :rows])
+        self.Wb = np.empty((rows, K_IN), np.uint16)
+        self.Y = np.empty((M_TOK, rows), np.float32)
+        self.dX = np.empty((M_TOK, K_IN), np.float32)
+
+    def step(self):
+        self.eng.dequant_bf16(self.Wq, 12, 0, self.rows, K_IN, out=self.Wb)
+        self.eng.cpu_gemm_fwd(self.X, self.Wb, out=self.Y)
+        self.eng.cpu_gemm_dx(self.dY, self.Wb, out=self.dX)
+
+    def calibrate(self, Wq, X, dY, target_s):
+        """Rows of the workload whose step takes about target_s on the host.
+        Probes grow (at most 8x at a time) until one takes a quarter of the
+        target; the run is sized from it."""
+        rows = 64
+        self.prepare(Wq, X, dY, rows)
+        self.step()           # pool start-up and the GEMMs' first-touch of their buffers, untimed
+        while True:
+            self.prepare(Wq, X, dY, rows)
+            t0 = time.perf_counter()
+            self.step()
+            dt = max(time.perf_counter() - t0, 1e-3)
+            want = max(16, min(N_OUT, int(rows * target_s / dt) // 16 * 16))
+            if dt >= target_s / 4 or rows == N_OUT:
+                return want
+            rows = max(16, min(N_OUT, want, rows * 8))
+
+    def sample_text(self, rows):
+        return (f"Q4_K rows 0..{rows} of {N_OUT} (K={K_IN}), M={M_TOK} fp32 tokens, fwd + dX per step: the "
+                f"reference engine's cpu_gemm_fwd / cpu_gemm_dx (tier/tier.cpp:1015-1099, extracted, AVX2) on "
+                f"its q_val rows rounded to bf16, {self.threads} pool threads; rate scaled to the unit by FLOPs")
+
+
+def numpy_baseline(Wq, X, dY, seconds):
+    """gguf-py dequantize + numpy matmuls on a row sample sized to ~seconds."""
+    import numpy as np
+    try:
+        from gguf import GGMLQuantizationType, quants
+        import gguf
+    except ImportError:
+        return None
+    rows = 64
+    while True:
+        t0 = time.perf_counter()
+        W = quants.dequantize(Wq[:rows], GGMLQuantizationType.Q4_K)
+        Y = X @ W.T
+        dX = np.ascontiguousarray(dY[:, :rows]) @ W
+        dt = time.perf_counter() - t0
+        if dt >= seconds / 4 or rows >= N_OUT:
+            break
+        rows = min(N_OUT, rows * 4)
+    v = 2 * 2.0 * M_TOK * rows * K_IN / dt / 1e12
+    del Y, dX
+    return {"value": v, "unit": "TFLOP/s", "cores": os.cpu_count() or 1, "kind": "reference-test oracle",
+            "sample": f"Q4_K rows 0..{rows} of {N_OUT}, M={M_TOK}: gguf-py {getattr(gguf, '__version__', '?')} "
+                      f"quants.dequantize + numpy float32 X.W^T and dY.W (tier/check_quant.py:71), one pass "
+                      f"({dt:.1f} s)"}
+
+
 def run_reference(args):
     """The reference's CPU path on a bounded sample (rank 0 only)."""
     world, rank, _ = dist_env()
     if rank != 0:
         return
-    import numpy as np
-    from oracle.oracle import RefOracle, Oracle
     threads = os.cpu_count() or 1
+    if not RefCPU.available():
+        return print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref (the reference's CPU code built "
+                                                                     "from its sources) is not present"}))
     Wq, X, dY = make_inputs()
-    kind = "reference" if RefOracle.available() else "port"
-    eng = RefOracle() if kind == "reference" else None
-    if eng is None:
-        return print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref not built and no port timing"}))
-    per_step = min(args.ref_seconds, 150.0 / (args.steps + args.warmup))   # whole run within a few minutes
-    rows = calibrate_rows(eng, Wq, X, dY, threads, target_s=per_step)
+    ref = RefCPU(threads)
+    per_step = min(args.ref_seconds, 120.0 / (args.steps + args.warmup))   # whole run within a few minutes
+    rows = ref.calibrate(Wq, X, dY, target_s=per_step)
+    ref.prepare(Wq, X, dY, rows)
     times = []
     for i in range(args.warmup + args.steps):
         t0 = time.perf_counter()
-        eng.qgemm_fwd(Wq, 12, 0, rows, K_IN, X, threads)
-        eng.qgemm_dx(Wq, 12, 0, rows, K_IN, dY[:, :rows], threads)
+        ref.step()
         dt = time.perf_counter() - t0
         if i >= args.warmup:
             times.append(dt)
     t = statistics.median(times)
     flop = 2 * 2.0 * M_TOK * rows * K_IN
     v = flop / t / 1e12
-    sample = (f"Q4_K rows 0..{rows} of {N_OUT} (K={K_IN}), M={M_TOK} fp32 tokens, fwd+dX per step; "
-              f"reference quant.h q_val + cpu_gemm_fwd/dx loop structure, {threads} threads")
     line = {"metric": METRIC, "value": v, "unit": "TFLOP/s", "n_gpus": args.gpus, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": t * 1e3, "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded, tests/gen.py)", "impl": "reference",
-            "config": {"workload": "C2 Q4_K 14336x4096 fwd+dX, M=4096 (sampled rows)", "rows_sampled": rows},
-            "cpu_baseline": {"value": v, "unit": "TFLOP/s", "cores": threads, "kind": kind, "sample": sample},
-            "e2e": {"value": v, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+            "vs_baseline": None, "dtype": "f32 (bf16 weights)", "data": "synthetic (seeded, tests/gen.py)",
+            "impl": "reference",
+            "config": {"workload": "C2 Q4_K 14336x4096 fwd+dX, M=4096 (sampled weight rows)", "rows_sampled": rows},
+            "cpu_baseline": {"value": v, "unit": "TFLOP/s", "cores": threads, "kind": "reference",
+                             "sample": ref.sample_text(rows)},
+            "e2e": {"value": v, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "numpy_baseline": numpy_baseline(Wq, X, dY, 8.0)}
     print(json.dumps(line))
 
 
-def calibrate_rows(eng, Wq, X, dY, threads, target_s):
-    """Rows of the workload that take about target_s on the host.  The
-    per-row cost falls as fixed costs amortise, so probes grow (at most 8x at
-    a time) until one takes a quarter of the target; the run is sized from it."""
-    rows = 16
-    while True:
-        t0 = time.perf_counter()
-        eng.qgemm_fwd(Wq, 12, 0, rows, K_IN, X, threads)
-        eng.qgemm_dx(Wq, 12, 0, rows, K_IN, dY[:, :rows], threads)
-        dt = max(time.perf_counter() - t0, 1e-3)
-        want = max(16, min(N_OUT, int(rows * target_s / dt) // 16 * 16))
-        if dt >= target_s / 4 or rows == N_OUT:
-            return want
-        rows = max(16, min(N_OUT, want, rows * 8))
-
-
 def cpu_baseline(Wq, X, dY, seconds):
-    from oracle.oracle import RefOracle
     threads = os.cpu_count() or 1
-    if not RefOracle.available():
+    if not RefCPU.available():
         return None
-    eng = RefOracle()
-    rows = calibrate_rows(eng, Wq, X, dY, threads, target_s=seconds)
+    ref = RefCPU(threads)
+    rows = ref.calibrate(Wq, X, dY, target_s=seconds)
+    ref.prepare(Wq, X, dY, rows)
     t0 = time.perf_counter()
-    eng.qgemm_fwd(Wq, 12, 0, rows, K_IN, X, threads)
-    eng.qgemm_dx(Wq, 12, 0, rows, K_IN, dY[:, :rows], threads)
+    ref.step()
     t = time.perf_counter() - t0
     v = 2 * 2.0 * M_TOK * rows * K_IN / t / 1e12
     return {"value": v, "unit": "TFLOP/s", "cores": threads, "kind": "reference",
-            "sample": f"Q4_K rows 0..{rows} of {N_OUT}, M={M_TOK}, fwd+dX, one pass ({t:.1f} s); reference quant.h "
-                      f"q_val row expansion + cpu_gemm_fwd/dx loop structure on {threads} threads"}
+            "sample": ref.sample_text(rows) + f"; one pass ({t:.1f} s)"}
 
 
 CHECK_TOL = 2e-3        # the stated bound of the bf16-activation quant GEMM (relative, vs fp64)

@@ -10,13 +10,14 @@ The recipe reads tier/tier.cpp where it lies and adds four hooks:
     tk_linear_dx and returns;
   * in `chat_lin` (tier/tier.cpp:2351), the quantized branch tries tk_gemv /
     tk_linear_fwd first.
-It writes the patched engine to oracle/_ref/tier_tk.cpp (build output beside
-the other reference builds: git-ignored, never committed) and compiles it
+It writes the patched engine to integration/_build/tier_tk.cpp (build output:
+git-ignored, never committed) and compiles it
 with the reference's own nvcc line (tier/build.sh:89) for sm_100, linked to
 libtierk.so.  The binary is not run here: it needs model files.
 
 usage: python integration/build_patched_tier.py [REF_DIR]
-       (REF_DIR defaults to $TK_REF_DIR, else the directory oracle/Makefile uses)
+       (REF_DIR defaults to $TIER_REF, else the reference checkout beside this
+        repository, ../reference/tier)
 """
 from __future__ import annotations
 
@@ -27,12 +28,13 @@ import sys
 from pathlib import Path
 
 ROOT = Path(__file__).resolve().parents[1]
-OUT_DIR = ROOT / "oracle" / "_ref"
+OUT_DIR = ROOT / "integration" / "_build"
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 
 
 def default_ref() -> Path:
-    return Path(os.environ.get("TK_REF_DIR", "/root/reference/tier"))   # as oracle/Makefile's REF
+    env = os.environ.get("TIER_REF")
+    return Path(env) if env else ROOT.parent / "reference" / "tier"
 
 
 # (pattern, replacement builder, what it hooks).  Each pattern must match once.
@@ -71,7 +73,7 @@ def patch(src: str) -> str:
 
 
 def build(ref: Path, hooked: bool = True) -> Path:
-    """Build the engine into oracle/_ref/: tier_tk (hooked, linked to
+    """Build the engine into integration/_build/: tier_tk (hooked, linked to
     libtierk.so) or, with hooked=False, tier_ref (the reference unchanged,
     compiled from tier.cpp where it lies with the same command line)."""
     tier = ref / "tier.cpp"

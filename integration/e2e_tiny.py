@@ -1,11 +1,11 @@
 #!/usr/bin/env python3
 """End-to-end check of the hooked engine: tierlm's own training step run by
-the reference engine unchanged (oracle/_ref/tier_ref) and by the engine with
-its linear path on libtierk (oracle/_ref/tier_tk), on the same tiny model and
+the reference engine unchanged (integration/_build/tier_ref) and by the engine with
+its linear path on libtierk (integration/_build/tier_tk), on the same tiny model and
 tokens; the two step losses must agree.
 
   prepare   (where the reference tree is, no GPU needed) writes
-            oracle/_ref/tiny/: a random-init 2-layer Llama (hidden 256,
+            integration/_build/tiny/: a random-init 2-layer Llama (hidden 256,
             vocab 2048) saved as bf16 safetensors by transformers, its
             tier_arch.txt written by the reference's own arch.py, and
             seq_len int32 token ids; then builds both engines.

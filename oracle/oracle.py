@@ -24,9 +24,21 @@ def _p(a: np.ndarray):
     return a.ctypes.data_as(P)
 
 
+def reference_dir() -> Path | None:
+    """The reference's tier/ directory: $TIER_REF, else the checkout beside
+    this repository (../reference/tier); None when neither exists (the GPU box
+    has no reference tree and uses the prebuilt _ref)."""
+    import os
+    env = os.environ.get("TIER_REF")
+    cand = Path(env) if env else HERE.parent.parent / "reference" / "tier"
+    return cand if (cand / "quant.h").exists() else None
+
+
 def build(quiet: bool = True) -> None:
     """Run oracle/Makefile (compiles _ref too when the reference tree exists)."""
-    r = subprocess.run(["make", "-C", str(HERE)], capture_output=True, text=True)
+    ref = reference_dir()
+    cmd = ["make", "-C", str(HERE)] + ([f"REF={ref}"] if ref else [])
+    r = subprocess.run(cmd, capture_output=True, text=True)
     if r.returncode:
         raise RuntimeError("oracle build failed:\n" + r.stdout + r.stderr)
     if not quiet:
@@ -178,6 +190,35 @@ class RefOracle:
         self.L.ref_lse_chunk(_p(np.ascontiguousarray(lg, np.float32)), _p(rmax), _p(rsum), _p(amax), _p(tgt),
                              _p(np.ascontiguousarray(tokens, np.int32)), _p(np.ascontiguousarray(mask, np.uint8)),
                              n_pred, vc, v0)
+
+    # -- the engine's own CPU GEMMs (tier/tier.cpp:1015-1099), extracted --
+    def engine_pool(self, threads: int):
+        """Start the reference's thread pool with `threads` workers."""
+        self.L.ref_cpu_pool(int(threads))
+
+    def dequant_bf16(self, blocks, qtype, n0, nrows, K, out=None):
+        """q_val rows n0 .. n0+nrows rounded to bf16 (uint16 [nrows, K])."""
+        b = np.ascontiguousarray(blocks, dtype=np.uint8)
+        out = np.empty((nrows, K), np.uint16) if out is None else out
+        rb = int(self.L.ref_row_bytes(qtype, K))
+        self.L.ref_dequant_bf16(_p(b), ctypes.c_size_t(rb), qtype, n0, nrows, K, _p(out))
+        return out
+
+    def cpu_gemm_fwd(self, X, Wbf16, out=None):
+        """cpu_gemm_fwd: out[M, N] = X[M, K] . W^T, W bf16 [N, K]."""
+        M, K = X.shape
+        N = Wbf16.shape[0]
+        out = np.empty((M, N), np.float32) if out is None else out
+        self.L.ref_cpu_gemm_fwd(_p(X), _p(Wbf16), _p(out), M, K, N)
+        return out
+
+    def cpu_gemm_dx(self, dY, Wbf16, out=None):
+        """cpu_gemm_dx: out[M, K] = dY[M, N] . W, W bf16 [N, K]."""
+        M, N = dY.shape
+        K = Wbf16.shape[1]
+        out = np.empty((M, K), np.float32) if out is None else out
+        self.L.ref_cpu_gemm_dx(_p(dY), _p(Wbf16), _p(out), M, K, N)
+        return out
 
     def qgemm_fwd(self, blocks, qtype, n0, nrows, K, X, threads):
         """CPU baseline: Y[M, nrows] via q_val row expansion + fp32 dots."""

@@ -17,11 +17,15 @@
 //   ref_lse_chunk                tier/tier.cpp:750-759 (lse_chunk_kernel, extracted;
 //                                each block runs as 256 host threads with a
 //                                barrier for __syncthreads, as launched at 3219)
-//   ref_cpu_qgemm_fwd / _dx      CPU baseline: q_val row expansion + the
-//                                cpu_gemm_fwd / cpu_gemm_dx loop structure
-//                                (tier/tier.cpp:1049-1099) over fp32 rows,
-//                                rows split across threads like pool_run
-//                                (tier/tier.cpp:1041-1046).
+//   ref_cpu_qgemm_fwd / _dx      a restatement (not the reference's code):
+//                                q_val row expansion + the cpu_gemm_fwd /
+//                                cpu_gemm_dx loop structure over fp32 rows
+//   ref_cpu_pool, ref_cpu_gemm_fwd / _dx, ref_dequant_bf16
+//                                the engine's own CPU GEMMs, extracted
+//                                (cpu_gemm_fwd / cpu_gemm_dx with pool_run and
+//                                its workers, tier/tier.cpp:1015-1099): AVX2 FMA
+//                                over bf16 weight rows; ref_dequant_bf16 feeds
+//                                them q_val rounded to bf16 (nearest even).
 #include "quant.h"
 #include <cstdint>
 #include <cstring>
@@ -209,3 +213,53 @@ void ref_cpu_qgemm_dx(const uint8_t* W, size_t rb, int type, int n0, int nrows, 
 }
 
 }  // extern "C"
+
+// ---- the engine's CPU GEMMs (tier/tier.cpp:1015-1099), extracted ----
+#include <immintrin.h>
+#include <atomic>
+#include <chrono>
+static int g_cpu_thr = 1;   // the engine's CPU thread count (pool_init starts that many workers)
+#include "ref_cpu_gemm.inc"
+
+extern "C" {
+
+// Start the reference's thread pool with `threads` workers (once; later
+// calls with another count restart it, as pool_init does).
+void ref_cpu_pool(int threads)
+{
+    g_cpu_thr = threads;
+    pool_init();
+}
+
+void ref_cpu_gemm_fwd(const float* X, const uint16_t* Wbf16, float* out, int M, int K, int N)
+{
+    cpu_gemm_fwd(X, Wbf16, out, M, K, N);
+}
+
+void ref_cpu_gemm_dx(const float* dY, const uint16_t* Wbf16, float* dX, int M, int K, int N)
+{
+    cpu_gemm_dx(dY, Wbf16, dX, M, K, N);
+}
+
+// rows n0 .. n0+nrows of a block-quantized W as bf16 (q_val, then nearest
+// even), the weight form the engine's CPU GEMMs read; rows split over
+// the pool like the GEMMs themselves.
+void ref_dequant_bf16(const uint8_t* W, size_t rb, int type, int n0, int nrows, int K, uint16_t* out)
+{
+    pool_run(nrows, [&](int a, int b) {
+        for (int i = a; i < b; ++i) {
+            const uint8_t* row = W + (size_t)(n0 + i) * rb;
+            uint16_t* o = out + (size_t)i * K;
+            for (int k = 0; k < K; ++k) {
+                float f = q_val(row, type, k);
+                uint32_t u;
+                std::memcpy(&u, &f, 4);
+                u += 0x7FFFu + ((u >> 16) & 1u);
+                o[k] = (uint16_t)(u >> 16);
+            }
+        }
+    });
+}
+
+}  // extern "C"
+

@@ -6,6 +6,7 @@ reproduces it byte for byte.
 
 usage: python tests/golden/gen_tq_golden.py /path/to/reference/tier
 """
+import os
 import sys
 from pathlib import Path
 
@@ -36,4 +37,6 @@ def main(ref_tier):
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference/tier")
+    if len(sys.argv) < 2 and not os.environ.get("TIER_REF"):
+        raise SystemExit("usage: gen_tq_golden.py <reference tier/ directory>  (or set TIER_REF)")
+    main(sys.argv[1] if len(sys.argv) > 1 else os.environ["TIER_REF"])

@@ -488,17 +488,25 @@ tk_status launch_act_split(tk_ctx* ctx, const void* X, int x_dtype, int M, int K
     return cuda_fail(cudaGetLastError(), "act_split launch");
 }
 
+// fp32 -> fp16 bits as tier_fp16::from_float (tier/gpu_compat.h:151-171):
+// round to nearest even, overflow to inf, and every NaN encoded as its sign
+// with 0x7e00 (the hardware conversion would keep NaN payload bits).
+__device__ __forceinline__ uint16_t f2h_ref(float v) {
+    if (isnan(v)) return (uint16_t)(((__float_as_uint(v) >> 16) & 0x8000u) | 0x7e00u);
+    return f2h_bits(v);
+}
+
 // split3_fp_k exactly (no scaling): h = f16(x), m = f16(x-h), l = f16(x-h-m).
 __global__ void split3_raw_kernel(const float* __restrict__ x, size_t n, uint16_t* __restrict__ h,
                                   uint16_t* __restrict__ m, uint16_t* __restrict__ l) {
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
         const float v = x[i];
-        const uint16_t a = f2h_bits(v);
+        const uint16_t a = f2h_ref(v);
         const float r = v - h2f_bits(a);
-        const uint16_t b = f2h_bits(r);
+        const uint16_t b = f2h_ref(r);
         h[i] = a;
         m[i] = b;
-        l[i] = f2h_bits(r - h2f_bits(b));
+        l[i] = f2h_ref(r - h2f_bits(b));
     }
 }
 
