@@ -199,6 +199,117 @@ def numpy_baseline(Wq, X, dY, seconds):
                       f"({dt:.1f} s)"}
 
 
+def reference_gpu(steps=5):
+    """The reference engine's own GPU path on this box (oracle/ref_gpu.cu:
+    tier.cpp compiled whole with cuBLAS / cuBLASLt, as its build.sh does),
+    on the configurations the repository's arm measures:
+      C1  gemv_q, q8_0 4096x4096 and 14336x4096, one token (as chat_lin
+          launches it), rotating weight copies over 4x the L2;
+      C3  fp3gemm (split3_fp_k + three cuBLASLt GEMMs) forward + dX of the
+          seven 12B-class projections, fp16 W, fp32 X, M = 4096;
+      C2  the training path for a Q4_K weight: dq_launch to fp16, then
+          fp3gemm forward and dX on fp32 X / dY (the engine's activations are
+          fp32), M = 4096.
+    Every record carries an fp64 check of its output.  CUDA events on the
+    legacy default stream, which the reference launches on."""
+    import numpy as np
+    import torch
+    from oracle.oracle import RefGPU
+    from gen import blocks_for
+    if not torch.cuda.is_available():
+        return {"unavailable": "no CUDA device"}
+    if not RefGPU.available():
+        return {"unavailable": "oracle/_ref/libtierref_gpu.so not built (reference tree absent at build time)"}
+    ref = RefGPU()
+    hbm, tf_burst = peaks()[0], peaks()[1]
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+    def timed(fn, n):
+        fn()
+        ref.sync()
+        ev0.record()
+        for _ in range(n):
+            fn()
+        ev1.record()
+        torch.cuda.synchronize()
+        return ev0.elapsed_time(ev1) / n
+
+    out = {}
+    rng = np.random.default_rng(0)
+    for (N, K) in ((4096, 4096), (14336, 4096)):
+        b = blocks_for(rng, 8, N, K)
+        rb = b.shape[1]
+        copies = int(np.ceil(4 * 126e6 / b.nbytes))
+        W = torch.from_numpy(b).cuda()
+        pool = [W.clone() for _ in range(copies)]
+        x = torch.from_numpy(rng.standard_normal(K).astype(np.float32)).cuda()
+        y = torch.empty(N, device="cuda")
+        ref.gemv_q(W, 8, rb, x, y, N, K)
+        ref.sync()
+        Wd = torch.from_numpy(np.ascontiguousarray(b)).cuda()
+        W16 = torch.empty(N, K, dtype=torch.float16, device="cuda")
+        ref.dequant_f16(Wd, 8, rb, N, K, W16)
+        ref.sync()
+        want = W16.double() @ x.double()
+        err = float((y.double() - want).norm() / want.norm())
+
+        def run():
+            for w in pool:
+                ref.gemv_q(w, 8, rb, x, y, N, K)
+        ms = timed(run, max(2, steps)) / copies
+        gbs = (b.nbytes + 4 * (N + K)) / (ms * 1e-3) / 1e9
+        out[f"gemv_q q8_0 {N}x{K} M=1"] = {"us_per_launch": ms * 1e3, "GB_s": gbs, "frac_of_hbm": gbs / hbm,
+                                           "check_rel_err": err}
+        del pool, W, Wd, W16
+    # C3: seven projections, fp3gemm fwd + dX
+    M, H, I = 4096, 5120, 14336
+    shapes = [(4096, H), (1024, H), (1024, H), (H, 4096), (I, H), (I, H), (H, I)]
+    g = torch.Generator(device="cuda").manual_seed(2)
+    Ws, xs, dys = [], {}, []
+    for (n, k) in shapes:
+        Ws.append((torch.randn(n, k, device="cuda", generator=g) * 0.02).half())
+        if k not in xs:
+            xs[k] = torch.randn(M, k, device="cuda", generator=g)
+        dys.append(torch.randn(M, n, device="cuda", generator=g))
+    ys = [torch.empty(M, n, device="cuda") for n, _ in shapes]
+    dxs = [torch.empty(M, k, device="cuda") for _, k in shapes]
+
+    def c3():
+        for W16, (n, k), y, dy, dx in zip(Ws, shapes, ys, dys, dxs):
+            ref.fp3gemm_fwd(W16, xs[k], y, M, k, n)
+            ref.fp3gemm_dx(W16, dy, dx, M, k, n)
+    ms = timed(c3, steps)
+    want = xs[H][1].double() @ Ws[0].double().T
+    err = float((ys[0][1].double() - want).norm() / want.norm())
+    useful = 2 * 2.0 * M * sum(n * k for n, k in shapes)
+    out["C3 fp3gemm 12B layer fwd+dX"] = {"ms_per_step": ms, "tflops_useful": useful / (ms * 1e-3) / 1e12,
+                                          "tflops_executed": 3 * useful / (ms * 1e-3) / 1e12,
+                                          "frac_of_bf16_burst_executed": 3 * useful / (ms * 1e-3) / 1e12 / tf_burst,
+                                          "check_rel_err": err}
+    del Ws, xs, dys, ys, dxs
+    # C2 the reference's way: dq_k to fp16 + fp3gemm on fp32 activations
+    Wq, X, dY = make_inputs()
+    Wd = torch.from_numpy(Wq).cuda()
+    W16 = torch.empty(N_OUT, K_IN, dtype=torch.float16, device="cuda")
+    Xd = torch.from_numpy(X).cuda()
+    dYd = torch.from_numpy(dY).cuda()
+    Y = torch.empty(M_TOK, N_OUT, device="cuda")
+    dX = torch.empty(M_TOK, K_IN, device="cuda")
+
+    def c2():
+        ref.dequant_f16(Wd, 12, Wq.shape[1], N_OUT, K_IN, W16)
+        ref.fp3gemm_fwd(W16, Xd, Y, M_TOK, K_IN, N_OUT)
+        ref.fp3gemm_dx(W16, dYd, dX, M_TOK, K_IN, N_OUT)
+    ms = timed(c2, steps)
+    want = Xd[7].double() @ W16.double().T
+    err = float((Y[7].double() - want).norm() / want.norm())
+    out["C2 Q4_K fp32 activations: dq_k + fp3gemm fwd+dX"] = {
+        "ms_per_step": ms, "tflops_useful": 2 * FLOP_DIR / (ms * 1e-3) / 1e12, "check_rel_err": err}
+    del Wd, W16, Xd, dYd, Y, dX
+    torch.cuda.empty_cache()
+    return out
+
+
 def run_reference(args):
     """The reference's CPU path on a bounded sample (rank 0 only)."""
     world, rank, _ = dist_env()
@@ -232,6 +343,11 @@ def run_reference(args):
                              "sample": ref.sample_text(rows)},
             "e2e": {"value": v, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
             "numpy_baseline": numpy_baseline(Wq, X, dY, 8.0)}
+    if not args.no_extra:
+        try:
+            line["reference_gpu"] = reference_gpu()
+        except Exception as e:            # the CPU arm stands on its own
+            line["reference_gpu"] = {"unavailable": f"{type(e).__name__}: {e}"}
     print(json.dumps(line))
 
 
@@ -374,7 +490,7 @@ def run_ours(args):
             works.append(dist.all_gather_into_tensor(Yfull, Y, group=group, async_op=True))
         if dx_mode == "fused":
             # one kernel: dX tiles go to their owner rank over NVLink as they finish
-            ctx.linear_dx_rs(w, dYin, M_TOK, dXr, dy_dtype=tk.DT_BF16, products=tk.WREUSE)
+            ctx.linear_dx_rs(w, dYin, M_TOK, dXr if dXo is None else dXo, dy_dtype=tk.DT_BF16, products=tk.WREUSE)
         elif dx_mode == "rs-nccl":
             ctx.linear_dx(w, dYin, M_TOK, dX, dy_dtype=tk.DT_BF16, products=tk.WREUSE)
             works.append(dist.reduce_scatter_tensor(dXr, dX, group=group, async_op=True))
@@ -446,6 +562,30 @@ def run_ours(args):
         dx_check, dx_row0 = dX, 0
     check = check_outputs(ctx, Wq, Xb, dY, Y, r0, r1, dx_check, dx_row0, dev, group)
 
+    # ---- where a step's time goes: each phase alone, max over ranks ----
+    def phase_ms(fn, n=5):
+        fn()
+        barrier()
+        ev0.record(stream)
+        for _ in range(n):
+            fn()
+        ev1.record(stream)
+        barrier()
+        v = torch.tensor([ev0.elapsed_time(ev1) / n], device=dev)
+        if world > 1:
+            import torch.distributed as dist
+            dist.all_reduce(v, op=dist.ReduceOp.MAX, group=group)
+        return float(v.item())
+
+    phases = {"fwd": phase_ms(lambda: ctx.linear(w, Xd, M_TOK, Y, x_dtype=tk.DT_BF16))}
+    if world == 1:
+        phases["dx"] = phase_ms(lambda: ctx.linear_dx(w, dYd, M_TOK, dX, dy_dtype=tk.DT_BF16, products=tk.WREUSE))
+    elif dx_mode == "fused":
+        phases["dx_reduce_scatter"] = phase_ms(
+            lambda: ctx.linear_dx_rs(w, dYd, M_TOK, dXr, dy_dtype=tk.DT_BF16, products=tk.WREUSE))
+        phases["dx_local_no_exchange"] = phase_ms(
+            lambda: ctx.linear_dx(w, dYd, M_TOK, dX, dy_dtype=tk.DT_BF16, products=tk.WREUSE))
+
     # ---- end to end through the C ABI with host buffers ----
     Xh = Xb.pin_memory()
     dYh = dYb.pin_memory()
@@ -462,7 +602,9 @@ def run_ours(args):
         Yh.copy_(Y, non_blocking=True)
         dXh.copy_(dX_out, non_blocking=True)
 
-    pipelined = world == 1
+    # the step's work stays on the compute stream at one GPU and with the dX
+    # reduce-scatter fused into the GEMM (no NCCL call inside the step)
+    pipelined = world == 1 or (dx_mode == "fused" and not args.gather_y)
     if pipelined:
         # copy-in, compute and copy-out on three streams with two buffer sets:
         # step i's inputs come in while step i-1 computes and step i-2's
@@ -470,7 +612,7 @@ def run_ours(args):
         # still moves all of its inputs and outputs inside the timed region.
         s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
         Xs2, dYs2 = [Xs, torch.empty_like(Xs)], [dYs, torch.empty_like(dYs)]
-        Y2, dX2 = [Y, torch.empty_like(Y)], [dX, torch.empty_like(dX)]
+        Y2, dX2 = [Y, torch.empty_like(Y)], [dX_out, torch.empty_like(dX_out)]
         ev_in = [torch.cuda.Event() for _ in range(2)]
         ev_cmp = [torch.cuda.Event() for _ in range(2)]
         ev_out = [torch.cuda.Event() for _ in range(2)]
@@ -572,6 +714,7 @@ def run_ours(args):
             "check": check,
             "kernels_ms_per_step": {"gemm": gemm_ms / args.steps, "dequant": deq_ms / args.steps,
                                     "act_split": spl_ms / args.steps},
+            "phases_ms": phases,
             "e2e": {"value": e2e_val, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "steps": e_steps,
                     "schedule": ("pinned host X, dY in and Y, dX out every step; copy-in, compute and copy-out "
@@ -581,6 +724,16 @@ def run_ours(args):
             "gpu_launches": launches,
             "clocks": clk,
         }
+        if world == 1 and not args.no_extra:
+            # the other configurations, each timed on its own after the headline
+            del Xh, dYh, Yh, dXh
+            torch.cuda.empty_cache()
+            line["configs"] = {
+                "C1 q8_0 4096x4096 M=1": measure_c1(ctx, tk.Q8_0, 4096, 4096, [1], 50),
+                "decode q8_0 14336x4096 M=1": measure_c1(ctx, tk.Q8_0, 14336, 4096, [1], 50),
+                "C3 x3 layer (fp32 W hi/lo)": measure_c3(ctx, 5, "hhl"),
+                "C4 LM head single pass": measure_c4(ctx, 3),
+            }
         if world == 1 and not args.no_cpu:
             line["cpu_baseline"] = cpu_baseline(Wq, X, dY, args.ref_seconds)
         print(json.dumps(line))
@@ -650,23 +803,20 @@ def _timed(ctx, fn, steps, warmup, kind):
 C1_TYPES = {"q8_0": 8, "q4_k": 12, "q5_k": 13, "q6_k": 14}
 
 
-def run_c1(args):
-    """C1: q8_0 decode GEMV W[4096, 4096], M = 1, rotating over distinct
-    weight copies (>= 4x the 126 MB L2) so every launch reads HBM.  The
-    launches are captured in one CUDA graph and the graph is replayed, so the
-    timing measures back-to-back kernels, not the host's launch rate.
-    --c1-type / --c1-shape / --c1-m run the same measurement for the other
-    block types and the decode shapes of the 40-layer sweep."""
+def measure_c1(ctx, qt, N, K, Ms, steps, seed=0):
+    """Decode GEMV W[N, K] of block type qt for each token count in Ms,
+    rotating over distinct weight copies (>= 4x the 126 MB L2) so every
+    launch reads HBM.  The launches are captured in one CUDA graph and the
+    graph is replayed, so the timing measures back-to-back kernels, not the
+    host's launch rate.  The first M's output is checked against an fp64
+    matmul of tk_dequant's fp32 weight."""
     import numpy as np
     import torch
     import tier_b200 as tk
     from gen import blocks_for
-    ctx = tk.Context(0)
-    qt = C1_TYPES[args.c1_type]
-    N, K = (int(v) for v in args.c1_shape.lower().split("x"))
-    Ms = [int(m) for m in args.c1_m.split(",")]
-    rng = np.random.default_rng(0)
+    rng = np.random.default_rng(seed)
     out = {}
+    check = None
     for M in Ms:
         b = blocks_for(rng, qt, N, K)
         wbytes = b.nbytes
@@ -677,6 +827,14 @@ def run_c1(args):
         y = torch.empty(M, N, device="cuda")
         ctx.gemv(qt, pool[0], N, K, x, y, M=M)                 # module load / attributes outside capture
         torch.cuda.synchronize()
+        if check is None:
+            W32 = torch.empty(N, K, device="cuda")
+            ctx.dequant(qt, W, N, K, W32)
+            want = x.double() @ W32.double().T
+            err = float((y.double() - want).norm() / want.norm())
+            check = {"rel_err": err, "tol": 2e-3, "ok": bool(err < 2e-3), "M": M,
+                     "against": "fp64 matmul of tk_dequant's fp32 W (bit-exact to q_val in the tests)"}
+            del W32, want
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g):
             for w in pool:
@@ -692,48 +850,68 @@ def run_c1(args):
             torch.cuda.synchronize()
         ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         ev0.record()
-        for _ in range(args.steps):
+        for _ in range(steps):
             g.replay()
         ev1.record()
         torch.cuda.synchronize()
         clk = clocks.stop()
-        per_launch = ev0.elapsed_time(ev1) / (args.steps * copies)
+        per_launch = ev0.elapsed_time(ev1) / (steps * copies)
         bytes_launch = wbytes + 4 * K * M + 4 * N * M
         gbs = bytes_launch / (per_launch * 1e-3) / 1e9
-        out[M] = (per_launch, gbs, copies, clk)
-        del pool, g
+        out[M] = (per_launch, gbs, copies, clk, bytes_launch)
+        del pool, g, W
     hbm = peaks()[0]
     m0 = Ms[0]
-    per_launch, gbs, copies, clk = out[m0]
-    shape = f"{args.c1_type} {N}x{K}"
-    print(json.dumps({"metric": f"decode GEMV HBM GB/s ({shape}, M={m0})", "value": gbs, "unit": "GB/s",
-                      "n_gpus": 1, "steps": args.steps, "higher_is_better": True,
-                      "us_per_launch": per_launch * 1e3,
-                      "by_M": {m: {"us_per_launch": v[0] * 1e3, "GB_s": v[1]} for m, v in out.items()},
-                      "config": {"workload": f"{'C1' if shape == 'q8_0 4096x4096' else 'decode'} GEMV {shape}",
-                                 "rotating_copies": copies,
-                                 "bytes_per_launch": tk.row_bytes(qt, K) * N + 4 * (K + N) * m0,
-                                 "timing": "CUDA graph replay"},
-                      "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s",
-                                   "frac": gbs / hbm}, "clocks": clk}))
+    per_launch, gbs, copies, clk, bytes_launch = out[m0]
+    name = {8: "q8_0", 12: "q4_k", 13: "q5_k", 14: "q6_k"}.get(qt, str(qt))
+    shape = f"{name} {N}x{K}"
+    return {"metric": f"decode GEMV HBM GB/s ({shape}, M={m0})", "value": gbs, "unit": "GB/s",
+            "n_gpus": 1, "steps": steps, "higher_is_better": True, "us_per_launch": per_launch * 1e3,
+            "by_M": {m: {"us_per_launch": v[0] * 1e3, "GB_s": v[1], "frac": v[1] / hbm} for m, v in out.items()},
+            "config": {"workload": f"{'C1' if shape == 'q8_0 4096x4096' else 'decode'} GEMV {shape}",
+                       "rotating_copies": copies, "bytes_per_launch": bytes_launch,
+                       "timing": "CUDA graph replay of one launch per weight copy, CUDA events"},
+            "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s", "frac": gbs / hbm,
+                         "peak_source": "measured hbm_gbs (MEASURED_PEAKS.json)"},
+            "check": check, "clocks": clk}
 
 
-def run_c3(args):
+def run_c1(args):
+    """C1: q8_0 decode GEMV W[4096, 4096], M = 1 (measure_c1).  --c1-type /
+    --c1-shape / --c1-m run the same measurement for the other block types
+    and the decode shapes of the 40-layer sweep."""
+    import tier_b200 as tk
+    ctx = tk.Context(0)
+    N, K = (int(v) for v in args.c1_shape.lower().split("x"))
+    print(json.dumps(measure_c1(ctx, C1_TYPES[args.c1_type], N, K, [int(m) for m in args.c1_m.split(",")],
+                                args.steps)))
+
+
+def measure_c3(ctx, steps, products="hhl"):
     """C3: the seven projections of one 12B-class layer (hidden 5120, q 4096,
-    k/v 1024, o, SwiGLU 14336), fp32 weights split into fp16 hi/lo, fp32 X
-    (M = 4096 tokens); forward + dX of every projection per step, products
-    Xh.Wh + Xh.Wl + Xl.Wh."""
+    k/v 1024, o, SwiGLU 14336), M = 4096 fp32 tokens, forward + dX of every
+    projection per step.  products "hhl": fp32 W split into fp16 hi/lo,
+    Xh.Wh + Xh.Wl + Xl.Wh (<= 1e-5 against fp32 W); "ref": the reference's
+    fp3gemm products W.xl + W.xm + W.xh on fp16 W.  Two rows of every
+    projection's outputs are checked against fp64 after the timed steps."""
     import torch
     import tier_b200 as tk
     from tier_b200.host import LinearPath
-    ctx = tk.Context(0)
     M, H, I = 4096, 5120, 14336
     shapes = [(4096, H), (1024, H), (1024, H), (H, 4096), (I, H), (I, H), (H, I)]   # q k v o gate up down
     g = torch.Generator(device="cuda").manual_seed(2)
-    lps, xs, dys = [], {}, []
+    ws, wref, xs, dys = [], [], {}, []
+    prod = tk.X3_HHL if products == "hhl" else tk.X3_REF
     for (n, k) in shapes:
         W = torch.randn(n, k, device="cuda", generator=g) * 0.02
-        lps.append(LinearPath.from_f32_split(ctx, W))
+        if products == "hhl":
+            lp = LinearPath.from_f32_split(ctx, W)
+            ws.append((lp.W, lp.data))
+            wref.append(W[[0, n - 1]].double())
+        else:
+            W16 = W.half()
+            ws.append((tk.make_weight(tk.F16, n, k, W16), W16))
+            wref.append(W16.double())
         del W
         if k not in xs:
             xs[k] = torch.randn(M, k, device="cuda", generator=g)
@@ -742,24 +920,52 @@ def run_c3(args):
     dxs = [torch.empty(M, k, device="cuda") for (_, k) in shapes]
 
     def fn():
-        for lp, (n, k), y, dy, dx in zip(lps, shapes, outs, dys, dxs):
-            ctx.linear(lp.W, xs[k], M, y, products=tk.X3_HHL)
-            ctx.linear_dx(lp.W, dy, M, dx, products=tk.X3_HHL)
+        for (w, _), (n, k), y, dy, dx in zip(ws, shapes, outs, dys, dxs):
+            ctx.linear(w, xs[k], M, y, products=prod)
+            ctx.linear_dx(w, dy, M, dx, products=prod)
 
-    t_ms, k_ms, k_n, clk = _timed(ctx, fn, args.steps, 3, tk.PROF_GEMM)
+    t_ms, k_ms, k_n, clk = _timed(ctx, fn, steps, 3, tk.PROF_GEMM)
+    # check: Y rows 1 and M-1 of every projection (and dX rows with ref products)
+    errs = []
+    for (n, k), y, dy, dx, wr in zip(shapes, outs, dys, dxs, wref):
+        for r in (1, M - 1):
+            if products == "hhl":
+                # wr holds W rows 0 and n-1: the checked outputs are those columns of Y
+                want = xs[k][r].double() @ wr.T
+                got = y[r, [0, n - 1]].double()
+            else:
+                want = xs[k][r].double() @ wr.T
+                got = y[r].double()
+                wdx = dy[r].double() @ wr
+                errs.append(float((dx[r].double() - wdx).norm() / wdx.norm()))
+            errs.append(float((got - want).norm() / want.norm()))
+    err = max(errs)
     snk = sum(n * k for n, k in shapes)
     useful = 2 * 2.0 * M * snk
-    ms = t_ms / args.steps
+    ms = t_ms / steps
     tf_burst = peaks()[1]
-    gemm_tf_exec = 3 * useful / (k_ms / args.steps * 1e-3) / 1e12
-    print(json.dumps({"metric": "fp16 x3 split GEMM TFLOP/s (12B layer, fwd + dX)", "value": useful / (ms * 1e-3) / 1e12,
-                      "unit": "TFLOP/s (fp32-equivalent useful)", "executed_tflops": 3 * useful / (ms * 1e-3) / 1e12,
-                      "ms_per_step": ms, "steps": args.steps, "n_gpus": 1,
-                      "config": {"workload": "C3 12B layer x3 (Xh.Wh+Xh.Wl+Xl.Wh), M=4096, fp32 X and W",
-                                 "useful_tflop_per_step": useful / 1e12},
-                      "roofline": {"bound": "tensor", "achieved": gemm_tf_exec, "peak": tf_burst, "unit": "TFLOP/s",
-                                   "frac": gemm_tf_exec / tf_burst, "kernel": "gemm_tc_kernel (executed products)"},
-                      "clocks": clk}))
+    gemm_tf_exec = 3 * useful / (k_ms / steps * 1e-3) / 1e12
+    return {"metric": "fp16 x3 split GEMM TFLOP/s (12B layer, fwd + dX)", "value": useful / (ms * 1e-3) / 1e12,
+            "unit": "TFLOP/s (fp32-equivalent useful)", "executed_tflops": 3 * useful / (ms * 1e-3) / 1e12,
+            "ms_per_step": ms, "steps": steps, "n_gpus": 1,
+            "config": {"workload": ("C3 12B layer x3, M=4096, fp32 X; " +
+                                    ("fp32 W as fp16 hi/lo, Xh.Wh+Xh.Wl+Xl.Wh" if products == "hhl" else
+                                     "fp16 W, the reference's W.xl+W.xm+W.xh")),
+                       "useful_tflop_per_step": useful / 1e12},
+            "roofline": {"bound": "tensor", "achieved": gemm_tf_exec, "peak": tf_burst, "unit": "TFLOP/s",
+                         "frac": gemm_tf_exec / tf_burst, "kernel": "gemm_tc_kernel (executed products)",
+                         "peak_source": "measured bf16 burst (MEASURED_PEAKS.json)"},
+            "gemm_ms_per_step": k_ms / steps,
+            "check": {"rel_err": err, "tol": 1e-5, "ok": bool(err < 1e-5),
+                      "against": "fp64 matmul of the same fp32 X and the unsplit weight, rows 1 and M-1 of every "
+                                 "projection"},
+            "clocks": clk}
+
+
+def run_c3(args):
+    import tier_b200 as tk
+    ctx = tk.Context(0)
+    print(json.dumps(measure_c3(ctx, args.steps, args.c3_products)))
 
 
 def _c5_blocks(qt, n, k, g):
@@ -909,16 +1115,17 @@ def run_c5(args):
         torch.cuda.empty_cache()
 
 
-def run_c4(args):
+def measure_c4(ctx, steps, two_pass=False):
     """C4: chunked-vocab LM head + CE: W fp16 [262144, 3840], hidden fp32
     [8192, 3840], labels uniform, chunk 16384.  Default: the single pass
     (one logits GEMM per chunk with the x3 split of X, then the dX GEMM with
-    the hi/lo probabilities); --c4-two-pass runs the reference's two passes
-    (logits recomputed in pass 2, dlogit split in three)."""
+    the hi/lo probabilities); two_pass runs the reference's two passes
+    (logits recomputed in pass 2, dlogit split in three).  After the timed
+    steps the loss terms and dX of two rows are checked against fp64
+    (vocabulary in chunks, on the GPU)."""
     import torch
     import tier_b200 as tk
     from tier_b200.host import LMHead
-    ctx = tk.Context(0)
     V, H, T, chunk = 262144, 3840, 8192, 16384
     g = torch.Generator(device="cuda").manual_seed(3)
     W = (torch.randn(V, H, device="cuda", generator=g) * 0.02).half()
@@ -928,18 +1135,42 @@ def run_c4(args):
     head = LMHead(ctx, W, 0, chunk=chunk, products=tk.X3_REF)
     dX = torch.zeros(T, H, device="cuda")
     n_loss = T - 1
-    two_pass = args.c4_two_pass
+    res = {}
 
     def fn():
         if two_pass:
             rmax, rsum, amax, tgt = head.stats(X, labels, mask)
-            head.loss(T, labels, mask, rmax, rsum, amax, tgt)
+            res["loss"] = head.loss(T, labels, mask, rmax, rsum, amax, tgt)[0]
             head.grad(X, labels, mask, n_loss, rmax, rsum, dX=dX)
+            res["dX"] = dX
         else:
-            head.step_fused(X, labels, mask, n_loss=n_loss)
+            out = head.step_fused(X, labels, mask, n_loss=n_loss)
+            res["loss"], res["dX"] = out[0], out[4]
 
-    steps = max(1, min(args.steps, 5))
+    steps = max(1, min(steps, 5))
     t_ms, k_ms, k_n, clk = _timed(ctx, fn, steps, 1, tk.PROF_GEMM)
+    # fp64 check of rows 0 and T-2: lse - target and the dX row
+    rows = [0, T - 2]
+    Xr = X[rows].double()
+    lab = labels[[r + 1 for r in rows]].long()
+    m = torch.full((2,), -float("inf"), dtype=torch.float64, device="cuda")
+    ssum = torch.zeros(2, dtype=torch.float64, device="cuda")
+    for v0 in range(0, V, chunk):
+        L = (Xr @ W[v0:v0 + chunk].double().T).float().double()   # logits rounded to fp32, as the GEMM stores them
+        nm = torch.maximum(m, L.max(1).values)
+        ssum = ssum * torch.exp(m - nm) + torch.exp(L - nm[:, None]).sum(1)
+        m = nm
+    lse = m + torch.log(ssum)
+    d = torch.zeros(2, H, dtype=torch.float64, device="cuda")
+    for v0 in range(0, V, chunk):
+        Wc = W[v0:v0 + chunk].double()
+        P = torch.exp((Xr @ Wc.T).float().double() - lse[:, None])
+        for i in range(2):
+            if v0 <= int(lab[i]) < v0 + chunk:
+                P[i, int(lab[i]) - v0] -= 1.0
+        d += (P / n_loss) @ Wc
+    got = res["dX"][rows].double()
+    err = float(((got - d).norm(dim=1) / d.norm(dim=1)).max())
     ms = t_ms / steps
     useful = 2 * 2.0 * T * V * H
     # executed products: logits x3 (+ x3 recompute + x3 dX in two passes;
@@ -947,16 +1178,28 @@ def run_c4(args):
     executed = (3 + 3 + 3 if two_pass else 3 + 2) * 2.0 * T * V * H
     tf_burst = peaks()[1]
     gemm_exec = executed / (k_ms / steps * 1e-3) / 1e12
-    print(json.dumps({"metric": "LM head + CE TFLOP/s (useful: logits + dX GEMMs)", "value": useful / (ms * 1e-3) / 1e12,
-                      "unit": "TFLOP/s", "executed_tflops": executed / (ms * 1e-3) / 1e12, "ms_per_step": ms,
-                      "steps": steps, "n_gpus": 1,
-                      "config": {"workload": "C4 V=262144 H=3840 T=8192 chunk=16384, " +
-                                 ("two-pass, x3 split of X and dlogit" if two_pass else
-                                  "single pass, x3 split of X, hi/lo probabilities")},
-                      "roofline": {"bound": "tensor", "achieved": gemm_exec, "peak": tf_burst, "unit": "TFLOP/s",
-                                   "frac": gemm_exec / tf_burst, "kernel": "gemm_tc_kernel (executed products)"},
-                      "gemm_ms_per_step": k_ms / steps,
-                      "clocks": clk}))
+    rec = {"metric": "LM head + CE TFLOP/s (useful: logits + dX GEMMs)", "value": useful / (ms * 1e-3) / 1e12,
+           "unit": "TFLOP/s", "executed_tflops": executed / (ms * 1e-3) / 1e12, "ms_per_step": ms,
+           "steps": steps, "n_gpus": 1,
+           "config": {"workload": "C4 V=262144 H=3840 T=8192 chunk=16384, " +
+                      ("two-pass, x3 split of X and dlogit" if two_pass else
+                       "single pass, x3 split of X, hi/lo probabilities")},
+           "roofline": {"bound": "tensor", "achieved": gemm_exec, "peak": tf_burst, "unit": "TFLOP/s",
+                        "frac": gemm_exec / tf_burst, "kernel": "gemm_tc_kernel (executed products)",
+                        "peak_source": "measured bf16 burst (MEASURED_PEAKS.json)"},
+           "gemm_ms_per_step": k_ms / steps,
+           "check": {"rel_err": err, "tol": 1e-5, "ok": bool(err < 1e-5),
+                     "against": "fp64 two-pass LM head (logits rounded to fp32) on rows 0 and T-2: dX rows"},
+           "clocks": clk}
+    del W, X, dX, head
+    torch.cuda.empty_cache()
+    return rec
+
+
+def run_c4(args):
+    import tier_b200 as tk
+    ctx = tk.Context(0)
+    print(json.dumps(measure_c4(ctx, args.steps, args.c4_two_pass)))
 
 
 def main():
@@ -976,6 +1219,10 @@ def main():
     ap.add_argument("--c1-shape", default="4096x4096", help="c1: N x K of the weight")
     ap.add_argument("--c1-m", default="1,4,16", help="c1: token counts (the first is the headline)")
     ap.add_argument("--c4-two-pass", action="store_true", help="c4: the reference's two passes")
+    ap.add_argument("--c3-products", default="hhl", choices=["hhl", "ref"],
+                    help="c3: fp32 W as hi/lo planes (hhl) or the reference's products on fp16 W (ref)")
+    ap.add_argument("--no-extra", action="store_true",
+                    help="headline only: skip the C1/C3/C4 sub-records measured after it on one GPU")
     ap.add_argument("--c5-kinds", default="q8_0,q4_k_s,fp16x3", help="c5: weight kinds")
     ap.add_argument("--c5-m", default="1,16,512,4096,16384", help="c5: token counts")
     ap.add_argument("--config", default="c2", choices=["c1", "c2", "c3", "c4", "c5"],

@@ -7,6 +7,9 @@ product (tier_b200/).
   RefOracle   -- oracle/_ref/libtkref.so, the reference's own quant.h and
                  kernel bodies compiled from its sources (ref_harness.cpp);
                  absent when the reference tree was not available at build time.
+  RefGPU      -- oracle/_ref/libtierref_gpu.so, the reference engine's GPU
+                 linear path (fp3gemm / dq_k / gemv_q) compiled from tier.cpp
+                 (ref_gpu.cu); timed beside libtierk by bench.py's reference arm.
 """
 from __future__ import annotations
 
@@ -239,3 +242,43 @@ class RefOracle:
         self.L.ref_cpu_qgemm_dx(_p(b), ctypes.c_size_t(rb), qtype, n0, nrows, K, _p(dY), dY.shape[1], M, _p(dX),
                                 threads)
         return dX
+
+
+class RefGPU:
+    """The reference engine's own GPU functions (oracle/ref_gpu.cu) on device
+    pointers (torch tensors' data_ptr()), on the legacy default stream."""
+
+    SO = HERE / "_ref" / "libtierref_gpu.so"
+
+    @classmethod
+    def available(cls) -> bool:
+        return cls.SO.exists()
+
+    def __init__(self):
+        L = ctypes.CDLL(str(self.SO))
+        I, Z = ctypes.c_int, ctypes.c_size_t
+        L.refgpu_fp3gemm_fwd.argtypes = [P, P, P, I, I, I]
+        L.refgpu_fp3gemm_dx.argtypes = [P, P, P, I, I, I]
+        L.refgpu_dequant_f16.argtypes = [P, I, Z, I, I, P]
+        L.refgpu_gemv_q.argtypes = [P, I, Z, P, P, I, I]
+        self.L = L
+
+    @staticmethod
+    def _ok(rc, what):
+        if rc:
+            raise RuntimeError(f"reference {what}: CUDA error {rc}")
+
+    def fp3gemm_fwd(self, W16, X, Y, M, K, N):
+        self._ok(self.L.refgpu_fp3gemm_fwd(W16.data_ptr(), X.data_ptr(), Y.data_ptr(), M, K, N), "fp3gemm fwd")
+
+    def fp3gemm_dx(self, W16, dY, dX, M, K, N):
+        self._ok(self.L.refgpu_fp3gemm_dx(W16.data_ptr(), dY.data_ptr(), dX.data_ptr(), M, K, N), "fp3gemm dx")
+
+    def dequant_f16(self, W, qtype, rb, rows, cols, out):
+        self._ok(self.L.refgpu_dequant_f16(W.data_ptr(), qtype, rb, rows, cols, out.data_ptr()), "dq_launch")
+
+    def gemv_q(self, W, qtype, rb, x, y, N, K):
+        self._ok(self.L.refgpu_gemv_q(W.data_ptr(), qtype, rb, x.data_ptr(), y.data_ptr(), N, K), "gemv_q")
+
+    def sync(self):
+        self._ok(self.L.refgpu_sync(), "sync")

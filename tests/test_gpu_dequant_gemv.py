@@ -71,7 +71,9 @@ def test_dequant_large_rows_and_offset(ctx, oracle, qtype):
                                         # Q6_K: one chunk, 7 chunks of 2048, and 16-byte-unaligned rows (scalar kernel)
                                         (14, 4096, 4096), (14, 3000, 14336), (14, 700, 5120),
                                         # several K-chunks per row group and few slots per ring
-                                        (8, 5120, 14336), (12, 5120, 14336)])
+                                        (8, 5120, 14336), (12, 5120, 14336),
+                                        # one-token Q8_0 dp4a kernel: 1, 2, 3 and 4 K segments, few rows
+                                        (8, 4096, 5120), (8, 300, 8192), (8, 37, 2048), (8, 14336, 4096)])
 @pytest.mark.parametrize("M", [1, 2, 3, 16])
 def test_gemv_vs_f64(ctx, oracle, qtype, N, K, M):
     import torch

@@ -263,6 +263,9 @@ static int popcount_chunks(int M) {
 tk_status launch_gemv(tk_ctx* ctx, int t, const void* Wv, size_t rb, int N, int K, const float* x, int ldx, int M,
                       float* y, int ldy, cudaStream_t s, bool frozen) {
     if (N == 0 || M == 0) return TK_OK;
+    // One Q8_0 token: dp4a with x in registers (tk_gemv8.cu).
+    if (M == 1 && (reinterpret_cast<uintptr_t>(Wv) & 15) == 0 && gemv_dp_ok(t, rb, N, K, M, ctx->num_sms))
+        return launch_gemv_dp(ctx, Wv, rb, N, K, x, y, frozen, s);
     // Integer tensor-core kernel (tk_gemv6.cu) for one or two tokens.
     if (M <= 2 && gemv_imma_ok(t, rb, K, M) && (reinterpret_cast<uintptr_t>(Wv) & 15) == 0)
         return launch_gemv_imma(ctx, t, Wv, rb, N, K, x, ldx, M, y, ldy, frozen, s);

@@ -105,6 +105,10 @@ tk_status launch_gemv_wide(tk_ctx* ctx, int qtype, const void* W, size_t rb, int
 tk_status launch_gemv_imma(tk_ctx* ctx, int qtype, const void* W, size_t rb, int N, int K, const float* x, int ldx,
                            int M, float* y, int ldy, bool frozen, cudaStream_t s);
 
+// ---- tk_gemv8.cu (decode GEMV, one token, Q8_0, dp4a with x in registers) ----
+bool gemv_dp_ok(int t, size_t rb, int N, int K, int M, int num_sms);
+tk_status launch_gemv_dp(tk_ctx* ctx, const void* W, size_t rb, int N, int K, const float* x, float* y, bool frozen,
+                         cudaStream_t s);
 // ---- tk_gemv.cu ----
 bool gemv_supported(int qtype);
 tk_status launch_gemv(tk_ctx* ctx, int qtype, const void* W, size_t rb, int N, int K, const float* x, int ldx,
