@@ -72,8 +72,9 @@ def test_dequant_large_rows_and_offset(ctx, oracle, qtype):
                                         (14, 4096, 4096), (14, 3000, 14336), (14, 700, 5120),
                                         # several K-chunks per row group and few slots per ring
                                         (8, 5120, 14336), (12, 5120, 14336),
-                                        # one-token Q8_0 dp4a kernel: 1, 2, 3 and 4 K segments, few rows
-                                        (8, 4096, 5120), (8, 300, 8192), (8, 37, 2048), (8, 14336, 4096)])
+                                        # one-token Q8_0 dp4a kernel (>= 32 MB of weight): 1, 2 and 4 K
+                                        # segments, a short last segment
+                                        (8, 14336, 4096), (8, 7000, 5120), (8, 2300, 14336), (8, 4000, 8192)])
 @pytest.mark.parametrize("M", [1, 2, 3, 16])
 def test_gemv_vs_f64(ctx, oracle, qtype, N, K, M):
     import torch
@@ -104,15 +105,14 @@ def test_gemv_c1_matches_reference_order_closely(ctx, oracle):
     assert np.abs(got[:256] - ref_order).max() / np.abs(ref_order).max() < 1e-5
 
 
-@pytest.mark.parametrize("qtype", [8, 12, 14])
-def test_gemv_frozen_chain(ctx, oracle, qtype):
+@pytest.mark.parametrize("qtype,K", [(8, 4096), (12, 4096), (14, 4096), (8, 6144)])
+def test_gemv_frozen_chain(ctx, oracle, qtype, K):
     """TK_WFROZEN lets a GEMV fetch its (never written) weight before the
     previous kernel ends, but x is still read after it: a chain whose x is
     the previous GEMV's y gives the same bits as the chain without the flag."""
     import torch
     import tier_b200 as tk
     rng = np.random.default_rng(9 + qtype)
-    K = 4096
     bs = [dev(blocks_for(rng, qtype, K, K)) for _ in range(3)]
     x0 = dev(rng.standard_normal((1, K)).astype(np.float32))
     outs = []
