@@ -9,7 +9,10 @@ The recipe reads tier/tier.cpp where it lies and adds four hooks:
     (tier/tier.cpp:1202-1238) that hands fp16-x3 weights to tk_linear_fwd /
     tk_linear_dx and returns;
   * in `chat_lin` (tier/tier.cpp:2351), the quantized branch tries tk_gemv /
-    tk_linear_fwd first.
+    tk_linear_fwd first;
+  * in the LM head (tier/tier.cpp:3184-3266), the chunk size is rounded to 256
+    rows and each chunk of the two vocabulary loops tries tk_lmhead_stats /
+    tk_lmhead_grad right after its rows reach the device.
 It writes the patched engine to integration/_build/tier_tk.cpp (build output:
 git-ignored, never committed) and compiles it
 with the reference's own nvcc line (tier/build.sh:89) for sm_100, linked to
@@ -57,6 +60,31 @@ CHAT_SIG = r"static void chat_lin\(ChatMat& m, const float\* x, float\* y, int M
 CHAT_QT = r"if\(m\.qt\)\{"
 
 
+# The LM head: the chunk size, and the statement that uploads a chunk, which
+# opens both vocabulary loops (pass 1, then pass 2).
+LM_CHUNK = "const int CHUNK=lm_chunk(seq_len);"
+LM_UPLOAD = ("HIP_CHECK(hipMemcpy(d_chunk_bf,(const char*)head_h+(size_t)v0*row_bytes,(size_t)vc*row_bytes,"
+             "hipMemcpyHostToDevice));")
+LM_PASS1 = (" if(!g_gen && g_fp16_storage && n_pred>0 && tk_bridge_lm_stats(d_chunk_bf,v0,vc,HIDDEN,normed_final,"
+            "seq_len,d_tokens,d_lmask,SOFTCAP,d_running_max,d_running_sum,d_amax,d_tgt)){ if(g_prog && !g_is_ev) "
+            "printf(\"prog h %d\\n\", v0/CHUNK+1); continue; }")
+LM_PASS2 = (" if(g_fp16_storage && tk_bridge_lm_grad(d_chunk_bf,v0,vc,HIDDEN,normed_final,seq_len,d_tokens,d_lmask,"
+            "n_loss,SOFTCAP,d_running_max,d_running_sum,d_normed_final)){ if(g_prog && !g_is_ev) "
+            "printf(\"prog g %d\\n\", v0/CHUNK+1); continue; }")
+
+
+def patch_lm_head(src: str) -> str:
+    if src.count(LM_CHUNK) != 1:
+        raise SystemExit(f"hook 'lm_chunk': expected one match, found {src.count(LM_CHUNK)}")
+    src = src.replace(LM_CHUNK, "const int CHUNK=tk_bridge_lm_chunk(lm_chunk(seq_len));")
+    if src.count(LM_UPLOAD) != 2:
+        raise SystemExit(f"hook 'lm head loops': expected two chunk uploads, found {src.count(LM_UPLOAD)}")
+    i = src.index(LM_UPLOAD) + len(LM_UPLOAD)
+    src = src[:i] + LM_PASS1 + src[i:]
+    j = src.index(LM_UPLOAD, i) + len(LM_UPLOAD)
+    return src[:j] + LM_PASS2 + src[j:]
+
+
 def patch(src: str) -> str:
     for pat, rep, name in HOOKS:
         hits = re.findall(pat, src)
@@ -69,7 +97,8 @@ def patch(src: str) -> str:
     q = re.compile(CHAT_QT).search(src, m.end())
     if not q:
         raise SystemExit("hook 'chat_lin': quantized branch not found")
-    return src[:q.start()] + "if(m.qt && tk_bridge_chat(m,W,x,y,M,g_chat_cs)){ } else if(m.qt){" + src[q.end():]
+    src = src[:q.start()] + "if(m.qt && tk_bridge_chat(m,W,x,y,M,g_chat_cs)){ } else if(m.qt){" + src[q.end():]
+    return patch_lm_head(src)
 
 
 def build(ref: Path, hooked: bool = True) -> Path:

@@ -10,6 +10,14 @@
 //     reference runs fp3gemm's three cuBLASLt GEMMs (tier/tier.cpp:922-943);
 //     here that is one tk_linear_fwd / tk_linear_dx with TK_X3_REF, i.e. the
 //     same products W.xl + W.xm + W.xh in one tcgen05 GEMM.
+//   * the LM head's two chunk loops (tier/tier.cpp:3209-3266), fp16 head
+//     chunks whose row count is a multiple of 256: pass 1 (fp16 -> fp32
+//     expansion, fp32 logits GEMM, softcap, lse_chunk_kernel) becomes one
+//     tk_lmhead_stats per chunk, pass 2 (the same logits again, dlogit_kernel,
+//     linear_dx_acc) one tk_lmhead_grad.  Both update the reference's own
+//     running state (double max and sum, int argmax, float target logit), so
+//     a chunk the bridge declines runs the reference's code on the same
+//     state.  The chunk size is rounded down to a multiple of 256.
 //   * chat_lin's quantized branch (tier/tier.cpp:2356-2360): gemv_q for one
 //     token and dq_launch + chat_linear_ld slabs beyond it become tk_gemv for
 //     up to 16 tokens and tk_linear_fwd above that.  Resident weights
@@ -77,4 +85,27 @@ static bool tk_bridge_chat(const ChatMatT& m, const void* W, const float* x, flo
     }
     tk_weight w{m.qt, m.rows, m.cols, 0, m.rb, W};
     return tk_bridge_ok(tk_linear_fwd(g_tk, &w, x, TK_DT_F32, M, m.cols, y, m.rows, 0.0f, TK_X3_AUTO, s));
+}
+
+// LM head chunk size: the reference's lm_chunk, rounded down to a multiple of
+// 256 rows (the tile of libtierk's LM-head kernels) when it is at least 512.
+static int tk_bridge_lm_chunk(int chunk) { return chunk >= 512 ? chunk / 256 * 256 : chunk; }
+
+// Pass 1 over one chunk: Wc = the chunk's fp16 rows [vc, H] on the device,
+// v0 = its first vocabulary row; X = the final hidden states [T, H] fp32.
+static bool tk_bridge_lm_stats(const void* Wc, int v0, int vc, int H, const float* X, int T, const int32_t* tokens,
+                               const unsigned char* mask, float softcap, double* rmax, double* rsum, int* amax,
+                               float* tgt) {
+    if (vc % 256 || H % 8 || !tk_bridge_ready()) return false;
+    return tk_bridge_ok(tk_lmhead_stats(g_tk, static_cast<const uint16_t*>(Wc), v0, vc, H, X, T, tokens, mask, softcap,
+                                        vc, TK_X3_REF, rmax, rsum, amax, tgt, nullptr));
+}
+
+// Pass 2 over one chunk: dX[T, H] += dlogit . Wc (linear_dx_acc of the reference).
+static bool tk_bridge_lm_grad(const void* Wc, int v0, int vc, int H, const float* X, int T, const int32_t* tokens,
+                              const unsigned char* mask, int n_loss, float softcap, const double* rmax,
+                              const double* rsum, float* dX) {
+    if (vc % 256 || H % 8 || !tk_bridge_ready()) return false;
+    return tk_bridge_ok(tk_lmhead_grad(g_tk, static_cast<const uint16_t*>(Wc), v0, vc, H, X, T, tokens, mask, n_loss,
+                                       softcap, vc, TK_X3_REF, rmax, rsum, dX, nullptr));
 }

@@ -45,6 +45,23 @@ tk_status tk_gemv(tk_ctx*, int qtype, const void* W, size_t rb, int N, int K, co
     last_qtype = qtype; last_w.data = W; last_rb = rb; last_N = N; last_K = K; last_in = x; last_ldin = ldx; last_M = M;
     last_out = y; last_ldout = ldy; last_stream = stream; return (tk_status)ret();
 }
+static int last_v0, last_vs, last_H, last_T, last_chunk, last_nloss;
+static float last_cap;
+static const void *last_lab, *last_mask, *last_state;
+tk_status tk_lmhead_stats(tk_ctx*, const uint16_t* W, int v0, int V_shard, int H, const float* X, int T,
+                          const int32_t* labels, const uint8_t* mask, float softcap, int chunk, int products,
+                          double* rmax, double*, int32_t*, float*, void* stream) {
+    last_w.data = W; last_v0 = v0; last_vs = V_shard; last_H = H; last_in = X; last_T = T; last_lab = labels;
+    last_mask = mask; last_cap = softcap; last_chunk = chunk; last_products = products; last_state = rmax;
+    last_stream = stream; return (tk_status)ret();
+}
+tk_status tk_lmhead_grad(tk_ctx*, const uint16_t* W, int v0, int V_shard, int H, const float* X, int T,
+                         const int32_t* labels, const uint8_t* mask, int n_loss, float softcap, int chunk, int products,
+                         const double* rmax, const double*, float* dX, void* stream) {
+    last_w.data = W; last_v0 = v0; last_vs = V_shard; last_H = H; last_in = X; last_T = T; last_lab = labels;
+    last_mask = mask; last_nloss = n_loss; last_cap = softcap; last_chunk = chunk; last_products = products;
+    last_state = rmax; last_out = dX; last_stream = stream; return (tk_status)ret();
+}
 }
 
 #include "tier_bridge.h"
@@ -99,5 +116,26 @@ int main() {
     // not quantized: the reference's chat branches
     ChatMat dense{W, 0, N, 256, 0};
     CHECK("chat_dense_not_routed", !tk_bridge_chat(dense, W, x, y, 1, nullptr));
+    // LM head: chunk size rounded to 256 rows; a 256-multiple chunk goes to
+    // libtierk on the reference's running state, any other stays on the reference path
+    CHECK("lm_chunk_rounding", tk_bridge_lm_chunk(60032) == 59904 && tk_bridge_lm_chunk(1024) == 1024 &&
+                                   tk_bridge_lm_chunk(384) == 384);
+    static double rmax[8], rsum[8];
+    static int amax[8];
+    static float tgt[8];
+    static int32_t tok[8];
+    static unsigned char msk[8];
+    ok = tk_bridge_lm_stats(W, 2048, 1024, 64, x, 8, tok, msk, 30.0f, rmax, rsum, amax, tgt);
+    CHECK("lm_stats_args", ok && last_w.data == W && last_v0 == 2048 && last_vs == 1024 && last_chunk == 1024 &&
+                               last_H == 64 && last_in == x && last_T == 8 && last_lab == tok && last_mask == msk &&
+                               last_cap == 30.0f && last_products == TK_X3_REF && last_state == rmax &&
+                               last_stream == nullptr);
+    ok = tk_bridge_lm_grad(W, 0, 512, 64, x, 8, tok, msk, 7, 0.0f, rmax, rsum, y);
+    CHECK("lm_grad_args", ok && last_vs == 512 && last_chunk == 512 && last_nloss == 7 && last_out == y &&
+                              last_state == rmax && last_products == TK_X3_REF);
+    const int c0 = calls;
+    CHECK("lm_ragged_chunk_not_routed", !tk_bridge_lm_stats(W, 0, 1000, 64, x, 8, tok, msk, 0.0f, rmax, rsum, amax, tgt) &&
+                                            !tk_bridge_lm_grad(W, 0, 1000, 64, x, 8, tok, msk, 7, 0.0f, rmax, rsum, y) &&
+                                            calls == c0);
     return 0;
 }

@@ -21,13 +21,21 @@ def test_patch_hooks_each_call_site_once():
     src = ("static void linear(hipblasHandle_t h, const float* x, const float* W, float* out, int M, int K, int N){ a; }\n"
            "static void linear_dx(hipblasHandle_t h, const float* dY, const float* W, float* dX, int M, int K, int N){ b; }\n"
            "static void linear_dx_acc(hipblasHandle_t h, const float* dY, const float* W, float* dX, int M, int K, int N)"
-           "{ c; }\nstatic void chat_lin(ChatMat& m, const float* x, float* y, int M){ if(m.qt){ q; } else { r; } }\n")
+           "{ c; }\nstatic void chat_lin(ChatMat& m, const float* x, float* y, int M){ if(m.qt){ q; } else { r; } }\n"
+           "int main(){ const int CHUNK=lm_chunk(seq_len);\n"
+           "for(int v0=0; v0<VOCAB; v0+=CHUNK){ HIP_CHECK(hipMemcpy(d_chunk_bf,(const char*)head_h+(size_t)v0*row_bytes,"
+           "(size_t)vc*row_bytes,hipMemcpyHostToDevice)); p1; }\n"
+           "for(int v0=0; v0<VOCAB; v0+=CHUNK){ HIP_CHECK(hipMemcpy(d_chunk_bf,(const char*)head_h+(size_t)v0*row_bytes,"
+           "(size_t)vc*row_bytes,hipMemcpyHostToDevice)); p2; } }\n")
     out = patch(src)
     assert out.count('#include "tier_bridge.h"') == 1
     assert "if(tk_bridge_fwd(x,W,out,M,K,N)) return; a;" in out
     assert "if(tk_bridge_dx(dY,W,dX,M,K,N,0.0f)) return; b;" in out
     assert "if(tk_bridge_dx(dY,W,dX,M,K,N,1.0f)) return; c;" in out
     assert "if(m.qt && tk_bridge_chat(m,W,x,y,M,g_chat_cs)){ } else if(m.qt){ q; }" in out
+    assert "const int CHUNK=tk_bridge_lm_chunk(lm_chunk(seq_len));" in out
+    i1, i2 = out.index("tk_bridge_lm_stats("), out.index("tk_bridge_lm_grad(")
+    assert i1 < out.index("p1;") < i2 < out.index("p2;")
     with pytest.raises(SystemExit):
         patch(src.replace("linear_dx_acc", "other"))
 
@@ -65,7 +73,7 @@ def test_bridge_routing_and_call_arguments(tmp_path):
     r = subprocess.run([str(exe)], capture_output=True, text=True, timeout=60)
     assert r.returncode == 0, r.stderr
     lines = [ln.split() for ln in r.stdout.splitlines() if ln.strip()]
-    assert len(lines) == 12
+    assert len(lines) == 16
     assert all(v == "1" for _, v in lines), [n for n, v in lines if v != "1"]
 
 
