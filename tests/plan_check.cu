@@ -5,6 +5,7 @@
 #include "../tier_b200/csrc/tk_gemv5.cu"
 #include "../tier_b200/csrc/tk_gemv6.cu"
 #include "../tier_b200/csrc/tk_gemv7.cu"
+#include "../tier_b200/csrc/tk_gemv8.cu"
 
 #include <cstdio>
 
@@ -85,6 +86,29 @@ int main() {
                           "gemv7 t %d K %d", t, K);
                 }
             }
+    // one-token dp4a kernel (Q8_0): segments cover K exactly, every bulk copy
+    // (one row's segment) starts and ends on 16 bytes, warps divide into teams
+    long n4 = 0;
+    for (int K = 1024; K <= 65536; K += 1024)
+        for (int N : Ns) {
+            const int grid = N < 148 ? N : 148;
+            GdPlan p;
+            if (!gd_plan(N, K, rowb(QT_Q8_0, K), grid, p)) continue;
+            ++n4;
+            const int J = K / 1024;
+            const int nused = (J + p.jseg - 1) / p.jseg;
+            CHECK(p.smem <= GD_SMEM_MAX, "gemv8 K %d N %d smem %zu", K, N, p.smem);
+            CHECK(GD_CW % p.nseg == 0 && p.jseg >= 1 && p.jseg <= GD_JMAX, "gemv8 K %d nseg %d jseg %d", K, p.nseg,
+                  p.jseg);
+            CHECK(nused <= p.nseg && (nused - 1) * p.jseg < J && nused * p.jseg >= J, "gemv8 K %d cover", K);
+            CHECK(p.slot_bytes % 16 == 0 && (34u * 32u * p.jseg) % 16 == 0 && (34u * 32u * (J - (nused - 1) * p.jseg)) % 16 == 0,
+                  "gemv8 K %d copy sizes", K);
+            CHECK(p.x_off % 128 == 0 && p.xs_off % 16 == 0 && p.bar_off % 8 == 0, "gemv8 K %d offsets", K);
+        }
+    for (int K : {4096, 5120, 14336}) {
+        GdPlan p;
+        CHECK(gd_plan(14336, K, rowb(QT_Q8_0, K), 148, p), "no dp4a plan for K %d", K);
+    }
     // every decode shape of a 12B-class layer (hidden 5120, q 4096, k/v 1024,
     // MLP 14336) has an integer plan: Q6_K needs 16-byte rows (K % 2048 == 0)
     const int Ks[3] = {4096, 5120, 14336};
@@ -99,6 +123,6 @@ int main() {
             for (int M = 3; M <= (t == QT_Q6_K ? 8 : 16); ++M)
                 CHECK(gemv_wide_ok(t, rb, K, M), "no 3..16 plan t %d K %d M %d", t, K, M);
         }
-    printf("plans checked: %ld fp16-MMA, %ld integer, %ld streamed-x; %d failures\n", n1, n2, n3, g_bad);
+    printf("plans checked: %ld fp16-MMA, %ld integer, %ld streamed-x, %ld dp4a; %d failures\n", n1, n2, n3, n4, g_bad);
     return g_bad ? 1 : 0;
 }
