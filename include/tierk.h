@@ -290,6 +290,32 @@ tk_status tk_comm_connect(tk_ctx *ctx, const void *handles);
 tk_status tk_linear_dx_rs(tk_ctx *ctx, const tk_weight *W, const void *dY, int dy_dtype, int M, int lddy,
                           float *dX_rows, int ldd, int products, void *stream);
 
+/* Collectives of the sharded path on the same peer buffers (stores over
+ * NVLink, no NCCL), so that a C or C++ caller -- the reference's engine is
+ * one -- can shard without another communication library.  No counterpart in
+ * the reference (it runs on one GPU).  Every rank makes the same sequence of
+ * these and tk_linear_dx_rs calls; a rank that does not take part makes the
+ * others' bounded waits (2 s) report TK_ERR_TIMEOUT through tk_sync_status.
+ * Sizes and pointers 16-byte aligned; world * bytes <= recv_bytes of
+ * tk_comm_init. */
+/* dst[world * bytes] = every rank's src[bytes], in rank order: the all-gather
+ * of output shards (a row-split linear's Y columns, a decode GEMV's y). */
+tk_status tk_allgather(tk_ctx *ctx, const void *src, size_t bytes, void *dst, void *stream);
+/* buf[i] = sum over ranks of buf[i] (n % 4 == 0), added in rank order so that
+ * every rank holds the same bits: the LM head's dX over vocabulary shards. */
+tk_status tk_allreduce_f32(tk_ctx *ctx, float *buf, size_t n, void *stream);
+/* Vocabulary-shard merge of the LM head's running state, rank r holding the
+ * r-th vocabulary range: afterwards every rank holds the state of the whole
+ * vocabulary -- rmax = max over ranks; rsum = sum over ranks (rank order) of
+ * rsum_r * exp(rmax_r - rmax); amax = the argmax of the first rank whose
+ * rmax_r equals rmax (lowest vocabulary index on ties, as the reference);
+ * tgt = sum of tgt_r -- and rows t < n of the single-pass accumulator dX
+ * [n, H] (nullable) are scaled by exp(rmax_local - rmax), as
+ * tk_lmhead_rescale does.  The step between pass 1 (or tk_lmhead_fused) and
+ * tk_lmhead_loss / tk_lmhead_grad / tk_lmhead_finish. */
+tk_status tk_lmhead_merge(tk_ctx *ctx, int n, double *rmax, double *rsum, int32_t *amax, float *tgt,
+                          float *dX, int H, void *stream);
+
 /* ---- LM head + cross-entropy over a vocabulary shard --------------------- */
 /* The reference runs two passes over vocab chunks (tier/tier.cpp:3184-3266).
  * W: fp16 [V_shard, H] rows v0 .. v0+V_shard of the full head; X: fp32 [T, H]

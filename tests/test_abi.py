@@ -57,6 +57,10 @@ def test_null_context_is_rejected_not_crashed(lib):
     assert st == 1 and b"null context" in lib.tk_last_error_string()
     st = lib.tk_set_iq_grids(None, None)
     assert st == 1 and b"null context" in lib.tk_last_error_string()
+    # the peer collectives refuse a null context and an unconnected one alike
+    assert lib.tk_allgather(None, None, 16, None, None) == 1
+    assert lib.tk_allreduce_f32(None, None, 4, None) == 1
+    assert lib.tk_lmhead_merge(None, 4, None, None, None, None, None, 0, None) == 1
 
 
 def test_qtype_values_and_names_match_header(lib):

@@ -1,8 +1,9 @@
 """Row-sharded linear and decode and vocab-sharded LM head across 2 GPUs (one
-process per GPU, NCCL), and the dX reduce-scatter done inside the GEMM over peer
-memory: every rank's gathered / reduced / scattered result equals the
-single-GPU result within the path's tolerance.  Skipped with fewer than 2
-GPUs."""
+process per GPU), with the collectives of torch.distributed (NCCL) and then
+with the library's own over peer memory (tk_allgather, tk_allreduce_f32,
+tk_lmhead_merge), and the dX reduce-scatter done inside the GEMM: every
+rank's gathered / reduced / scattered result equals the single-GPU result
+within the path's tolerance.  Skipped with fewer than 2 GPUs."""
 import os
 import socket
 
@@ -60,6 +61,33 @@ def _worker(rank, world, port, q):
             torch.cuda.synchronize()
             derr.append(float((yd - yd1).norm() / yd1.norm()))
         out["decode"] = max(derr)
+        # --- LM head, vocab split: torch.distributed first, then the library's
+        # peer collectives (tk_lmhead_merge, tk_allreduce_f32) once connected ---
+        V, H, T = 4096, 256, 64
+        W = (torch.randn(V, H, device="cuda", generator=g) * 0.02).half()
+        Xh = torch.randn(T, H, device="cuda", generator=g)
+        labels = torch.randint(0, V, (T,), device="cuda", generator=g, dtype=torch.int32)
+        mask = torch.ones(T, dtype=torch.uint8, device="cuda")
+        va, vb = shard_rows(V, world, rank, align=256)
+        h1 = LMHead(ctx, W, 0, chunk=512)
+        loss1, _, hits1, amax1, dXh1 = h1.step(Xh, labels, mask)
+
+        def lm_checks(prefix):
+            hs = LMHead(ctx, W[va:vb].contiguous(), va, chunk=512, group=dist.group.WORLD)
+            loss, n, hits, amax, dXh = hs.step(Xh, labels, mask)
+            torch.cuda.synchronize()
+            out[prefix + "lm_loss"] = abs(loss.item() - loss1.item()) / abs(loss1.item())
+            out[prefix + "lm_dx"] = float((dXh - dXh1).norm() / dXh1.norm())
+            out[prefix + "lm_amax"] = bool(torch.equal(amax, amax1)) and hits.item() == hits1.item()
+            # single pass: accumulator rescaled to the global max, finished, summed
+            lossf, _, hitsf, amaxf, dXf = hs.step_fused(Xh, labels, mask)
+            torch.cuda.synchronize()
+            out[prefix + "lmf_loss"] = abs(lossf.item() - loss1.item()) / abs(loss1.item())
+            out[prefix + "lmf_dx"] = float((dXf - dXh1).norm() / dXh1.norm())
+            out[prefix + "lmf_amax"] = bool(torch.equal(amaxf, amax1)) and hitsf.item() == hits1.item()
+            return dXh, dXf
+
+        t_dx, t_dxf = lm_checks("")
         # dX reduce-scattered inside the GEMM over peer memory: this rank's
         # token rows of the sum; three calls in a row cover both buffer
         # parities and the acknowledgement path; fp32 dY (x3, several
@@ -78,27 +106,27 @@ def _worker(rank, world, port, q):
             errs.append(float((part - want).norm() / want.norm()))
         ctx.sync_status()
         out["rs_dx"] = max(errs)
-        # --- LM head, vocab split ---
-        V, H, T = 4096, 256, 64
-        W = (torch.randn(V, H, device="cuda", generator=g) * 0.02).half()
-        Xh = torch.randn(T, H, device="cuda", generator=g)
-        labels = torch.randint(0, V, (T,), device="cuda", generator=g, dtype=torch.int32)
-        mask = torch.ones(T, dtype=torch.uint8, device="cuda")
-        va, vb = shard_rows(V, world, rank, align=256)
-        hs = LMHead(ctx, W[va:vb].contiguous(), va, chunk=512, group=dist.group.WORLD)
-        loss, n, hits, amax, dXh = hs.step(Xh, labels, mask)
-        h1 = LMHead(ctx, W, 0, chunk=512)
-        loss1, _, hits1, amax1, dXh1 = h1.step(Xh, labels, mask)
+        # the same operations over the library's peer collectives (no NCCL on
+        # the data path): all-gathered forward and decode, LM-head merge and
+        # dX all-reduce; every rank holds the same bits
+        assert ctx.peers == (rank, world)
+        Yp = lp.forward(X)
         torch.cuda.synchronize()
-        out["lm_loss"] = abs(loss.item() - loss1.item()) / abs(loss1.item())
-        out["lm_dx"] = float((dXh - dXh1).norm() / dXh1.norm())
-        out["lm_amax"] = bool(torch.equal(amax, amax1)) and hits.item() == hits1.item()
-        # single pass: accumulator rescaled to the global max, finished, summed
-        lossf, _, hitsf, amaxf, dXf = hs.step_fused(Xh, labels, mask)
+        out["p_lin_fwd"] = float((Yp - Y1).norm() / Y1.norm())
+        derr = []
+        for Md in (1, 3, 12):
+            xd = torch.from_numpy(rng.standard_normal((Md, K)).astype(np.float32)).cuda()
+            yd, yd1 = lp.decode(xd), full.decode(xd)
+            torch.cuda.synchronize()
+            derr.append(float((yd - yd1).norm() / yd1.norm()))
+        out["p_decode"] = max(derr)
+        p_dx, p_dxf = lm_checks("p_")
+        mine = torch.cat([p_dx.flatten(), p_dxf.flatten()])
+        both = torch.empty(world * mine.numel(), device="cuda")
+        ctx.allgather(mine, both)
         torch.cuda.synchronize()
-        out["lmf_loss"] = abs(lossf.item() - loss1.item()) / abs(loss1.item())
-        out["lmf_dx"] = float((dXf - dXh1).norm() / dXh1.norm())
-        out["lmf_amax"] = bool(torch.equal(amaxf, amax1)) and hitsf.item() == hits1.item()
+        out["p_same_bits"] = bool(torch.equal(both[: mine.numel()], both[mine.numel():]))
+        ctx.sync_status()
         ctx.close()
     except Exception as e:  # report, never hang the other rank
         out["error"] = repr(e)
@@ -126,5 +154,7 @@ def test_two_gpu_shards_match_single_gpu():
         assert o["lin_fwd"] < 1e-6 and o["lin_dx"] < 1e-5, o
         assert o["decode"] < 1e-5, o
         assert o["rs_dx"] < 1e-5, o
-        assert o["lm_loss"] < 1e-6 and o["lm_dx"] < 1e-5 and o["lm_amax"], o
-        assert o["lmf_loss"] < 1e-6 and o["lmf_dx"] < 1e-5 and o["lmf_amax"], o
+        for pre in ("", "p_"):
+            assert o[pre + "lm_loss"] < 1e-6 and o[pre + "lm_dx"] < 1e-5 and o[pre + "lm_amax"], (pre, o)
+            assert o[pre + "lmf_loss"] < 1e-6 and o[pre + "lmf_dx"] < 1e-5 and o[pre + "lmf_amax"], (pre, o)
+        assert o["p_lin_fwd"] < 1e-6 and o["p_decode"] < 1e-5 and o["p_same_bits"], o

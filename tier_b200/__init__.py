@@ -132,6 +132,9 @@ SIGNATURES = [
     ("tk_comm_init", _I, [_P, _I, _I, _SZ, _P]),
     ("tk_comm_connect", _I, [_P, _P]),
     ("tk_linear_dx_rs", _I, [_P, ctypes.POINTER(Weight), _P, _I, _I, _I, _P, _I, _I, _P]),
+    ("tk_allgather", _I, [_P, _P, _SZ, _P, _P]),
+    ("tk_allreduce_f32", _I, [_P, _P, _SZ, _P]),
+    ("tk_lmhead_merge", _I, [_P, _I, _P, _P, _P, _P, _P, _I, _P]),
     ("tk_lmhead_stats", _I, [_P, _P, _I, _I, _I, _P, _I, _P, _P, _F, _I, _I, _P, _P, _P, _P, _P]),
     ("tk_lmhead_grad", _I, [_P, _P, _I, _I, _I, _P, _I, _P, _P, _I, _F, _I, _I, _P, _P, _P, _P]),
     ("tk_lmhead_loss", _I, [_P, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P]),
@@ -197,6 +200,7 @@ class Context:
         _check(self.lib.tk_init(device, ctypes.byref(h)))
         self.h = h
         self.device = device
+        self.peers = None        # (rank, world) once host.connect_peers has set up the peer buffers
 
     def close(self):
         if self.h:
@@ -309,6 +313,22 @@ class Context:
         _check(self.lib.tk_linear_dx_rs(self.h, ctypes.byref(W), _ptr(dY), dy_dtype, M, lddy or W.rows, _ptr(dX_rows),
                                         ldd or W.cols, products, _stream(stream)))
         return dX_rows
+
+    def allgather(self, src, dst, nbytes=None, stream=None):
+        """dst = every rank's src in rank order (tk_allgather)."""
+        nb = nbytes if nbytes is not None else src.numel() * src.element_size()
+        _check(self.lib.tk_allgather(self.h, _ptr(src), nb, _ptr(dst), _stream(stream)))
+        return dst
+
+    def allreduce_f32(self, buf, stream=None):
+        """buf = sum over ranks, in rank order (tk_allreduce_f32)."""
+        _check(self.lib.tk_allreduce_f32(self.h, _ptr(buf), buf.numel(), _stream(stream)))
+        return buf
+
+    def lmhead_merge(self, n, rmax, rsum, amax, tgt, dX=None, H=0, stream=None):
+        """Merge the vocabulary shards' running LM-head state (tk_lmhead_merge)."""
+        _check(self.lib.tk_lmhead_merge(self.h, n, _ptr(rmax), _ptr(rsum), _ptr(amax), _ptr(tgt), _ptr(dX), H,
+                                        _stream(stream)))
 
     def weight_split_f32(self, W32, rows, cols, planes, stream=None) -> int:
         sc = _I(0)

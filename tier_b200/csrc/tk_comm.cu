@@ -150,6 +150,196 @@ tk_status rs_finish(tk_ctx* ctx, const RsDesc& rs, int K, float* out, long ldo, 
     return cuda_fail(cudaGetLastError(), "reduce-scatter reduce launch");
 }
 
+// ---------------------------------------------------------------------------
+// Collectives on the same buffers (no NCCL): an exchange of epoch e copies
+// every rank's contribution into slot `rank` of parity (e & 1) of every rank's
+// receive region, publishes done[e & 1][rank] to every rank, and each rank
+// consumes its own region and acknowledges -- the reduce-scatter's protocol,
+// so both kinds share epochs, flags and acks and may follow each other in any
+// order, as long as every rank issues the same sequence.
+struct CmPush {
+    uint4* dst[TK_MAX_RANKS];    // per rank: my slot in its receive region (this parity)
+    int* done[TK_MAX_RANKS];     // per rank: its done flag for me (this parity)
+    int world, epoch;
+    int* counter;                // blocks finished (local), reset by the last
+};
+
+__global__ void cm_push_kernel(const __grid_constant__ CmPush a, const uint4* __restrict__ src, size_t n16) {
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n16; i += (size_t)gridDim.x * blockDim.x) {
+        const uint4 v = src[i];
+        for (int o = 0; o < a.world; ++o) a.dst[o][i] = v;
+    }
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const int old = atomicAdd(a.counter, 1);
+        if (old == (int)gridDim.x - 1) {
+            *a.counter = 0;
+            __threadfence_system();
+            for (int o = 0; o < a.world; ++o) st_release_sys_c(a.done[o], a.epoch);
+        }
+    }
+}
+
+struct CmConsume {
+    const int* done;             // my done flags of this parity, [world]
+    int* red_ctr;
+    int* const* peer_ack;        // device table of every rank's ack array
+    int world, epoch, me;
+    int* status;
+};
+
+// Wait (thread 0, bounded) until every rank's contribution arrived.
+__device__ bool cm_wait_all(const CmConsume& c) {
+    __shared__ int ok;
+    if (threadIdx.x == 0) {
+        int good = 1;
+        for (int src = 0; src < c.world && good; ++src) good = wait_ge(c.done + src, c.epoch, c.status);
+        ok = good;
+    }
+    __syncthreads();
+    return ok != 0;
+}
+// After the block consumed its part: the last block acknowledges the epoch to every rank.
+__device__ void cm_ack(const CmConsume& c, bool ok) {
+    __syncthreads();
+    if (threadIdx.x == 0 && ok) {
+        __threadfence_system();
+        const int old = atomicAdd(c.red_ctr, 1);
+        if (old == (int)gridDim.x - 1) {
+            *c.red_ctr = 0;
+            __threadfence_system();
+            for (int o = 0; o < c.world; ++o) st_release_sys_c(c.peer_ack[o] + c.me, c.epoch);
+        }
+    }
+}
+
+// all-gather: dst = the world slots in rank order
+__global__ void cm_gather_kernel(const __grid_constant__ CmConsume c, const uint4* __restrict__ recv, size_t n16_all,
+                                 uint4* __restrict__ dst) {
+    const bool ok = cm_wait_all(c);
+    if (ok)
+        for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n16_all; i += (size_t)gridDim.x * blockDim.x)
+            dst[i] = recv[i];
+    cm_ack(c, ok);
+}
+
+// all-reduce: out[i] = sum of the world slots' element i, in rank order
+__global__ void cm_sum_kernel(const __grid_constant__ CmConsume c, const float4* __restrict__ recv, size_t n4,
+                              float4* __restrict__ out) {
+    const bool ok = cm_wait_all(c);
+    if (ok)
+        for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n4; i += (size_t)gridDim.x * blockDim.x) {
+            float4 acc = recv[i];
+            for (int r = 1; r < c.world; ++r) {
+                const float4 v = recv[(size_t)r * n4 + i];
+                acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+            }
+            out[i] = acc;
+        }
+    cm_ack(c, ok);
+}
+
+// LM-head vocabulary-shard merge.  Slot layout per rank (n rows, padded to
+// 16 bytes per array): rmax f64 [n], rsum f64 [n], amax i32 [n], tgt f32 [n].
+__host__ __device__ inline size_t lm_pack_bytes(int n) {
+    return ((size_t)n * 8 + 15) / 16 * 16 * 2 + ((size_t)n * 4 + 15) / 16 * 16 * 2;
+}
+__global__ void lm_pack_kernel(int n, const double* rmax, const double* rsum, const int32_t* amax, const float* tgt,
+                               uint8_t* out) {
+    const size_t o1 = ((size_t)n * 8 + 15) / 16 * 16, o2 = 2 * o1, o3 = o2 + ((size_t)n * 4 + 15) / 16 * 16;
+    for (int t = blockIdx.x * blockDim.x + threadIdx.x; t < n; t += gridDim.x * blockDim.x) {
+        reinterpret_cast<double*>(out)[t] = rmax[t];
+        reinterpret_cast<double*>(out + o1)[t] = rsum[t];
+        reinterpret_cast<int32_t*>(out + o2)[t] = amax[t];
+        reinterpret_cast<float*>(out + o3)[t] = tgt[t];
+    }
+}
+// Every rank computes the same merged row from the gathered slots (rank order
+// = vocabulary order): max; sum of rsum_r * exp(rmax_r - max); the argmax of
+// the first rank that reaches the max; sum of the target logits.  The local
+// single-pass accumulator row is rescaled by exp(rmax_local - max).
+__global__ void lm_merge_kernel(const __grid_constant__ CmConsume c, const uint8_t* __restrict__ recv, int n,
+                                size_t slot, int me, double* rmax, double* rsum, int32_t* amax, float* tgt, float* dX,
+                                int H) {
+    const bool ok = cm_wait_all(c);
+    const size_t o1 = ((size_t)n * 8 + 15) / 16 * 16, o2 = 2 * o1, o3 = o2 + ((size_t)n * 4 + 15) / 16 * 16;
+    if (ok)
+        for (int t = blockIdx.x; t < n; t += gridDim.x) {
+            double m = -1e300;
+            int best = 0;
+            for (int r = 0; r < c.world; ++r) {
+                const double v = reinterpret_cast<const double*>(recv + r * slot)[t];
+                if (v > m) { m = v; best = r; }
+            }
+            const double mine = reinterpret_cast<const double*>(recv + me * slot)[t];
+            if (dX) {
+                const float f = (float)exp(mine - m);
+                for (int h = threadIdx.x; h < H; h += blockDim.x) dX[(size_t)t * H + h] *= f;
+            }
+            __syncthreads();    // every thread has read this row's state before thread 0 rewrites it
+            if (threadIdx.x == 0) {
+                double s = 0.0;
+                float tg = 0.0f;
+                for (int r = 0; r < c.world; ++r) {
+                    const uint8_t* b = recv + r * slot;
+                    s += reinterpret_cast<const double*>(b + o1)[t] * exp(reinterpret_cast<const double*>(b)[t] - m);
+                    tg += reinterpret_cast<const float*>(b + o3)[t];
+                }
+                rmax[t] = m;
+                rsum[t] = s;
+                amax[t] = reinterpret_cast<const int32_t*>(recv + best * slot + o2)[t];
+                tgt[t] = tg;
+            }
+        }
+    cm_ack(c, ok);
+}
+
+// Start an exchange of `slot` bytes per rank: capacity check, epoch, wait for
+// the acks of the parity's previous use, push `src` into every rank's region.
+static tk_status cm_start(tk_ctx* ctx, const void* src, size_t slot, CmConsume& c, const uint8_t** recv,
+                          cudaStream_t s) {
+    tk_comm_state* cs = ctx->comm;
+    if (!cs || !cs->connected) return fail(TK_ERR_INVALID, "collective: tk_comm_init / tk_comm_connect first");
+    if (slot % 16 || (reinterpret_cast<uintptr_t>(src) & 15))
+        return fail(TK_ERR_INVALID, "collective: 16-byte aligned data and sizes required");
+    if (slot * cs->world > cs->recv_bytes)
+        return fail(TK_ERR_INVALID, "collective: world * bytes exceeds the recv_bytes given to tk_comm_init");
+    const int epoch = (int)++cs->epoch;
+    const int par = epoch & 1;
+    rs_wait_ack_kernel<<<1, 32, 0, s>>>(hdr_int(cs->buf, kAckOff), cs->world, epoch - 2, ctx->status);
+    ctx->launches++;
+    CmPush a;
+    for (int o = 0; o < cs->world; ++o) {
+        a.dst[o] = reinterpret_cast<uint4*>(cs->peer[o] + kHdr + (size_t)par * cs->recv_bytes + (size_t)cs->rank * slot);
+        a.done[o] = hdr_int(cs->peer[o], kDoneOff) + par * 8 + cs->rank;
+    }
+    a.world = cs->world;
+    a.epoch = epoch;
+    a.counter = hdr_int(cs->buf, kGemmCtr);
+    const size_t n16 = slot / 16;
+    int blocks = (int)((n16 + 255) / 256);
+    if (blocks > 2 * ctx->num_sms) blocks = 2 * ctx->num_sms;
+    if (blocks < 1) blocks = 1;
+    cm_push_kernel<<<blocks, 256, 0, s>>>(a, static_cast<const uint4*>(src), n16);
+    ctx->launches++;
+    c.done = hdr_int(cs->buf, kDoneOff) + par * 8;
+    c.red_ctr = hdr_int(cs->buf, kRedCtr);
+    c.peer_ack = reinterpret_cast<int* const*>(cs->buf + 1024);
+    c.world = cs->world;
+    c.epoch = epoch;
+    c.me = cs->rank;
+    c.status = ctx->status;
+    *recv = cs->buf + kHdr + (size_t)par * cs->recv_bytes;
+    return cuda_fail(cudaGetLastError(), "collective push launch");
+}
+
+static int cm_blocks(tk_ctx* ctx, size_t n) {
+    size_t b = (n + 255) / 256;
+    if (b > (size_t)(2 * ctx->num_sms)) b = 2 * ctx->num_sms;
+    return b < 1 ? 1 : (int)b;
+}
+
 void comm_destroy(tk_ctx* ctx) {
     tk_comm_state* c = ctx->comm;
     if (!c) return;
@@ -220,6 +410,60 @@ tk_status tk_comm_connect(tk_ctx* ctx, const void* handles) {
     if (e != cudaSuccess) return cuda_fail(e, "tk_comm_connect: ack table");
     c->connected = true;
     return TK_OK;
+}
+
+tk_status tk_allgather(tk_ctx* ctx, const void* src, size_t bytes, void* dst, void* stream) {
+    if (!ctx || (bytes && (!src || !dst))) return fail(TK_ERR_INVALID, "tk_allgather: null argument");
+    if (reinterpret_cast<uintptr_t>(dst) & 15) return fail(TK_ERR_INVALID, "tk_allgather: dst must be 16-byte aligned");
+    if (bytes == 0) return TK_OK;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    CmConsume c;
+    const uint8_t* recv = nullptr;
+    tk_status st = cm_start(ctx, src, bytes, c, &recv, s);
+    if (st != TK_OK) return st;
+    const size_t n16 = bytes / 16 * c.world;
+    cm_gather_kernel<<<cm_blocks(ctx, n16), 256, 0, s>>>(c, reinterpret_cast<const uint4*>(recv), n16,
+                                                        static_cast<uint4*>(dst));
+    ctx->launches++;
+    return cuda_fail(cudaGetLastError(), "tk_allgather launch");
+}
+
+tk_status tk_allreduce_f32(tk_ctx* ctx, float* buf, size_t n, void* stream) {
+    if (!ctx || (n && !buf)) return fail(TK_ERR_INVALID, "tk_allreduce_f32: null argument");
+    if (n % 4) return fail(TK_ERR_INVALID, "tk_allreduce_f32: n must be a multiple of 4");
+    if (n == 0) return TK_OK;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    CmConsume c;
+    const uint8_t* recv = nullptr;
+    tk_status st = cm_start(ctx, buf, n * 4, c, &recv, s);
+    if (st != TK_OK) return st;
+    cm_sum_kernel<<<cm_blocks(ctx, n / 4), 256, 0, s>>>(c, reinterpret_cast<const float4*>(recv), n / 4,
+                                                        reinterpret_cast<float4*>(buf));
+    ctx->launches++;
+    return cuda_fail(cudaGetLastError(), "tk_allreduce_f32 launch");
+}
+
+tk_status tk_lmhead_merge(tk_ctx* ctx, int n, double* rmax, double* rsum, int32_t* amax, float* tgt, float* dX, int H,
+                          void* stream) {
+    if (!ctx || n < 0 || (n && (!rmax || !rsum || !amax || !tgt)))
+        return fail(TK_ERR_INVALID, "tk_lmhead_merge: null argument");
+    if (dX && H <= 0) return fail(TK_ERR_INVALID, "tk_lmhead_merge: H must be positive with dX");
+    if (n == 0) return TK_OK;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const size_t slot = lm_pack_bytes(n);
+    tk_status st = ws_ensure(ctx, slot, s);
+    if (st != TK_OK) return st;
+    uint8_t* pack = static_cast<uint8_t*>(ctx->ws);
+    lm_pack_kernel<<<cm_blocks(ctx, (size_t)n), 256, 0, s>>>(n, rmax, rsum, amax, tgt, pack);
+    ctx->launches++;
+    CmConsume c;
+    const uint8_t* recv = nullptr;
+    st = cm_start(ctx, pack, slot, c, &recv, s);
+    if (st != TK_OK) return st;
+    int blocks = n < 4 * ctx->num_sms ? n : 4 * ctx->num_sms;
+    lm_merge_kernel<<<blocks, 128, 0, s>>>(c, recv, n, slot, c.me, rmax, rsum, amax, tgt, dX, H);
+    ctx->launches++;
+    return cuda_fail(cudaGetLastError(), "tk_lmhead_merge launch");
 }
 
 }  // extern "C"

@@ -89,12 +89,42 @@ def gather_cols(local: torch.Tensor, group) -> torch.Tensor:
     return torch.cat([buf[r * M:(r + 1) * M, : ns[r]] for r in range(world)], dim=1)
 
 
+def connect_peers(ctx: Context, group, recv_bytes: int) -> None:
+    """Set up the library's peer buffers on every rank of `group` (one
+    exchange of CUDA IPC handles through torch.distributed, then a barrier).
+    Afterwards the context's collectives (tk_allgather, tk_allreduce_f32,
+    tk_lmhead_merge, tk_linear_dx_rs) run over NVLink without NCCL; a C++
+    caller does the same exchange with its own bootstrap."""
+    import torch.distributed as dist
+    world, rank = dist.get_world_size(group), dist.get_rank(group)
+    h = ctx.comm_init(rank, world, recv_bytes)
+    mine = torch.tensor(list(h), dtype=torch.uint8, device=torch.device("cuda", ctx.device))
+    allh = [torch.empty_like(mine) for _ in range(world)]
+    dist.all_gather(allh, mine, group=group)
+    ctx.comm_connect(bytes(torch.cat(allh).cpu().tolist()))
+    dist.barrier(group=group)
+    ctx.peers = (rank, world)
+
+
+def gather_cols_peer(ctx: Context, local: torch.Tensor, widths: list[int]) -> torch.Tensor:
+    """gather_cols over the library's peer buffers (tk_allgather): every
+    rank's [M, widths[r]] shard, padded to the widest, in rank order."""
+    M, n = local.shape
+    nmax = (max(widths) + 3) // 4 * 4        # whole 16-byte rows of fp32
+    send = local.contiguous() if n == nmax else torch.zeros(M, nmax, device=local.device, dtype=local.dtype)
+    if n != nmax:
+        send[:, :n] = local
+    buf = torch.empty(len(widths) * M, nmax, device=local.device, dtype=local.dtype)
+    ctx.allgather(send, buf)
+    return torch.cat([buf[r * M:(r + 1) * M, : widths[r]] for r in range(len(widths))], dim=1)
+
+
 class LinearPath:
     """One frozen projection W[N, K] (block-quantized, fp16, or fp32 split into
     fp16 hi/lo) on this rank's device, optionally row-sharded across `group`."""
 
     def __init__(self, ctx: Context, qtype: int, rows: int, cols: int, data: torch.Tensor, scale_log2: int = 0,
-                 group=None, n_total: int | None = None, row0: int = 0):
+                 group=None, n_total: int | None = None, row0: int = 0, align: int = 1):
         self.ctx = ctx
         self.data = data
         self.W: Weight = make_weight(qtype, rows, cols, data, scale_log2)
@@ -102,6 +132,7 @@ class LinearPath:
         self.group = group
         self.n_total = n_total if n_total is not None else rows
         self.row0 = row0
+        self.align = align          # row-shard boundaries are multiples of this (shard_rows)
 
     @staticmethod
     def from_f32_split(ctx: Context, W32: torch.Tensor, **kw) -> "LinearPath":
@@ -121,7 +152,7 @@ class LinearPath:
                         beta=beta if direct else 0.0, products=products)
         if self.group is None or not gather:
             return local
-        full = gather_cols(local, self.group)
+        full = self._gather(local)
         if Y is not None:
             if beta:
                 Y += full
@@ -145,24 +176,31 @@ class LinearPath:
                       row_bytes_=self.W.row_bytes)
         if self.group is None or not gather:
             return local
-        full = gather_cols(local, self.group)
+        full = self._gather(local)
         if y is not None:
             y.copy_(full)
             return y
         return full
 
+    def _gather(self, local: torch.Tensor) -> torch.Tensor:
+        """The output shards of every rank side by side: over the library's
+        peer buffers once they are connected, else with torch.distributed."""
+        if getattr(self.ctx, "peers", None) is None:
+            return gather_cols(local, self.group)
+        rank, world = self.ctx.peers
+        widths = [shard_rows(self.n_total, world, r, self.align)[1] - shard_rows(self.n_total, world, r, self.align)[0]
+                  for r in range(world)]
+        return gather_cols_peer(self.ctx, local, widths)
+
     def enable_reduce_scatter(self, M_max: int):
-        """Set up the peer buffers for `dx_rs` (one collective exchange of
-        IPC handles, then a barrier); M_max bounds the token count."""
+        """Set up the peer buffers for `dx_rs` and the peer all-gather (one
+        collective exchange of IPC handles, then a barrier); M_max bounds the
+        token count."""
         import torch.distributed as dist
-        world, rank = dist.get_world_size(self.group), dist.get_rank(self.group)
-        h = self.ctx.comm_init(rank, world, M_max * self.K * 4)
-        mine = torch.tensor(list(h), dtype=torch.uint8, device=torch.device("cuda", self.ctx.device))
-        allh = [torch.empty_like(mine) for _ in range(world)]
-        dist.all_gather(allh, mine, group=self.group)
-        self.ctx.comm_connect(bytes(torch.cat(allh).cpu().tolist()))
-        dist.barrier(group=self.group)
-        self.rs_world, self.rs_rank = world, rank
+        world = dist.get_world_size(self.group)
+        nmax = (-(-self.n_total // world) + self.align + 3) // 4 * 4
+        connect_peers(self.ctx, self.group, max(M_max * self.K * 4, world * M_max * nmax * 4))
+        self.rs_world, self.rs_rank = world, self.ctx.peers[0]
 
     def dx_rs(self, dY: torch.Tensor, out: torch.Tensor | None = None, products: int = X3_AUTO) -> torch.Tensor:
         """This rank's token rows (rank * M/world ...) of dX = sum_g dY_g . W_g,
@@ -220,8 +258,11 @@ class LMHead:
         self.ctx.lmhead_stats(self.W, self.v0, self.V_shard, self.H, X, T, labels, mask, softcap, self.chunk, rmax,
                               rsum, amax, tgt, products=self.products)
         if self.group is not None:
-            amax = merge_vocab_shards(rmax, rsum, amax, tgt, self.group,
-                                      lambda rl, sl, rg, d: self.ctx.lmhead_rescale(T - 1, rl, sl, rg))
+            if getattr(self.ctx, "peers", None) is not None:
+                self.ctx.lmhead_merge(T - 1, rmax, rsum, amax, tgt)
+            else:
+                amax = merge_vocab_shards(rmax, rsum, amax, tgt, self.group,
+                                          lambda rl, sl, rg, d: self.ctx.lmhead_rescale(T - 1, rl, sl, rg))
         return rmax, rsum, amax, tgt
 
     def loss(self, T, labels, mask, rmax, rsum, amax, tgt):
@@ -241,10 +282,16 @@ class LMHead:
         self.ctx.lmhead_grad(self.W, self.v0, self.V_shard, self.H, X, T, labels, mask, n_loss, softcap, self.chunk,
                              rmax, rsum, part, products=self.products)
         if self.group is not None:
-            import torch.distributed as dist
-            dist.all_reduce(part, group=self.group)
+            self._allreduce(part)
             dX += part
         return dX
+
+    def _allreduce(self, buf):
+        if getattr(self.ctx, "peers", None) is not None:
+            self.ctx.allreduce_f32(buf)
+        else:
+            import torch.distributed as dist
+            dist.all_reduce(buf, group=self.group)
 
     def step(self, X, labels, mask, softcap=0.0, dX=None):
         """Both passes: returns (loss_sum, n_loss, hits, amax, dX)."""
@@ -272,15 +319,18 @@ class LMHead:
         self.ctx.lmhead_fused(self.W, self.v0, self.V_shard, self.H, X, T, labels, mask, softcap, self.chunk, rmax,
                               rsum, amax, tgt, dX, products=self.products)
         if self.group is not None:
-            amax = merge_vocab_shards(rmax, rsum, amax, tgt, self.group,
-                                      lambda rl, sl, rg, d: self.ctx.lmhead_rescale(T - 1, rl, sl, rg, d, H),
-                                      dX=dX)
+            if getattr(self.ctx, "peers", None) is not None:
+                self.ctx.lmhead_merge(T - 1, rmax, rsum, amax, tgt, dX, H)
+            else:
+                amax = merge_vocab_shards(rmax, rsum, amax, tgt, self.group,
+                                          lambda rl, sl, rg, d: self.ctx.lmhead_rescale(T - 1, rl, sl, rg, d, H),
+                                          dX=dX)
         self.ctx.lmhead_finish(self.W, self.v0, self.V_shard, self.H, T, labels, mask, n_loss, softcap, rsum, tgt, dX)
         if self.group is not None:
-            import torch.distributed as dist
-            dist.all_reduce(dX, group=self.group)
+            self._allreduce(dX)
         loss, hits = self.loss(T, labels, mask, rmax, rsum, amax, tgt)
         return loss, n_loss, hits, amax, dX
 
 
-__all__ = ["LinearPath", "LMHead", "shard_rows", "merge_vocab_shards", "gather_cols"]
+__all__ = ["LinearPath", "LMHead", "shard_rows", "merge_vocab_shards", "gather_cols", "gather_cols_peer",
+           "connect_peers"]
