@@ -106,17 +106,24 @@ def connect_peers(ctx: Context, group, recv_bytes: int) -> None:
     ctx.peers = (rank, world)
 
 
-def gather_cols_peer(ctx: Context, local: torch.Tensor, widths: list[int]) -> torch.Tensor:
-    """gather_cols over the library's peer buffers (tk_allgather): every
-    rank's [M, widths[r]] shard, padded to the widest, in rank order."""
+def gather_cols_peer(ctx: Context, local: torch.Tensor) -> torch.Tensor:
+    """gather_cols over the library's peer buffers (tk_allgather): the ranks'
+    widths first (one 16-byte record each), then every rank's [M, n_rank]
+    shard padded to the widest, in rank order."""
     M, n = local.shape
+    world = ctx.peers[1]
+    rec = torch.zeros(4, dtype=torch.int32, device=local.device)
+    rec[0] = n
+    allrec = torch.empty(4 * world, dtype=torch.int32, device=local.device)
+    ctx.allgather(rec, allrec)
+    widths = [int(v) for v in allrec.view(world, 4)[:, 0].tolist()]
     nmax = (max(widths) + 3) // 4 * 4        # whole 16-byte rows of fp32
     send = local.contiguous() if n == nmax else torch.zeros(M, nmax, device=local.device, dtype=local.dtype)
     if n != nmax:
         send[:, :n] = local
-    buf = torch.empty(len(widths) * M, nmax, device=local.device, dtype=local.dtype)
+    buf = torch.empty(world * M, nmax, device=local.device, dtype=local.dtype)
     ctx.allgather(send, buf)
-    return torch.cat([buf[r * M:(r + 1) * M, : widths[r]] for r in range(len(widths))], dim=1)
+    return torch.cat([buf[r * M:(r + 1) * M, : widths[r]] for r in range(world)], dim=1)
 
 
 class LinearPath:
@@ -187,10 +194,7 @@ class LinearPath:
         peer buffers once they are connected, else with torch.distributed."""
         if getattr(self.ctx, "peers", None) is None:
             return gather_cols(local, self.group)
-        rank, world = self.ctx.peers
-        widths = [shard_rows(self.n_total, world, r, self.align)[1] - shard_rows(self.n_total, world, r, self.align)[0]
-                  for r in range(world)]
-        return gather_cols_peer(self.ctx, local, widths)
+        return gather_cols_peer(self.ctx, local)
 
     def enable_reduce_scatter(self, M_max: int):
         """Set up the peer buffers for `dx_rs` and the peer all-gather (one
@@ -198,7 +202,7 @@ class LinearPath:
         token count."""
         import torch.distributed as dist
         world = dist.get_world_size(self.group)
-        nmax = (-(-self.n_total // world) + self.align + 3) // 4 * 4
+        nmax = (max(self.N, -(-self.n_total // world)) + self.align + 3) // 4 * 4   # widest output shard
         connect_peers(self.ctx, self.group, max(M_max * self.K * 4, world * M_max * nmax * 4))
         self.rs_world, self.rs_rank = world, self.ctx.peers[0]
 
