@@ -450,9 +450,19 @@ def run_ours(args):
     mc = M_TOK // chunks
     dx_mode = args.dx_mode if world > 1 else "local"
     dXr = None
-    if dx_mode in ("fused", "rs-nccl"):
+    if dx_mode in ("fused", "rs-nccl", "reshard"):
         dXr = torch.empty(M_TOK // world, K_IN, dtype=torch.float32, device=dev)
-    if dx_mode == "fused":
+    w_full = dYrows = side = None
+    if dx_mode == "reshard":
+        # the frozen weight is held whole by every rank (33 MB of Q4_K); the
+        # forward still uses this rank's rows of it (a view), and the dX GEMM
+        # takes this rank's token rows of dY against the whole weight
+        Wfull_d = torch.from_numpy(Wq).to(dev)
+        w_full = tk.make_weight(tk.Q4_K, N_OUT, K_IN, Wfull_d)
+        w = tk.make_weight(tk.Q4_K, n_loc, K_IN, Wfull_d[r0:r1])
+        dYrows = torch.empty(M_TOK // world, N_OUT, dtype=torch.bfloat16, device=dev)
+        side = torch.cuda.Stream(dev)
+    if dx_mode in ("fused", "reshard"):
         # peer buffers for the reduce-scatter inside the dX GEMM: exchange the
         # IPC handles once, outside the timed region.  If any rank cannot map
         # its peers, every rank falls back to GEMM + NCCL reduce-scatter.
@@ -474,10 +484,21 @@ def run_ours(args):
                 ok.zero_()
             dist.all_reduce(ok, op=dist.ReduceOp.MIN, group=group)
         if not int(ok.item()):
+            if dx_mode == "reshard":
+                raise SystemExit("--dx-mode reshard: the peer buffers could not be set up")
             dx_mode = "rs-nccl"
         dist.barrier(group=group)
 
     def step(Xin, dYin, Yo=None, dXo=None):
+        if dx_mode == "reshard":
+            # dY's column shards become token-row shards over NVLink on a side
+            # stream while the forward GEMM runs; then the local dX GEMM
+            side.wait_stream(torch.cuda.current_stream(dev))
+            ctx.reshard_cols(dYin, dYrows, stream=side)
+            ctx.linear(w, Xin, M_TOK, Y if Yo is None else Yo, x_dtype=tk.DT_BF16)
+            torch.cuda.current_stream(dev).wait_stream(side)
+            ctx.linear_dx(w_full, dYrows, M_TOK // world, dXr if dXo is None else dXo, dy_dtype=tk.DT_BF16)
+            return
         ctx.linear(w, Xin, M_TOK, Y if Yo is None else Yo, x_dtype=tk.DT_BF16)
         # the dX GEMM reuses the forward's fp16 expansion of W (same frozen
         # weight, same step): one dequant per step
@@ -556,7 +577,7 @@ def run_ours(args):
     value = flop_step / (ms_step * 1e-3) / 1e12
 
     # ---- correctness of the timed outputs (every rank, every N) ----
-    if dx_mode in ("fused", "rs-nccl"):
+    if dx_mode in ("fused", "rs-nccl", "reshard"):
         dx_check, dx_row0 = dXr, rank * (M_TOK // world)
     else:
         dx_check, dx_row0 = dX, 0
@@ -580,6 +601,10 @@ def run_ours(args):
     phases = {"fwd": phase_ms(lambda: ctx.linear(w, Xd, M_TOK, Y, x_dtype=tk.DT_BF16))}
     if world == 1:
         phases["dx"] = phase_ms(lambda: ctx.linear_dx(w, dYd, M_TOK, dX, dy_dtype=tk.DT_BF16, products=tk.WREUSE))
+    elif dx_mode == "reshard":
+        phases["dy_reshard"] = phase_ms(lambda: ctx.reshard_cols(dYd, dYrows))
+        phases["dx_local_rows"] = phase_ms(
+            lambda: ctx.linear_dx(w_full, dYrows, M_TOK // world, dXr, dy_dtype=tk.DT_BF16))
     elif dx_mode == "fused":
         phases["dx_reduce_scatter"] = phase_ms(
             lambda: ctx.linear_dx_rs(w, dYd, M_TOK, dXr, dy_dtype=tk.DT_BF16, products=tk.WREUSE))
@@ -604,7 +629,7 @@ def run_ours(args):
 
     # the step's work stays on the compute stream at one GPU and with the dX
     # reduce-scatter fused into the GEMM (no NCCL call inside the step)
-    pipelined = world == 1 or (dx_mode == "fused" and not args.gather_y)
+    pipelined = world == 1 or (dx_mode in ("fused", "reshard") and not args.gather_y)
     if pipelined:
         # copy-in, compute and copy-out on three streams with two buffer sets:
         # step i's inputs come in while step i-1 computes and step i-2's
@@ -696,7 +721,11 @@ def run_ours(args):
                                      {"fused": "; dX reduce-scattered by token rows inside the dX GEMM "
                                                "(tiles stored into the owner GPU's memory over NVLink)",
                                       "rs-nccl": "; dX reduce-scattered by token rows (NCCL after the GEMM)",
-                                      "allreduce": f"; dX all-reduced in {chunks} M-chunks overlapped with the GEMMs"
+                                      "allreduce": f"; dX all-reduced in {chunks} M-chunks overlapped with the GEMMs",
+                                      "reshard": ("; dY's column shards turned into token-row shards over NVLink "
+                                                  "(tk_reshard_cols, overlapping the forward GEMM) and each rank's "
+                                                  "dX rows computed against the whole frozen weight, which every "
+                                                  "rank holds (dequantized to fp16 by that dX GEMM every step)")
                                       }[dx_mode])
                        if world > 1 else "1 GPU",
                        "l2": "working set per step ~0.5 GB > 126 MB L2 (no explicit flush)"},
@@ -1212,9 +1241,10 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--gather-y", action="store_true", help="multi-GPU: all-gather the full Y every step")
     ap.add_argument("--dx-chunks", type=int, default=4, help="multi-GPU allreduce mode: dX GEMM / all-reduce chunks")
-    ap.add_argument("--dx-mode", default="fused", choices=["fused", "rs-nccl", "allreduce"],
+    ap.add_argument("--dx-mode", default="fused", choices=["fused", "rs-nccl", "allreduce", "reshard"],
                     help="multi-GPU dX: reduce-scatter by token rows inside the GEMM over NVLink (fused), "
-                         "GEMM then NCCL reduce-scatter (rs-nccl), or chunked NCCL all-reduce of the full dX")
+                         "GEMM then NCCL reduce-scatter (rs-nccl), chunked NCCL all-reduce of the full dX "
+                         "(allreduce), or dY resharded to token rows and dX computed locally (reshard)")
     ap.add_argument("--c1-type", default="q8_0", choices=sorted(C1_TYPES), help="c1: weight block type")
     ap.add_argument("--c1-shape", default="4096x4096", help="c1: N x K of the weight")
     ap.add_argument("--c1-m", default="1,4,16", help="c1: token counts (the first is the headline)")

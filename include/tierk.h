@@ -301,6 +301,15 @@ tk_status tk_linear_dx_rs(tk_ctx *ctx, const tk_weight *W, const void *dY, int d
 /* dst[world * bytes] = every rank's src[bytes], in rank order: the all-gather
  * of output shards (a row-split linear's Y columns, a decode GEMV's y). */
 tk_status tk_allgather(tk_ctx *ctx, const void *src, size_t bytes, void *dst, void *stream);
+/* Column shards to row shards (an all-to-all): rank g holds A[M, n] = columns
+ * g*n .. (g+1)*n of a [M, world*n] matrix (row stride ld_src elements of
+ * elem_bytes); afterwards dst[M/world, world*n] (row stride ld_dst) holds rows
+ * g*M/world .. (g+1)*M/world of the whole matrix.  Every rank passes the same
+ * M and n; M % world == 0; n * elem_bytes % 16 == 0.  Used for dX of a
+ * row-split linear: moving dY (bf16, M*N*2*(world-1)/world^2 bytes out per
+ * rank) instead of the fp32 partial sums of dX (M*K*4*(world-1)/world). */
+tk_status tk_reshard_cols(tk_ctx *ctx, const void *src, int M, int n, size_t ld_src, int elem_bytes,
+                          void *dst, size_t ld_dst, void *stream);
 /* buf[i] = sum over ranks of buf[i] (n % 4 == 0), added in rank order so that
  * every rank holds the same bits: the LM head's dX over vocabulary shards. */
 tk_status tk_allreduce_f32(tk_ctx *ctx, float *buf, size_t n, void *stream);

@@ -120,6 +120,13 @@ def _worker(rank, world, port, q):
             torch.cuda.synchronize()
             derr.append(float((yd - yd1).norm() / yd1.norm()))
         out["p_decode"] = max(derr)
+        # dY column shards -> token-row shards over the peer buffers, bf16 and fp32
+        for dt in (torch.bfloat16, torch.float32):
+            full_dy = torch.from_numpy(rng.standard_normal((Mr, N)).astype(np.float32)).cuda().to(dt)
+            rows_dy = torch.empty(Mr // world, N, dtype=dt, device="cuda")
+            ctx.reshard_cols(full_dy[:, a:b].contiguous(), rows_dy)
+            torch.cuda.synchronize()
+            out[f"p_reshard_{str(dt)[6:]}"] = bool(torch.equal(rows_dy, full_dy[rank * rows:(rank + 1) * rows]))
         p_dx, p_dxf = lm_checks("p_")
         mine = torch.cat([p_dx.flatten(), p_dxf.flatten()])
         both = torch.empty(world * mine.numel(), device="cuda")
@@ -159,3 +166,4 @@ def test_two_gpu_shards_match_single_gpu():
             assert o[pre + "lm_loss"] < 1e-6 and o[pre + "lm_dx"] < 1e-5 and o[pre + "lm_amax"], (pre, o)
             assert o[pre + "lmf_loss"] < 1e-6 and o[pre + "lmf_dx"] < 1e-5 and o[pre + "lmf_amax"], (pre, o)
         assert o["p_lin_fwd"] < 1e-6 and o["p_decode"] < 1e-5 and o["p_same_bits"], o
+        assert o["p_reshard_bfloat16"] and o["p_reshard_float32"], o

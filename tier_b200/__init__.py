@@ -134,6 +134,7 @@ SIGNATURES = [
     ("tk_linear_dx_rs", _I, [_P, ctypes.POINTER(Weight), _P, _I, _I, _I, _P, _I, _I, _P]),
     ("tk_allgather", _I, [_P, _P, _SZ, _P, _P]),
     ("tk_allreduce_f32", _I, [_P, _P, _SZ, _P]),
+    ("tk_reshard_cols", _I, [_P, _P, _I, _I, _SZ, _I, _P, _SZ, _P]),
     ("tk_lmhead_merge", _I, [_P, _I, _P, _P, _P, _P, _P, _I, _P]),
     ("tk_lmhead_stats", _I, [_P, _P, _I, _I, _I, _P, _I, _P, _P, _F, _I, _I, _P, _P, _P, _P, _P]),
     ("tk_lmhead_grad", _I, [_P, _P, _I, _I, _I, _P, _I, _P, _P, _I, _F, _I, _I, _P, _P, _P, _P]),
@@ -318,6 +319,13 @@ class Context:
         """dst = every rank's src in rank order (tk_allgather)."""
         nb = nbytes if nbytes is not None else src.numel() * src.element_size()
         _check(self.lib.tk_allgather(self.h, _ptr(src), nb, _ptr(dst), _stream(stream)))
+        return dst
+
+    def reshard_cols(self, src, dst, stream=None):
+        """Column shards src [M, n] -> row shard dst [M/world, world*n] (tk_reshard_cols)."""
+        M, n = src.shape
+        _check(self.lib.tk_reshard_cols(self.h, _ptr(src), M, n, src.stride(0), src.element_size(), _ptr(dst),
+                                        dst.stride(0), _stream(stream)))
         return dst
 
     def allreduce_f32(self, buf, stream=None):

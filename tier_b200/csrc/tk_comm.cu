@@ -295,13 +295,53 @@ __global__ void lm_merge_kernel(const __grid_constant__ CmConsume c, const uint8
     cm_ack(c, ok);
 }
 
+// Column shards to row shards: rank g holds A[M, n] (its columns g*n ..
+// (g+1)*n of a [M, world*n] matrix, row stride ld_src bytes) and sends rows
+// h*M/world .. of it to rank h, packed (row_bytes = n * element bytes).
+__global__ void cm_push_rows_kernel(const __grid_constant__ CmPush a, const uint8_t* __restrict__ src, size_t ld_src,
+                                    int rows_per, size_t row_bytes) {
+    const size_t nv = row_bytes / 16, total = (size_t)rows_per * a.world * nv;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+        const size_t rg = i / nv, v = i - rg * nv;
+        const int h = (int)(rg / rows_per), r = (int)(rg - (size_t)h * rows_per);
+        a.dst[h][(size_t)r * nv + v] = *reinterpret_cast<const uint4*>(src + rg * ld_src + v * 16);
+    }
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const int old = atomicAdd(a.counter, 1);
+        if (old == (int)gridDim.x - 1) {
+            *a.counter = 0;
+            __threadfence_system();
+            for (int o = 0; o < a.world; ++o) st_release_sys_c(a.done[o], a.epoch);
+        }
+    }
+}
+
+// ... and assembles its rows: dst[r, g*n + c] = slot g [r, c] (row stride ld_dst bytes).
+__global__ void cm_rows_kernel(const __grid_constant__ CmConsume c, const uint8_t* __restrict__ recv, int rows_per,
+                               size_t row_bytes, uint8_t* __restrict__ dst, size_t ld_dst) {
+    const bool ok = cm_wait_all(c);
+    const size_t nv = row_bytes / 16, slot = (size_t)rows_per * row_bytes;
+    const size_t total = (size_t)c.world * rows_per * nv;
+    if (ok)
+        for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+            const size_t gr = i / nv, v = i - gr * nv;
+            const int g = (int)(gr / rows_per), r = (int)(gr - (size_t)g * rows_per);
+            *reinterpret_cast<uint4*>(dst + (size_t)r * ld_dst + g * row_bytes + v * 16) =
+                *reinterpret_cast<const uint4*>(recv + g * slot + (size_t)r * row_bytes + v * 16);
+        }
+    cm_ack(c, ok);
+}
+
 // Start an exchange of `slot` bytes per rank: capacity check, epoch, wait for
 // the acks of the parity's previous use, push `src` into every rank's region.
 static tk_status cm_start(tk_ctx* ctx, const void* src, size_t slot, CmConsume& c, const uint8_t** recv,
-                          cudaStream_t s) {
+                          cudaStream_t s, const uint8_t* rows_src = nullptr, size_t ld_src = 0, int rows_per = 0,
+                          size_t row_bytes = 0) {
     tk_comm_state* cs = ctx->comm;
     if (!cs || !cs->connected) return fail(TK_ERR_INVALID, "collective: tk_comm_init / tk_comm_connect first");
-    if (slot % 16 || (reinterpret_cast<uintptr_t>(src) & 15))
+    if (slot % 16 || (reinterpret_cast<uintptr_t>(rows_src ? rows_src : src) & 15))
         return fail(TK_ERR_INVALID, "collective: 16-byte aligned data and sizes required");
     if (slot * cs->world > cs->recv_bytes)
         return fail(TK_ERR_INVALID, "collective: world * bytes exceeds the recv_bytes given to tk_comm_init");
@@ -317,11 +357,12 @@ static tk_status cm_start(tk_ctx* ctx, const void* src, size_t slot, CmConsume& 
     a.world = cs->world;
     a.epoch = epoch;
     a.counter = hdr_int(cs->buf, kGemmCtr);
-    const size_t n16 = slot / 16;
+    const size_t n16 = rows_src ? slot / 16 * cs->world : slot / 16;
     int blocks = (int)((n16 + 255) / 256);
     if (blocks > 2 * ctx->num_sms) blocks = 2 * ctx->num_sms;
     if (blocks < 1) blocks = 1;
-    cm_push_kernel<<<blocks, 256, 0, s>>>(a, static_cast<const uint4*>(src), n16);
+    if (rows_src) cm_push_rows_kernel<<<blocks, 256, 0, s>>>(a, rows_src, ld_src, rows_per, row_bytes);
+    else cm_push_kernel<<<blocks, 256, 0, s>>>(a, static_cast<const uint4*>(src), n16);
     ctx->launches++;
     c.done = hdr_int(cs->buf, kDoneOff) + par * 8;
     c.red_ctr = hdr_int(cs->buf, kRedCtr);
@@ -426,6 +467,33 @@ tk_status tk_allgather(tk_ctx* ctx, const void* src, size_t bytes, void* dst, vo
                                                         static_cast<uint4*>(dst));
     ctx->launches++;
     return cuda_fail(cudaGetLastError(), "tk_allgather launch");
+}
+
+tk_status tk_reshard_cols(tk_ctx* ctx, const void* src, int M, int n, size_t ld_src, int elem_bytes, void* dst,
+                          size_t ld_dst, void* stream) {
+    if (!ctx || !src || !dst) return fail(TK_ERR_INVALID, "tk_reshard_cols: null argument");
+    tk_comm_state* cs = ctx->comm;
+    if (!cs || !cs->connected) return fail(TK_ERR_INVALID, "tk_reshard_cols: tk_comm_init / tk_comm_connect first");
+    if (M <= 0 || n <= 0 || elem_bytes <= 0 || M % cs->world)
+        return fail(TK_ERR_INVALID, "tk_reshard_cols: M must be a positive multiple of world");
+    const size_t row_bytes = (size_t)n * elem_bytes;
+    if (row_bytes % 16 || (ld_src * elem_bytes) % 16 || (ld_dst * elem_bytes) % 16 ||
+        (reinterpret_cast<uintptr_t>(dst) & 15) || ld_src < (size_t)n || ld_dst < (size_t)n * cs->world)
+        return fail(TK_ERR_INVALID, "tk_reshard_cols: rows of whole 16-byte units and 16-byte aligned pointers");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const int rows_per = M / cs->world;
+    CmConsume c;
+    const uint8_t* recv = nullptr;
+    tk_status st = cm_start(ctx, nullptr, (size_t)rows_per * row_bytes, c, &recv, s, static_cast<const uint8_t*>(src),
+                            ld_src * elem_bytes, rows_per, row_bytes);
+    if (st != TK_OK) return st;
+    const size_t nv = (size_t)cs->world * rows_per * (row_bytes / 16);
+    int blocks = cm_blocks(ctx, nv);
+    if (blocks > ctx->num_sms / 4) blocks = ctx->num_sms / 4 > 0 ? ctx->num_sms / 4 : 1;   // leaves SMs to a GEMM
+    cm_rows_kernel<<<blocks, 256, 0, s>>>(c, recv, rows_per, row_bytes, static_cast<uint8_t*>(dst),
+                                         ld_dst * elem_bytes);
+    ctx->launches++;
+    return cuda_fail(cudaGetLastError(), "tk_reshard_cols launch");
 }
 
 tk_status tk_allreduce_f32(tk_ctx* ctx, float* buf, size_t n, void* stream) {

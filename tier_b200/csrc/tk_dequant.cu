@@ -196,7 +196,9 @@ tk_status launch_dequant(tk_ctx* ctx, int t, const void* W, size_t rb, int r0, i
         if ((size_t)nrows * (cols / 32) >= (1ull << 32))
             return fail(TK_ERR_INVALID, "tk_dequant: more than 2^32 sub-blocks in one call");
         const size_t total = (size_t)nrows * (cols / 32);
-        size_t want = (total + 255) / 256, cap = (size_t)ctx->num_sms * 32;
+        // one sub-block per thread up to 64 blocks per SM: a second, partly
+        // empty pass over the grid costs more than the extra blocks
+        size_t want = (total + 255) / 256, cap = (size_t)ctx->num_sms * 64;
         const dim3 grid((unsigned)(want < cap ? want : cap));
         ProfScope ps(ctx, s, PK_DEQUANT);
         const uint8_t* w = static_cast<const uint8_t*>(W);
