@@ -388,23 +388,23 @@ __device__ __forceinline__ void dec_raw(const RawChunk<XT>& r, float (&v)[8]) {
     }
 }
 
-template <int XT, int NP>
-__global__ void __launch_bounds__(AS_THREADS) act_split_vec_kernel(const void* __restrict__ X, int M, int K, long ldx,
+template <int XT, int NP, int TH>
+__global__ void __launch_bounds__(TH) act_split_vec_kernel(const void* __restrict__ X, int M, int K, long ldx,
                                                                    long ldp, bool scaled, uint16_t* __restrict__ planes,
                                                                    int* __restrict__ row_exp) {
-    __shared__ float red[AS_THREADS / 32];
+    __shared__ float red[TH / 32];
     const int m = blockIdx.x;
     const int nch = K >> 3;
     RawChunk<XT> raw[AS_MAXCH];
     float a = 0.0f;
 #pragma unroll
     for (int i = 0; i < AS_MAXCH; ++i) {
-        const int c = threadIdx.x + i * AS_THREADS;
+        const int c = threadIdx.x + i * TH;
         if (c < nch) ld_raw<XT>(X, (size_t)m * ldx + (size_t)c * 8, raw[i]);
     }
 #pragma unroll
     for (int i = 0; i < AS_MAXCH; ++i) {
-        const int c = threadIdx.x + i * AS_THREADS;
+        const int c = threadIdx.x + i * TH;
         if (c < nch) {
             float v[8];
             dec_raw<XT>(raw[i], v);
@@ -420,7 +420,7 @@ __global__ void __launch_bounds__(AS_THREADS) act_split_vec_kernel(const void* _
         __syncthreads();
         a = red[0];
 #pragma unroll
-        for (int w = 1; w < AS_THREADS / 32; ++w) a = fmaxf(a, red[w]);
+        for (int w = 1; w < TH / 32; ++w) a = fmaxf(a, red[w]);
         e = row_exponent(a);
     }
     if (threadIdx.x == 0 && row_exp) row_exp[m] = e;
@@ -429,7 +429,7 @@ __global__ void __launch_bounds__(AS_THREADS) act_split_vec_kernel(const void* _
     uint16_t* orow = planes + (size_t)m * ldp;
 #pragma unroll
     for (int i = 0; i < AS_MAXCH; ++i) {
-        const int c = threadIdx.x + i * AS_THREADS;
+        const int c = threadIdx.x + i * TH;
         if (c >= nch) continue;
         float v[8];
         dec_raw<XT>(raw[i], v);
@@ -468,17 +468,26 @@ tk_status launch_act_split(tk_ctx* ctx, const void* X, int x_dtype, int M, int K
                      (reinterpret_cast<uintptr_t>(X) % 16) == 0 && (reinterpret_cast<uintptr_t>(planes) % 16) == 0 &&
                      (ldx * esz) % 16 == 0;
     if (vec) {
+        // rows of up to 4096 elements take 128-thread blocks (4 chunks per
+        // thread): twice the blocks per SM, so more bytes in flight per SM
+        const bool narrow = K <= 128 * 4 * 8;
+#define TK_SPLIT_VEC_TH(XT, TH)                                                                                       \
+    do {                                                                                                              \
+        if (nplanes == 1) act_split_vec_kernel<XT, 1, TH><<<M, TH, 0, s>>>(X, M, K, ldx, ldp, scaled, planes, row_exp); \
+        else if (nplanes == 2) act_split_vec_kernel<XT, 2, TH><<<M, TH, 0, s>>>(X, M, K, ldx, ldp, scaled, planes, row_exp); \
+        else act_split_vec_kernel<XT, 3, TH><<<M, TH, 0, s>>>(X, M, K, ldx, ldp, scaled, planes, row_exp);          \
+    } while (0)
 #define TK_SPLIT_VEC(XT)                                                                                              \
     do {                                                                                                              \
-        if (nplanes == 1) act_split_vec_kernel<XT, 1><<<M, AS_THREADS, 0, s>>>(X, M, K, ldx, ldp, scaled, planes, row_exp); \
-        else if (nplanes == 2) act_split_vec_kernel<XT, 2><<<M, AS_THREADS, 0, s>>>(X, M, K, ldx, ldp, scaled, planes, row_exp); \
-        else act_split_vec_kernel<XT, 3><<<M, AS_THREADS, 0, s>>>(X, M, K, ldx, ldp, scaled, planes, row_exp);          \
+        if (narrow) TK_SPLIT_VEC_TH(XT, 128);                                                                         \
+        else TK_SPLIT_VEC_TH(XT, AS_THREADS);                                                                         \
     } while (0)
         if (x_dtype == TK_DT_F32) TK_SPLIT_VEC(TK_DT_F32);
         else if (x_dtype == TK_DT_F16) TK_SPLIT_VEC(TK_DT_F16);
         else if (x_dtype == TK_DT_BF16) TK_SPLIT_VEC(TK_DT_BF16);
         else return fail(TK_ERR_INVALID, "activation dtype " + std::to_string(x_dtype));
 #undef TK_SPLIT_VEC
+#undef TK_SPLIT_VEC_TH
         ctx->launches++;
         return cuda_fail(cudaGetLastError(), "act_split launch");
     }
