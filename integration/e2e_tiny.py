@@ -11,8 +11,10 @@ tokens; the two step losses must agree.
             seq_len int32 token ids; then builds both engines.
   run       (on a GPU) runs one training step of each engine with --bf3
             (the fp16-x3 linear path the bridge routes) and --log, and
-            prints both losses as one JSON line; exit 1 if they differ by
-            more than the tolerance.
+            prints both losses and the hooked engine's count of calls
+            routed to libtierk as one JSON line; exit 1 if the losses differ
+            by more than the tolerance or no linear or LM-head pass took the
+            library path.
 
 The model is random, so its loss is near ln(vocab) and the engine's start-up
 check that stops a model it computes wrongly would fire:
@@ -63,14 +65,15 @@ def prepare(ref: Path) -> None:
     print(TINY)
 
 
-def step_loss(engine: Path, work: Path, timeout: int = 600) -> float:
-    """One training step on the tiny model; the loss from the step log."""
+def step_loss(engine: Path, work: Path, timeout: int = 600) -> tuple[float, dict]:
+    """One training step on the tiny model: the loss from the step log and,
+    for the hooked engine, the bridge's count of calls routed to libtierk."""
     work.mkdir(parents=True, exist_ok=True)
     log = work / "step.log"
     for f in (log, work / "adam.bin", work / "tier1.bin"):
         if f.exists():
             f.unlink()
-    env = dict(os.environ, TIER_NO_SELFCHECK="1")
+    env = dict(os.environ, TIER_NO_SELFCHECK="1", TIERK_BRIDGE_STATS="1")
     cmd = [str(engine), str(TINY / "model.safetensors"), str(TINY / "tokens.bin"), str(SEQ), str(work / "adam.bin"),
            str(work / "tier1.bin"), "1e-5", str(LAYERS), "1", "--bf3", "--log", str(log)]
     r = subprocess.run(cmd, capture_output=True, text=True, timeout=timeout, env=env, cwd=str(work))
@@ -80,16 +83,21 @@ def step_loss(engine: Path, work: Path, timeout: int = 600) -> float:
     m = re.search(r"===== step \d+ .*? loss ([-0-9.eE+]+)", log.read_text())
     if not m:
         raise SystemExit(f"{engine.name}: no step loss in {log}")
-    return float(m.group(1))
+    st = re.search(r"libtierk bridge: fwd (\d+) dx (\d+) chat (\d+) lm_stats (\d+) lm_grad (\d+)", r.stderr)
+    routed = dict(zip(("fwd", "dx", "chat", "lm_stats", "lm_grad"), map(int, st.groups()))) if st else {}
+    return float(m.group(1)), routed
 
 
 def run(tol: float) -> int:
-    ref_loss = step_loss(OUT_DIR / "tier_ref", TINY / "run_ref")
-    tk_loss = step_loss(OUT_DIR / "tier_tk", TINY / "run_tk")
+    ref_loss, _ = step_loss(OUT_DIR / "tier_ref", TINY / "run_ref")
+    tk_loss, routed = step_loss(OUT_DIR / "tier_tk", TINY / "run_tk")
     diff = abs(tk_loss - ref_loss)
+    # the hooked engine must have taken the library path for the layers'
+    # linears and both LM-head passes, not fallen back to the reference's code
+    took = all(routed.get(k, 0) > 0 for k in ("fwd", "dx", "lm_stats", "lm_grad"))
     print(json.dumps({"check": "tiny llama, one --bf3 training step", "loss_reference": ref_loss,
-                      "loss_libtierk": tk_loss, "abs_diff": diff, "tol": tol}))
-    return 0 if diff <= tol else 1
+                      "loss_libtierk": tk_loss, "abs_diff": diff, "tol": tol, "routed_to_libtierk": routed}))
+    return 0 if diff <= tol and took else 1
 
 
 if __name__ == "__main__":

@@ -32,10 +32,21 @@
 // safety net.
 #pragma once
 #include <cstdio>
+#include <cstdlib>
 
 #include "tierk.h"
 
 static tk_ctx* g_tk = nullptr;
+
+// Calls the bridge routed to libtierk, by kind; printed to stderr at exit when
+// TIERK_BRIDGE_STATS is set, so a run can show which of its linears took the
+// library path.
+enum { TKB_FWD, TKB_DX, TKB_CHAT, TKB_LM1, TKB_LM2, TKB_KINDS };
+static long g_tkb_calls[TKB_KINDS];
+static void tk_bridge_report() {
+    fprintf(stderr, "libtierk bridge: fwd %ld dx %ld chat %ld lm_stats %ld lm_grad %ld\n", g_tkb_calls[TKB_FWD],
+            g_tkb_calls[TKB_DX], g_tkb_calls[TKB_CHAT], g_tkb_calls[TKB_LM1], g_tkb_calls[TKB_LM2]);
+}
 
 // One context per process, on the device current at the first call (the
 // engine uses one GPU per process).
@@ -45,12 +56,13 @@ static bool tk_bridge_ready() {
         int dev = 0;
         state = (cudaGetDevice(&dev) == cudaSuccess && tk_init(dev, &g_tk) == TK_OK) ? 1 : 0;
         if (!state) fprintf(stderr, "libtierk: %s (reference path kept)\n", tk_last_error_string());
+        if (getenv("TIERK_BRIDGE_STATS")) atexit(tk_bridge_report);
     }
     return state == 1;
 }
 
-static bool tk_bridge_ok(tk_status st) {
-    if (st == TK_OK) return true;
+static bool tk_bridge_ok(tk_status st, int kind) {
+    if (st == TK_OK) { ++g_tkb_calls[kind]; return true; }
     fprintf(stderr, "libtierk: %s (reference path used)\n", tk_last_error_string());
     return false;
 }
@@ -64,14 +76,14 @@ static bool tk_bridge_fp16_x3(const float* W) {
 static bool tk_bridge_fwd(const float* x, const float* W, float* out, int M, int K, int N) {
     if (!tk_bridge_fp16_x3(W) || !tk_bridge_ready()) return false;
     tk_weight w{TK_F16, N, K, 0, (size_t)K * 2, W};
-    return tk_bridge_ok(tk_linear_fwd(g_tk, &w, x, TK_DT_F32, M, K, out, N, 0.0f, TK_X3_REF, nullptr));
+    return tk_bridge_ok(tk_linear_fwd(g_tk, &w, x, TK_DT_F32, M, K, out, N, 0.0f, TK_X3_REF, nullptr), TKB_FWD);
 }
 
 // dX[M, K] (=|+=) dY[M, N] . W (linear_dx with beta 0, linear_dx_acc with beta 1).
 static bool tk_bridge_dx(const float* dY, const float* W, float* dX, int M, int K, int N, float beta) {
     if (!tk_bridge_fp16_x3(W) || !tk_bridge_ready()) return false;
     tk_weight w{TK_F16, N, K, 0, (size_t)K * 2, W};
-    return tk_bridge_ok(tk_linear_dx(g_tk, &w, dY, TK_DT_F32, M, N, dX, K, beta, TK_X3_REF, nullptr));
+    return tk_bridge_ok(tk_linear_dx(g_tk, &w, dY, TK_DT_F32, M, N, dX, K, beta, TK_X3_REF, nullptr), TKB_DX);
 }
 
 // chat_lin, quantized weight m (block type m.qt, m.rows x m.cols, m.rb bytes
@@ -81,10 +93,10 @@ static bool tk_bridge_chat(const ChatMatT& m, const void* W, const float* x, flo
     if (!m.qt || !tk_bridge_ready()) return false;
     if (M <= 16) {
         const int qt = m.qt | (m.dev ? TK_WFROZEN : 0);
-        return tk_bridge_ok(tk_gemv(g_tk, qt, W, m.rb, m.rows, m.cols, x, m.cols, M, y, m.rows, s));
+        return tk_bridge_ok(tk_gemv(g_tk, qt, W, m.rb, m.rows, m.cols, x, m.cols, M, y, m.rows, s), TKB_CHAT);
     }
     tk_weight w{m.qt, m.rows, m.cols, 0, m.rb, W};
-    return tk_bridge_ok(tk_linear_fwd(g_tk, &w, x, TK_DT_F32, M, m.cols, y, m.rows, 0.0f, TK_X3_AUTO, s));
+    return tk_bridge_ok(tk_linear_fwd(g_tk, &w, x, TK_DT_F32, M, m.cols, y, m.rows, 0.0f, TK_X3_AUTO, s), TKB_CHAT);
 }
 
 // LM head chunk size: the reference's lm_chunk, rounded down to a multiple of
@@ -98,7 +110,8 @@ static bool tk_bridge_lm_stats(const void* Wc, int v0, int vc, int H, const floa
                                float* tgt) {
     if (vc % 256 || H % 8 || !tk_bridge_ready()) return false;
     return tk_bridge_ok(tk_lmhead_stats(g_tk, static_cast<const uint16_t*>(Wc), v0, vc, H, X, T, tokens, mask, softcap,
-                                        vc, TK_X3_REF, rmax, rsum, amax, tgt, nullptr));
+                                        vc, TK_X3_REF, rmax, rsum, amax, tgt, nullptr),
+                        TKB_LM1);
 }
 
 // Pass 2 over one chunk: dX[T, H] += dlogit . Wc (linear_dx_acc of the reference).
@@ -107,5 +120,6 @@ static bool tk_bridge_lm_grad(const void* Wc, int v0, int vc, int H, const float
                               const double* rsum, float* dX) {
     if (vc % 256 || H % 8 || !tk_bridge_ready()) return false;
     return tk_bridge_ok(tk_lmhead_grad(g_tk, static_cast<const uint16_t*>(Wc), v0, vc, H, X, T, tokens, mask, n_loss,
-                                       softcap, vc, TK_X3_REF, rmax, rsum, dX, nullptr));
+                                       softcap, vc, TK_X3_REF, rmax, rsum, dX, nullptr),
+                        TKB_LM2);
 }

@@ -133,6 +133,8 @@ int main() {
     ok = tk_bridge_lm_grad(W, 0, 512, 64, x, 8, tok, msk, 7, 0.0f, rmax, rsum, y);
     CHECK("lm_grad_args", ok && last_vs == 512 && last_chunk == 512 && last_nloss == 7 && last_out == y &&
                               last_state == rmax && last_products == TK_X3_REF);
+    CHECK("routed_counts", g_tkb_calls[TKB_FWD] >= 1 && g_tkb_calls[TKB_DX] == 2 && g_tkb_calls[TKB_CHAT] == 3 &&
+                               g_tkb_calls[TKB_LM1] == 1 && g_tkb_calls[TKB_LM2] == 1);
     const int c0 = calls;
     CHECK("lm_ragged_chunk_not_routed", !tk_bridge_lm_stats(W, 0, 1000, 64, x, 8, tok, msk, 0.0f, rmax, rsum, amax, tgt) &&
                                             !tk_bridge_lm_grad(W, 0, 1000, 64, x, 8, tok, msk, 7, 0.0f, rmax, rsum, y) &&

@@ -73,7 +73,7 @@ def test_bridge_routing_and_call_arguments(tmp_path):
     r = subprocess.run([str(exe)], capture_output=True, text=True, timeout=60)
     assert r.returncode == 0, r.stderr
     lines = [ln.split() for ln in r.stdout.splitlines() if ln.strip()]
-    assert len(lines) == 16
+    assert len(lines) == 17
     assert all(v == "1" for _, v in lines), [n for n, v in lines if v != "1"]
 
 
