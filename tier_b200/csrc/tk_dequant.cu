@@ -433,6 +433,17 @@ __global__ void __launch_bounds__(TH) act_split_vec_kernel(const void* __restric
         if (c >= nch) continue;
         float v[8];
         dec_raw<XT>(raw[i], v);
+        if constexpr (NP == 1) {
+            // one packed conversion per pair (round to nearest even, as f2h_bits)
+            uint32_t hp[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const __half2 p2 = __floats2half2_rn(v[2 * j] * f, v[2 * j + 1] * f);
+                hp[j] = *reinterpret_cast<const uint32_t*>(&p2);
+            }
+            *reinterpret_cast<uint4*>(orow + (size_t)c * 8) = make_uint4(hp[0], hp[1], hp[2], hp[3]);
+            continue;
+        }
         uint16_t h[8], mm[8], l[8];
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
