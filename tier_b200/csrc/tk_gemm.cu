@@ -604,12 +604,11 @@ static tk_status make_map(CUtensorMap* m, const void* base, long cols, long rows
 template <int CG, bool B_MN, int EPI>
 static tk_status go(tk_ctx* ctx, const GemmParams& gp, const EpiParams& ep, cudaStream_t s) {
     using G = Geo<CG>;
-    static bool attr_set = false;   // per instantiation
+    static std::atomic<uint64_t> attr_done{0};   // per instantiation, one bit per device
     auto kern = gemm_tc_kernel<CG, B_MN, EPI>;
-    if (!attr_set) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)G::SMEM);
+    {
+        const cudaError_t e = smem_attr_once(kern, (int)G::SMEM, ctx->device, attr_done);
         if (e != cudaSuccess) return cuda_fail(e, "gemm smem attribute");
-        attr_set = true;
     }
     const int tiles = gp.tiles_m * gp.tiles_n * gp.splits;   // work units
     const int groups_max = ctx->num_sms / CG;

@@ -338,11 +338,10 @@ bool gemm_q_supported(int qtype) { return qtype == QT_Q4_K || qtype == QT_Q5_K |
 template <int T, bool DX>
 static tk_status go_q(tk_ctx* ctx, const gq::Params& gp, cudaStream_t s) {
     auto kern = gq::gemm_q_kernel<T, DX>;
-    static bool attr_set = false;
-    if (!attr_set) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gq::SMEM);
+    static std::atomic<uint64_t> attr_done{0};   // per instantiation, one bit per device
+    {
+        const cudaError_t e = smem_attr_once(kern, (int)gq::SMEM, ctx->device, attr_done);
         if (e != cudaSuccess) return cuda_fail(e, "gemm_q smem attribute");
-        attr_set = true;
     }
     const int tiles = gp.tiles_m * gp.tiles_n;
     const int groups = tiles < ctx->num_sms / 2 ? tiles : ctx->num_sms / 2;

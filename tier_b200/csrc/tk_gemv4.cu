@@ -435,11 +435,10 @@ static tk_status go_sk(tk_ctx* ctx, const uint8_t* W, size_t rb, int N, int K, c
     GvPlan p;
     if (!gv_plan(rb, N, K, M, grid, p)) return fail(TK_ERR_UNSUPPORTED, "gemv stream: shape does not fit shared memory");
     auto kern = gemv_sk_kernel<T, M>;
-    static bool attr_set = false;   // per instantiation: one limit for every launch
-    if (!attr_set) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)GV_SMEM_MAX + 1024);
+    static std::atomic<uint64_t> attr_done{0};   // per instantiation, one bit per device
+    {
+        const cudaError_t e = smem_attr_once(kern, (int)GV_SMEM_MAX + 1024, ctx->device, attr_done);
         if (e != cudaSuccess) return cuda_fail(e, "gemv smem attribute");
-        attr_set = true;
     }
     GvArgs a;
     a.W = W; a.rb = rb; a.N = N; a.K = K; a.x = x; a.ldx = ldx; a.y = y; a.ldy = ldy;

@@ -571,11 +571,10 @@ static tk_status go_mma(tk_ctx* ctx, const uint8_t* W, size_t rb, int N, int K, 
     if (!gm_plan(T, N, K, M, grid, p)) return fail(TK_ERR_UNSUPPORTED, "gemv mma: shape does not fit shared memory");
     (void)rb;
     auto kern = gemv_mma_kernel<T>;
-    static bool attr_set = false;   // per instantiation
-    if (!attr_set) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)GM_SMEM_MAX + 1024);
+    static std::atomic<uint64_t> attr_done{0};   // per instantiation, one bit per device
+    {
+        const cudaError_t e = smem_attr_once(kern, (int)GM_SMEM_MAX + 1024, ctx->device, attr_done);
         if (e != cudaSuccess) return cuda_fail(e, "gemv mma smem attribute");
-        attr_set = true;
     }
     GmArgs a;
     a.W = W; a.rb = rb; a.N = N; a.K = K; a.M = M; a.x = x; a.ldx = ldx; a.y = y; a.ldy = ldy;

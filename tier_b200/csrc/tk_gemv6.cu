@@ -616,11 +616,10 @@ static tk_status go_imma(tk_ctx* ctx, const uint8_t* W, size_t rb, int N, int K,
     if (!gi_plan(T, N, K, rb, M, grid, p, seg == nullptr))
         return fail(TK_ERR_UNSUPPORTED, "gemv imma: shape does not fit shared memory");
     auto kern = gemv_imma_kernel<T>;
-    static bool attr_set = false;   // per instantiation
-    if (!attr_set) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)GI_SMEM_MAX + 1024);
+    static std::atomic<uint64_t> attr_done{0};   // per instantiation, one bit per device
+    {
+        const cudaError_t e = smem_attr_once(kern, (int)GI_SMEM_MAX + 1024, ctx->device, attr_done);
         if (e != cudaSuccess) return cuda_fail(e, "gemv imma smem attribute");
-        attr_set = true;
     }
     GiArgs a;
     a.W = W; a.rb = rb; a.N = N; a.K = K; a.M = M; a.x = x; a.ldx = ldx; a.y = y; a.ldy = ldy;

@@ -524,11 +524,10 @@ static tk_status go_wide(tk_ctx* ctx, const uint8_t* W, size_t rb, int N, int K,
     GwPlan p;
     if (!gw_plan(T, N, K, rb, M, grid, p)) return fail(TK_ERR_UNSUPPORTED, "gemv wide: shape does not fit shared memory");
     auto kern = gemv_wide_kernel<T, NH>;
-    static bool attr_set = false;   // per instantiation
-    if (!attr_set) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)GW_SMEM_MAX + 1024);
+    static std::atomic<uint64_t> attr_done{0};   // per instantiation, one bit per device
+    {
+        const cudaError_t e = smem_attr_once(kern, (int)GW_SMEM_MAX + 1024, ctx->device, attr_done);
         if (e != cudaSuccess) return cuda_fail(e, "gemv wide smem attribute");
-        attr_set = true;
     }
     GwArgs a;
     a.W = W; a.rb = rb; a.N = N; a.K = K; a.M = M; a.xr = xr; a.y = y; a.ldy = ldy;

@@ -322,12 +322,10 @@ bool gemv_dp_ok(int t, size_t rb, int N, int K, int M, int num_sms) {
 
 template <int JS>
 static tk_status go_dp(tk_ctx* ctx, const GdArgs& a, const GdPlan& p, int grid, cudaStream_t s) {
-    static bool attr_set = false;   // per instantiation
-    if (!attr_set) {
-        cudaError_t e = cudaFuncSetAttribute(gemv_dp_kernel<JS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             (int)GD_SMEM_MAX);
+    static std::atomic<uint64_t> attr_done{0};   // per instantiation, one bit per device
+    {
+        const cudaError_t e = smem_attr_once(gemv_dp_kernel<JS>, (int)GD_SMEM_MAX, ctx->device, attr_done);
         if (e != cudaSuccess) return cuda_fail(e, "gemv dp4a smem attribute");
-        attr_set = true;
     }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid, 1, 1);

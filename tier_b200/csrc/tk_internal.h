@@ -1,5 +1,6 @@
 // tk_internal.h -- host-side declarations shared by the tierk .cu files.
 #pragma once
+#include <atomic>
 #include <cstddef>
 #include <cstdint>
 #include <string>
@@ -51,6 +52,19 @@ namespace tk {
 #define TK_SEG_KB 16
 #endif
 constexpr int kSegKb = TK_SEG_KB;
+
+// The dynamic shared-memory limit set by cudaFuncSetAttribute holds for the
+// device current at the call only: record it per device (bit `device` of
+// `done`, one mask per kernel instantiation), so that contexts on several
+// devices of one process each get it before their first launch.
+template <class K>
+inline cudaError_t smem_attr_once(K* kern, int bytes, int device, std::atomic<uint64_t>& done) {
+    const uint64_t bit = 1ull << (device & 63);
+    if (done.load(std::memory_order_relaxed) & bit) return cudaSuccess;
+    const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (e == cudaSuccess) done.fetch_or(bit);
+    return e;
+}
 
 // Kernel families for tk_profile_read (TK_PROF_* in tierk.h).
 enum ProfKind { PK_GEMM = 0, PK_DEQUANT = 1, PK_SPLIT = 2, PK_GEMV = 3, PK_LMHEAD = 4, PK_COUNT = 5 };
