@@ -494,9 +494,10 @@ def run_ours(args):
             # dY's column shards become token-row shards over NVLink on a side
             # stream while the forward GEMM runs; then the local dX GEMM
             side.wait_stream(torch.cuda.current_stream(dev))
-            ctx.reshard_cols(dYin, dYrows, stream=side)
+            ctx.reshard_cols_send(dYin, stream=side)
             ctx.linear(w, Xin, M_TOK, Y if Yo is None else Yo, x_dtype=tk.DT_BF16)
             torch.cuda.current_stream(dev).wait_stream(side)
+            ctx.reshard_cols_recv(dYrows)
             ctx.linear_dx(w_full, dYrows, M_TOK // world, dXr if dXo is None else dXo, dy_dtype=tk.DT_BF16)
             return
         ctx.linear(w, Xin, M_TOK, Y if Yo is None else Yo, x_dtype=tk.DT_BF16)

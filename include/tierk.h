@@ -310,6 +310,14 @@ tk_status tk_allgather(tk_ctx *ctx, const void *src, size_t bytes, void *dst, vo
  * rank) instead of the fp32 partial sums of dX (M*K*4*(world-1)/world). */
 tk_status tk_reshard_cols(tk_ctx *ctx, const void *src, int M, int n, size_t ld_src, int elem_bytes,
                           void *dst, size_t ld_dst, void *stream);
+/* The same in two halves, so that the transfer overlaps other work: _send
+ * pushes this rank's blocks to their owners (stream-ordered after src is
+ * ready; it can run beside a GEMM on another stream), _recv (later, any
+ * stream ordered after _send) waits for every rank's blocks and assembles
+ * dst.  One exchange is open per context at a time. */
+tk_status tk_reshard_cols_send(tk_ctx *ctx, const void *src, int M, int n, size_t ld_src, int elem_bytes,
+                               void *stream);
+tk_status tk_reshard_cols_recv(tk_ctx *ctx, void *dst, size_t ld_dst, int elem_bytes, void *stream);
 /* buf[i] = sum over ranks of buf[i] (n % 4 == 0), added in rank order so that
  * every rank holds the same bits: the LM head's dX over vocabulary shards. */
 tk_status tk_allreduce_f32(tk_ctx *ctx, float *buf, size_t n, void *stream);

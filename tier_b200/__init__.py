@@ -135,6 +135,8 @@ SIGNATURES = [
     ("tk_allgather", _I, [_P, _P, _SZ, _P, _P]),
     ("tk_allreduce_f32", _I, [_P, _P, _SZ, _P]),
     ("tk_reshard_cols", _I, [_P, _P, _I, _I, _SZ, _I, _P, _SZ, _P]),
+    ("tk_reshard_cols_send", _I, [_P, _P, _I, _I, _SZ, _I, _P]),
+    ("tk_reshard_cols_recv", _I, [_P, _P, _SZ, _I, _P]),
     ("tk_lmhead_merge", _I, [_P, _I, _P, _P, _P, _P, _P, _I, _P]),
     ("tk_lmhead_stats", _I, [_P, _P, _I, _I, _I, _P, _I, _P, _P, _F, _I, _I, _P, _P, _P, _P, _P]),
     ("tk_lmhead_grad", _I, [_P, _P, _I, _I, _I, _P, _I, _P, _P, _I, _F, _I, _I, _P, _P, _P, _P]),
@@ -326,6 +328,15 @@ class Context:
         M, n = src.shape
         _check(self.lib.tk_reshard_cols(self.h, _ptr(src), M, n, src.stride(0), src.element_size(), _ptr(dst),
                                         dst.stride(0), _stream(stream)))
+        return dst
+
+    def reshard_cols_send(self, src, stream=None):
+        M, n = src.shape
+        _check(self.lib.tk_reshard_cols_send(self.h, _ptr(src), M, n, src.stride(0), src.element_size(),
+                                             _stream(stream)))
+
+    def reshard_cols_recv(self, dst, stream=None):
+        _check(self.lib.tk_reshard_cols_recv(self.h, _ptr(dst), dst.stride(0), dst.element_size(), _stream(stream)))
         return dst
 
     def allreduce_f32(self, buf, stream=None):

@@ -23,6 +23,8 @@
 #include "tk_internal.h"
 
 #include <cstring>
+#include <utility>
+#include <vector>
 
 struct tk_comm_state {
     int rank = 0, world = 0;
@@ -298,13 +300,33 @@ __global__ void lm_merge_kernel(const __grid_constant__ CmConsume c, const uint8
 // Column shards to row shards: rank g holds A[M, n] (its columns g*n ..
 // (g+1)*n of a [M, world*n] matrix, row stride ld_src bytes) and sends rows
 // h*M/world .. of it to rank h, packed (row_bytes = n * element bytes).
+// Column shards to row shards: rank g holds A[M, n] (its columns g*n ..
+// (g+1)*n of a [M, world*n] matrix, row stride ld_src bytes) and sends rows
+// h*M/world .. of it to rank h, packed (row_bytes = n * element bytes).  Four
+// 16-byte loads are in flight per thread before their stores.
 __global__ void cm_push_rows_kernel(const __grid_constant__ CmPush a, const uint8_t* __restrict__ src, size_t ld_src,
                                     int rows_per, size_t row_bytes) {
     const size_t nv = row_bytes / 16, total = (size_t)rows_per * a.world * nv;
-    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
-        const size_t rg = i / nv, v = i - rg * nv;
-        const int h = (int)(rg / rows_per), r = (int)(rg - (size_t)h * rows_per);
-        a.dst[h][(size_t)r * nv + v] = *reinterpret_cast<const uint4*>(src + rg * ld_src + v * 16);
+    const size_t stride = (size_t)gridDim.x * blockDim.x;
+    for (size_t i0 = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i0 < total; i0 += 4 * stride) {
+        uint4 v[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const size_t i = i0 + u * stride;
+            if (i < total) {
+                const size_t rg = i / nv, c = i - rg * nv;
+                v[u] = *reinterpret_cast<const uint4*>(src + rg * ld_src + c * 16);
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const size_t i = i0 + u * stride;
+            if (i < total) {
+                const size_t rg = i / nv, c = i - rg * nv;
+                const int h = (int)(rg / rows_per), r = (int)(rg - (size_t)h * rows_per);
+                a.dst[h][(size_t)r * nv + c] = v[u];
+            }
+        }
     }
     __threadfence_system();
     __syncthreads();
@@ -324,14 +346,25 @@ __global__ void cm_rows_kernel(const __grid_constant__ CmConsume c, const uint8_
     const bool ok = cm_wait_all(c);
     const size_t nv = row_bytes / 16, slot = (size_t)rows_per * row_bytes;
     const size_t total = (size_t)c.world * rows_per * nv;
+    const size_t stride = (size_t)gridDim.x * blockDim.x;
     if (ok)
-        for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
-            const size_t gr = i / nv, v = i - gr * nv;
-            const int g = (int)(gr / rows_per), r = (int)(gr - (size_t)g * rows_per);
-            *reinterpret_cast<uint4*>(dst + (size_t)r * ld_dst + g * row_bytes + v * 16) =
-                *reinterpret_cast<const uint4*>(recv + g * slot + (size_t)r * row_bytes + v * 16);
+        for (size_t i0 = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i0 < total; i0 += 4 * stride) {
+            uint4 v[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+                if (i0 + u * stride < total) v[u] = reinterpret_cast<const uint4*>(recv)[i0 + u * stride];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const size_t i = i0 + u * stride;
+                if (i < total) {
+                    const size_t gr = i / nv, cc = i - gr * nv;
+                    const int g = (int)(gr / rows_per), r = (int)(gr - (size_t)g * rows_per);
+                    *reinterpret_cast<uint4*>(dst + (size_t)r * ld_dst + g * row_bytes + cc * 16) = v[u];
+                }
+            }
         }
     cm_ack(c, ok);
+    (void)slot;
 }
 
 // Start an exchange of `slot` bytes per rank: capacity check, epoch, wait for
@@ -469,31 +502,66 @@ tk_status tk_allgather(tk_ctx* ctx, const void* src, size_t bytes, void* dst, vo
     return cuda_fail(cudaGetLastError(), "tk_allgather launch");
 }
 
-tk_status tk_reshard_cols(tk_ctx* ctx, const void* src, int M, int n, size_t ld_src, int elem_bytes, void* dst,
-                          size_t ld_dst, void* stream) {
-    if (!ctx || !src || !dst) return fail(TK_ERR_INVALID, "tk_reshard_cols: null argument");
-    tk_comm_state* cs = ctx->comm;
-    if (!cs || !cs->connected) return fail(TK_ERR_INVALID, "tk_reshard_cols: tk_comm_init / tk_comm_connect first");
-    if (M <= 0 || n <= 0 || elem_bytes <= 0 || M % cs->world)
-        return fail(TK_ERR_INVALID, "tk_reshard_cols: M must be a positive multiple of world");
-    const size_t row_bytes = (size_t)n * elem_bytes;
-    if (row_bytes % 16 || (ld_src * elem_bytes) % 16 || (ld_dst * elem_bytes) % 16 ||
-        (reinterpret_cast<uintptr_t>(dst) & 15) || ld_src < (size_t)n || ld_dst < (size_t)n * cs->world)
-        return fail(TK_ERR_INVALID, "tk_reshard_cols: rows of whole 16-byte units and 16-byte aligned pointers");
-    cudaStream_t s = static_cast<cudaStream_t>(stream);
-    const int rows_per = M / cs->world;
+// The send half records its exchange here for the receive half.
+struct ReshardPending {
+    bool open = false;
     CmConsume c;
     const uint8_t* recv = nullptr;
-    tk_status st = cm_start(ctx, nullptr, (size_t)rows_per * row_bytes, c, &recv, s, static_cast<const uint8_t*>(src),
-                            ld_src * elem_bytes, rows_per, row_bytes);
+    int rows_per = 0;
+    size_t row_bytes = 0;
+};
+static ReshardPending& reshard_pending(tk_ctx* ctx) {
+    static thread_local std::vector<std::pair<tk_ctx*, ReshardPending>> table;
+    for (auto& e : table)
+        if (e.first == ctx) return e.second;
+    table.emplace_back(ctx, ReshardPending());
+    return table.back().second;
+}
+
+tk_status tk_reshard_cols_send(tk_ctx* ctx, const void* src, int M, int n, size_t ld_src, int elem_bytes,
+                               void* stream) {
+    if (!ctx || !src) return fail(TK_ERR_INVALID, "tk_reshard_cols_send: null argument");
+    tk_comm_state* cs = ctx->comm;
+    if (!cs || !cs->connected) return fail(TK_ERR_INVALID, "tk_reshard_cols_send: tk_comm_init / tk_comm_connect first");
+    if (M <= 0 || n <= 0 || elem_bytes <= 0 || M % cs->world)
+        return fail(TK_ERR_INVALID, "tk_reshard_cols_send: M must be a positive multiple of world");
+    const size_t row_bytes = (size_t)n * elem_bytes;
+    if (row_bytes % 16 || (ld_src * elem_bytes) % 16 || ld_src < (size_t)n)
+        return fail(TK_ERR_INVALID, "tk_reshard_cols_send: rows of whole 16-byte units and a 16-byte aligned source");
+    ReshardPending& pe = reshard_pending(ctx);
+    if (pe.open) return fail(TK_ERR_INVALID, "tk_reshard_cols_send: the previous exchange was not received");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const int rows_per = M / cs->world;
+    tk_status st = cm_start(ctx, nullptr, (size_t)rows_per * row_bytes, pe.c, &pe.recv, s,
+                            static_cast<const uint8_t*>(src), ld_src * elem_bytes, rows_per, row_bytes);
     if (st != TK_OK) return st;
-    const size_t nv = (size_t)cs->world * rows_per * (row_bytes / 16);
-    int blocks = cm_blocks(ctx, nv);
-    if (blocks > ctx->num_sms / 4) blocks = ctx->num_sms / 4 > 0 ? ctx->num_sms / 4 : 1;   // leaves SMs to a GEMM
-    cm_rows_kernel<<<blocks, 256, 0, s>>>(c, recv, rows_per, row_bytes, static_cast<uint8_t*>(dst),
-                                         ld_dst * elem_bytes);
+    pe.open = true;
+    pe.rows_per = rows_per;
+    pe.row_bytes = row_bytes;
+    return TK_OK;
+}
+
+tk_status tk_reshard_cols_recv(tk_ctx* ctx, void* dst, size_t ld_dst, int elem_bytes, void* stream) {
+    if (!ctx || !dst || elem_bytes <= 0) return fail(TK_ERR_INVALID, "tk_reshard_cols_recv: null argument");
+    ReshardPending& pe = reshard_pending(ctx);
+    if (!pe.open) return fail(TK_ERR_INVALID, "tk_reshard_cols_recv: no exchange sent (tk_reshard_cols_send first)");
+    if ((ld_dst * elem_bytes) % 16 || (reinterpret_cast<uintptr_t>(dst) & 15) ||
+        ld_dst * elem_bytes < pe.row_bytes * ctx->comm->world)
+        return fail(TK_ERR_INVALID, "tk_reshard_cols_recv: 16-byte aligned rows of at least world * n elements");
+    pe.open = false;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const size_t nv = (size_t)pe.c.world * pe.rows_per * (pe.row_bytes / 16);
+    cm_rows_kernel<<<cm_blocks(ctx, (nv + 3) / 4), 256, 0, s>>>(pe.c, pe.recv, pe.rows_per, pe.row_bytes,
+                                                                 static_cast<uint8_t*>(dst), ld_dst * elem_bytes);
     ctx->launches++;
-    return cuda_fail(cudaGetLastError(), "tk_reshard_cols launch");
+    return cuda_fail(cudaGetLastError(), "tk_reshard_cols_recv launch");
+}
+
+tk_status tk_reshard_cols(tk_ctx* ctx, const void* src, int M, int n, size_t ld_src, int elem_bytes, void* dst,
+                          size_t ld_dst, void* stream) {
+    tk_status st = tk_reshard_cols_send(ctx, src, M, n, ld_src, elem_bytes, stream);
+    if (st != TK_OK) return st;
+    return tk_reshard_cols_recv(ctx, dst, ld_dst, elem_bytes, stream);
 }
 
 tk_status tk_allreduce_f32(tk_ctx* ctx, float* buf, size_t n, void* stream) {

@@ -136,20 +136,41 @@ __global__ void __launch_bounds__(DQ_THREADS) dequant_kernel(const uint8_t* __re
 // ---------------------------------------------------------------------------
 // Sub-block kernel for Q4_K / Q5_K / Q8_0 -> fp16 (the tensor-core path's
 // format): one thread per 32-element sub-block (decoder sub32_to_f16 in
-// tk_device.cuh), 64 B of output per thread as four 16-byte stores.
-// Threads run flat over (row, sub-block): one 32-bit division per 32 weights.
+// tk_device.cuh), 64 B of output per thread.  A warp's 32 consecutive
+// sub-blocks are 2 KB of consecutive output: they are staged in shared memory
+// and written as four fully coalesced 512-byte stores instead of each lane
+// writing its own 64 bytes (16 bytes per lane per instruction, 64 bytes
+// apart).  Threads run flat over (row, sub-block): one 32-bit division per 32
+// weights.
 template <int T>
 __global__ void __launch_bounds__(256) dequant_sub_f16_kernel(const uint8_t* __restrict__ W, size_t rb, int r0,
                                                               int nrows, int cols, uint16_t* __restrict__ out) {
+    __shared__ uint4 stage[8][32 * 4];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const unsigned spr = (unsigned)cols >> 5;       // sub-blocks per row
     const unsigned total = (unsigned)nrows * spr;
-    for (unsigned g = blockIdx.x * blockDim.x + threadIdx.x; g < total; g += gridDim.x * blockDim.x) {
-        const unsigned r = g / spr, sb = g - r * spr;
-        uint32_t h[16];
-        sub32_to_f16<T>(W + (size_t)(r0 + r) * rb, (int)sb, h);
-        uint4* o = reinterpret_cast<uint4*>(out + (size_t)r * cols + (size_t)sb * 32);
+    const unsigned stride = gridDim.x * blockDim.x;
+    for (unsigned base = blockIdx.x * blockDim.x + warp * 32; base < total; base += stride) {
+        const unsigned g = base + lane;
+        if (g < total) {
+            const unsigned r = g / spr, sb = g - r * spr;
+            uint32_t h[16];
+            sub32_to_f16<T>(W + (size_t)(r0 + r) * rb, (int)sb, h);
 #pragma unroll
-        for (int c = 0; c < 4; ++c) o[c] = make_uint4(h[4 * c], h[4 * c + 1], h[4 * c + 2], h[4 * c + 3]);
+            for (int c = 0; c < 4; ++c) {
+                const int q = (c + lane) & 3;        // spreads the lanes of one instruction over the banks
+                stage[warp][lane * 4 + q] = make_uint4(h[4 * q], h[4 * q + 1], h[4 * q + 2], h[4 * q + 3]);
+            }
+        }
+        __syncwarp();
+        // output of sub-blocks base .. base+31 is contiguous (row stride = cols)
+        uint4* o = reinterpret_cast<uint4*>(out + (size_t)base * 32);
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            const int idx = c * 32 + lane;           // 16-byte unit of the warp's 2 KB
+            if (base + (unsigned)(idx >> 2) < total) o[idx] = stage[warp][idx];
+        }
+        __syncwarp();
     }
 }
 
