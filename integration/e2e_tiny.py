@@ -65,6 +65,27 @@ def prepare(ref: Path) -> None:
     print(TINY)
 
 
+PROJ = ("q_proj", "k_proj", "v_proj", "o_proj", "gate_proj", "up_proj", "down_proj")
+NORMS = ("input_layernorm", "post_attn_ln", "pre_ffn_ln", "post_ffn_ln", "q_norm", "k_norm")
+
+
+def write_tier_file(path: Path) -> None:
+    """The engine's slice layout (the format load_tier_assignment reads,
+    tier/tier.cpp:1411-1433: "name tier n ntr" per slot): every layer
+    projection at tier 2, frozen, so the engine stores it as fp16 and runs
+    it through the x3 linear path the bridge routes; the norms at tier 1,
+    trainable, so the step still updates weights. Without this file the
+    engine's device budget covers the whole tiny model and every projection
+    is a trainable fp32 matrix, which the bridge leaves to the engine.
+    Names the architecture lacks are skipped by the loader."""
+    lines = ["# slot tier n ntr"]
+    for l in range(LAYERS):
+        lines += [f"layer_{l}.{s} 2 0 0" for s in PROJ]
+        lines += [f"layer_{l}.{s} 1 0 0" for s in NORMS]
+    lines.append("layer_-1.final_norm 1 0 0")
+    path.write_text("\n".join(lines) + "\n")
+
+
 def step_loss(engine: Path, work: Path, timeout: int = 600) -> tuple[float, dict]:
     """One training step on the tiny model: the loss from the step log and,
     for the hooked engine, the bridge's count of calls routed to libtierk."""
@@ -73,6 +94,7 @@ def step_loss(engine: Path, work: Path, timeout: int = 600) -> tuple[float, dict
     for f in (log, work / "adam.bin", work / "tier1.bin"):
         if f.exists():
             f.unlink()
+    write_tier_file(work / "tier_assignment.txt")
     env = dict(os.environ, TIER_NO_SELFCHECK="1", TIERK_BRIDGE_STATS="1")
     cmd = [str(engine), str(TINY / "model.safetensors"), str(TINY / "tokens.bin"), str(SEQ), str(work / "adam.bin"),
            str(work / "tier1.bin"), "1e-5", str(LAYERS), "1", "--bf3", "--log", str(log)]
