@@ -489,6 +489,8 @@ def run_ours(args):
             dx_mode = "rs-nccl"
         dist.barrier(group=group)
 
+    pair = args.step_call == "pair"
+
     def step(Xin, dYin, Yo=None, dXo=None):
         if dx_mode == "reshard":
             # dY's column shards become token-row shards over NVLink on a side
@@ -499,6 +501,19 @@ def run_ours(args):
             torch.cuda.current_stream(dev).wait_stream(side)
             ctx.reshard_cols_recv(dYrows)
             ctx.linear_dx(w_full, dYrows, M_TOK // world, dXr if dXo is None else dXo, dy_dtype=tk.DT_BF16)
+            return
+        if pair and dx_mode in ("local", "fused"):
+            # forward and dX GEMMs in one launch (tiles interleaved); W
+            # expanded once; at N > 1 the dX tiles go to their owners over NVLink
+            if world == 1:
+                ctx.linear_fwd_dx(w, Xin, M_TOK, Y if Yo is None else Yo, dYin, M_TOK, dX if dXo is None else dXo,
+                                  x_dtype=tk.DT_BF16)
+                return
+            ctx.linear_fwd_dx_rs(w, Xin, M_TOK, Y if Yo is None else Yo, dYin, M_TOK, dXr if dXo is None else dXo,
+                                 x_dtype=tk.DT_BF16)
+            if args.gather_y:
+                import torch.distributed as dist
+                dist.all_gather_into_tensor(Yfull, Y if Yo is None else Yo, group=group)
             return
         ctx.linear(w, Xin, M_TOK, Y if Yo is None else Yo, x_dtype=tk.DT_BF16)
         # the dX GEMM reuses the forward's fp16 expansion of W (same frozen
@@ -611,6 +626,8 @@ def run_ours(args):
             lambda: ctx.linear_dx_rs(w, dYd, M_TOK, dXr, dy_dtype=tk.DT_BF16, products=tk.WREUSE))
         phases["dx_local_no_exchange"] = phase_ms(
             lambda: ctx.linear_dx(w, dYd, M_TOK, dX, dy_dtype=tk.DT_BF16, products=tk.WREUSE))
+    if pair and dx_mode in ("local", "fused"):
+        phases["fwd_dx_one_launch"] = phase_ms(lambda: step(Xd, dYd))
 
     # ---- end to end through the C ABI with host buffers ----
     Xh = Xb.pin_memory()
@@ -716,7 +733,11 @@ def run_ours(args):
             "data": "synthetic (seeded, tests/gen.py)",
             "config": {"workload": "C2 Q4_K 14336x4096, M=4096 tokens, fwd + dX per step",
                        "x_dtype": "bf16",
-                       "dequant": "W expanded to fp16 once per step by the forward; the dX GEMM reuses it (TK_WREUSE)",
+                       "dequant": ("W expanded to fp16 once per step; forward and dX GEMMs in one launch, their "
+                                   "tiles interleaved (tk_linear_fwd_dx" + ("_rs)" if world > 1 else ")")
+                                   if pair and dx_mode in ("local", "fused") else
+                                   "W expanded to fp16 once per step by the forward; the dX GEMM reuses it "
+                                   "(TK_WREUSE)"),
                        "partition": (f"W rows split over {world} GPUs; Y " + ("all-gathered" if args.gather_y else
                                      "kept row-sharded (column-parallel: consumed where produced)") +
                                      {"fused": "; dX reduce-scattered by token rows inside the dX GEMM "
@@ -1238,6 +1259,9 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--gather-y", action="store_true", help="multi-GPU: all-gather the full Y every step")
     ap.add_argument("--dx-chunks", type=int, default=4, help="multi-GPU allreduce mode: dX GEMM / all-reduce chunks")
+    ap.add_argument("--step-call", default="pair", choices=["pair", "separate"],
+                    help="pair: forward and dX in one call and one GEMM launch (tk_linear_fwd_dx[_rs]); "
+                         "separate: tk_linear_fwd then tk_linear_dx[_rs]")
     ap.add_argument("--dx-mode", default="fused", choices=["fused", "rs-nccl", "allreduce", "reshard"],
                     help="multi-GPU dX: reduce-scatter by token rows inside the GEMM over NVLink (fused), "
                          "GEMM then NCCL reduce-scatter (rs-nccl), chunked NCCL all-reduce of the full dX "

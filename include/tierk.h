@@ -235,6 +235,20 @@ tk_status tk_linear_fwd(tk_ctx *ctx, const tk_weight *W, const void *X, int x_dt
 tk_status tk_linear_dx(tk_ctx *ctx, const tk_weight *W, const void *dY, int dy_dtype, int M,
                        int lddy, float *dX, int lddx, float beta, int products, void *stream);
 
+/* Y[Mx, N] = X . W^T and dX[Md, K] = dY . W (beta = 0) for one weight in
+ * one call: the training step's forward and input gradient, as
+ * tk_linear_fwd followed by tk_linear_dx.  W is expanded once, and both
+ * GEMMs run in one persistent tensor-core launch whose tiles interleave, so
+ * that neither GEMM's last wave of tiles leaves SMs idle.  This call never
+ * splits K: Y and dX equal tk_linear_fwd's and tk_linear_dx's bit for bit
+ * wherever those run one K split (always for a reduction length below 2048)
+ * and are within the product set's tolerance elsewhere.  With Mx or Md <= 128, or TK_QFUSED, the two operations run
+ * one after the other.  No counterpart in the reference, whose training step
+ * calls linear and linear_dx at different points (tier/tier.cpp:1186-1238). */
+tk_status tk_linear_fwd_dx(tk_ctx *ctx, const tk_weight *W, const void *X, int x_dtype, int Mx, int ldx,
+                           float *Y, int ldy, const void *dY, int dy_dtype, int Md, int lddy, float *dX,
+                           int lddx, int products, void *stream);
+
 /* tk_linear_fwd for callers that cannot allocate device memory -- an engine
  * that budgets all VRAM through its own arena, or code that must not call
  * cudaMalloc once running.  No counterpart in the reference.  Same arguments
@@ -289,6 +303,14 @@ tk_status tk_comm_connect(tk_ctx *ctx, const void *handles);
  * TK_ERR_TIMEOUT through tk_sync_status if a rank does not take part. */
 tk_status tk_linear_dx_rs(tk_ctx *ctx, const tk_weight *W, const void *dY, int dy_dtype, int M, int lddy,
                           float *dX_rows, int ldd, int products, void *stream);
+/* tk_linear_fwd_dx with the dX half reduce-scattered as tk_linear_dx_rs:
+ * Y[Mx, W->rows] = X . W^T (this rank's columns) and dX_rows[Md/world, ldd]
+ * = this rank's token rows of sum over ranks of dY . W, in one launch whose
+ * forward tiles compute while the dX tiles' stores cross NVLink.  Same
+ * results as tk_linear_fwd then tk_linear_dx_rs, bit for bit. */
+tk_status tk_linear_fwd_dx_rs(tk_ctx *ctx, const tk_weight *W, const void *X, int x_dtype, int Mx, int ldx,
+                              float *Y, int ldy, const void *dY, int dy_dtype, int Md, int lddy,
+                              float *dX_rows, int ldd, int products, void *stream);
 
 /* Collectives of the sharded path on the same peer buffers (stores over
  * NVLink, no NCCL), so that a C or C++ caller -- the reference's engine is

@@ -61,6 +61,10 @@ def test_null_context_is_rejected_not_crashed(lib):
     assert lib.tk_allgather(None, None, 16, None, None) == 1
     assert lib.tk_allreduce_f32(None, None, 4, None) == 1
     assert lib.tk_lmhead_merge(None, 4, None, None, None, None, None, 0, None) == 1
+    # forward + dX in one launch, plain and reduce-scattered
+    for fn in (lib.tk_linear_fwd_dx, lib.tk_linear_fwd_dx_rs):
+        assert fn(None, None, None, 0, 256, 64, None, 64, None, 0, 256, 64, None, 64, 0, None) == 1
+        assert b"null context" in lib.tk_last_error_string()
 
 
 def test_qtype_values_and_names_match_header(lib):

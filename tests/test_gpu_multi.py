@@ -106,6 +106,24 @@ def _worker(rank, world, port, q):
             errs.append(float((part - want).norm() / want.norm()))
         ctx.sync_status()
         out["rs_dx"] = max(errs)
+        # forward and reduce-scattered dX in one launch: dX the same bits as
+        # tk_linear_dx_rs (neither splits K); Y within the x3 tolerance of
+        # tk_linear_fwd, which splits this shape's K = 2048 in two (measured
+        # 1.5e-6 apart; bf16 one product, fp32 x3 with several segments)
+        same, ydiff = [], []
+        for dt in (torch.bfloat16, torch.float32):
+            Xr = torch.from_numpy(rng.standard_normal((Mr, K)).astype(np.float32)).cuda().to(dt)
+            dYr = torch.from_numpy(rng.standard_normal((Mr, N)).astype(np.float32)).cuda().to(dt)
+            dYs = dYr[:, a:b].contiguous()
+            Yp, part = lp.fwd_dx_rs(Xr, dYs)
+            Y2 = lp.forward(Xr, gather=False)
+            part2 = lp.dx_rs(dYs)
+            torch.cuda.synchronize()
+            same.append(bool(torch.equal(part, part2)))
+            ydiff.append(float((Yp - Y2).norm() / Y2.norm()))
+        ctx.sync_status()
+        out["fwd_dx_rs_dx_same"] = all(same)
+        out["fwd_dx_rs_y"] = max(ydiff)
         # the same operations over the library's peer collectives (no NCCL on
         # the data path): all-gathered forward and decode, LM-head merge and
         # dX all-reduce; every rank holds the same bits
@@ -162,6 +180,7 @@ def test_two_gpu_shards_match_single_gpu():
         assert o["lin_fwd"] < 1e-6 and o["lin_dx"] < 1e-5, o
         assert o["decode"] < 1e-5, o
         assert o["rs_dx"] < 1e-5, o
+        assert o["fwd_dx_rs_dx_same"] and o["fwd_dx_rs_y"] < 1e-5, o
         for pre in ("", "p_"):
             assert o[pre + "lm_loss"] < 1e-6 and o[pre + "lm_dx"] < 1e-5 and o[pre + "lm_amax"], (pre, o)
             assert o[pre + "lmf_loss"] < 1e-6 and o[pre + "lmf_dx"] < 1e-5 and o[pre + "lmf_amax"], (pre, o)

@@ -132,6 +132,9 @@ SIGNATURES = [
     ("tk_comm_init", _I, [_P, _I, _I, _SZ, _P]),
     ("tk_comm_connect", _I, [_P, _P]),
     ("tk_linear_dx_rs", _I, [_P, ctypes.POINTER(Weight), _P, _I, _I, _I, _P, _I, _I, _P]),
+    ("tk_linear_fwd_dx", _I, [_P, ctypes.POINTER(Weight), _P, _I, _I, _I, _P, _I, _P, _I, _I, _I, _P, _I, _I, _P]),
+    ("tk_linear_fwd_dx_rs", _I, [_P, ctypes.POINTER(Weight), _P, _I, _I, _I, _P, _I, _P, _I, _I, _I, _P, _I, _I,
+                                 _P]),
     ("tk_allgather", _I, [_P, _P, _SZ, _P, _P]),
     ("tk_allreduce_f32", _I, [_P, _P, _SZ, _P]),
     ("tk_reshard_cols", _I, [_P, _P, _I, _I, _SZ, _I, _P, _SZ, _P]),
@@ -291,6 +294,15 @@ class Context:
     def linear_dx_acc(self, W: Weight, dY, M, dX, **kw):
         return self.linear_dx(W, dY, M, dX, beta=1.0, **kw)
 
+    def linear_fwd_dx(self, W: Weight, X, Mx, Y, dY, Md, dX, x_dtype=DT_F32, dy_dtype=None, ldx=None, ldy=None,
+                      lddy=None, lddx=None, products=X3_AUTO, stream=None):
+        """Y = X . W^T and dX = dY . W in one launch (tk_linear_fwd_dx)."""
+        dy_dtype = x_dtype if dy_dtype is None else dy_dtype
+        _check(self.lib.tk_linear_fwd_dx(self.h, ctypes.byref(W), _ptr(X), x_dtype, Mx, ldx or W.cols, _ptr(Y),
+                                         ldy or W.rows, _ptr(dY), dy_dtype, Md, lddy or W.rows, _ptr(dX),
+                                         lddx or W.cols, products, _stream(stream)))
+        return Y, dX
+
     def quantize(self, qtype, x, rows, cols, out, x_dtype=DT_F32, ldx=None, row_bytes_=None, stream=None):
         """out (uint8 [rows, row_bytes]) = x quantized to qtype, byte-exact with the reference's q_row."""
         rb = row_bytes_ if row_bytes_ is not None else row_bytes(qtype, cols)
@@ -316,6 +328,16 @@ class Context:
         _check(self.lib.tk_linear_dx_rs(self.h, ctypes.byref(W), _ptr(dY), dy_dtype, M, lddy or W.rows, _ptr(dX_rows),
                                         ldd or W.cols, products, _stream(stream)))
         return dX_rows
+
+    def linear_fwd_dx_rs(self, W: Weight, X, Mx, Y, dY, Md, dX_rows, x_dtype=DT_F32, dy_dtype=None, ldx=None,
+                         ldy=None, lddy=None, ldd=None, products=X3_AUTO, stream=None):
+        """Y = X . W^T (this rank's columns) and this rank's token rows of the
+        summed dY . W, in one launch (tk_linear_fwd_dx_rs)."""
+        dy_dtype = x_dtype if dy_dtype is None else dy_dtype
+        _check(self.lib.tk_linear_fwd_dx_rs(self.h, ctypes.byref(W), _ptr(X), x_dtype, Mx, ldx or W.cols, _ptr(Y),
+                                            ldy or W.rows, _ptr(dY), dy_dtype, Md, lddy or W.rows, _ptr(dX_rows),
+                                            ldd or W.cols, products, _stream(stream)))
+        return Y, dX_rows
 
     def allgather(self, src, dst, nbytes=None, stream=None):
         """dst = every rank's src in rank order (tk_allgather)."""

@@ -287,6 +287,129 @@ static tk_status linear(tk_ctx* ctx, const tk_weight* W, const void* A, int a_dt
     return rs_finish(ctx, rs, d_cols, out, ldo, s);
 }
 
+// Forward and input gradient of one weight in one GEMM launch
+// (tk_linear_fwd_dx, tk_linear_fwd_dx_rs): W is expanded once, both
+// activations are split, and the two GEMMs share one persistent launch whose
+// tiles interleave (launch_gemm_pair), so the dX epilogue's stores (over
+// NVLink for the reduce-scatter) overlap the forward's MMAs and neither
+// GEMM's last wave leaves SMs idle.
+static tk_status linear_pair(tk_ctx* ctx, const tk_weight* W, const void* X, int x_dtype, int Mx, int ldx, float* Y,
+                             int ldy, const void* dY, int dy_dtype, int Md, int lddy, float* dX, int ld_dx,
+                             int products, cudaStream_t s, bool rs_scatter) {
+    const char* fn = rs_scatter ? "tk_linear_fwd_dx_rs" : "tk_linear_fwd_dx";
+    if (!ctx) return fail(TK_ERR_INVALID, std::string(fn) + ": null context");
+    if (rs_scatter && !ctx->comm) return fail(TK_ERR_INVALID, std::string(fn) + ": tk_comm_init / tk_comm_connect first");
+    tk_status st = check_weight(W, fn);
+    if (st != TK_OK) return st;
+    if (Mx < 0 || Md < 0) return fail(TK_ERR_INVALID, std::string(fn) + ": negative M");
+    const bool want_fused = (products & TK_QFUSED) != 0;
+    const bool want_reuse = (products & TK_WREUSE) != 0;
+    const int prod = products & ~(TK_QFUSED | TK_WREUSE);
+    if (Mx <= 128 || Md <= 128 || want_fused) {
+        // a side too small for CTA-pair tiles, or the weight decoded inside
+        // the GEMM: the two operations one after the other
+        st = linear(ctx, W, X, x_dtype, Mx, ldx, Y, ldy, 0.0f, products, s, false);
+        if (st != TK_OK) return st;
+        return linear(ctx, W, dY, dy_dtype, Md, lddy, dX, ld_dx, 0.0f, products | TK_WREUSE, s, true, rs_scatter);
+    }
+    if (!X || !Y || !dY || !dX) return fail(TK_ERR_INVALID, std::string(fn) + ": null activation or output");
+    const int N = W->rows, K = W->cols;
+    if (ldx < K || ldy < N || lddy < N || ld_dx < K)
+        return fail(TK_ERR_INVALID, std::string(fn) + ": leading dimension too small");
+    for (int dt : {x_dtype, dy_dtype})
+        if (dt != TK_DT_F32 && dt != TK_DT_F16 && dt != TK_DT_BF16)
+            return fail(TK_ERR_INVALID, std::string(fn) + ": activation dtype");
+    if (!aligned16(Y) || ldy % 4 || !aligned16(dX) || ld_dx % 4)
+        return fail(TK_ERR_INVALID, std::string(fn) + ": outputs must be 16-byte aligned, ld % 4 == 0");
+    Plan px, pd;
+    st = plan_products(W, x_dtype, prod, px);
+    if (st != TK_OK) return st;
+    st = plan_products(W, dy_dtype, prod, pd);
+    if (st != TK_OK) return st;
+    const bool quant = W->qtype != TK_F16 && W->qtype != TK_F16X2;
+    const long ax_ld = (K + 7) / 8 * 8, ad_ld = (N + 7) / 8 * 8;   // split-plane row strides (TMA: 16 bytes)
+    const size_t ex = (size_t)Mx * ax_ld, ed = (size_t)Md * ad_ld;
+    const bool rs_scratch = rs_scatter && pd.nprod > 1;
+    const size_t need = (quant ? align256((size_t)N * K * 2) : 0) + align256(ex * 2 * px.x_planes) +
+                        align256((size_t)Mx * 4) + align256(ed * 2 * pd.x_planes) + align256((size_t)Md * 4) +
+                        (rs_scratch ? align256((size_t)Md * K * 4) : 0);
+    const bool reuse = quant && want_reuse && ctx->wexp_valid && ctx->wexp_data == W->data &&
+                       ctx->wexp_qtype == W->qtype && ctx->wexp_rows == N && ctx->wexp_cols == K &&
+                       ctx->wexp_rb == W->row_bytes;
+    const void* ws_before = ctx->ws;
+    st = ws_ensure(ctx, need, s);
+    if (st != TK_OK) return st;
+    Carve cv(ctx->ws);
+    uint16_t* wf = quant ? cv.take<uint16_t>((size_t)N * K) : nullptr;   // at the start of ws (TK_WREUSE)
+    uint16_t* xp = cv.take<uint16_t>(ex * px.x_planes);
+    int* xexp = cv.take<int>(Mx);
+    uint16_t* dp = cv.take<uint16_t>(ed * pd.x_planes);
+    int* dexp = cv.take<int>(Md);
+    const uint16_t* wplanes[2] = {nullptr, nullptr};
+    if (quant) {
+        if (!(reuse && ctx->ws == ws_before)) {
+            st = launch_dequant(ctx, W->qtype, W->data, W->row_bytes, 0, N, K, TK_DT_F16, wf, s);
+            if (st != TK_OK) return st;
+        }
+        ctx->wexp_valid = true;
+        ctx->wexp_data = W->data;
+        ctx->wexp_qtype = W->qtype;
+        ctx->wexp_rows = N;
+        ctx->wexp_cols = K;
+        ctx->wexp_rb = W->row_bytes;
+        wplanes[0] = wf;
+    } else {
+        wplanes[0] = static_cast<const uint16_t*>(W->data);
+        if (W->qtype == TK_F16X2) wplanes[1] = wplanes[0] + (size_t)N * K;
+    }
+    if ((px.w_two || pd.w_two) && !wplanes[1])
+        return fail(TK_ERR_INVALID, std::string(fn) + ": product set needs two weight planes");
+    st = launch_act_split(ctx, X, x_dtype, Mx, K, ldx, px.x_planes, true, xp, xexp, s, ax_ld);
+    if (st != TK_OK) return st;
+    st = launch_act_split(ctx, dY, dy_dtype, Md, N, lddy, pd.x_planes, true, dp, dexp, s, ad_ld);
+    if (st != TK_OK) return st;
+    auto desc = [&](const Plan& pl, const uint16_t* planes, size_t elems, long lda, int M, bool dx, float* D, long ldd,
+                    const int* rexp) {
+        GemmDesc g;
+        for (int i = 0; i < pl.x_planes; ++i) g.A[i] = planes + (size_t)i * elems;
+        g.B[0] = wplanes[0];
+        g.B[1] = wplanes[1];
+        g.lda = lda;
+        g.ldb = K;
+        g.b_mn = dx;
+        g.M = M;
+        g.N = dx ? K : N;
+        g.K = dx ? N : K;
+        g.nprod = pl.nprod;
+        for (int i = 0; i < 3; ++i) { g.pa[i] = pl.pa[i]; g.pb[i] = pl.pb[i]; }
+        g.D = D;
+        g.ldd = ldd;
+        g.row_exp = rexp;
+        g.col_exp = W->qtype == TK_F16X2 ? W->scale_log2 : 0;
+        g.seg_kb = pl.nprod > 1 ? kSegKb : 0;
+        return g;
+    };
+    const GemmDesc gx = desc(px, xp, ex, ax_ld, Mx, false, Y, ldy, xexp);
+    GemmDesc gd = desc(pd, dp, ed, ad_ld, Md, true, dX, ld_dx, dexp);
+    RsDesc rs;
+    if (rs_scatter) {
+        st = rs_begin(ctx, Md, K, rs, s);
+        if (st != TK_OK) return st;
+        // the GEMM writes [Md, K] rows of stride K: earlier segments to a local
+        // scratch, the last one to the owners (a single segment leaves D unread)
+        gd.D = rs_scratch ? cv.take<float>((size_t)Md * K) : dX;
+        gd.ldd = K;
+        gd.rs = &rs;
+    }
+    st = gemm_pair_ok(gx, gd) ? launch_gemm_pair(ctx, gx, gd, s) : launch_gemm(ctx, gx, s);
+    if (st != TK_OK) return st;
+    if (!gemm_pair_ok(gx, gd)) {
+        st = launch_gemm(ctx, gd, s);
+        if (st != TK_OK) return st;
+    }
+    return rs_scatter ? rs_finish(ctx, rs, K, dX, ld_dx, s) : TK_OK;
+}
+
 }  // namespace tk
 
 using namespace tk;
@@ -334,6 +457,7 @@ void tk_destroy(tk_ctx* ctx) {
     if (ctx->status) cudaFree(ctx->status);
     if (ctx->flags) cudaFree(ctx->flags);
     if (ctx->iq_tab) cudaFree(ctx->iq_tab);
+    if (ctx->sched) cudaFree(ctx->sched);
     comm_destroy(ctx);
     for (cudaEvent_t e : ctx->prof.ev) cudaEventDestroy(e);
     delete ctx;
@@ -513,6 +637,20 @@ tk_status tk_linear_fwd(tk_ctx* ctx, const tk_weight* W, const void* X, int x_dt
 tk_status tk_linear_dx(tk_ctx* ctx, const tk_weight* W, const void* dY, int dy_dtype, int M, int lddy, float* dX,
                        int lddx, float beta, int products, void* stream) {
     return linear(ctx, W, dY, dy_dtype, M, lddy, dX, lddx, beta, products, static_cast<cudaStream_t>(stream), true);
+}
+
+tk_status tk_linear_fwd_dx(tk_ctx* ctx, const tk_weight* W, const void* X, int x_dtype, int Mx, int ldx, float* Y,
+                           int ldy, const void* dY, int dy_dtype, int Md, int lddy, float* dX, int lddx, int products,
+                           void* stream) {
+    return linear_pair(ctx, W, X, x_dtype, Mx, ldx, Y, ldy, dY, dy_dtype, Md, lddy, dX, lddx, products,
+                       static_cast<cudaStream_t>(stream), false);
+}
+
+tk_status tk_linear_fwd_dx_rs(tk_ctx* ctx, const tk_weight* W, const void* X, int x_dtype, int Mx, int ldx, float* Y,
+                              int ldy, const void* dY, int dy_dtype, int Md, int lddy, float* dX_rows, int ldd,
+                              int products, void* stream) {
+    return linear_pair(ctx, W, X, x_dtype, Mx, ldx, Y, ldy, dY, dy_dtype, Md, lddy, dX_rows, ldd, products,
+                       static_cast<cudaStream_t>(stream), true);
 }
 
 tk_status tk_weight_split_f32(tk_ctx* ctx, const float* W32, int rows, int cols, uint16_t* planes, int* scale_log2,

@@ -31,11 +31,21 @@
 // Every path computes D = fl(P0 + P1), so the result does not depend on the
 // order.  No CTA ever waits for another, so the kernel cannot deadlock when
 // other kernels (e.g. NCCL) hold some SMs.
+// Two problems in one launch (gemm_pair_kernel): the persistent CTAs walk one
+// list of units.  While both problems' operands fit in L2 together, the
+// second problem's tiles are spread evenly among the first's, so that e.g. a
+// forward GEMM's MMAs and an input-gradient GEMM whose epilogue stores over
+// NVLink overlap; otherwise the second problem's tiles come first.  Either
+// way neither problem's last wave leaves SMs idle and there is one launch
+// gap less.  Each problem keeps its own operands, tile width, B layout,
+// products and epilogue target; neither splits K.
 // All waits are bounded (tk_device.cuh); a timeout records a status code and
 // the roles drain out instead of hanging.
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <mutex>
+#include <queue>
+#include <vector>
 #include "tk_device.cuh"
 #include "tk_internal.h"
 
@@ -89,7 +99,17 @@ struct __align__(64) GemmParams {
     int* rs_counter;                 // CTAs finished (local), reset by the last
     int rs_world, rs_rpo, rs_epoch;
     int col_exp;
+    int b_mn;              // B is N-major (read where the kernel picks the layout per problem)
+    // pair launches (first problem's copy): CTA pair c runs the units
+    // sched[sched_off[c] .. sched_off[c + 1]); unit u < tiles of problem 1 is
+    // that problem's tile u, the rest are problem 0's tiles u - tiles(1)
+    const int* sched;
+    const int* sched_off;
     int* status;
+};
+
+struct GemmPair {
+    GemmParams p[2];
 };
 
 struct EpiParams {
@@ -110,9 +130,53 @@ __device__ __forceinline__ int ld_acquire_gpu(const int* p) {
     return v;
 }
 
-template <int CG, bool B_MN, int EPI>
-__global__ void __launch_bounds__(GEMM_THREADS, 1)
-    gemm_tc_kernel(const __grid_constant__ GemmParams p, const __grid_constant__ EpiParams ep) {
+// A work unit: problem, output tile, K split.
+struct Unit {
+    int prob, tile, sp;
+};
+
+template <int NPROB>
+__device__ __forceinline__ int num_units_of(const GemmParams* ps) {
+    if constexpr (NPROB == 1) return ps[0].tiles_m * ps[0].tiles_n * ps[0].splits;
+    else return ps[0].tiles_m * ps[0].tiles_n + ps[1].tiles_m * ps[1].tiles_n;
+}
+
+template <int NPROB>
+__device__ __forceinline__ Unit unit_of(const GemmParams* ps, int u) {
+    Unit r;
+    if constexpr (NPROB == 1) {
+        const int nt = ps[0].tiles_m * ps[0].tiles_n;
+        r.prob = 0;
+        r.tile = u % nt;
+        r.sp = u / nt;
+    } else {
+        const int t1 = ps[1].tiles_m * ps[1].tiles_n;
+        r.sp = 0;
+        if (u < t1) { r.prob = 1; r.tile = u; }
+        else { r.prob = 0; r.tile = u - t1; }
+    }
+    return r;
+}
+
+// The units of CTA group `cid`: a stride over all units for one problem, the
+// host-built schedule for a pair.
+template <int NPROB>
+struct UnitRange {
+    int i, end, step;
+    const int* list;
+    __device__ __forceinline__ UnitRange(const GemmParams* ps, int cid, int ncl) {
+        if constexpr (NPROB == 1) {
+            i = cid; end = num_units_of<1>(ps); step = ncl; list = nullptr;
+        } else {
+            i = ps[0].sched_off[cid]; end = ps[0].sched_off[cid + 1]; step = 1; list = ps[0].sched;
+        }
+    }
+    __device__ __forceinline__ int unit(int j) const { return NPROB == 1 ? j : list[j]; }
+};
+
+// BMODE: 0 B K-major, 1 B N-major, 2 per problem (GemmParams::b_mn).
+template <int CG, int BMODE, int EPI, int NPROB>
+__device__ __forceinline__ void gemm_body(const GemmParams* ps, const EpiParams* ep) {
     using G = Geo<CG>;
     constexpr int STAGES = G::STAGES;
     extern __shared__ uint8_t smem_raw[];
@@ -129,6 +193,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t rank = CG == 2 ? cluster_ctarank() : 0;
     const int cid = blockIdx.x / CG, ncl = gridDim.x / CG;      // tile-group index / count
+    int* const status = ps[0].status;
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
             mbar_init(&full[s], 1);
@@ -142,8 +207,10 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         fence_async_shared();
     }
     if (warp == 0 && lane == 0) {
-        for (int i = 0; i < p.nprod; ++i) tma_prefetch_desc(&p.tmA[p.pa[i]]);
-        tma_prefetch_desc(&p.tmB[0]);
+        for (int j = 0; j < NPROB; ++j) {
+            for (int i = 0; i < ps[j].nprod; ++i) tma_prefetch_desc(&ps[j].tmA[ps[j].pa[i]]);
+            tma_prefetch_desc(&ps[j].tmB[0]);
+        }
     }
     if (warp == 1) {
         if constexpr (CG == 2) {
@@ -160,27 +227,27 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
 
-    const int num_tiles = p.tiles_m * p.tiles_n;
-    const int num_units = num_tiles * p.splits;
-    const int kblocks = (p.K + BK - 1) / BK;
-    const int kb_per_split = (kblocks + p.splits - 1) / p.splits;
-
     if (warp == 0) {
         // ---------------- TMA producer (each CTA loads its own operands) ----------------
         if (lane == 0) {
             int s = 0;
             uint32_t ph = 0;
             bool ok = true;
-            for (int u0 = cid; u0 < num_units && ok; u0 += ncl) {
-                const int tile = u0 % num_tiles, sp = u0 / num_tiles;
-                const int mb = tile % p.tiles_m, nb = tile / p.tiles_m;
+            const UnitRange<NPROB> ur(ps, cid, ncl);
+            for (int j = ur.i; j < ur.end && ok; j += ur.step) {
+                const Unit un = unit_of<NPROB>(ps, ur.unit(j));
+                const GemmParams& p = ps[un.prob];
+                const bool bmn = BMODE == 2 ? p.b_mn != 0 : BMODE == 1;
+                const int kblocks = (p.K + BK - 1) / BK;
+                const int kb_per_split = (kblocks + p.splits - 1) / p.splits;
+                const int mb = un.tile % p.tiles_m, nb = un.tile / p.tiles_m;
                 const int arow = (mb * CG + (int)rank) * BM;
                 const int brows = p.bn / CG;                          // B rows this CTA loads
                 const int bcol = nb * p.bn + (int)rank * brows;
-                const int kbs = sp * kb_per_split, kbe = kbs + kb_per_split < kblocks ? kbs + kb_per_split : kblocks;
+                const int kbs = un.sp * kb_per_split, kbe = kbs + kb_per_split < kblocks ? kbs + kb_per_split : kblocks;
                 for (int kb = kbs; kb < kbe && ok; ++kb) {
                     for (int q = 0; q < p.nprod; ++q) {
-                        if (!mbar_wait(&empty[s], ph ^ 1, p.status)) { ok = false; break; }
+                        if (!mbar_wait(&empty[s], ph ^ 1, status)) { ok = false; break; }
                         uint8_t* a_dst = sA + s * G::A_BYTES;
                         uint8_t* b_dst = sB + s * G::B_BYTES;
                         const void* ma = &p.tmA[p.pa[q]];
@@ -189,7 +256,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
                         if constexpr (CG == 1) {
                             mbar_arrive_expect_tx(&full[s], stage_tx);
                             tma_load_2d(a_dst, ma, &full[s], kb * BK, arow);
-                            if constexpr (!B_MN) {
+                            if (!bmn) {
                                 tma_load_2d(b_dst, mbm, &full[s], kb * BK, bcol);
                             } else {
                                 for (int j = 0; j < brows / 64; ++j)
@@ -200,7 +267,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
                             const uint32_t fb = mapa_shared(smem_u32(&full[s]), 0);
                             if (rank == 0) mbar_arrive_expect_tx(&full[s], 2 * stage_tx);
                             tma_load_2d_cg2(a_dst, ma, fb, kb * BK, arow);
-                            if constexpr (!B_MN) {
+                            if (!bmn) {
                                 tma_load_2d_cg2(b_dst, mbm, fb, kb * BK, bcol);
                             } else {
                                 for (int j = 0; j < brows / 64; ++j)
@@ -216,30 +283,36 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     } else if (warp == 1) {
         // ---------------- MMA issuer (the leader CTA of a pair) ----------------
         if (lane == 0 && rank == 0) {
-            const uint32_t idesc = idesc_f16(BM * CG, p.bn, 0, 0, B_MN ? 1 : 0);
             int s = 0;
             uint32_t ph = 0;
             bool ok = true;
             int u = 0;   // accumulation units (tile, split, segment) processed
-            for (int u0 = cid; u0 < num_units && ok; u0 += ncl) {
-                const int sp = u0 / num_tiles;
-                const int kbs = sp * kb_per_split, kbe = kbs + kb_per_split < kblocks ? kbs + kb_per_split : kblocks;
-                for (int kb0 = kbs; kb0 < kbe && ok; kb0 += p.seg_kb, ++u) {
-                    const int kb1 = kb0 + p.seg_kb < kbe ? kb0 + p.seg_kb : kbe;
+            const UnitRange<NPROB> ur(ps, cid, ncl);
+            for (int j = ur.i; j < ur.end && ok; j += ur.step) {
+                const Unit un = unit_of<NPROB>(ps, ur.unit(j));
+                const GemmParams& p = ps[un.prob];
+                const bool bmn = BMODE == 2 ? p.b_mn != 0 : BMODE == 1;
+                const uint32_t idesc = idesc_f16(BM * CG, p.bn, 0, 0, bmn ? 1 : 0);
+                const int kblocks = (p.K + BK - 1) / BK;
+                const int kb_per_split = (kblocks + p.splits - 1) / p.splits;
+                const int kbs = un.sp * kb_per_split, kbe = kbs + kb_per_split < kblocks ? kbs + kb_per_split : kblocks;
+                const int nprod = p.nprod, seg_kb = p.seg_kb;
+                for (int kb0 = kbs; kb0 < kbe && ok; kb0 += seg_kb, ++u) {
+                    const int kb1 = kb0 + seg_kb < kbe ? kb0 + seg_kb : kbe;
                     const int acc = u & 1;
-                    if (!mbar_wait(&tempty[acc], ((u >> 1) & 1) ^ 1, p.status)) { ok = false; break; }
+                    if (!mbar_wait(&tempty[acc], ((u >> 1) & 1) ^ 1, status)) { ok = false; break; }
                     tc_fence_after();
                     const uint32_t d_tmem = tmem_base + acc * 256;
-                    const int nst = (kb1 - kb0) * p.nprod;
+                    const int nst = (kb1 - kb0) * nprod;
                     for (int st = 0; st < nst; ++st) {
-                        if (!mbar_wait(&full[s], ph, p.status)) { ok = false; break; }
+                        if (!mbar_wait(&full[s], ph, status)) { ok = false; break; }
                         tc_fence_after();
                         const uint32_t a0 = smem_u32(sA + s * G::A_BYTES), b0 = smem_u32(sB + s * G::B_BYTES);
 #pragma unroll
                         for (int kk = 0; kk < BK / 16; ++kk) {
                             const uint64_t ad = sdesc_sw128(a0 + kk * 32, 16, 1024);
-                            const uint64_t bd = B_MN ? sdesc_sw128(b0 + kk * 2048, 64 * BK * 2, 1024)
-                                                     : sdesc_sw128(b0 + kk * 32, 16, 1024);
+                            const uint64_t bd = bmn ? sdesc_sw128(b0 + kk * 2048, 64 * BK * 2, 1024)
+                                                    : sdesc_sw128(b0 + kk * 32, 16, 1024);
                             if constexpr (CG == 2) tc_mma_f16_cg2(d_tmem, ad, bd, idesc, (st | kk) ? 1u : 0u);
                             else tc_mma_f16(d_tmem, ad, bd, idesc, (st | kk) ? 1u : 0u);
                         }
@@ -270,9 +343,14 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         const int quarter = warp & 3;                 // TMEM lanes this warp may access
         int u = 0;
         bool ok = true;
-        for (int u0 = cid; u0 < num_units && ok; u0 += ncl) {
-          const int tile = u0 % num_tiles, sp = u0 / num_tiles;
+        const UnitRange<NPROB> ur(ps, cid, ncl);
+        for (int j = ur.i; j < ur.end && ok; j += ur.step) {
+          const Unit un = unit_of<NPROB>(ps, ur.unit(j));
+          const GemmParams& p = ps[un.prob];
+          const int tile = un.tile, sp = un.sp;
           const int mb = tile % p.tiles_m, nb = tile / p.tiles_m;
+          const int kblocks = (p.K + BK - 1) / BK;
+          const int kb_per_split = (kblocks + p.splits - 1) / p.splits;
           const int kbs = sp * kb_per_split, kbe = kbs + kb_per_split < kblocks ? kbs + kb_per_split : kblocks;
           // one flag per (tile, CTA half, warp quarter): the same warp quarter of
           // both splits owns the same 32 rows, so warps pair up one to one
@@ -280,7 +358,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           const int arrived = p.epoch * 16 + 1;
           for (int kb0 = kbs; kb0 < kbe; kb0 += p.seg_kb, ++u) {
             const int acc = u & 1;
-            const bool w = mbar_wait(&tfull[acc], (u >> 1) & 1, p.status);
+            const bool w = mbar_wait(&tfull[acc], (u >> 1) & 1, status);
             if (!__all_sync(0xffffffffu, w)) { ok = false; break; }   // warp-uniform exit
             tc_fence_after();
             const int row = (mb * CG + (int)rank) * BM + quarter * 32 + lane;
@@ -426,7 +504,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
                 // Per (row, tile) partial statistics of the softcapped logits:
                 // max, lowest index of the max, sum exp(l - max) in fp64, and
                 // the label's logit when the label falls in this tile.
-                const LseDesc& L = ep.lse;
+                const LseDesc& L = ep->lse;
                 const int label = row_ok ? L.labels[row + 1] - L.v0 : -1;
                 float mx = -1e30f;
                 int arg = 0x7fffffff;
@@ -475,7 +553,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             } else {
                 // dlogit = ((softmax - onehot) / n_loss) * (1 - y^2) * mask,
                 // scaled by 2^dl_exp and split into fp16 planes.
-                const DlogitDesc& G = ep.dl;
+                const DlogitDesc& G = ep->dl;
                 const bool live = row_ok && row < G.T - 1 && G.mask[row] != 0;
                 const double lse = live ? G.rmax[row] + log(G.rsum[row]) : 0.0;
                 const int label = live ? G.labels[row + 1] - G.v0 : -1;
@@ -539,20 +617,22 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         }
     }
 
-    if (EPI == EPI_STORE && p.rs_world) __threadfence_system();   // peer stores before the done flag
+    // the problem (at most one) whose result is reduce-scattered to its owners
+    const GemmParams* rsp = ps[0].rs_world ? &ps[0] : (NPROB == 2 && ps[NPROB - 1].rs_world ? &ps[NPROB - 1] : nullptr);
+    if (EPI == EPI_STORE && rsp) __threadfence_system();   // peer stores before the done flag
     tc_fence_before();
     __syncthreads();
     if constexpr (CG == 2) cluster_sync();   // the pair finishes together: no remote signal after exit
     if constexpr (EPI == EPI_STORE) {
-        if (p.rs_world && threadIdx.x == 0) {
+        if (rsp && threadIdx.x == 0) {
             // every epilogue thread fenced its peer stores (system scope) before
             // the barriers above; the last CTA of the launch tells each owner
             __threadfence_system();
-            const int old = atomicAdd(p.rs_counter, 1);
+            const int old = atomicAdd(rsp->rs_counter, 1);
             if (old == (int)gridDim.x - 1) {
-                *p.rs_counter = 0;
+                *rsp->rs_counter = 0;
                 __threadfence_system();
-                for (int o = 0; o < p.rs_world; ++o) st_release_sys(p.rs_done[o], p.rs_epoch);
+                for (int o = 0; o < rsp->rs_world; ++o) st_release_sys(rsp->rs_done[o], rsp->rs_epoch);
             }
         }
     }
@@ -561,6 +641,18 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         if constexpr (CG == 2) tmem_dealloc_cg2(tmem_base, TMEM_COLS);
         else tmem_dealloc(tmem_base, TMEM_COLS);
     }
+}
+
+template <int CG, bool B_MN, int EPI>
+__global__ void __launch_bounds__(GEMM_THREADS, 1)
+    gemm_tc_kernel(const __grid_constant__ GemmParams p, const __grid_constant__ EpiParams ep) {
+    gemm_body<CG, B_MN ? 1 : 0, EPI, 1>(&p, &ep);
+}
+
+// Two plain-store problems in one persistent launch (see the file header).
+template <int CG>
+__global__ void __launch_bounds__(GEMM_THREADS, 1) gemm_pair_kernel(const __grid_constant__ GemmPair pp) {
+    gemm_body<CG, 2, EPI_STORE, 2>(pp.p, nullptr);
 }
 
 // ---------------------------------------------------------------------------
@@ -680,8 +772,8 @@ static tk_status build(const GemmDesc& g, tk_ctx* ctx, GemmParams& gp, int cg, i
         gp.rs_rpo = g.rs->rpo;
         gp.rs_epoch = g.rs->epoch;
     }
+    gp.b_mn = g.b_mn ? 1 : 0;
     gp.status = ctx->status;
-    (void)ctx;
     return TK_OK;
 }
 
@@ -755,6 +847,140 @@ tk_status launch_gemm(tk_ctx* ctx, const GemmDesc& g, cudaStream_t s) {
     memset(&ep, 0, sizeof(ep));
     if (cg == 2) return g.b_mn ? go<2, true, EPI_STORE>(ctx, gp, ep, s) : go<2, false, EPI_STORE>(ctx, gp, ep, s);
     return g.b_mn ? go<1, true, EPI_STORE>(ctx, gp, ep, s) : go<1, false, EPI_STORE>(ctx, gp, ep, s);
+}
+
+// Operand bytes a pair launch reads (A planes, and B planes once when the
+// two problems share them, as the forward and dX of one weight do).
+static size_t pair_operand_bytes(const GemmDesc& g0, const GemmDesc& g1) {
+    auto planes = [](const uint16_t* const* p, int n) {
+        int c = 0;
+        for (int i = 0; i < n; ++i) c += p[i] != nullptr;
+        return c;
+    };
+    size_t b = 0;
+    for (const GemmDesc* g : {&g0, &g1}) b += (size_t)g->M * g->K * 2 * planes(g->A, 3);
+    const size_t wb = (size_t)g0.N * g0.K * 2 * planes(g0.B, 2);
+    b += wb;
+    if (g1.B[0] != g0.B[0]) b += (size_t)g1.N * g1.K * 2 * planes(g1.B, 2);
+    return b;
+}
+constexpr size_t kPairL2Bytes = 96ull << 20;
+
+// The units of a pair launch assigned to the CTA pairs by list scheduling:
+// in the launch's unit order (interleaved, or problem 1 first), each unit goes
+// to the CTA pair that frees up first, by an estimate of its time (k-blocks x
+// products + segments' epilogues).  Unit costs differ between the problems
+// (e.g. a dX tile over all 14336 rows of W against a forward tile over 4096
+// columns), where a plain stride over the units would leave some CTA pairs
+// several units longer than others.  The table goes to the device once per
+// shape (ctx->sched, ordered on the stream like the launch that reads it).
+static tk_status pair_schedule(tk_ctx* ctx, const GemmParams& p0, const GemmParams& p1, int groups, bool interleave,
+                               cudaStream_t s) {
+    const int t0 = p0.tiles_m * p0.tiles_n, t1 = p1.tiles_m * p1.tiles_n, t = t0 + t1;
+    const std::vector<long> key = {t0, t1, p0.K, p1.K, p0.nprod, p1.nprod, p0.seg_kb, p1.seg_kb, groups, interleave};
+    if (ctx->sched && ctx->sched_key == key) return TK_OK;
+    std::vector<int> order(t);
+    for (int u = 0; u < t; ++u) {
+        if (!interleave) { order[u] = u; continue; }
+        // ceil(u * t1 / t) units of problem 1 come before position u: its
+        // tiles spread evenly, one at the start of each period
+        const int c = (int)(((long)u * t1 + t - 1) / t), cn = (int)(((long)(u + 1) * t1 + t - 1) / t);
+        order[u] = cn > c ? c : t1 + (u - c);
+    }
+    auto cost = [&](int id) {
+        const GemmParams& q = id < t1 ? p1 : p0;
+        const long kb = (q.K + BK - 1) / BK;
+        return kb * q.nprod + 4 * ((kb + q.seg_kb - 1) / q.seg_kb);
+    };
+    std::priority_queue<std::pair<long, int>, std::vector<std::pair<long, int>>, std::greater<std::pair<long, int>>> free_at;
+    for (int g = 0; g < groups; ++g) free_at.push({0, g});
+    std::vector<std::vector<int>> per(groups);
+    for (int id : order) {
+        const auto [load, g] = free_at.top();
+        free_at.pop();
+        per[g].push_back(id);
+        free_at.push({load + cost(id), g});
+    }
+    std::vector<int> host((size_t)groups + 1 + t);
+    int o = 0;
+    for (int g = 0; g < groups; ++g) {
+        host[g] = o;
+        for (int id : per[g]) host[groups + 1 + o++] = id;
+    }
+    host[groups] = o;
+    if (host.size() > ctx->sched_cap) {
+        cudaError_t e = cudaDeviceSynchronize();   // a launch in flight may still read the old table
+        if (e != cudaSuccess) return cuda_fail(e, "pair schedule sync");
+        if (ctx->sched) cudaFree(ctx->sched);
+        ctx->sched = nullptr;
+        ctx->sched_cap = 0;
+        e = cudaMalloc(&ctx->sched, host.size() * sizeof(int));
+        if (e != cudaSuccess) return cuda_fail(e, "pair schedule table");
+        ctx->sched_cap = host.size();
+    }
+    // from pageable memory: the call returns once the table is staged
+    cudaError_t e = cudaMemcpyAsync(ctx->sched, host.data(), host.size() * sizeof(int), cudaMemcpyHostToDevice, s);
+    if (e != cudaSuccess) return cuda_fail(e, "pair schedule upload");
+    ctx->sched_key = key;
+    return TK_OK;
+}
+
+// Both problems of a pair with CTA pairs and 256-wide tiles (an N-major B
+// loads 64-column boxes, so 256 suits both layouts); the combined unit list
+// takes care of the waves, so the per-problem tile-width choice is not needed.
+bool gemm_pair_ok(const GemmDesc& g0, const GemmDesc& g1) {
+    for (const GemmDesc* g : {&g0, &g1})
+        if (pick_cg(*g) != 2 || g->split_ws || (g->rs && g != &g1)) return false;
+    return true;
+}
+
+tk_status launch_gemm_pair(tk_ctx* ctx, const GemmDesc& g0, const GemmDesc& g1, cudaStream_t s) {
+    if (!gemm_pair_ok(g0, g1)) return fail(TK_ERR_INVALID, "GEMM pair needs two CTA-pair problems without split-K");
+    GemmPair pp;
+    tk_status st = build(g0, ctx, pp.p[0], 2, BN);
+    if (st != TK_OK) return st;
+    st = build(g1, ctx, pp.p[1], 2, BN);
+    if (st != TK_OK) return st;
+    const int units = pp.p[0].tiles_m * pp.p[0].tiles_n + pp.p[1].tiles_m * pp.p[1].tiles_n;
+    const int groups_max = ctx->num_sms / 2;
+    const int groups = units < groups_max ? units : groups_max;
+    // Interleaving the two tile lists halves each problem's tiles in flight,
+    // so each operand panel is shared by fewer concurrent tiles; that only
+    // pays while both problems' operands stay in L2 together.  Measured on
+    // B200 (forward + dX of W[ng, 4096], M = 4096, bf16): interleaved beats
+    // two launches at 61 and 90 MB of operands (ng = 1792, 3584: 125 vs 136,
+    // 220 vs 244 us) and loses at 148 and 266 MB (ng = 7168, 14336), where
+    // its DRAM reads grew 3.6x.  Above the threshold the problems run one
+    // after the other in one launch.
+    const bool interleave = pair_operand_bytes(g0, g1) <= kPairL2Bytes;
+    st = pair_schedule(ctx, pp.p[0], pp.p[1], groups, interleave, s);
+    if (st != TK_OK) return st;
+    pp.p[0].sched_off = ctx->sched;
+    pp.p[0].sched = ctx->sched + groups + 1;
+    using G = Geo<2>;
+    static std::atomic<uint64_t> attr_done{0};
+    auto kern = gemm_pair_kernel<2>;
+    {
+        const cudaError_t e = smem_attr_once(kern, (int)G::SMEM, ctx->device, attr_done);
+        if (e != cudaSuccess) return cuda_fail(e, "gemm pair smem attribute");
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(groups * 2, 1, 1);
+    cfg.blockDim = dim3(GEMM_THREADS, 1, 1);
+    cfg.dynamicSmemBytes = G::SMEM;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    ProfScope ps(ctx, s, PK_GEMM);
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kern, pp);
+    ctx->launches++;
+    if (e != cudaSuccess) return cuda_fail(e, "gemm pair launch");
+    return cuda_fail(cudaGetLastError(), "gemm pair launch");
 }
 
 tk_status launch_gemm_lse(tk_ctx* ctx, const GemmDesc& g, const LseDesc& e, cudaStream_t s) {

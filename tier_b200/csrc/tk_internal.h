@@ -38,6 +38,12 @@ struct tk_ctx {
     // IQ1/IQ2/IQ3 lattice tables registered by tk_set_iq_grids (device,
     // tkq::GRID_BYTES, layout in tk_qgrid.h); null until then
     int8_t* iq_tab = nullptr;
+    // schedule of the last two-problem GEMM launch (tk_gemm.cu): per CTA pair
+    // its units in order, [offsets (pairs + 1) | unit ids], on the device;
+    // rebuilt when the key (shapes, tile counts, grid) changes
+    int* sched = nullptr;
+    size_t sched_cap = 0;            // ints
+    std::vector<long> sched_key;
 };
 
 namespace tk {
@@ -182,6 +188,11 @@ tk_status rs_finish(tk_ctx* ctx, const RsDesc& rs, int K, float* out, long ldo, 
 // K splits launch_gemm would use for g given a split workspace (1 or 2).
 int gemm_splits(const tk_ctx* ctx, const GemmDesc& g);
 tk_status launch_gemm(tk_ctx* ctx, const GemmDesc& g, cudaStream_t s);
+// Two GEMMs in one persistent launch, their tiles interleaved.  Both need CTA
+// pairs (M > 128) and no split-K; only g1 may carry a reduce-scatter.  Each
+// result equals its own launch_gemm without split-K bit for bit.
+bool gemm_pair_ok(const GemmDesc& g0, const GemmDesc& g1);
+tk_status launch_gemm_pair(tk_ctx* ctx, const GemmDesc& g0, const GemmDesc& g1, cudaStream_t s);
 
 // Fused-dequant GEMM (tk_gemm_q.cu): B is the raw quantized weight W[w_rows,
 // row_bytes]; dx == false: D[M, N] = A . W^T with N = w_rows, K = cols of W;

@@ -217,6 +217,19 @@ class LinearPath:
                               products=products)
         return out
 
+    def fwd_dx_rs(self, X: torch.Tensor, dY: torch.Tensor, products: int = X3_AUTO):
+        """The training step's two passes through this shard in one launch:
+        (Y, dX rows) with Y = X . W_g^T (this rank's columns, not gathered)
+        and dX rows as `dx_rs`; the forward tiles compute while the dX tiles'
+        stores cross NVLink (tk_linear_fwd_dx_rs)."""
+        Mx, M = X.shape[0], dY.shape[0]
+        Y = torch.empty(Mx, self.N, device=X.device, dtype=torch.float32)
+        out = torch.empty(M // self.rs_world, self.K, device=dY.device, dtype=torch.float32)
+        self.ctx.linear_fwd_dx_rs(self.W, X, Mx, Y, dY, M, out, x_dtype=_DT[X.dtype], dy_dtype=_DT[dY.dtype],
+                                  ldx=X.stride(0), ldy=Y.stride(0), lddy=dY.stride(0), ldd=out.stride(0),
+                                  products=products)
+        return Y, out
+
     def dx(self, dY: torch.Tensor, dX: torch.Tensor | None = None, beta: float = 0.0,
            products: int = X3_AUTO) -> torch.Tensor:
         """dX = dY . W (`linear_dx`; beta=1 is `linear_dx_acc`).  dY holds this
