@@ -720,9 +720,12 @@ def run_ours(args):
         # time per step; launches per step vary (dX may run in M-chunks)
         gemm_ms_step = gemm_ms / args.steps
         achieved = flop_step / world / (gemm_ms_step * 1e-3) / 1e12
-        traffic = None   # dram read+write bytes per GEMM launch from the committed ncu summary
-        tf = ROOT / "profiles" / "gemm_tc_kernel_c2_q4k_m4096.md"
-        if tf.exists():
+        # dram read+write bytes per GEMM launch from the committed ncu summary of
+        # the launch the step runs (one pair launch, or the fwd and dX launches)
+        traffic = None
+        one_launch = pair and dx_mode in ("local", "fused")
+        tf = ROOT / "profiles" / ("gemm_pair_kernel_c2_q4k_m4096.md" if one_launch else "gemm_tc_kernel_c2_q4k_m4096.md")
+        if tf.exists() and world == 1:   # the summaries are of the one-GPU shape
             for ln in tf.read_text().splitlines():
                 if ln.startswith("traffic_bytes_per_launch:"):
                     traffic = float(ln.split(":")[1].split()[0])
@@ -756,10 +759,14 @@ def run_ours(args):
             # the timed region is tens of milliseconds: the burst GEMM figure is the peak
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": tf_burst, "unit": "TFLOP/s",
                          "frac": achieved / tf_burst, "traffic": traffic,
-                         "traffic_source": ("ncu dram__bytes_read.sum + dram__bytes_write.sum per GEMM launch "
+                         "traffic_source": ("ncu dram__bytes_read.sum + dram__bytes_write.sum of the step's one "
+                                            "GEMM launch (fwd + dX) at this shape on one GPU, from "
+                                            "profiles/gemm_pair_kernel_c2_q4k_m4096.md; not measured in this run"
+                                            if one_launch else
+                                            "ncu dram__bytes_read.sum + dram__bytes_write.sum per GEMM launch "
                                             "(mean of the fwd and dX launches at this shape on one GPU), from "
                                             "profiles/gemm_tc_kernel_c2_q4k_m4096.md; not measured in this run"),
-                         "kernel": "gemm_tc_kernel",
+                         "kernel": "gemm_pair_kernel" if one_launch else "gemm_tc_kernel",
                          "peak_source": f"{src} bf16 burst (MEASURED_PEAKS.json)",
                          "sustained_peak": tf_sus, "frac_of_sustained": achieved / tf_sus},
             "check": check,
