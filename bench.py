@@ -579,6 +579,7 @@ def run_ours(args):
     gemm_ms, gemm_n = ctx.profile_read(tk.PROF_GEMM)
     deq_ms, deq_n = ctx.profile_read(tk.PROF_DEQUANT)
     spl_ms, spl_n = ctx.profile_read(tk.PROF_SPLIT)
+    comm_ms, comm_n = ctx.profile_read(tk.PROF_COMM)
     ctx.profile(False)
     launches = ctx.launches() - n0
     clk = clocks.stop()
@@ -771,7 +772,10 @@ def run_ours(args):
                          "sustained_peak": tf_sus, "frac_of_sustained": achieved / tf_sus},
             "check": check,
             "kernels_ms_per_step": {"gemm": gemm_ms / args.steps, "dequant": deq_ms / args.steps,
-                                    "act_split": spl_ms / args.steps},
+                                    "act_split": spl_ms / args.steps,
+                                    # the owner's reduce of the dX reduce-scatter, its wait for the
+                                    # peers' tiles included (N > 1, fused and reshard modes)
+                                    "rs_reduce_and_collectives": comm_ms / args.steps},
             "phases_ms": phases,
             "e2e": {"value": e2e_val, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "steps": e_steps,

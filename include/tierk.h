@@ -121,8 +121,11 @@ uint64_t tk_launch_count(const tk_ctx *ctx);
  * every launch is bracketed by CUDA events on its own stream (up to 8192
  * launches; later launches are not recorded).  tk_profile resets the record.
  * tk_profile_read synchronizes the device and returns the summed event time
- * (ms) and number of recorded launches of one kernel family. */
-enum { TK_PROF_GEMM = 0, TK_PROF_DEQUANT = 1, TK_PROF_SPLIT = 2, TK_PROF_GEMV = 3, TK_PROF_LMHEAD = 4 };
+ * (ms) and number of recorded launches of one kernel family.  TK_PROF_COMM:
+ * the reduce-scatter's owner reduce (with its wait for the peers' tiles) and
+ * the peer collectives' kernels. */
+enum { TK_PROF_GEMM = 0, TK_PROF_DEQUANT = 1, TK_PROF_SPLIT = 2, TK_PROF_GEMV = 3, TK_PROF_LMHEAD = 4,
+       TK_PROF_COMM = 5 };
 tk_status tk_profile(tk_ctx *ctx, int enable);
 tk_status tk_profile_read(tk_ctx *ctx, int kind, double *total_ms, uint64_t *launches);
 

@@ -49,7 +49,7 @@ IPC_HANDLE_BYTES = 64   # TK_IPC_HANDLE_BYTES
 WFROZEN = 0x200  # OR into tk_gemv's qtype: W is never written by earlier kernels (early weight fetch)
 WREUSE = 0x400   # OR into linear products: reuse the previous call's fp16 expansion of the same (unchanged) W
 # kernel families for profiling
-PROF_GEMM, PROF_DEQUANT, PROF_SPLIT, PROF_GEMV, PROF_LMHEAD = range(5)
+PROF_GEMM, PROF_DEQUANT, PROF_SPLIT, PROF_GEMV, PROF_LMHEAD, PROF_COMM = range(6)
 
 
 class TierkError(RuntimeError):

@@ -145,7 +145,7 @@ tk_status rs_finish(tk_ctx* ctx, const RsDesc& rs, int K, float* out, long ldo, 
     const long n4 = (long)rs.rpo * (K / 4);
     int blocks = (int)((n4 + 255) / 256);
     if (blocks > 4 * ctx->num_sms) blocks = 4 * ctx->num_sms;
-    ProfScope ps(ctx, s, PK_GEMM);
+    ProfScope ps(ctx, s, PK_COMM);
     rs_reduce_kernel<<<blocks, 256, 0, s>>>(hdr_int(c->buf, kDoneOff) + par * 8, recv, rs.world, rs.rpo, K, out, ldo,
                                            rs.epoch, hdr_int(c->buf, kRedCtr), peer_ack, c->rank, ctx->status);
     ctx->launches++;
@@ -394,6 +394,7 @@ static tk_status cm_start(tk_ctx* ctx, const void* src, size_t slot, CmConsume& 
     int blocks = (int)((n16 + 255) / 256);
     if (blocks > 2 * ctx->num_sms) blocks = 2 * ctx->num_sms;
     if (blocks < 1) blocks = 1;
+    ProfScope ps(ctx, s, PK_COMM);
     if (rows_src) cm_push_rows_kernel<<<blocks, 256, 0, s>>>(a, rows_src, ld_src, rows_per, row_bytes);
     else cm_push_kernel<<<blocks, 256, 0, s>>>(a, static_cast<const uint4*>(src), n16);
     ctx->launches++;
@@ -496,6 +497,7 @@ tk_status tk_allgather(tk_ctx* ctx, const void* src, size_t bytes, void* dst, vo
     tk_status st = cm_start(ctx, src, bytes, c, &recv, s);
     if (st != TK_OK) return st;
     const size_t n16 = bytes / 16 * c.world;
+    ProfScope ps(ctx, s, PK_COMM);
     cm_gather_kernel<<<cm_blocks(ctx, n16), 256, 0, s>>>(c, reinterpret_cast<const uint4*>(recv), n16,
                                                         static_cast<uint4*>(dst));
     ctx->launches++;
@@ -551,6 +553,7 @@ tk_status tk_reshard_cols_recv(tk_ctx* ctx, void* dst, size_t ld_dst, int elem_b
     pe.open = false;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     const size_t nv = (size_t)pe.c.world * pe.rows_per * (pe.row_bytes / 16);
+    ProfScope ps(ctx, s, PK_COMM);
     cm_rows_kernel<<<cm_blocks(ctx, (nv + 3) / 4), 256, 0, s>>>(pe.c, pe.recv, pe.rows_per, pe.row_bytes,
                                                                  static_cast<uint8_t*>(dst), ld_dst * elem_bytes);
     ctx->launches++;
@@ -573,6 +576,7 @@ tk_status tk_allreduce_f32(tk_ctx* ctx, float* buf, size_t n, void* stream) {
     const uint8_t* recv = nullptr;
     tk_status st = cm_start(ctx, buf, n * 4, c, &recv, s);
     if (st != TK_OK) return st;
+    ProfScope ps(ctx, s, PK_COMM);
     cm_sum_kernel<<<cm_blocks(ctx, n / 4), 256, 0, s>>>(c, reinterpret_cast<const float4*>(recv), n / 4,
                                                         reinterpret_cast<float4*>(buf));
     ctx->launches++;
@@ -597,6 +601,7 @@ tk_status tk_lmhead_merge(tk_ctx* ctx, int n, double* rmax, double* rsum, int32_
     st = cm_start(ctx, pack, slot, c, &recv, s);
     if (st != TK_OK) return st;
     int blocks = n < 4 * ctx->num_sms ? n : 4 * ctx->num_sms;
+    ProfScope ps(ctx, s, PK_COMM);
     lm_merge_kernel<<<blocks, 128, 0, s>>>(c, recv, n, slot, c.me, rmax, rsum, amax, tgt, dX, H);
     ctx->launches++;
     return cuda_fail(cudaGetLastError(), "tk_lmhead_merge launch");

@@ -73,7 +73,7 @@ inline cudaError_t smem_attr_once(K* kern, int bytes, int device, std::atomic<ui
 }
 
 // Kernel families for tk_profile_read (TK_PROF_* in tierk.h).
-enum ProfKind { PK_GEMM = 0, PK_DEQUANT = 1, PK_SPLIT = 2, PK_GEMV = 3, PK_LMHEAD = 4, PK_COUNT = 5 };
+enum ProfKind { PK_GEMM = 0, PK_DEQUANT = 1, PK_SPLIT = 2, PK_GEMV = 3, PK_LMHEAD = 4, PK_COMM = 5, PK_COUNT = 6 };
 int prof_begin(tk_ctx* ctx, cudaStream_t s);
 void prof_end(tk_ctx* ctx, cudaStream_t s, int slot, int kind);
 struct ProfScope {
