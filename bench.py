@@ -870,8 +870,15 @@ def measure_c1(ctx, qt, N, K, Ms, steps, seed=0):
     rotating over distinct weight copies (>= 4x the 126 MB L2) so every
     launch reads HBM.  The launches are captured in one CUDA graph and the
     graph is replayed, so the timing measures back-to-back kernels, not the
-    host's launch rate.  The first M's output is checked against an fp64
-    matmul of tk_dequant's fp32 weight."""
+    host's launch rate.  Two graphs per M:
+      isolated  each GEMV starts after the previous one has finished;
+      frozen    the weights are flagged TK_WFROZEN (never written by earlier
+                kernels, as every projection of a decode step is), so each
+                GEMV is launched as a programmatic dependent of the previous
+                one and fetches its weight while that one finishes; x and y
+                are still read and written only after it.
+    The first M's output is checked against an fp64 matmul of tk_dequant's
+    fp32 weight, from both graphs."""
     import numpy as np
     import torch
     import tier_b200 as tk
@@ -879,6 +886,7 @@ def measure_c1(ctx, qt, N, K, Ms, steps, seed=0):
     rng = np.random.default_rng(seed)
     out = {}
     check = None
+    clk = None
     for M in Ms:
         b = blocks_for(rng, qt, N, K)
         wbytes = b.nbytes
@@ -887,52 +895,66 @@ def measure_c1(ctx, qt, N, K, Ms, steps, seed=0):
         pool = [W.clone() for _ in range(copies)]
         x = torch.from_numpy(rng.standard_normal((M, K)).astype(np.float32)).cuda()
         y = torch.empty(M, N, device="cuda")
-        ctx.gemv(qt, pool[0], N, K, x, y, M=M)                 # module load / attributes outside capture
-        torch.cuda.synchronize()
-        if check is None:
-            W32 = torch.empty(N, K, device="cuda")
-            ctx.dequant(qt, W, N, K, W32)
-            want = x.double() @ W32.double().T
-            err = float((y.double() - want).norm() / want.norm())
-            check = {"rel_err": err, "tol": 2e-3, "ok": bool(err < 2e-3), "M": M,
-                     "against": "fp64 matmul of tk_dequant's fp32 W (bit-exact to q_val in the tests)"}
-            del W32, want
-        g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g):
-            for w in pool:
-                ctx.gemv(qt, w, N, K, x, y, M=M)
-        for _ in range(3):
-            g.replay()
-        torch.cuda.synchronize()
-        clocks = Clocks(torch.cuda.current_device())
-        clocks.start()
-        t0 = time.perf_counter()
-        while time.perf_counter() - t0 < 0.4:
-            g.replay()
-            torch.cuda.synchronize()
-        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        ev0.record()
-        for _ in range(steps):
-            g.replay()
-        ev1.record()
-        torch.cuda.synchronize()
-        clk = clocks.stop()
-        per_launch = ev0.elapsed_time(ev1) / (steps * copies)
         bytes_launch = wbytes + 4 * K * M + 4 * N * M
-        gbs = bytes_launch / (per_launch * 1e-3) / 1e9
-        out[M] = (per_launch, gbs, copies, clk, bytes_launch)
-        del pool, g, W
+        res = {}
+        for mode, t in (("isolated", qt), ("frozen", qt | tk.WFROZEN)):
+            ctx.gemv(t, pool[0], N, K, x, y, M=M)                 # module load / attributes outside capture
+            torch.cuda.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                for w in pool:
+                    ctx.gemv(t, w, N, K, x, y, M=M)
+            for _ in range(3):
+                g.replay()
+            torch.cuda.synchronize()
+            clocks = Clocks(torch.cuda.current_device())
+            clocks.start()
+            t0 = time.perf_counter()
+            while time.perf_counter() - t0 < 0.4:
+                g.replay()
+                torch.cuda.synchronize()
+            ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            ev0.record()
+            for _ in range(steps):
+                g.replay()
+            ev1.record()
+            torch.cuda.synchronize()
+            res[mode] = (ev0.elapsed_time(ev1) / (steps * copies), clocks.stop())
+            if M == Ms[0]:
+                W32 = torch.empty(N, K, device="cuda")
+                ctx.dequant(qt, W, N, K, W32)
+                want = x.double() @ W32.double().T
+                err = float((y.double() - want).norm() / want.norm())   # y of the last replayed launch
+                if check is None or err > check["rel_err"]:
+                    check = {"rel_err": err, "tol": 2e-3, "ok": bool(err < 2e-3), "M": M,
+                             "against": "fp64 matmul of tk_dequant's fp32 W (bit-exact to q_val in the tests); "
+                                        "worst of the isolated and frozen graphs"}
+                del W32, want
+            del g
+        out[M] = {mode: (v[0], bytes_launch / (v[0] * 1e-3) / 1e9) for mode, v in res.items()}
+        if clk is None:
+            clk = res["frozen"][1]
+        out[M]["copies"] = copies
+        out[M]["bytes"] = bytes_launch
+        del pool, W
     hbm = peaks()[0]
     m0 = Ms[0]
-    per_launch, gbs, copies, clk, bytes_launch = out[m0]
+    per_launch, gbs = out[m0]["frozen"]
+    iso_launch, iso_gbs = out[m0]["isolated"]
     name = {8: "q8_0", 12: "q4_k", 13: "q5_k", 14: "q6_k"}.get(qt, str(qt))
     shape = f"{name} {N}x{K}"
     return {"metric": f"decode GEMV HBM GB/s ({shape}, M={m0})", "value": gbs, "unit": "GB/s",
             "n_gpus": 1, "steps": steps, "higher_is_better": True, "us_per_launch": per_launch * 1e3,
-            "by_M": {m: {"us_per_launch": v[0] * 1e3, "GB_s": v[1], "frac": v[1] / hbm} for m, v in out.items()},
+            "isolated": {"us_per_launch": iso_launch * 1e3, "GB_s": iso_gbs, "frac": iso_gbs / hbm},
+            "by_M": {m: {"us_per_launch": v["frozen"][0] * 1e3, "GB_s": v["frozen"][1], "frac": v["frozen"][1] / hbm,
+                         "isolated_us_per_launch": v["isolated"][0] * 1e3, "isolated_GB_s": v["isolated"][1],
+                         "isolated_frac": v["isolated"][1] / hbm} for m, v in out.items()},
             "config": {"workload": f"{'C1' if shape == 'q8_0 4096x4096' else 'decode'} GEMV {shape}",
-                       "rotating_copies": copies, "bytes_per_launch": bytes_launch,
-                       "timing": "CUDA graph replay of one launch per weight copy, CUDA events"},
+                       "rotating_copies": out[m0]["copies"], "bytes_per_launch": out[m0]["bytes"],
+                       "timing": ("CUDA graph replay of one launch per weight copy, CUDA events; value: frozen "
+                                  "weights (TK_WFROZEN: each GEMV fetches its weight while the previous one "
+                                  "finishes, as a decode step's projections run); 'isolated': each launch "
+                                  "after the previous one ends")},
             "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s", "frac": gbs / hbm,
                          "peak_source": "measured hbm_gbs (MEASURED_PEAKS.json)"},
             "check": check, "clocks": clk}
