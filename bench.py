@@ -4,15 +4,19 @@
 Default workload (the metric's single-GPU configuration):
   Q4_K weight W[14336, 4096] (SwiGLU up-proj), X bf16 [4096, 4096], dY bf16
   [4096, 14336]; one step = forward Y = X.W^T plus input gradient dX = dY.W,
-  both through the C ABI (tk_linear_fwd / tk_linear_dx): bit-exact dequant of
-  W to fp16, activation conversion, tcgen05 GEMM with fp32 accumulation.
-  Useful work per step: 2 x 2*M*N*K = 962.1 GFLOP.
+  both through the C ABI in one call (tk_linear_fwd_dx; --step-call separate:
+  tk_linear_fwd then tk_linear_dx): bit-exact dequant of W to fp16 once,
+  activation conversion, one tcgen05 GEMM launch for both products with fp32
+  accumulation.  Useful work per step: 2 x 2*M*N*K = 962.1 GFLOP.
 
-Multi-GPU (torchrun, one process per GPU, NCCL): W is split by output rows;
-each rank computes its Y columns (kept sharded, as a column-parallel layer's
+Multi-GPU (torchrun, one process per GPU): W is split by output rows; each
+rank computes its Y columns (kept sharded, as a column-parallel layer's
 consumer takes them; --gather-y all-gathers the full Y) and its partial dX,
-which is all-reduced in M-chunks overlapped with the next chunk's GEMM.
+whose tiles the GEMM stores into the owner rank's memory over NVLink
+(tk_linear_fwd_dx_rs; --dx-mode chooses NCCL variants or the dY reshard).
 Total work is fixed (strong scaling); value = total FLOP / max-over-ranks time.
+Timing: CUDA events around the timed steps, max over ranks; per-launch events
+(kernel breakdown, roofline) on one timed step in four.
 
 --impl reference: the reference's CPU implementation of the same operation
 (the engine's own cpu_gemm_fwd / cpu_gemm_dx and thread pool, extracted and
@@ -35,6 +39,7 @@ import time
 from pathlib import Path
 
 ROOT = Path(__file__).resolve().parent
+PROF_EVERY = 4          # timed steps per step with per-launch events
 sys.path.insert(0, str(ROOT))
 sys.path.insert(0, str(ROOT / "tests"))
 
@@ -567,12 +572,24 @@ def run_ours(args):
         step(Xd, dYd)
     barrier()
     n0 = ctx.launches()
+    # Per-launch CUDA events (the kernel breakdown and the roofline's GEMM
+    # time) bracket every launch of one timed step in PROF_EVERY: an event
+    # between two kernels holds the second back until the first has ended,
+    # which on every step would add ~35 us to a 0.95 ms step.
     ctx.profile(True)
+    ctx.profile(False)
+    n_prof = 0
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier()
     ev0.record(stream)
-    for _ in range(args.steps):
+    for i in range(args.steps):
+        sample = i % PROF_EVERY == PROF_EVERY - 1 or (i == args.steps - 1 and n_prof == 0)
+        if sample:
+            ctx.profile(True, resume=True)
+            n_prof += 1
         step(Xd, dYd)
+        if sample:
+            ctx.profile(False)
     ev1.record(stream)
     barrier()
     t_ms = ev0.elapsed_time(ev1)
@@ -580,7 +597,6 @@ def run_ours(args):
     deq_ms, deq_n = ctx.profile_read(tk.PROF_DEQUANT)
     spl_ms, spl_n = ctx.profile_read(tk.PROF_SPLIT)
     comm_ms, comm_n = ctx.profile_read(tk.PROF_COMM)
-    ctx.profile(False)
     launches = ctx.launches() - n0
     clk = clocks.stop()
     t_max = t_ms
@@ -719,7 +735,7 @@ def run_ours(args):
         hbm, tf_burst, tf_sus, src = peaks()
         # this rank's GEMM FLOPs per step (fwd + dX over its rows) over its GEMM
         # time per step; launches per step vary (dX may run in M-chunks)
-        gemm_ms_step = gemm_ms / args.steps
+        gemm_ms_step = gemm_ms / n_prof
         achieved = flop_step / world / (gemm_ms_step * 1e-3) / 1e12
         # dram read+write bytes per GEMM launch from the committed ncu summary of
         # the launch the step runs (one pair launch, or the fwd and dX launches)
@@ -771,11 +787,13 @@ def run_ours(args):
                          "peak_source": f"{src} bf16 burst (MEASURED_PEAKS.json)",
                          "sustained_peak": tf_sus, "frac_of_sustained": achieved / tf_sus},
             "check": check,
-            "kernels_ms_per_step": {"gemm": gemm_ms / args.steps, "dequant": deq_ms / args.steps,
-                                    "act_split": spl_ms / args.steps,
+            "kernels_ms_per_step": {"gemm": gemm_ms / n_prof, "dequant": deq_ms / n_prof,
+                                    "act_split": spl_ms / n_prof,
                                     # the owner's reduce of the dX reduce-scatter, its wait for the
                                     # peers' tiles included (N > 1, fused and reshard modes)
-                                    "rs_reduce_and_collectives": comm_ms / args.steps},
+                                    "rs_reduce_and_collectives": comm_ms / n_prof,
+                                    "sampled": (f"CUDA events around every launch of {n_prof} of the "
+                                                f"{args.steps} timed steps (1 in {PROF_EVERY})")},
             "phases_ms": phases,
             "e2e": {"value": e2e_val, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "steps": e_steps,

@@ -119,7 +119,11 @@ uint64_t tk_launch_count(const tk_ctx *ctx);
 
 /* Per-kernel timing (diagnostics; no reference counterpart).  While enabled,
  * every launch is bracketed by CUDA events on its own stream (up to 8192
- * launches; later launches are not recorded).  tk_profile resets the record.
+ * launches; later launches are not recorded).  tk_profile(ctx, 1) starts a
+ * new record, 2 resumes recording into the current one, 0 pauses (the
+ * record is kept), so that a caller can time a sample of its launches
+ * without events between all the others (an event between two kernels holds
+ * the second back until the first has finished and the event is written).
  * tk_profile_read synchronizes the device and returns the summed event time
  * (ms) and number of recorded launches of one kernel family.  TK_PROF_COMM:
  * the reduce-scatter's owner reduce (with its wait for the peers' tiles) and

@@ -226,8 +226,10 @@ class Context:
     def sync_status(self, stream=None):
         _check(self.lib.tk_sync_status(self.h, _stream(stream)))
 
-    def profile(self, enable: bool):
-        _check(self.lib.tk_profile(self.h, 1 if enable else 0))
+    def profile(self, enable: bool, resume: bool = False):
+        """Start a new per-launch timing record (enable), resume the current
+        one (enable and resume), or pause it (not enable; the record is kept)."""
+        _check(self.lib.tk_profile(self.h, (2 if resume else 1) if enable else 0))
 
     def profile_read(self, kind: int) -> tuple[float, int]:
         t = ctypes.c_double(0)

@@ -472,8 +472,9 @@ size_t tk_workspace_bytes(const tk_ctx* ctx) { return ctx ? ctx->ws_bytes : 0; }
 
 tk_status tk_profile(tk_ctx* ctx, int enable) {
     if (!ctx) return fail(TK_ERR_INVALID, "tk_profile: null context");
+    if (enable < 0 || enable > 2) return fail(TK_ERR_INVALID, "tk_profile: enable must be 0, 1 or 2");
     ctx->prof.on = enable != 0;
-    ctx->prof.used = 0;
+    if (enable == 1) ctx->prof.used = 0;
     return TK_OK;
 }
 
