@@ -145,6 +145,7 @@ __global__ void __launch_bounds__(DQ_THREADS) dequant_kernel(const uint8_t* __re
 template <int T>
 __global__ void __launch_bounds__(256) dequant_sub_f16_kernel(const uint8_t* __restrict__ W, size_t rb, int r0,
                                                               int nrows, int cols, uint16_t* __restrict__ out) {
+    pdl_trigger();
     __shared__ uint4 stage[8][32 * 4];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const unsigned spr = (unsigned)cols >> 5;       // sub-blocks per row
@@ -311,6 +312,7 @@ template <int XT, int NP>
 __global__ void __launch_bounds__(256) act_split_kernel(const void* __restrict__ X, int M, int K, long ldx,
                                                         long ldp, bool scaled, uint16_t* __restrict__ planes,
                                                         int* __restrict__ row_exp) {
+    pdl_trigger();
     __shared__ float red[8];
     const int m = blockIdx.x;
     const size_t xrow = (size_t)m * ldx;
@@ -413,6 +415,7 @@ template <int XT, int NP, int TH>
 __global__ void __launch_bounds__(TH) act_split_vec_kernel(const void* __restrict__ X, int M, int K, long ldx,
                                                                    long ldp, bool scaled, uint16_t* __restrict__ planes,
                                                                    int* __restrict__ row_exp) {
+    pdl_trigger();
     __shared__ float red[TH / 32];
     const int m = blockIdx.x;
     const int nch = K >> 3;

@@ -31,6 +31,16 @@ __device__ __forceinline__ void raise_status(int* status, int code) {
     if (status) atomicCAS(status, 0, code);
 }
 
+// Programmatic dependent launch.  A kernel launched with the programmatic
+// stream-serialization attribute may start once every CTA of the kernel
+// before it has called pdl_trigger (or exited); it must call pdl_wait before
+// it touches anything that kernel writes (pdl_wait returns once that kernel
+// has completed and its memory is visible).  The producers of a GEMM's
+// operands trigger at their start, so the GEMM's CTAs set up (barriers,
+// TMEM, descriptors) while the producer's last wave drains.
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }

@@ -226,6 +226,9 @@ __device__ __forceinline__ void gemm_body(const GemmParams* ps, const EpiParams*
     if constexpr (CG == 2) cluster_sync();   // peer barriers initialised before any remote signal
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    // launched as a programmatic dependent: the set-up above overlapped the
+    // previous kernel; its outputs (the operand planes) are read from here on
+    pdl_wait();
 
     if (warp == 0) {
         // ---------------- TMA producer (each CTA loads its own operands) ----------------
@@ -710,13 +713,15 @@ static tk_status go(tk_ctx* ctx, const GemmParams& gp, const EpiParams& ep, cuda
     cfg.blockDim = dim3(GEMM_THREADS, 1, 1);
     cfg.dynamicSmemBytes = G::SMEM;
     cfg.stream = s;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = CG;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = 2;
     ProfScope ps(ctx, s, PK_GEMM);
     cudaError_t e = cudaLaunchKernelEx(&cfg, kern, gp, ep);
     ctx->launches++;
@@ -969,13 +974,15 @@ tk_status launch_gemm_pair(tk_ctx* ctx, const GemmDesc& g0, const GemmDesc& g1, 
     cfg.blockDim = dim3(GEMM_THREADS, 1, 1);
     cfg.dynamicSmemBytes = G::SMEM;
     cfg.stream = s;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = 2;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = 2;
     ProfScope ps(ctx, s, PK_GEMM);
     cudaError_t e = cudaLaunchKernelEx(&cfg, kern, pp);
     ctx->launches++;
