@@ -1240,6 +1240,7 @@ def measure_c4(ctx, steps, two_pass=False):
         if two_pass:
             rmax, rsum, amax, tgt = head.stats(X, labels, mask)
             res["loss"] = head.loss(T, labels, mask, rmax, rsum, amax, tgt)[0]
+            dX.zero_()                     # pass 2 accumulates (the reference's dX += per chunk)
             head.grad(X, labels, mask, n_loss, rmax, rsum, dX=dX)
             res["dX"] = dX
         else:

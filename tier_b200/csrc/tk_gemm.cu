@@ -43,6 +43,7 @@
 // the roles drain out instead of hanging.
 #include <cuda.h>
 #include <cuda_runtime.h>
+#include <cmath>
 #include <mutex>
 #include <queue>
 #include <vector>
@@ -80,6 +81,7 @@ struct __align__(64) GemmParams {
     int nprod;
     int pa[3], pb[3];
     int tiles_m, tiles_n;  // in tiles of (128 * CG) x bn
+    int group_m;           // tile order: bands of group_m tile rows, each swept over every tile column
     int bn;                // tile width (output columns): 256, 224, 192 or 128
     int seg_kb;            // k-blocks per accumulation segment (>= 1)
     int splits;            // K splits per tile: 1 or 2 (work unit = tile x split)
@@ -128,6 +130,22 @@ __device__ __forceinline__ int ld_acquire_gpu(const int* p) {
     int v;
     asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
     return v;
+}
+
+// Output tile t -> (tile row mb, tile column nb).  Tiles run in bands of
+// group_m tile rows; inside a band the row index runs fastest.  The tiles in
+// flight at once then form a group_m x (groups / group_m) block, so every A
+// panel (a tile row's operand over all of K) and every B panel is shared by
+// several concurrent tiles, and a band's A panels stay in L2 while it sweeps
+// the columns.  group_m = tiles_m is plain row-fastest order.
+__device__ __forceinline__ void tile_coords(const GemmParams& p, int tile, int& mb, int& nb) {
+    const int per_band = p.group_m * p.tiles_n;
+    const int band = tile / per_band;
+    const int m0 = band * p.group_m;
+    const int gm = p.tiles_m - m0 < p.group_m ? p.tiles_m - m0 : p.group_m;
+    const int r = tile - band * per_band;
+    mb = m0 + r % gm;
+    nb = r / gm;
 }
 
 // A work unit: problem, output tile, K split.
@@ -243,7 +261,8 @@ __device__ __forceinline__ void gemm_body(const GemmParams* ps, const EpiParams*
                 const bool bmn = BMODE == 2 ? p.b_mn != 0 : BMODE == 1;
                 const int kblocks = (p.K + BK - 1) / BK;
                 const int kb_per_split = (kblocks + p.splits - 1) / p.splits;
-                const int mb = un.tile % p.tiles_m, nb = un.tile / p.tiles_m;
+                int mb, nb;
+                tile_coords(p, un.tile, mb, nb);
                 const int arow = (mb * CG + (int)rank) * BM;
                 const int brows = p.bn / CG;                          // B rows this CTA loads
                 const int bcol = nb * p.bn + (int)rank * brows;
@@ -351,7 +370,8 @@ __device__ __forceinline__ void gemm_body(const GemmParams* ps, const EpiParams*
           const Unit un = unit_of<NPROB>(ps, ur.unit(j));
           const GemmParams& p = ps[un.prob];
           const int tile = un.tile, sp = un.sp;
-          const int mb = tile % p.tiles_m, nb = tile / p.tiles_m;
+          int mb, nb;
+          tile_coords(p, tile, mb, nb);
           const int kblocks = (p.K + BK - 1) / BK;
           const int kb_per_split = (kblocks + p.splits - 1) / p.splits;
           const int kbs = sp * kb_per_split, kbe = kbs + kb_per_split < kblocks ? kbs + kb_per_split : kblocks;
@@ -505,8 +525,16 @@ __device__ __forceinline__ void gemm_body(const GemmParams* ps, const EpiParams*
                 }
             } else if constexpr (EPI == EPI_LSE) {
                 // Per (row, tile) partial statistics of the softcapped logits:
-                // max, lowest index of the max, sum exp(l - max) in fp64, and
-                // the label's logit when the label falls in this tile.
+                // max, lowest index of the max, sum exp(l - max), and the
+                // label's logit when the label falls in this tile.  The
+                // reference (lse_chunk_kernel, tier/tier.cpp:750-759) takes
+                // every exp in fp64; here each term is an fp32 expf of l - max
+                // <= 0 (relative error ~2^-22), a 32-column chunk's terms are
+                // added pairwise in fp32 and the chunk sums in fp64.  With
+                // one epilogue warp per SM sub-partition the fp64 exps were
+                // the launch's limiter (math-pipe throttle the top stall, the
+                // tensor pipe 46 % busy); the single-pass head already scales
+                // its probabilities with the same fp32 expf (lm_prob_kernel).
                 const LseDesc& L = ep->lse;
                 const int label = row_ok ? L.labels[row + 1] - L.v0 : -1;
                 float mx = -1e30f;
@@ -542,9 +570,15 @@ __device__ __forceinline__ void gemm_body(const GemmParams* ps, const EpiParams*
                         mx = cm;
                         arg = ci;
                     }
+                    float e[32];
 #pragma unroll
-                    for (int j = 0; j < 32; ++j)
-                        if (col0 + j < p.N) sum += exp((double)v[j] - (double)mx);
+                    for (int j = 0; j < 32; ++j) e[j] = expf(v[j] - mx);   // columns past N: exp(-inf) = 0
+#pragma unroll
+                    for (int w = 16; w >= 1; w >>= 1) {
+#pragma unroll
+                        for (int j = 0; j < w; ++j) e[j] += e[j + w];
+                    }
+                    sum += (double)e[0];
                 }
                 if (row_ok) {
                     const size_t o = (size_t)row * L.ld_part + nb;
@@ -577,7 +611,8 @@ __device__ __forceinline__ void gemm_body(const GemmParams* ps, const EpiParams*
                         if (live) {
                             float l = __uint_as_float(r[j]) * f;
                             if (G.cap > 0.0f) l = G.cap * tanhf(l / G.cap);
-                            const double sm = exp((double)l - lse);
+                            // fp32 exp of l - lse <= 0, as in the LSE epilogue above
+                            const double sm = (double)expf((float)((double)l - lse));
                             const double oh = (col0 + j == label) ? 1.0 : 0.0;
                             const float y = G.cap > 0.0f ? l / G.cap : 0.0f;
                             d = (float)((sm - oh) / G.n_loss) * (1.0f - y * y) * mval;
@@ -756,6 +791,25 @@ static tk_status build(const GemmDesc& g, tk_ctx* ctx, GemmParams& gp, int cg, i
     gp.tiles_m = (g.M + BM * cg - 1) / (BM * cg);
     gp.tiles_n = (g.N + bn - 1) / bn;
     gp.bn = bn;
+    {
+        // Band height: the in-flight block a x b (a x b = CTA groups) that
+        // reads the fewest operand bytes per k-step, a * A panel + b * B panel,
+        // is a = sqrt(groups * B panel / A panel).  Measured on B200 with plain
+        // row-fastest order: the LM-head logits GEMM (A = three X planes over
+        // 32 tile rows, 189 MB) read 7.1 GB from DRAM per 315 MB of operands.
+        int na = 0, nb_ = 0;
+        for (int i = 0; i < 3; ++i) na += g.A[i] != nullptr;
+        for (int i = 0; i < 2; ++i) nb_ += g.B[i] != nullptr;
+        const double groups = (double)(ctx->num_sms / cg);
+        const double a = std::sqrt(groups * (double)(bn * nb_) / (double)(BM * cg * (na > 0 ? na : 1)));
+        int gm = (int)(a + 0.5);
+        // every A panel fits in L2 at once (<= 48 MB): row-fastest order reads
+        // A and B once (the C2 forward, X 32 MB); measured on the C2 step the
+        // band choices agree within 1 %, except 4-row bands (3 % slower)
+        const double a_all = (double)gp.tiles_m * BM * cg * (double)g.K * 2.0 * (na > 0 ? na : 1);
+        if (a_all <= 48.0 * 1048576.0) gm = gp.tiles_m;
+        gp.group_m = gm < 1 ? 1 : (gm > gp.tiles_m ? gp.tiles_m : gm);
+    }
     gp.splits = 1;
     gp.flags = nullptr;
     gp.epoch = 0;
